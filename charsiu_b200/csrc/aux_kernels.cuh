@@ -1,0 +1,174 @@
+// SPDX-License-Identifier: GPL-2.0-or-later
+// The smaller kernels: the load-time repack, the activation quantiser, the
+// block-dot test hook, and the CUDA-core int8 matmul with the output stage.
+#pragma once
+
+#include "layout.h"
+#include "ptx.cuh"
+
+namespace cgpu {
+
+// GGUF blocks -> the layout of layout.h. raw holds `nrows` rows of this GPU's
+// slab starting at slab row `row0`; one thread per (row, block). The layout
+// buffer was zeroed first, which is what the padding rows need.
+__global__ void repack_kernel(const uint8_t *__restrict__ raw, uint32_t type, uint32_t nb,
+			      uint32_t row0, uint32_t nrows, uint8_t *__restrict__ dst)
+{
+	const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+	if (idx >= (uint64_t)nrows * nb)
+		return;
+	const uint32_t rl = (uint32_t)(idx / nb), b = (uint32_t)(idx % nb);
+	const uint32_t r = row0 + rl, g = r / RG, rr = r % RG;
+	const uint32_t seg = b / SB, bi = b % SB, sb = seg_blocks(nb, seg);
+	const uint32_t qb = quant_bytes(type), bsz = qb + 2;
+	const uint8_t *src = raw + ((uint64_t)rl * nb + b) * bsz;
+	uint8_t *segp = dst + (uint64_t)g * group_bytes(type, nb) + seg_offset(type, seg);
+	uint8_t *qd = segp + ((uint64_t)bi * RG + rr) * qb;
+	uint8_t *dd = segp + (uint64_t)sb * RG * qb + ((uint64_t)bi * RG + rr) * 2;
+
+	for (uint32_t j = 0; j < qb; j++)
+		qd[j] = src[2 + j];
+	dd[0] = src[0];
+	dd[1] = src[1];
+}
+
+// The integer block dots of rows [0, rows), read back out of the layout: the
+// test hook that pins both the repack and the dot against dotq_*'s t.
+__global__ void block_dots_kernel(const uint8_t *__restrict__ data, uint32_t type,
+				  uint32_t rows, uint32_t nb, const int8_t *__restrict__ q,
+				  int32_t *__restrict__ dots)
+{
+	const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+	if (idx >= (uint64_t)rows * nb)
+		return;
+	const uint32_t r = (uint32_t)(idx / nb), b = (uint32_t)(idx % nb);
+	const uint32_t g = r / RG, rr = r % RG, seg = b / SB, bi = b % SB;
+	const uint32_t qb = quant_bytes(type);
+	const uint8_t *qp = data + (uint64_t)g * group_bytes(type, nb) + seg_offset(type, seg) +
+			    ((uint64_t)bi * RG + rr) * qb;
+	const int8_t *x = q + (uint64_t)b * 32;
+	int t = 0;
+
+	if (type == TYPE_Q8_0) {
+		for (int j = 0; j < 32; j++)
+			t += (int)(int8_t)qp[j] * x[j];
+	} else {
+		for (int j = 0; j < 16; j++) {
+			t += ((qp[j] & 0x0f) - 8) * x[j];
+			t += ((qp[j] >> 4) - 8) * x[j + 16];
+		}
+	}
+	dots[idx] = t;
+}
+
+// charsiu_act_set (reference src/gguf.c:852-881) for m rows of k: one warp
+// per 32-element block. amax is a max, so any reduction order gives the same
+// float; d = amax / 127 and 1 / d are IEEE divisions; the quant is
+// round-to-nearest-even of v * (1 / d), as lrintf.
+__global__ void act_quantise_kernel(const float *__restrict__ x, uint32_t m, uint32_t k,
+				    uint32_t nb, int8_t *__restrict__ q, float *__restrict__ d)
+{
+	const uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+	const int lane = threadIdx.x & 31;
+	if (w >= (uint64_t)m * nb)
+		return;
+	const uint32_t row = (uint32_t)(w / nb), b = (uint32_t)(w % nb);
+	const uint32_t i = b * 32 + lane;
+	const float v = i < k ? x[(uint64_t)row * k + i] : 0.0f;
+	float amax = fabsf(v);
+
+	for (int o = 16; o; o >>= 1)
+		amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+	const float dd = __fdiv_rn(amax, 127.0f);
+	const float inv = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+	q[(uint64_t)row * nb * 32 + i] = (int8_t)__float2int_rn(__fmul_rn(v, inv));
+	if (lane == 0)
+		d[(uint64_t)row * nb + b] = dd;
+}
+
+// ---- the int8 matmul with the NPU's output stage -----------------------------
+//
+// acc = bias + sum_k (a - zp_a)(w - zp_w), a and w unsigned bytes. With
+// a_s = a - 128 and w_s = w - 128 (signed bytes):
+//   sum (a - zp_a)(w - zp_w) = sum a_s w_s + (128 - zp_w) sum a_s
+//                              + (128 - zp_a) sum w_s + K (128 - zp_a)(128 - zp_w)
+// the same zero-point folding the NPU's coefficient buffer does
+// (reference src/job.c:298-303, 344).
+//
+// Output stage: the reference's cpu_reference (tools/charsiu_matmul.c:64-77)
+//   v = (float)acc * mult + (float)zp_out;  rq = floor(v + 0.5)
+// and the NPU's form (src/job.c:137-177) out = clamp(max(rq + L, 0) + O,
+// -128, 127) with the lift L = 128 taken in the requant domain and the offset
+// O = -128 (zp_out already inside rq). For rq >= -128 the floor never binds
+// and out = clamp(rq); below it both forms give -128. So the two are the same
+// function, computed here with the reference's roundings.
+__device__ __forceinline__ int8_t output_stage(int64_t acc, float mult, float zp_out)
+{
+	const float v = __fadd_rn(__fmul_rn(__ll2float_rn(acc), mult), zp_out);
+	const float rq = floorf(__fadd_rn(v, 0.5f));
+	float o = fmaxf(__fadd_rn(rq, 128.0f), 0.0f);     // the fused floor, after the lift
+	o = __fadd_rn(o, -128.0f);                        // the offset takes the lift back
+	o = fminf(fmaxf(o, -128.0f), 127.0f);
+	return (int8_t)__float2int_rz(o);
+}
+
+struct I8Params {
+	const uint8_t *a, *w;
+	const int32_t *bias;
+	int8_t *out;
+	uint32_t m, k, n;
+	float mult, zp_out;
+	int zp_a, zp_w;
+};
+
+// CUDA cores, dp4a: a 32 (m) x 32 (n) tile per 256-thread CTA, K in steps of
+// 64 through shared memory; each thread keeps 4 m rows of one column.
+constexpr int I8_TK = 64;
+constexpr int I8_PAD = I8_TK + 4;
+
+__global__ void __launch_bounds__(256) i8mm_simt_kernel(const __grid_constant__ I8Params p)
+{
+	__shared__ __align__(16) int8_t As[32][I8_PAD];
+	__shared__ __align__(16) int8_t Ws[32][I8_PAD];
+	const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+	const uint32_t m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+	int acc[4] = {0, 0, 0, 0}, sa[4] = {0, 0, 0, 0}, sw = 0;
+
+	for (uint32_t k0 = 0; k0 < p.k; k0 += I8_TK) {
+		for (int i = threadIdx.x; i < 32 * I8_TK; i += 256) {
+			const int rr = i / I8_TK, kk = i % I8_TK;
+			const uint32_t gk = k0 + kk;
+			const uint32_t ma = m0 + rr, nw = n0 + rr;
+			As[rr][kk] = (ma < p.m && gk < p.k) ? (int8_t)(p.a[(uint64_t)ma * p.k + gk] ^ 0x80) : 0;
+			Ws[rr][kk] = (nw < p.n && gk < p.k) ? (int8_t)(p.w[(uint64_t)nw * p.k + gk] ^ 0x80) : 0;
+		}
+		__syncthreads();
+#pragma unroll 4
+		for (int kk = 0; kk < I8_TK; kk += 4) {
+			const uint32_t wv = *reinterpret_cast<const uint32_t *>(&Ws[tx][kk]);
+			sw = dp4a_ss(wv, 0x01010101u, sw);
+#pragma unroll
+			for (int j = 0; j < 4; j++) {
+				const uint32_t av = *reinterpret_cast<const uint32_t *>(&As[ty + 8 * j][kk]);
+				acc[j] = dp4a_ss(av, wv, acc[j]);
+				sa[j] = dp4a_ss(av, 0x01010101u, sa[j]);
+			}
+		}
+		__syncthreads();
+	}
+	const uint32_t col = n0 + tx;
+	if (col >= p.n)
+		return;
+	const int64_t ca = 128 - p.zp_a, cw = 128 - p.zp_w;
+#pragma unroll
+	for (int j = 0; j < 4; j++) {
+		const uint32_t row = m0 + ty + 8 * j;
+		if (row >= p.m)
+			continue;
+		const int64_t total = (int64_t)p.bias[col] + acc[j] + cw * sa[j] + ca * sw +
+				      (int64_t)p.k * ca * cw;
+		p.out[(uint64_t)row * p.n + col] = output_stage(total, p.mult, p.zp_out);
+	}
+}
+
+} // namespace cgpu

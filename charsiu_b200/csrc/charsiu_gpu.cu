@@ -1,0 +1,843 @@
+// SPDX-License-Identifier: GPL-2.0-or-later
+// The GPU device layer: the host side of include/charsiu_gpu.h.
+//
+// It plays the part src/npudev.c plays for the NPU: it owns the device, the
+// repacked weights and the staging buffers, turns one projection (or a group
+// of projections of one activation) into one kernel launch, waits with a
+// deadline, keeps the time split, retires itself after three slow or failed
+// calls, and says so.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <ctime>
+#include <string>
+#include <vector>
+
+#include "charsiu_gpu.h"
+
+#include "aux_kernels.cuh"
+#include "qmv.cuh"
+#include "ref_abi.h"
+
+using namespace cgpu;
+
+namespace {
+
+double now_us()
+{
+	timespec t;
+	clock_gettime(CLOCK_MONOTONIC, &t);
+	return (double)t.tv_sec * 1e6 + (double)t.tv_nsec / 1e3;
+}
+
+unsigned env_u(const char *name, unsigned dflt)
+{
+	const char *e = getenv(name);
+	return e ? (unsigned)strtoul(e, nullptr, 0) : dflt;
+}
+
+struct Ent {
+	const void *key;          // the caller's gguf_tensor, for re-adds
+	char name[80];
+	uint32_t type, nb;
+	uint64_t k, n;            // the whole tensor
+	uint64_t row0, rows;      // this GPU's slab
+	uint32_t groups;
+	uint8_t *data;
+	size_t bytes;
+	double weight_mb;         // of this GPU's slab
+};
+
+template <typename T>
+bool grow_dev(T *&p, size_t &cap, size_t want)
+{
+	if (want <= cap)
+		return true;
+	if (p)
+		cudaFree(p);
+	p = nullptr;
+	cap = 0;
+	if (cudaMalloc(&p, want * sizeof(T)) != cudaSuccess)
+		return false;
+	cap = want;
+	return true;
+}
+
+template <typename T>
+bool grow_host(T *&p, size_t &cap, size_t want)
+{
+	if (want <= cap)
+		return true;
+	if (p)
+		cudaFreeHost(p);
+	p = nullptr;
+	cap = 0;
+	if (cudaHostAlloc(&p, want * sizeof(T), cudaHostAllocDefault) != cudaSuccess)
+		return false;
+	cap = want;
+	return true;
+}
+
+} // namespace
+
+struct charsiu_gpu {
+	int device = 0;
+	unsigned rank = 0, world = 1, max_k = 0, max_n = 0, max_tensors = 0;
+	int sm_count = 0;
+	cudaStream_t stream = nullptr;
+	cudaEvent_t ev_k0 = nullptr, ev_k1 = nullptr, ev_done = nullptr;
+	std::vector<Ent> ent;
+
+	int8_t *d_q = nullptr, *h_q = nullptr;
+	float *d_d = nullptr, *h_d = nullptr, *d_y = nullptr, *h_y = nullptr;
+	size_t cap_dq = 0, cap_hq = 0, cap_dd = 0, cap_hd = 0, cap_dy = 0, cap_hy = 0;
+	uint8_t *d_i8 = nullptr, *h_i8 = nullptr;
+	size_t cap_di8 = 0, cap_hi8 = 0;
+	int32_t *d_dots = nullptr;
+	size_t cap_dots = 0;
+	int *d_err = nullptr;
+	bool smem_set[QMV_MAX_M + 1] = {};
+
+	unsigned long calls = 0, launches = 0, call_no = 0;
+	double busy_us = 0, h2d_us = 0, kern_ms = 0, d2h_us = 0, weight_mb = 0;
+	double slow_us = 100000;
+	int strikes = 0, dead = 0, whined = 0;
+	unsigned long inj_at = 0, inj_count = 0;
+	int inj_kind = 0;
+	std::string err;
+};
+
+namespace {
+
+// Say why, once (the reference's whine(), src/npudev.c:124-138): a silent
+// fallback to the CPU produces results that look like GPU evidence.
+void whine(charsiu_gpu *g, const char *fmt, ...)
+{
+	char buf[256];
+	va_list ap;
+	va_start(ap, fmt);
+	vsnprintf(buf, sizeof(buf), fmt, ap);
+	va_end(ap);
+	g->err = buf;
+	if (g->whined)
+		return;
+	g->whined = 1;
+	fprintf(stderr, "charsiu: NOT on the GPU -- %s\n", buf);
+}
+
+bool injected(charsiu_gpu *g, int kind)
+{
+	return g->inj_kind == kind && g->inj_count && g->call_no >= g->inj_at &&
+	       g->call_no < g->inj_at + g->inj_count;
+}
+
+void retire(charsiu_gpu *g, const char *why)
+{
+	if (g->dead)
+		return;
+	g->dead = 1;
+	g->strikes = 3;
+	fprintf(stderr, "charsiu: the GPU path is retired (%s); everything from here "
+			"runs on the CPU\n", why);
+}
+
+// Wait for ev_done with the reference's budget: CHARSIU_GPU_SLOW_US plus a
+// millisecond a megabyte (src/npudev.c:560-573). Slow counts a strike, three
+// in a row retire the layer. A call that has not finished 10 s past its
+// budget retires it at once; its buffers are then never touched again.
+int finish(charsiu_gpu *g, double t0, double mb, unsigned k, unsigned n)
+{
+	const double budget = g->slow_us + mb * 1000.0;
+	cudaError_t e;
+
+	while ((e = cudaEventQuery(g->ev_done)) == cudaErrorNotReady) {
+		if (now_us() - t0 > budget + 10e6) {
+			whine(g, "a call did not finish (K=%u N=%u)", k, n);
+			retire(g, "it stopped answering");
+			return -1;
+		}
+	}
+	if (e != cudaSuccess) {
+		whine(g, "CUDA error %s (K=%u N=%u)", cudaGetErrorString(e), k, n);
+		retire(g, "a CUDA error");
+		return -1;
+	}
+	int derr = 0;
+	cudaMemcpy(&derr, g->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+	if (derr) {
+		cudaMemset(g->d_err, 0, sizeof(int));
+		whine(g, "a kernel wait gave up (K=%u N=%u)", k, n);
+		retire(g, "a kernel wait gave up");
+		return -1;
+	}
+	double took = now_us() - t0;
+	if (injected(g, 2))
+		took = budget + 1.0;
+	if (took > budget) {
+		if (++g->strikes >= 3) {
+			whine(g, "three slow calls in a row (K=%u N=%u)", k, n);
+			retire(g, "it stopped answering in time");
+			return -1;
+		}
+	} else {
+		g->strikes = 0;
+	}
+	return 0;
+}
+
+int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st)
+{
+	const size_t smem = qmv_smem_bytes(m, p.nb);
+	const void *fn = nullptr;
+
+	switch (m) {
+	case 1: fn = (const void *)qmv_kernel<1>; break;
+	case 2: fn = (const void *)qmv_kernel<2>; break;
+	case 4: fn = (const void *)qmv_kernel<4>; break;
+	case 8: fn = (const void *)qmv_kernel<8>; break;
+	default: return -1;
+	}
+	if (!g->smem_set[m]) {
+		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+					 227 * 1024) != cudaSuccess)
+			return -1;
+		g->smem_set[m] = true;
+	}
+	int occ = 0;
+	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, QMV_WARPS * 32, smem) !=
+		    cudaSuccess || occ < 1)
+		return -1;
+	unsigned grid = (unsigned)occ * g->sm_count;
+	if (p.total_groups < grid)
+		grid = p.total_groups ? p.total_groups : 1;
+
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = dim3(grid);
+	cfg.blockDim = dim3(QMV_WARPS * 32);
+	cfg.dynamicSmemBytes = smem;
+	cfg.stream = st;
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = attr;
+	cfg.numAttrs = 1;
+	cudaError_t e;
+	switch (m) {
+	case 1: e = cudaLaunchKernelEx(&cfg, qmv_kernel<1>, p); break;
+	case 2: e = cudaLaunchKernelEx(&cfg, qmv_kernel<2>, p); break;
+	case 4: e = cudaLaunchKernelEx(&cfg, qmv_kernel<4>, p); break;
+	default: e = cudaLaunchKernelEx(&cfg, qmv_kernel<8>, p); break;
+	}
+	if (e != cudaSuccess)
+		return -1;
+	g->launches++;
+	return 0;
+}
+
+int check_ids(charsiu_gpu *g, const int *ids, unsigned n, unsigned k)
+{
+	if (!n || n > QMV_MAX_TENSORS)
+		return -1;
+	for (unsigned i = 0; i < n; i++) {
+		if (ids[i] < 0 || (unsigned)ids[i] >= g->ent.size())
+			return -1;
+		if (g->ent[ids[i]].k != k) {
+			whine(g, "the activation is not this tensor's K (%u vs %llu)", k,
+			      (unsigned long long)g->ent[ids[i]].k);
+			return -1;
+		}
+	}
+	return 0;
+}
+
+// Fill QmvParams for tensors ids[0..n) with outputs at ys[i] (device).
+void fill_params(charsiu_gpu *g, QmvParams &p, const int *ids, unsigned n, float *const *ys,
+		 uint32_t k, const int8_t *q, const float *d)
+{
+	memset(&p, 0, sizeof(p));
+	uint32_t acc = 0;
+	for (unsigned i = 0; i < n; i++) {
+		const Ent &e = g->ent[ids[i]];
+		QmvTensor &t = p.t[i];
+		t.data = e.data;
+		t.y = ys[i];
+		t.type = e.type;
+		t.rows = (uint32_t)e.rows;
+		t.groups = e.groups;
+		acc += e.groups;
+		t.group_end = acc;
+		t.y_stride = (uint32_t)e.rows;
+	}
+	p.ntensor = n;
+	p.total_groups = acc;
+	p.k = k;
+	p.nb = k / 32;
+	p.q = q;
+	p.d = d;
+	p.err = g->d_err;
+}
+
+// The host-pointer matvec: H2D of the activation, one launch per chunk of at
+// most QMV_MAX_M activation rows, D2H of every y, one fence.
+int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, const float *d,
+	       unsigned k, unsigned m, float **ys)
+{
+	g->call_no++;
+	if (g->dead) {
+		whine(g, "the GPU path is already retired");
+		return -1;
+	}
+	if (!q || !d || !ys || !m || k % 32 || check_ids(g, ids, n, k))
+		return -1;
+	if (injected(g, 1)) {
+		whine(g, "the launch failed (injected, K=%u)", k);
+		retire(g, "a launch failed");
+		return -1;
+	}
+	const uint32_t nb = k / 32;
+	size_t ytot = 0;
+	double mb = 0;
+	for (unsigned i = 0; i < n; i++) {
+		ytot += (size_t)m * g->ent[ids[i]].rows;
+		mb += g->ent[ids[i]].weight_mb;
+	}
+	if (!grow_dev(g->d_q, g->cap_dq, (size_t)m * nb * 32) ||
+	    !grow_dev(g->d_d, g->cap_dd, (size_t)m * nb) ||
+	    !grow_dev(g->d_y, g->cap_dy, ytot) ||
+	    !grow_host(g->h_q, g->cap_hq, (size_t)m * nb * 32) ||
+	    !grow_host(g->h_d, g->cap_hd, (size_t)m * nb) ||
+	    !grow_host(g->h_y, g->cap_hy, ytot)) {
+		whine(g, "a staging buffer would not allocate");
+		return -1;
+	}
+
+	const double t0 = now_us();
+	memcpy(g->h_q, q, (size_t)m * nb * 32);
+	memcpy(g->h_d, d, (size_t)m * nb * sizeof(float));
+	cudaMemcpyAsync(g->d_q, g->h_q, (size_t)m * nb * 32, cudaMemcpyHostToDevice, g->stream);
+	cudaMemcpyAsync(g->d_d, g->h_d, (size_t)m * nb * sizeof(float), cudaMemcpyHostToDevice,
+			g->stream);
+	const double t1 = now_us();
+
+	cudaEventRecord(g->ev_k0, g->stream);
+	for (unsigned m0 = 0, mc = 0; m0 < m; m0 += mc) {
+		const unsigned left = m - m0;
+		mc = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+		float *yd[QMV_MAX_TENSORS];
+		size_t off = 0;
+		for (unsigned i = 0; i < n; i++) {
+			yd[i] = g->d_y + off + (size_t)m0 * g->ent[ids[i]].rows;
+			off += (size_t)m * g->ent[ids[i]].rows;
+		}
+		QmvParams p;
+		fill_params(g, p, ids, n, yd, k, g->d_q + (size_t)m0 * nb * 32,
+			    g->d_d + (size_t)m0 * nb);
+		if (launch_qmv(g, (int)mc, p, g->stream)) {
+			whine(g, "the launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+			retire(g, "a launch failed");
+			return -1;
+		}
+	}
+	cudaEventRecord(g->ev_k1, g->stream);
+	cudaMemcpyAsync(g->h_y, g->d_y, ytot * sizeof(float), cudaMemcpyDeviceToHost, g->stream);
+	cudaEventRecord(g->ev_done, g->stream);
+	if (finish(g, t0, mb, k, (unsigned)g->ent[ids[0]].n))
+		return -1;
+	const double t2 = now_us();
+	size_t off = 0;
+	for (unsigned i = 0; i < n; i++) {
+		const size_t cnt = (size_t)m * g->ent[ids[i]].rows;
+		memcpy(ys[i], g->h_y + off, cnt * sizeof(float));
+		off += cnt;
+	}
+	float kms = 0;
+	cudaEventElapsedTime(&kms, g->ev_k0, g->ev_k1);
+	const double t3 = now_us();
+	g->calls++;
+	g->weight_mb += mb;
+	g->h2d_us += t1 - t0;
+	g->kern_ms += kms;
+	g->d2h_us += t3 - t2;
+	g->busy_us += t3 - t0;
+	return 0;
+}
+
+} // namespace
+
+extern "C" {
+
+struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned max_tensors,
+					int device, unsigned rank, unsigned world)
+{
+	int ndev = 0;
+	if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+		fprintf(stderr, "charsiu: no CUDA device %d\n", device);
+		return nullptr;
+	}
+	if (!world || rank >= world || !max_k || max_k % 32 || !max_tensors)
+		return nullptr;
+	cudaDeviceProp prop;
+	if (cudaSetDevice(device) != cudaSuccess ||
+	    cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+		return nullptr;
+	if (prop.major != 10 || prop.minor != 0) {
+		fprintf(stderr, "charsiu: device %d is sm_%d%d; this build is sm_100a only\n",
+			device, prop.major, prop.minor);
+		return nullptr;
+	}
+	charsiu_gpu *g = new charsiu_gpu;
+	g->device = device;
+	g->rank = rank;
+	g->world = world;
+	g->max_k = max_k;
+	g->max_n = max_n;
+	g->max_tensors = max_tensors;
+	g->sm_count = prop.multiProcessorCount;
+	g->slow_us = (double)env_u("CHARSIU_GPU_SLOW_US", 100000);
+	g->ent.reserve(max_tensors);
+	if (cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking) != cudaSuccess ||
+	    cudaEventCreate(&g->ev_k0) != cudaSuccess || cudaEventCreate(&g->ev_k1) != cudaSuccess ||
+	    cudaEventCreateWithFlags(&g->ev_done, cudaEventDisableTiming) != cudaSuccess ||
+	    cudaMalloc(&g->d_err, sizeof(int)) != cudaSuccess ||
+	    cudaMemset(g->d_err, 0, sizeof(int)) != cudaSuccess) {
+		charsiu_gpu_close(g);
+		return nullptr;
+	}
+	const size_t nb = max_k / 32;
+	if (!grow_dev(g->d_q, g->cap_dq, nb * 32) || !grow_dev(g->d_d, g->cap_dd, nb) ||
+	    !grow_dev(g->d_y, g->cap_dy, (size_t)max_n + 64) ||
+	    !grow_host(g->h_q, g->cap_hq, nb * 32) || !grow_host(g->h_d, g->cap_hd, nb) ||
+	    !grow_host(g->h_y, g->cap_hy, (size_t)max_n + 64)) {
+		charsiu_gpu_close(g);
+		return nullptr;
+	}
+	return g;
+}
+
+struct charsiu_gpu *charsiu_gpu_open(unsigned max_k, unsigned max_n, unsigned max_tensors)
+{
+	return charsiu_gpu_open_ex(max_k, max_n, max_tensors, 0, 0, 1);
+}
+
+void charsiu_gpu_close(struct charsiu_gpu *g)
+{
+	if (!g)
+		return;
+	cudaSetDevice(g->device);
+	if (!g->dead && g->stream)
+		cudaStreamSynchronize(g->stream);
+	for (Ent &e : g->ent)
+		if (e.data)
+			cudaFree(e.data);
+	cudaFree(g->d_q);
+	cudaFree(g->d_d);
+	cudaFree(g->d_y);
+	cudaFree(g->d_i8);
+	cudaFree(g->d_dots);
+	cudaFree(g->d_err);
+	cudaFreeHost(g->h_q);
+	cudaFreeHost(g->h_d);
+	cudaFreeHost(g->h_y);
+	cudaFreeHost(g->h_i8);
+	if (g->ev_k0)
+		cudaEventDestroy(g->ev_k0);
+	if (g->ev_k1)
+		cudaEventDestroy(g->ev_k1);
+	if (g->ev_done)
+		cudaEventDestroy(g->ev_done);
+	if (g->stream)
+		cudaStreamDestroy(g->stream);
+	delete g;
+}
+
+int charsiu_gpu_add_blocks(struct charsiu_gpu *g, uint32_t type, uint64_t k, uint64_t n,
+			   const void *blocks, const char *name)
+{
+	if (!g)
+		return -1;
+	g->call_no++;
+	if (g->dead) {
+		whine(g, "the GPU path is already retired");
+		return -1;
+	}
+	if (type != TYPE_Q8_0 && type != TYPE_Q4_0) {
+		whine(g, "type %u is not q8_0 or q4_0 (%s)", type, name ? name : "?");
+		return -1;
+	}
+	if (!blocks || !k || k % 32 || !n || k > g->max_k) {
+		whine(g, "K=%llu is not a multiple of 32 within the opened maximum (%s)",
+		      (unsigned long long)k, name ? name : "?");
+		return -1;
+	}
+	if (n > g->max_n) {
+		whine(g, "wider than the device was opened for (N=%llu, %s)",
+		      (unsigned long long)n, name ? name : "?");
+		return -1;
+	}
+	if (g->ent.size() >= g->max_tensors) {
+		whine(g, "no tensor slots left");
+		return -1;
+	}
+	cudaSetDevice(g->device);
+
+	Ent e;
+	memset(&e, 0, sizeof(e));
+	snprintf(e.name, sizeof(e.name), "%s", name ? name : "");
+	e.type = type;
+	e.k = k;
+	e.n = n;
+	e.nb = (uint32_t)(k / 32);
+	const uint64_t gtot = (n + RG - 1) / RG;
+	const uint64_t per = (gtot + g->world - 1) / g->world;
+	const uint64_t g0 = per * g->rank, g1 = g0 + per < gtot ? g0 + per : gtot;
+	e.row0 = g0 * RG < n ? g0 * RG : n;
+	const uint64_t rend = g1 * RG < n ? g1 * RG : n;
+	e.rows = rend > e.row0 ? rend - e.row0 : 0;
+	e.groups = (uint32_t)((e.rows + RG - 1) / RG);
+	e.bytes = (size_t)e.groups * group_bytes(type, e.nb);
+	const uint64_t rb = (uint64_t)e.nb * (quant_bytes(type) + 2);
+	e.weight_mb = (double)e.rows * rb / 1e6;
+
+	if (injected(g, 3) || (e.bytes && cudaMalloc(&e.data, e.bytes) != cudaSuccess)) {
+		e.data = nullptr;
+		whine(g, "a weight buffer would not allocate (%s, %.1f MB)", e.name, e.bytes / 1e6);
+		return -1;
+	}
+	if (e.bytes) {
+		uint8_t *stage = nullptr;
+		const uint64_t chunk_rows = ((64ull << 20) / rb) & ~(uint64_t)(RG - 1);
+		const uint64_t cr = chunk_rows ? chunk_rows : RG;
+		const size_t sbytes = (size_t)(cr < e.rows ? cr : e.rows) * rb;
+		bool ok = cudaMemsetAsync(e.data, 0, e.bytes, g->stream) == cudaSuccess &&
+			  cudaMalloc(&stage, sbytes) == cudaSuccess;
+		const uint8_t *src = static_cast<const uint8_t *>(blocks) + e.row0 * rb;
+		for (uint64_t r0 = 0; ok && r0 < e.rows; r0 += cr) {
+			const uint64_t nr = e.rows - r0 < cr ? e.rows - r0 : cr;
+			ok = cudaMemcpyAsync(stage, src + r0 * rb, nr * rb, cudaMemcpyHostToDevice,
+					     g->stream) == cudaSuccess;
+			const uint64_t thr = nr * e.nb;
+			repack_kernel<<<(unsigned)((thr + 255) / 256), 256, 0, g->stream>>>(
+				stage, type, e.nb, (uint32_t)r0, (uint32_t)nr, e.data);
+			ok = ok && cudaGetLastError() == cudaSuccess &&
+			     cudaStreamSynchronize(g->stream) == cudaSuccess;
+		}
+		if (stage)
+			cudaFree(stage);
+		if (!ok) {
+			cudaFree(e.data);
+			whine(g, "the weight upload failed (%s)", e.name);
+			return -1;
+		}
+	}
+	g->ent.push_back(e);
+	return (int)g->ent.size() - 1;
+}
+
+int charsiu_gpu_add(struct charsiu_gpu *g, const struct gguf_tensor *w)
+{
+	if (!g || !w)
+		return -1;
+	for (size_t i = 0; i < g->ent.size(); i++)
+		if (g->ent[i].key == (const void *)w)
+			return (int)i;
+	const RefGgufTensor *t = reinterpret_cast<const RefGgufTensor *>(w);
+	uint64_t rows = 1;
+	for (unsigned d = 1; d < t->n_dims && d < 4; d++)
+		rows *= t->ne[d];
+	const int id = charsiu_gpu_add_blocks(g, t->type, t->ne[0], rows, t->data, t->name);
+	if (id >= 0)
+		g->ent[id].key = w;
+	return id;
+}
+
+int charsiu_gpu_rows(const struct charsiu_gpu *g, int id, uint64_t *row0, uint64_t *nrows)
+{
+	if (!g || id < 0 || (size_t)id >= g->ent.size())
+		return -1;
+	if (row0)
+		*row0 = g->ent[id].row0;
+	if (nrows)
+		*nrows = g->ent[id].rows;
+	return 0;
+}
+
+int charsiu_gpu_matvec_q(struct charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q,
+			 const float *d, unsigned k, float **ys)
+{
+	if (!g)
+		return -1;
+	cudaSetDevice(g->device);
+	return run_matvec(g, ids, n, q, d, k, 1, ys);
+}
+
+int charsiu_gpu_matvec(struct charsiu_gpu *g, int id, const struct charsiu_act *a, float *y)
+{
+	if (!g || !a)
+		return -1;
+	const RefAct *act = reinterpret_cast<const RefAct *>(a);
+	if (!act->quantised) {
+		whine(g, "the activation is not quantised (CHARSIU_NO_QACT?)");
+		return -1;
+	}
+	float *ys[1] = {y};
+	return charsiu_gpu_matvec_q(g, &id, 1, act->q, act->d, (unsigned)act->n, ys);
+}
+
+int charsiu_gpu_matvec_group(struct charsiu_gpu *g, const int *ids, unsigned n,
+			     const struct charsiu_act *a, float **ys)
+{
+	if (!g || !a)
+		return -1;
+	const RefAct *act = reinterpret_cast<const RefAct *>(a);
+	if (!act->quantised)
+		return -1;
+	return charsiu_gpu_matvec_q(g, ids, n, act->q, act->d, (unsigned)act->n, ys);
+}
+
+int charsiu_gpu_matvec_batch(struct charsiu_gpu *g, int id, unsigned m, const int8_t *q,
+			     const float *d, unsigned k, float *y)
+{
+	if (!g)
+		return -1;
+	cudaSetDevice(g->device);
+	float *ys[1] = {y};
+	return run_matvec(g, &id, 1, q, d, k, m, ys);
+}
+
+int charsiu_gpu_matvec_dev(struct charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q,
+			   const float *d, float *const *ys, void *stream)
+{
+	if (!g || g->dead || !q || !d || !ys || ((uintptr_t)q & 15) || ((uintptr_t)d & 3))
+		return -1;
+	if (!n || n > QMV_MAX_TENSORS || ids[0] < 0 || (size_t)ids[0] >= g->ent.size())
+		return -1;
+	const unsigned k = (unsigned)g->ent[ids[0]].k;
+	if (check_ids(g, ids, n, k))
+		return -1;
+	cudaSetDevice(g->device);
+	QmvParams p;
+	fill_params(g, p, ids, n, ys, k, q, d);
+	return launch_qmv(g, 1, p, stream ? (cudaStream_t)stream : g->stream);
+}
+
+int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m, const int8_t *q,
+				 const float *d, float *y, void *stream)
+{
+	if (!g || g->dead || !q || !d || !y || !m || ((uintptr_t)q & 15))
+		return -1;
+	if (id < 0 || (size_t)id >= g->ent.size())
+		return -1;
+	cudaSetDevice(g->device);
+	const Ent &e = g->ent[id];
+	const uint32_t nb = e.nb;
+	cudaStream_t st = stream ? (cudaStream_t)stream : g->stream;
+	for (unsigned m0 = 0; m0 < m;) {
+		const unsigned left = m - m0;
+		const unsigned mc = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+		float *yd[1] = {y + (size_t)m0 * e.rows};
+		QmvParams p;
+		fill_params(g, p, &id, 1, yd, (uint32_t)e.k, q + (size_t)m0 * nb * 32,
+			    d + (size_t)m0 * nb);
+		if (launch_qmv(g, (int)mc, p, st))
+			return -1;
+		m0 += mc;
+	}
+	return 0;
+}
+
+int charsiu_gpu_act_quantise_dev(struct charsiu_gpu *g, const float *x, unsigned m, unsigned k,
+				 int8_t *q, float *d, void *stream)
+{
+	if (!g || g->dead || !x || !q || !d || !m || !k)
+		return -1;
+	cudaSetDevice(g->device);
+	const uint32_t nb = (k + 31) / 32;
+	const uint64_t threads = (uint64_t)m * nb * 32;
+	act_quantise_kernel<<<(unsigned)((threads + 255) / 256), 256, 0,
+			      stream ? (cudaStream_t)stream : g->stream>>>(x, m, k, nb, q, d);
+	if (cudaGetLastError() != cudaSuccess)
+		return -1;
+	g->launches++;
+	return 0;
+}
+
+int charsiu_gpu_matmul_i8_flat(struct charsiu_gpu *g, unsigned m, unsigned k, unsigned n,
+			       const uint8_t *a, const uint8_t *w, const int32_t *bias,
+			       float in_scale, float wt_scale, float out_scale, int in_zp,
+			       int wt_zp, int out_zp, int8_t *out)
+{
+	if (!g)
+		return -1;
+	g->call_no++;
+	if (g->dead) {
+		whine(g, "the GPU path is already retired");
+		return -1;
+	}
+	if (!m || !k || !n || !a || !w || !bias || !out)
+		return -1;
+	if (injected(g, 1)) {
+		whine(g, "the launch failed (injected, M=%u K=%u N=%u)", m, k, n);
+		retire(g, "a launch failed");
+		return -1;
+	}
+	cudaSetDevice(g->device);
+	const size_t sa = (size_t)m * k, sw = (size_t)n * k, sb = (size_t)n * 4;
+	const size_t oa = 0, ow = (sa + 15) & ~(size_t)15, ob = (ow + sw + 15) & ~(size_t)15;
+	const size_t oo = (ob + sb + 15) & ~(size_t)15, total = oo + (size_t)m * n;
+	if (!grow_dev(g->d_i8, g->cap_di8, total) || !grow_host(g->h_i8, g->cap_hi8, total)) {
+		whine(g, "a staging buffer would not allocate");
+		return -1;
+	}
+	const double t0 = now_us();
+	memcpy(g->h_i8 + oa, a, sa);
+	memcpy(g->h_i8 + ow, w, sw);
+	memcpy(g->h_i8 + ob, bias, sb);
+	cudaMemcpyAsync(g->d_i8, g->h_i8, oo, cudaMemcpyHostToDevice, g->stream);
+	const double t1 = now_us();
+
+	I8Params p;
+	p.a = g->d_i8 + oa;
+	p.w = g->d_i8 + ow;
+	p.bias = reinterpret_cast<const int32_t *>(g->d_i8 + ob);
+	p.out = reinterpret_cast<int8_t *>(g->d_i8 + oo);
+	p.m = m;
+	p.k = k;
+	p.n = n;
+	p.mult = in_scale * wt_scale / out_scale;     // tools/charsiu_matmul.c:45
+	p.zp_out = (float)out_zp;
+	p.zp_a = in_zp;
+	p.zp_w = wt_zp;
+	cudaEventRecord(g->ev_k0, g->stream);
+	i8mm_simt_kernel<<<dim3((n + 31) / 32, (m + 31) / 32), 256, 0, g->stream>>>(p);
+	if (cudaGetLastError() != cudaSuccess) {
+		whine(g, "the int8 launch failed");
+		retire(g, "a launch failed");
+		return -1;
+	}
+	g->launches++;
+	cudaEventRecord(g->ev_k1, g->stream);
+	cudaMemcpyAsync(g->h_i8 + oo, g->d_i8 + oo, (size_t)m * n, cudaMemcpyDeviceToHost,
+			g->stream);
+	cudaEventRecord(g->ev_done, g->stream);
+	const double mb = (double)(sa + sw) / 1e6;
+	if (finish(g, t0, mb, k, n))
+		return -1;
+	const double t2 = now_us();
+	memcpy(out, g->h_i8 + oo, (size_t)m * n);
+	float kms = 0;
+	cudaEventElapsedTime(&kms, g->ev_k0, g->ev_k1);
+	const double t3 = now_us();
+	g->calls++;
+	g->weight_mb += mb;
+	g->h2d_us += t1 - t0;
+	g->kern_ms += kms;
+	g->d2h_us += t3 - t2;
+	g->busy_us += t3 - t0;
+	return 0;
+}
+
+int charsiu_gpu_matmul_i8(struct charsiu_gpu *g, const struct charsiu_job *job,
+			  const uint8_t *a, const uint8_t *w, const int32_t *bias, int8_t *out)
+{
+	if (!g || !job)
+		return -1;
+	const RefJob *j = reinterpret_cast<const RefJob *>(job);
+	if (j->mm.wdtype != REF_INT8 || j->mm.adtype != REF_INT8) {
+		whine(g, "only int8 weights and activations (wdtype %d adtype %d)", j->mm.wdtype,
+		      j->mm.adtype);
+		return -1;
+	}
+	if (j->acc_out) {
+		whine(g, "acc_out jobs return the raw accumulator; use the matvec path");
+		return -1;
+	}
+	return charsiu_gpu_matmul_i8_flat(g, j->mm.m, j->mm.k, j->mm.n, a, w, bias, j->input_scale,
+					  j->weight_scale, j->output_scale, j->input_zero_point,
+					  j->weight_zero_point, j->output_zero_point, out);
+}
+
+unsigned long charsiu_gpu_calls(const struct charsiu_gpu *g)
+{
+	return g ? g->calls : 0;
+}
+
+unsigned long charsiu_gpu_launches(const struct charsiu_gpu *g)
+{
+	return g ? g->launches : 0;
+}
+
+const char *charsiu_gpu_error(const struct charsiu_gpu *g)
+{
+	return g ? g->err.c_str() : "no layer";
+}
+
+int charsiu_gpu_dead(const struct charsiu_gpu *g)
+{
+	return g ? g->dead : 1;
+}
+
+// What the device actually did, printed whether it went well or not
+// (src/npudev.c:264-295).
+void charsiu_gpu_report(const struct charsiu_gpu *g)
+{
+	if (!g)
+		return;
+	double mbs = 0;
+	for (const Ent &e : g->ent)
+		mbs += e.weight_mb;
+	fprintf(stderr, "charsiu GPU: device %d (rank %u of %u), %zu tensors (%.1f MB), "
+			"%lu calls, %lu launches, %.2f MB per call%s\n",
+		g->device, g->rank, g->world, g->ent.size(), mbs, g->calls, g->launches,
+		g->calls ? g->weight_mb / (double)g->calls : 0.0,
+		g->dead ? "  (RETIRED: it stopped answering)" : "");
+	if (g->calls)
+		fprintf(stderr,
+			"charsiu GPU: %.1f ms in the device path, %.2f GB/s of weights, %.1f us a "
+			"call\ncharsiu GPU: of that, %.1f ms copying in, %.2f ms in kernels, "
+			"%.1f ms reading back\n",
+			g->busy_us / 1e3, g->weight_mb / g->busy_us * 1e3,
+			g->busy_us / (double)g->calls, g->h2d_us / 1e3, g->kern_ms,
+			g->d2h_us / 1e3);
+	else
+		fprintf(stderr, "charsiu GPU: NOTHING RAN ON THE GPU. Every number in this run "
+				"came from the CPU.\n");
+}
+
+int charsiu_gpu_block_dots(struct charsiu_gpu *g, int id, const int8_t *q, int32_t *dots)
+{
+	if (!g || g->dead || !q || !dots || id < 0 || (size_t)id >= g->ent.size())
+		return -1;
+	cudaSetDevice(g->device);
+	const Ent &e = g->ent[id];
+	const size_t cnt = (size_t)e.rows * e.nb;
+	if (!grow_dev(g->d_q, g->cap_dq, (size_t)e.nb * 32) ||
+	    !grow_dev(g->d_dots, g->cap_dots, cnt ? cnt : 1))
+		return -1;
+	if (cudaMemcpy(g->d_q, q, (size_t)e.nb * 32, cudaMemcpyHostToDevice) != cudaSuccess)
+		return -1;
+	if (cnt) {
+		block_dots_kernel<<<(unsigned)((cnt + 255) / 256), 256, 0, g->stream>>>(
+			e.data, e.type, (uint32_t)e.rows, e.nb, g->d_q, g->d_dots);
+		g->launches++;
+	}
+	if (cudaStreamSynchronize(g->stream) != cudaSuccess ||
+	    cudaMemcpy(dots, g->d_dots, cnt * sizeof(int32_t), cudaMemcpyDeviceToHost) !=
+		    cudaSuccess)
+		return -1;
+	return 0;
+}
+
+int charsiu_gpu_inject(struct charsiu_gpu *g, unsigned long at, unsigned long count, int kind)
+{
+	if (!g || kind < 0 || kind > 3)
+		return -1;
+	g->inj_at = at;
+	g->inj_count = count;
+	g->inj_kind = count ? kind : 0;
+	return 0;
+}
+
+} // extern "C"

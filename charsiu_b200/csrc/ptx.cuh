@@ -1,0 +1,116 @@
+// SPDX-License-Identifier: GPL-2.0-or-later
+// Inline-PTX helpers for sm_100a: mbarriers, the untiled bulk copy engine
+// (global -> this CTA's shared memory, never multicast), programmatic
+// dependent launch, and the mixed-sign dp4a.
+#pragma once
+
+#include <cstdint>
+
+namespace cgpu {
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p)
+{
+	return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+	asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;"
+		     :: "r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init()
+{
+	asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// One arrival that also tells the barrier how many bytes the copy will land.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+	asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+		     :: "r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
+{
+	uint32_t ok;
+	asm volatile("{\n\t.reg .pred p;\n\t"
+		     "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+		     "selp.u32 %0, 1, 0, p;\n\t}"
+		     : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+	return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns()
+{
+	uint64_t t;
+	asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+	return t;
+}
+
+// Wait for phase `parity` of `bar`, for at most `limit_ns`. false: gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+						  uint64_t limit_ns)
+{
+	if (mbar_try_wait(bar, parity))
+		return true;
+	uint64_t t0 = globaltimer_ns();
+	while (!mbar_try_wait(bar, parity))
+		if (globaltimer_ns() - t0 > limit_ns)
+			return false;
+	return true;
+}
+
+// Untiled bulk copy, global -> shared memory of this CTA, completing `bytes`
+// of transaction count on `bar`. dst and src 16-byte aligned, bytes a
+// multiple of 16. No .multicast form anywhere in this library.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+					 uint64_t *bar)
+{
+	asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+		     " [%0], [%1], %2, [%3];"
+		     :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+		     : "memory");
+}
+
+// Order this thread's earlier generic-proxy accesses to shared memory before
+// later async-proxy (bulk copy) writes to it.
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+	asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Programmatic dependent launch: block until the grid this one depends on
+// has completed and its writes are visible; let the next grid start launching.
+__device__ __forceinline__ void pdl_wait()
+{
+	asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_launch_dependents()
+{
+	asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// sum of four (unsigned byte of a) * (signed byte of b), plus c
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)
+{
+	int d;
+	asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+	return d;
+}
+
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c)
+{
+	return __dp4a(static_cast<int>(a), static_cast<int>(b), c);
+}
+
+// fp16 bits -> fp32, exact for every finite value (subnormals included)
+__device__ __forceinline__ float half_bits_to_float(uint16_t h)
+{
+	float f;
+	asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+	return f;
+}
+
+} // namespace cgpu

@@ -1,0 +1,757 @@
+// SPDX-License-Identifier: GPL-2.0-or-later
+/*
+ * charsiu's decode loop with the projections on the GPU layer.
+ *
+ * The CPU steps restate src/llama.c:316-386 and 743-856 operation for
+ * operation (compiled with -std=c11 -ffp-contract=off, so each float op rounds
+ * on its own as in the reference); the activation quantiser restates
+ * charsiu_act_set (src/gguf.c:852-881). Every matmul goes through the C ABI of
+ * include/charsiu_gpu.h with host buffers, exactly as a routed llama.c would
+ * call it, so this file is also the end-to-end measurement of that boundary.
+ */
+#define _POSIX_C_SOURCE 200809L
+
+#include <fcntl.h>
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <time.h>
+#include <unistd.h>
+
+#include "charsiu_gpu_llama.h"
+
+#define API
+
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8 };
+
+/* ---- a GGUF v2/v3 reader (the format src/gguf.c:207-358 reads) ----------- */
+
+struct gt {
+	char name[80];
+	uint64_t ne[4];
+	uint32_t n_dims, type;
+	uint64_t offset;
+	const uint8_t *data;
+};
+
+struct gfile {
+	int fd;
+	const uint8_t *map;
+	size_t size;
+	struct gt *t;
+	uint64_t nt;
+	/* the keys the model needs */
+	char arch[64];
+	uint32_t u[16];
+	int have[16];
+	float f[4];
+	int have_f[4];
+	uint64_t n_tokens;
+};
+
+enum { K_EMBD, K_LAYERS, K_HEAD, K_HEAD_KV, K_FF, K_CTX, K_ROPE_DIM, K_ALIGN, K_NU };
+enum { F_EPS, F_BASE, K_NF };
+
+struct cur {
+	const uint8_t *p, *end;
+	int bad;
+};
+
+static int take(struct cur *c, void *dst, size_t n)
+{
+	if (c->bad || (size_t)(c->end - c->p) < n) {
+		c->bad = 1;
+		return -1;
+	}
+	if (dst)
+		memcpy(dst, c->p, n);
+	c->p += n;
+	return 0;
+}
+
+static uint64_t u64(struct cur *c)
+{
+	uint64_t v = 0;
+	take(c, &v, 8);
+	return v;
+}
+
+static uint32_t u32(struct cur *c)
+{
+	uint32_t v = 0;
+	take(c, &v, 4);
+	return v;
+}
+
+static const char *str(struct cur *c, uint64_t *len)
+{
+	uint64_t n = u64(c);
+	const char *s = (const char *)c->p;
+
+	if (c->bad || (uint64_t)(c->end - c->p) < n) {
+		c->bad = 1;
+		*len = 0;
+		return "";
+	}
+	c->p += n;
+	*len = n;
+	return s;
+}
+
+static size_t vsize(uint32_t t)
+{
+	static const size_t w[13] = { 1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8 };
+	return t < 13 ? w[t] : 0;
+}
+
+static int key_is(const char *k, uint64_t kl, const char *arch, const char *suffix)
+{
+	char full[128];
+
+	snprintf(full, sizeof(full), "%s.%s", arch, suffix);
+	return kl == strlen(full) && !memcmp(k, full, kl);
+}
+
+static uint64_t tensor_bytes(uint32_t type, const uint64_t ne[4])
+{
+	uint64_t n = ne[0] * ne[1] * ne[2] * ne[3];
+
+	switch (type) {
+	case T_F32: return n * 4;
+	case T_F16: return n * 2;
+	case T_Q8_0: return n / 32 * 34;
+	case T_Q4_0: return n / 32 * 18;
+	default: return 0;
+	}
+}
+
+static void gclose(struct gfile *g)
+{
+	free(g->t);
+	if (g->map && g->map != MAP_FAILED)
+		munmap((void *)g->map, g->size);
+	if (g->fd >= 0)
+		close(g->fd);
+	memset(g, 0, sizeof(*g));
+	g->fd = -1;
+}
+
+static int gopen(struct gfile *g, const char *path)
+{
+	static const char *ukeys[K_NU] = {
+		"embedding_length", "block_count", "attention.head_count",
+		"attention.head_count_kv", "feed_forward_length", "context_length",
+		"rope.dimension_count", NULL,
+	};
+	static const char *fkeys[K_NF] = { "attention.layer_norm_rms_epsilon", "rope.freq_base" };
+	struct stat st;
+	struct cur c;
+	uint64_t nkv, off, align = 32;
+	char magic[4];
+	uint32_t ver;
+
+	memset(g, 0, sizeof(*g));
+	strcpy(g->arch, "llama");
+	g->fd = open(path, O_RDONLY);
+	if (g->fd < 0 || fstat(g->fd, &st) < 0 || st.st_size < 24) {
+		fprintf(stderr, "charsiu: cannot read %s\n", path);
+		gclose(g);
+		return -1;
+	}
+	g->size = (size_t)st.st_size;
+	g->map = mmap(NULL, g->size, PROT_READ, MAP_PRIVATE, g->fd, 0);
+	if (g->map == MAP_FAILED) {
+		gclose(g);
+		return -1;
+	}
+	c.p = g->map;
+	c.end = g->map + g->size;
+	c.bad = 0;
+	take(&c, magic, 4);
+	ver = u32(&c);
+	if (memcmp(magic, "GGUF", 4) || ver < 2 || ver > 3) {
+		fprintf(stderr, "charsiu: %s is not GGUF v2/v3\n", path);
+		gclose(g);
+		return -1;
+	}
+	g->nt = u64(&c);
+	nkv = u64(&c);
+	if (c.bad || g->nt > 100000 || nkv > 100000) {
+		gclose(g);
+		return -1;
+	}
+	/* general.architecture comes first in practice, but do not rely on it:
+	 * keep the raw arch-prefixed keys and resolve after the walk */
+	{
+		const uint8_t *kv0 = c.p;
+
+		for (int pass = 0; pass < 2; pass++) {
+			c.p = kv0;
+			for (uint64_t i = 0; i < nkv && !c.bad; i++) {
+				uint64_t kl, sl;
+				const char *k = str(&c, &kl);
+				uint32_t vt = u32(&c);
+
+				if (vt == 8) {
+					const char *s = str(&c, &sl);
+
+					if (pass == 0 && kl == 20 && !memcmp(k, "general.architecture", 20) &&
+					    sl < sizeof(g->arch)) {
+						memcpy(g->arch, s, sl);
+						g->arch[sl] = 0;
+					}
+				} else if (vt == 9) {
+					uint32_t at = u32(&c);
+					uint64_t n = u64(&c);
+
+					if (pass == 1 && kl == 21 && !memcmp(k, "tokenizer.ggml.tokens", 21))
+						g->n_tokens = n;
+					if (vsize(at)) {
+						if (n > (uint64_t)(c.end - c.p) / vsize(at)) {
+							c.bad = 1;
+							break;
+						}
+						c.p += n * vsize(at);
+					} else if (at == 8) {
+						for (uint64_t j = 0; j < n && !c.bad; j++)
+							str(&c, &sl);
+					} else {
+						c.bad = 1;
+					}
+				} else if (vsize(vt)) {
+					uint64_t v = 0;
+					double fv = 0;
+
+					if (vt == 6) {
+						float f32 = 0;
+
+						take(&c, &f32, 4);
+						fv = f32;
+					} else if (vt == 12) {
+						take(&c, &fv, 8);
+					} else {
+						take(&c, &v, vsize(vt));
+					}
+					if (pass == 1) {
+						for (int j = 0; j < K_NU; j++)
+							if (ukeys[j] && key_is(k, kl, g->arch, ukeys[j])) {
+								g->u[j] = (uint32_t)v;
+								g->have[j] = 1;
+							}
+						for (int j = 0; j < K_NF; j++)
+							if (key_is(k, kl, g->arch, fkeys[j])) {
+								g->f[j] = (float)fv;
+								g->have_f[j] = 1;
+							}
+						if (kl == 17 && !memcmp(k, "general.alignment", 17) && v)
+							align = v;
+					}
+				} else {
+					c.bad = 1;
+				}
+			}
+		}
+	}
+	g->t = calloc(g->nt ? g->nt : 1, sizeof(*g->t));
+	if (c.bad || !g->t) {
+		fprintf(stderr, "charsiu: %s: bad key/value section\n", path);
+		gclose(g);
+		return -1;
+	}
+	for (uint64_t i = 0; i < g->nt; i++) {
+		struct gt *t = &g->t[i];
+		uint64_t nl;
+		const char *nm = str(&c, &nl);
+
+		if (nl >= sizeof(t->name))
+			nl = sizeof(t->name) - 1;
+		memcpy(t->name, nm, nl);
+		t->n_dims = u32(&c);
+		if (t->n_dims > 4) {
+			c.bad = 1;
+			break;
+		}
+		t->ne[0] = t->ne[1] = t->ne[2] = t->ne[3] = 1;
+		for (unsigned d = 0; d < t->n_dims; d++)
+			t->ne[d] = u64(&c);
+		t->type = u32(&c);
+		t->offset = u64(&c);
+	}
+	if (c.bad) {
+		gclose(g);
+		return -1;
+	}
+	off = (uint64_t)(c.p - g->map);
+	off = (off + align - 1) / align * align;
+	for (uint64_t i = 0; i < g->nt; i++) {
+		struct gt *t = &g->t[i];
+
+		if (off + t->offset + tensor_bytes(t->type, t->ne) > g->size) {
+			fprintf(stderr, "charsiu: %s runs past the end of the file\n", t->name);
+			gclose(g);
+			return -1;
+		}
+		t->data = g->map + off + t->offset;
+	}
+	return 0;
+}
+
+static const struct gt *gfind(const struct gfile *g, const char *name)
+{
+	for (uint64_t i = 0; i < g->nt; i++)
+		if (!strcmp(g->t[i].name, name))
+			return &g->t[i];
+	return NULL;
+}
+
+/* ---- the model ------------------------------------------------------------ */
+
+enum { P_Q, P_K, P_V, P_O, P_GATE, P_UP, P_DOWN, P_N };
+
+struct layer {
+	const float *attn_norm, *ffn_norm;
+	const struct gt *w[P_N];
+	int id[P_N];
+};
+
+struct charsiu_gpu_llama {
+	struct gfile g;
+	struct charsiu_gpu *dev;
+	uint32_t n_embd, n_layer, n_head, n_head_kv, n_ff, n_vocab, hd;
+	float eps, base;
+	const struct gt *tok, *out;
+	const float *out_norm;
+	int out_id;
+	struct layer *L;
+	int n_ctx, nogroup;
+	float *kcache, *vcache, *x, *xb, *xb2, *hb, *hb2, *q, *k, *v, *att, *logits;
+	int8_t *aq;
+	float *ad;
+};
+
+static float half_to_float(uint16_t h)
+{
+	uint32_t sign = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 0x1f, m = h & 0x3ff, bits;
+	float f;
+
+	if (e == 0x1f) {
+		bits = sign | 0x7f800000u | (m << 13);
+	} else if (e) {
+		bits = sign | ((e + 112u) << 23) | (m << 13);
+	} else if (!m) {
+		bits = sign;
+	} else {
+		int sh = 0;
+
+		while (!(m & 0x400)) {
+			m <<= 1;
+			sh++;
+		}
+		bits = sign | ((uint32_t)(113 - sh) << 23) | ((m & 0x3ff) << 13);
+	}
+	memcpy(&f, &bits, 4);
+	return f;
+}
+
+/* one row to fp32: the embedding lookup (src/gguf.c:1217-1256) */
+static int row_f32(const struct gt *t, uint64_t row, float *dst)
+{
+	uint64_t k = t->ne[0];
+	const uint8_t *p;
+
+	switch (t->type) {
+	case T_F32:
+		memcpy(dst, t->data + row * k * 4, k * 4);
+		return 0;
+	case T_Q8_0:
+		p = t->data + row * (k / 32 * 34);
+		for (uint64_t b = 0; b < k / 32; b++, p += 34) {
+			float d = half_to_float((uint16_t)(p[0] | p[1] << 8));
+
+			for (int j = 0; j < 32; j++)
+				dst[b * 32 + j] = d * (float)(int8_t)p[2 + j];
+		}
+		return 0;
+	case T_Q4_0:
+		p = t->data + row * (k / 32 * 18);
+		for (uint64_t b = 0; b < k / 32; b++, p += 18) {
+			float d = half_to_float((uint16_t)(p[0] | p[1] << 8));
+
+			for (int j = 0; j < 16; j++) {
+				dst[b * 32 + j] = d * (float)((p[2 + j] & 0x0f) - 8);
+				dst[b * 32 + j + 16] = d * (float)((p[2 + j] >> 4) - 8);
+			}
+		}
+		return 0;
+	default:
+		return -1;
+	}
+}
+
+/* charsiu_act_set's q8_0 form (src/gguf.c:852-881) */
+static void act_set(struct charsiu_gpu_llama *m, const float *x, int n)
+{
+	int nb = (n + 31) / 32;
+
+	for (int b = 0; b < nb; b++) {
+		float amax = 0.0f, d, id;
+
+		for (int j = 0; j < 32; j++) {
+			float v = b * 32 + j < n ? x[b * 32 + j] : 0.0f;
+			float av = v < 0.0f ? -v : v;
+
+			if (av > amax)
+				amax = av;
+		}
+		d = amax / 127.0f;
+		id = d != 0.0f ? 1.0f / d : 0.0f;
+		m->ad[b] = d;
+		for (int j = 0; j < 32; j++) {
+			float v = b * 32 + j < n ? x[b * 32 + j] : 0.0f;
+
+			m->aq[b * 32 + j] = (int8_t)lrintf(v * id);
+		}
+	}
+}
+
+static void rmsnorm(float *out, const float *x, const float *gw, uint32_t n, float eps)
+{
+	float ss = 0.0f, scale;
+
+	for (uint32_t i = 0; i < n; i++)
+		ss += x[i] * x[i];
+	scale = 1.0f / sqrtf(ss / (float)n + eps);
+	for (uint32_t i = 0; i < n; i++)
+		out[i] = x[i] * scale * gw[i];
+}
+
+static void softmax(float *x, int n)
+{
+	float mx = x[0], sum = 0.0f;
+
+	for (int i = 1; i < n; i++)
+		if (x[i] > mx)
+			mx = x[i];
+	for (int i = 0; i < n; i++) {
+		x[i] = expf(x[i] - mx);
+		sum += x[i];
+	}
+	for (int i = 0; i < n; i++)
+		x[i] /= sum;
+}
+
+static void rope(float *v, uint32_t nheads, uint32_t hd, int pos, float base)
+{
+	for (uint32_t h = 0; h < nheads; h++) {
+		float *p = v + h * hd;
+
+		for (uint32_t i = 0; i < hd / 2; i++) {
+			float theta = (float)pos * powf(base, -2.0f * (float)i / (float)hd);
+			float c = cosf(theta), s = sinf(theta);
+			float x0 = p[2 * i], x1 = p[2 * i + 1];
+
+			p[2 * i] = x0 * c - x1 * s;
+			p[2 * i + 1] = x0 * s + x1 * c;
+		}
+	}
+}
+
+/* quantise x once, then every projection of it as one group call (or one at
+ * a time under CHARSIU_GPU_NOGROUP, the control) */
+static int project(struct charsiu_gpu_llama *m, const float *x, uint32_t k, const int *ids,
+		   float **ys, unsigned n)
+{
+	act_set(m, x, (int)k);
+	if (n > 1 && !m->nogroup)
+		return charsiu_gpu_matvec_q(m->dev, ids, n, m->aq, m->ad, k, ys);
+	for (unsigned i = 0; i < n; i++)
+		if (charsiu_gpu_matvec_q(m->dev, &ids[i], 1, m->aq, m->ad, k, &ys[i]))
+			return -1;
+	return 0;
+}
+
+API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m)
+{
+	if (!m)
+		return;
+	charsiu_gpu_close(m->dev);
+	free(m->L);
+	free(m->kcache); free(m->vcache);
+	free(m->x); free(m->xb); free(m->xb2); free(m->hb); free(m->hb2);
+	free(m->q); free(m->k); free(m->v); free(m->att); free(m->logits);
+	free(m->aq); free(m->ad);
+	gclose(&m->g);
+	free(m);
+}
+
+static const struct gt *need(struct charsiu_gpu_llama *m, const char *name)
+{
+	const struct gt *t = gfind(&m->g, name);
+
+	if (!t)
+		fprintf(stderr, "charsiu: the file has no tensor %s\n", name);
+	return t;
+}
+
+API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *path, int n_ctx, int device)
+{
+	static const char *pname[P_N] = { "attn_q", "attn_k", "attn_v", "attn_output",
+					   "ffn_gate", "ffn_up", "ffn_down" };
+	struct charsiu_gpu_llama *m = calloc(1, sizeof(*m));
+	const struct gt *t;
+	char key[128];
+	size_t kvn;
+	uint32_t widest;
+
+	if (!m)
+		return NULL;
+	if (gopen(&m->g, path) < 0) {
+		free(m);
+		return NULL;
+	}
+	if (strcmp(m->g.arch, "llama") || !m->g.have[K_EMBD] || !m->g.have[K_LAYERS] ||
+	    !m->g.have[K_HEAD] || !m->g.have[K_FF]) {
+		fprintf(stderr, "charsiu: %s is not a llama model this can read\n", path);
+		goto fail;
+	}
+	m->n_embd = m->g.u[K_EMBD];
+	m->n_layer = m->g.u[K_LAYERS];
+	m->n_head = m->g.u[K_HEAD];
+	m->n_head_kv = m->g.have[K_HEAD_KV] ? m->g.u[K_HEAD_KV] : m->n_head;
+	m->n_ff = m->g.u[K_FF];
+	m->hd = m->g.have[K_ROPE_DIM] ? m->g.u[K_ROPE_DIM] : m->n_embd / m->n_head;
+	m->eps = m->g.have_f[F_EPS] ? m->g.f[F_EPS] : 1e-5f;
+	m->base = m->g.have_f[F_BASE] ? m->g.f[F_BASE] : 10000.0f;
+	m->n_vocab = (uint32_t)m->g.n_tokens;
+	m->nogroup = getenv("CHARSIU_GPU_NOGROUP") != NULL;
+	if (m->hd & 1 || !m->n_vocab || gfind(&m->g, "rope_freqs.weight")) {
+		fprintf(stderr, "charsiu: unsupported head dim, vocabulary or rope table\n");
+		goto fail;
+	}
+	{
+		uint32_t ctx_train = m->g.have[K_CTX] ? m->g.u[K_CTX] : 2048;
+
+		m->n_ctx = n_ctx > 0 ? n_ctx : (int)ctx_train;
+		if (n_ctx <= 0 && m->n_ctx > 4096)
+			m->n_ctx = 4096;
+	}
+	m->tok = need(m, "token_embd.weight");
+	t = need(m, "output_norm.weight");
+	if (!m->tok || !t || t->type != T_F32)
+		goto fail;
+	m->out_norm = (const float *)t->data;
+	m->out = gfind(&m->g, "output.weight");
+	if (!m->out)
+		m->out = m->tok;       /* tied, as Llama 3.2 1B (src/llama.c:463-466) */
+
+	widest = m->n_embd > m->n_ff ? m->n_embd : m->n_ff;
+	m->dev = charsiu_gpu_open_ex(widest, m->n_vocab > widest ? m->n_vocab : widest,
+				     m->n_layer * 9 + 2, device, 0, 1);
+	if (!m->dev)
+		goto fail;
+	m->L = calloc(m->n_layer, sizeof(*m->L));
+	if (!m->L)
+		goto fail;
+	for (uint32_t l = 0; l < m->n_layer; l++) {
+		struct layer *L = &m->L[l];
+
+		snprintf(key, sizeof(key), "blk.%u.attn_norm.weight", l);
+		if (!(t = need(m, key)) || t->type != T_F32)
+			goto fail;
+		L->attn_norm = (const float *)t->data;
+		snprintf(key, sizeof(key), "blk.%u.ffn_norm.weight", l);
+		if (!(t = need(m, key)) || t->type != T_F32)
+			goto fail;
+		L->ffn_norm = (const float *)t->data;
+		for (int p = 0; p < P_N; p++) {
+			snprintf(key, sizeof(key), "blk.%u.%s.weight", l, pname[p]);
+			if (!(L->w[p] = need(m, key)))
+				goto fail;
+			L->id[p] = charsiu_gpu_add_blocks(m->dev, L->w[p]->type, L->w[p]->ne[0],
+							  L->w[p]->ne[1], L->w[p]->data, key);
+			if (L->id[p] < 0)
+				goto fail;
+		}
+	}
+	m->out_id = charsiu_gpu_add_blocks(m->dev, m->out->type, m->out->ne[0], m->out->ne[1],
+					   m->out->data, m->out->name);
+	if (m->out_id < 0)
+		goto fail;
+
+	kvn = (size_t)m->n_layer * (size_t)m->n_ctx * m->n_head_kv * m->hd;
+	m->kcache = calloc(kvn, sizeof(float));
+	m->vcache = calloc(kvn, sizeof(float));
+	m->x = calloc(m->n_embd, sizeof(float));
+	m->xb = calloc(m->n_embd, sizeof(float));
+	m->xb2 = calloc(m->n_embd, sizeof(float));
+	m->hb = calloc(m->n_ff, sizeof(float));
+	m->hb2 = calloc(m->n_ff, sizeof(float));
+	m->q = calloc((size_t)m->n_head * m->hd, sizeof(float));
+	m->k = calloc((size_t)m->n_head_kv * m->hd, sizeof(float));
+	m->v = calloc((size_t)m->n_head_kv * m->hd, sizeof(float));
+	m->att = calloc((size_t)m->n_head * m->n_ctx, sizeof(float));
+	m->logits = calloc(m->n_vocab, sizeof(float));
+	m->aq = calloc((size_t)(widest + 31) / 32 * 32, 1);
+	m->ad = calloc((size_t)(widest + 31) / 32, sizeof(float));
+	if (!m->kcache || !m->vcache || !m->x || !m->xb || !m->xb2 || !m->hb || !m->hb2 ||
+	    !m->q || !m->k || !m->v || !m->att || !m->logits || !m->aq || !m->ad)
+		goto fail;
+	return m;
+fail:
+	charsiu_gpu_llama_close(m);
+	return NULL;
+}
+
+API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t token, int pos)
+{
+	uint32_t hd = m->hd, kvdim = m->n_head_kv * hd, gqa = m->n_head / m->n_head_kv;
+	float scale = 1.0f / sqrtf((float)hd);
+
+	if (pos < 0 || pos >= m->n_ctx || token < 0 || (uint32_t)token >= m->tok->ne[1])
+		return NULL;
+	if (row_f32(m->tok, (uint64_t)token, m->x))
+		return NULL;
+
+	for (uint32_t l = 0; l < m->n_layer; l++) {
+		const struct layer *L = &m->L[l];
+		float *kc = m->kcache + ((size_t)l * m->n_ctx + pos) * kvdim;
+		float *vc = m->vcache + ((size_t)l * m->n_ctx + pos) * kvdim;
+
+		rmsnorm(m->xb, m->x, L->attn_norm, m->n_embd, m->eps);
+		{
+			int ids[3] = { L->id[P_Q], L->id[P_K], L->id[P_V] };
+			float *ys[3] = { m->q, m->k, m->v };
+
+			if (project(m, m->xb, m->n_embd, ids, ys, 3))
+				return NULL;
+		}
+		rope(m->q, m->n_head, hd, pos, m->base);
+		rope(m->k, m->n_head_kv, hd, pos, m->base);
+		memcpy(kc, m->k, kvdim * sizeof(float));
+		memcpy(vc, m->v, kvdim * sizeof(float));
+
+		for (uint32_t h = 0; h < m->n_head; h++) {
+			const float *qh = m->q + h * hd;
+			float *att = m->att + (size_t)h * m->n_ctx;
+			uint32_t kvh = h / gqa;
+			float *out = m->xb + h * hd;
+
+			for (int t = 0; t <= pos; t++) {
+				const float *kt = m->kcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
+				float a = 0.0f;
+
+				for (uint32_t i = 0; i < hd; i++)
+					a += qh[i] * kt[i];
+				att[t] = a * scale;
+			}
+			softmax(att, pos + 1);
+			memset(out, 0, hd * sizeof(float));
+			for (int t = 0; t <= pos; t++) {
+				const float *vt = m->vcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
+				float a = att[t];
+
+				for (uint32_t i = 0; i < hd; i++)
+					out[i] += a * vt[i];
+			}
+		}
+		{
+			int id = L->id[P_O];
+			float *ys[1] = { m->xb2 };
+
+			if (project(m, m->xb, m->n_embd, &id, ys, 1))
+				return NULL;
+		}
+		for (uint32_t i = 0; i < m->n_embd; i++)
+			m->x[i] += m->xb2[i];
+
+		rmsnorm(m->xb, m->x, L->ffn_norm, m->n_embd, m->eps);
+		{
+			int ids[2] = { L->id[P_GATE], L->id[P_UP] };
+			float *ys[2] = { m->hb, m->hb2 };
+
+			if (project(m, m->xb, m->n_embd, ids, ys, 2))
+				return NULL;
+		}
+		for (uint32_t i = 0; i < m->n_ff; i++) {
+			float g = m->hb[i];
+
+			g *= 1.0f / (1.0f + expf(-g));
+			m->hb[i] = g * m->hb2[i];
+		}
+		{
+			int id = L->id[P_DOWN];
+			float *ys[1] = { m->xb2 };
+
+			if (project(m, m->hb, m->n_ff, &id, ys, 1))
+				return NULL;
+		}
+		for (uint32_t i = 0; i < m->n_embd; i++)
+			m->x[i] += m->xb2[i];
+	}
+	rmsnorm(m->xb, m->x, m->out_norm, m->n_embd, m->eps);
+	{
+		float *ys[1] = { m->logits };
+
+		if (project(m, m->xb, m->n_embd, &m->out_id, ys, 1))
+			return NULL;
+	}
+	return m->logits;
+}
+
+API int32_t charsiu_gpu_llama_argmax(const float *logits, uint32_t n)
+{
+	int32_t best = 0;
+
+	for (uint32_t i = 1; i < n; i++)
+		if (logits[i] > logits[best])
+			best = (int32_t)i;
+	return best;
+}
+
+static double now_ms(void)
+{
+	struct timespec t;
+
+	clock_gettime(CLOCK_MONOTONIC, &t);
+	return (double)t.tv_sec * 1e3 + (double)t.tv_nsec / 1e6;
+}
+
+API int charsiu_gpu_llama_greedy(struct charsiu_gpu_llama *m, const int32_t *prompt,
+				 int n_prompt, int n_gen, int32_t *out, float *logits,
+				 double *gen_ms)
+{
+	const float *lg = NULL;
+	int pos = 0;
+	double t0;
+
+	if (!m || n_prompt < 1 || n_gen < 0 || n_prompt + n_gen > m->n_ctx)
+		return -1;
+	for (int i = 0; i < n_prompt; i++)
+		if (!(lg = charsiu_gpu_llama_forward(m, prompt[i], pos++)))
+			return -1;
+	t0 = now_ms();
+	for (int i = 0; i < n_gen; i++) {
+		out[i] = charsiu_gpu_llama_argmax(lg, m->n_vocab);
+		if (logits)
+			memcpy(logits + (size_t)i * m->n_vocab, lg, (size_t)m->n_vocab * sizeof(float));
+		/* as charsiu_run: every generated token is fed back */
+		if (!(lg = charsiu_gpu_llama_forward(m, out[i], pos++)))
+			return -1;
+	}
+	if (gen_ms)
+		*gen_ms = now_ms() - t0;
+	return n_gen;
+}
+
+API uint32_t charsiu_gpu_llama_vocab(const struct charsiu_gpu_llama *m)
+{
+	return m ? m->n_vocab : 0;
+}
+
+API struct charsiu_gpu *charsiu_gpu_llama_layer(struct charsiu_gpu_llama *m)
+{
+	return m ? m->dev : NULL;
+}

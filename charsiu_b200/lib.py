@@ -1,0 +1,268 @@
+"""ctypes binding of libcharsiu_gpu.so: the C ABI of include/charsiu_gpu.h and
+include/charsiu_gpu_llama.h, one method per entry point.
+
+This is how Python reaches the CUDA path (tests, bench.py, smoke). It never
+computes anything itself: if the library is missing it raises, and every
+method is a thin call into the shared object.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libcharsiu_gpu.so")
+
+_lib = None
+
+_i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_vp = C.c_void_p
+
+# (name, restype, argtypes) of every exported entry point
+SIGNATURES = [
+    ("charsiu_gpu_open", _vp, [C.c_uint, C.c_uint, C.c_uint]),
+    ("charsiu_gpu_open_ex", _vp, [C.c_uint, C.c_uint, C.c_uint, C.c_int, C.c_uint, C.c_uint]),
+    ("charsiu_gpu_close", None, [_vp]),
+    ("charsiu_gpu_add", C.c_int, [_vp, _vp]),
+    ("charsiu_gpu_add_blocks", C.c_int, [_vp, C.c_uint32, C.c_uint64, C.c_uint64, _vp, C.c_char_p]),
+    ("charsiu_gpu_rows", C.c_int, [_vp, C.c_int, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    ("charsiu_gpu_matvec", C.c_int, [_vp, C.c_int, _vp, _vp]),
+    ("charsiu_gpu_matvec_group", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp]),
+    ("charsiu_gpu_matvec_q", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp, C.c_uint, _vp]),
+    ("charsiu_gpu_matvec_batch", C.c_int, [_vp, C.c_int, C.c_uint, _vp, _vp, C.c_uint, _vp]),
+    ("charsiu_gpu_matmul_i8", C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    ("charsiu_gpu_matmul_i8_flat", C.c_int, [_vp, C.c_uint, C.c_uint, C.c_uint, _vp, _vp, _vp,
+                                             C.c_float, C.c_float, C.c_float, C.c_int, C.c_int,
+                                             C.c_int, _vp]),
+    ("charsiu_gpu_matvec_dev", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp, _vp, _vp]),
+    ("charsiu_gpu_matvec_batch_dev", C.c_int, [_vp, C.c_int, C.c_uint, _vp, _vp, _vp, _vp]),
+    ("charsiu_gpu_act_quantise_dev", C.c_int, [_vp, _vp, C.c_uint, C.c_uint, _vp, _vp, _vp]),
+    ("charsiu_gpu_calls", C.c_ulong, [_vp]),
+    ("charsiu_gpu_launches", C.c_ulong, [_vp]),
+    ("charsiu_gpu_report", None, [_vp]),
+    ("charsiu_gpu_error", C.c_char_p, [_vp]),
+    ("charsiu_gpu_dead", C.c_int, [_vp]),
+    ("charsiu_gpu_block_dots", C.c_int, [_vp, C.c_int, _vp, _vp]),
+    ("charsiu_gpu_inject", C.c_int, [_vp, C.c_ulong, C.c_ulong, C.c_int]),
+    ("charsiu_gpu_llama_open", _vp, [C.c_char_p, C.c_int, C.c_int]),
+    ("charsiu_gpu_llama_close", None, [_vp]),
+    ("charsiu_gpu_llama_forward", C.POINTER(C.c_float), [_vp, C.c_int32, C.c_int]),
+    ("charsiu_gpu_llama_argmax", C.c_int32, [_vp, C.c_uint32]),
+    ("charsiu_gpu_llama_greedy", C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp, _vp,
+                                           C.POINTER(C.c_double)]),
+    ("charsiu_gpu_llama_vocab", C.c_uint32, [_vp]),
+    ("charsiu_gpu_llama_layer", _vp, [_vp]),
+]
+
+
+def lib():
+    """Load libcharsiu_gpu.so. Raises if it was not built: there is no
+    fallback implementation to use instead."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: run `python -m charsiu_b200.build` "
+                               "(the CUDA extension is required; there is no CPU path)")
+        L = C.CDLL(LIB_PATH)
+        for name, res, args in SIGNATURES:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+class GpuError(RuntimeError):
+    pass
+
+
+class Layer:
+    """One charsiu_gpu device layer (one GPU, one column slab)."""
+
+    def __init__(self, max_k: int, max_n: int, max_tensors: int = 16, device: int = 0,
+                 rank: int = 0, world: int = 1):
+        self.L = lib()
+        self.h = self.L.charsiu_gpu_open_ex(max_k, max_n, max_tensors, device, rank, world)
+        if not self.h:
+            raise GpuError(f"charsiu_gpu_open_ex failed on device {device}")
+        self._keep = {}
+
+    def close(self):
+        if self.h:
+            self.L.charsiu_gpu_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def _check(self, rc, what):
+        if rc != 0:
+            raise GpuError(f"{what}: {self.error()}")
+
+    def error(self) -> str:
+        return self.L.charsiu_gpu_error(self.h).decode()
+
+    @property
+    def calls(self) -> int:
+        return self.L.charsiu_gpu_calls(self.h)
+
+    @property
+    def launches(self) -> int:
+        return self.L.charsiu_gpu_launches(self.h)
+
+    @property
+    def dead(self) -> bool:
+        return bool(self.L.charsiu_gpu_dead(self.h))
+
+    def report(self):
+        self.L.charsiu_gpu_report(self.h)
+
+    def add_blocks(self, qtype: int, k: int, n: int, blocks: np.ndarray, name: str = "") -> int:
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        tid = self.L.charsiu_gpu_add_blocks(self.h, qtype, k, n, _p(blocks), name.encode())
+        if tid < 0:
+            raise GpuError(f"add {name}: {self.error()}")
+        return tid
+
+    def try_add_blocks(self, qtype, k, n, blocks, name="") -> int:
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        return self.L.charsiu_gpu_add_blocks(self.h, qtype, k, n, _p(blocks), name.encode())
+
+    def rows(self, tid: int):
+        r0, nr = C.c_uint64(), C.c_uint64()
+        self._check(self.L.charsiu_gpu_rows(self.h, tid, C.byref(r0), C.byref(nr)), "rows")
+        return r0.value, nr.value
+
+    def matvec(self, ids, q: np.ndarray, d: np.ndarray, k: int):
+        """y for each id (this GPU's rows), host buffers in and out."""
+        ids = list(ids)
+        ys = [np.empty(self.rows(i)[1], dtype=np.float32) for i in ids]
+        rc = self.try_matvec(ids, q, d, k, ys)
+        self._check(rc, "matvec")
+        return ys
+
+    def try_matvec(self, ids, q, d, k, ys) -> int:
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        d = np.ascontiguousarray(d, dtype=np.float32)
+        idarr = (C.c_int * len(ids))(*ids)
+        yarr = (C.c_void_p * len(ids))(*[_p(y) for y in ys])
+        return self.L.charsiu_gpu_matvec_q(self.h, C.addressof(idarr), len(ids), _p(q), _p(d), k,
+                                           C.addressof(yarr))
+
+    def batch(self, tid: int, q: np.ndarray, d: np.ndarray):
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        d = np.ascontiguousarray(d, dtype=np.float32)
+        m, kq = q.shape
+        y = np.empty((m, self.rows(tid)[1]), dtype=np.float32)
+        self._check(self.L.charsiu_gpu_matvec_batch(self.h, tid, m, _p(q), _p(d), kq, _p(y)),
+                    "batch")
+        return y
+
+    def matmul_i8(self, a, w, bias, in_scale, wt_scale, out_scale, in_zp=128, wt_zp=128,
+                  out_zp=0):
+        a = np.ascontiguousarray(a, dtype=np.uint8)
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        bias = np.ascontiguousarray(bias, dtype=np.int32)
+        m, k = a.shape
+        n = w.shape[0]
+        out = np.full((m, n), 0x5a, dtype=np.int8)
+        self._check(self.L.charsiu_gpu_matmul_i8_flat(self.h, m, k, n, _p(a), _p(w), _p(bias),
+                                                      in_scale, wt_scale, out_scale, in_zp,
+                                                      wt_zp, out_zp, _p(out)), "matmul_i8")
+        return out
+
+    def block_dots(self, tid: int, q: np.ndarray):
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        rows = self.rows(tid)[1]
+        nb = q.size // 32
+        out = np.empty((rows, nb), dtype=np.int32)
+        self._check(self.L.charsiu_gpu_block_dots(self.h, tid, _p(q), _p(out)), "block_dots")
+        return out
+
+    def inject(self, at: int, count: int, kind: int):
+        self._check(self.L.charsiu_gpu_inject(self.h, at, count, kind), "inject")
+
+    # device-pointer forms (pointers are ints, e.g. torch tensor.data_ptr())
+    def matvec_dev(self, ids, q_ptr: int, d_ptr: int, y_ptrs, stream: int = 0) -> int:
+        ids = list(ids)
+        idarr = (C.c_int * len(ids))(*ids)
+        yarr = (C.c_void_p * len(ids))(*y_ptrs)
+        return self.L.charsiu_gpu_matvec_dev(self.h, C.addressof(idarr), len(ids), q_ptr, d_ptr,
+                                             C.addressof(yarr), stream or None)
+
+    def batch_dev(self, tid: int, m: int, q_ptr: int, d_ptr: int, y_ptr: int,
+                  stream: int = 0) -> int:
+        return self.L.charsiu_gpu_matvec_batch_dev(self.h, tid, m, q_ptr, d_ptr, y_ptr,
+                                                   stream or None)
+
+    def act_quantise_dev(self, x_ptr: int, m: int, k: int, q_ptr: int, d_ptr: int,
+                         stream: int = 0) -> int:
+        return self.L.charsiu_gpu_act_quantise_dev(self.h, x_ptr, m, k, q_ptr, d_ptr,
+                                                   stream or None)
+
+
+class Llama:
+    """charsiu_gpu_llama: the decode loop with every projection on the GPU."""
+
+    def __init__(self, path: str, n_ctx: int = 0, device: int = 0):
+        self.L = lib()
+        self.h = self.L.charsiu_gpu_llama_open(path.encode(), n_ctx, device)
+        if not self.h:
+            raise GpuError(f"charsiu_gpu_llama_open failed for {path}")
+        self.n_vocab = self.L.charsiu_gpu_llama_vocab(self.h)
+
+    def close(self):
+        if self.h:
+            self.L.charsiu_gpu_llama_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    @property
+    def layer_handle(self):
+        return self.L.charsiu_gpu_llama_layer(self.h)
+
+    def report(self):
+        self.L.charsiu_gpu_report(self.layer_handle)
+
+    @property
+    def launches(self) -> int:
+        return self.L.charsiu_gpu_launches(self.layer_handle)
+
+    @property
+    def calls(self) -> int:
+        return self.L.charsiu_gpu_calls(self.layer_handle)
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        p = self.L.charsiu_gpu_llama_forward(self.h, token, pos)
+        if not p:
+            raise GpuError(f"forward failed: {self.L.charsiu_gpu_error(self.layer_handle)}")
+        return np.ctypeslib.as_array(p, shape=(self.n_vocab,)).copy()
+
+    def greedy(self, prompt, n_gen: int, want_logits: bool = False):
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_gen, dtype=np.int32)
+        lg = np.zeros((n_gen, self.n_vocab), dtype=np.float32) if want_logits else None
+        ms = C.c_double()
+        rc = self.L.charsiu_gpu_llama_greedy(self.h, _p(p), p.size, n_gen, _p(out),
+                                             _p(lg) if lg is not None else None, C.byref(ms))
+        if rc != n_gen:
+            raise GpuError(f"greedy failed: {self.L.charsiu_gpu_error(self.layer_handle)}")
+        return out, lg, ms.value

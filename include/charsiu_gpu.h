@@ -1,0 +1,183 @@
+/* SPDX-License-Identifier: GPL-2.0-or-later */
+#ifndef CHARSIU_GPU_H
+#define CHARSIU_GPU_H
+
+/*
+ * The GPU device layer: a drop-in for charsiu's NPU device layer on NVIDIA
+ * B200 (sm_100a).
+ *
+ * Every call below is the GPU twin of one charsiu_npu_* call (declared in the
+ * reference at include/charsiu_llm.h:186-200, implemented in src/npudev.c),
+ * with the same conventions:
+ *
+ *   - NULL / -1 on failure, never abort. A failed call leaves the caller's
+ *     output undefined and the caller recomputes on the CPU, as llama.c does
+ *     for the NPU (src/llama.c:269-282).
+ *   - Three slow or failed calls in a row retire the layer; every call after
+ *     that returns -1 (src/npudev.c:560-602). The first refusal is printed once
+ *     (src/npudev.c:124-138) and the report says if nothing ran on the GPU.
+ *   - Not re-entrant: one decode thread calls it, before any pool fan-out
+ *     (src/llama.c:261-282).
+ *
+ * The NPU layer takes the NPU's own per-channel int8 format; this layer takes
+ * the GGUF tensor itself and computes charsiu's GGML block arithmetic
+ * (src/gguf.c:1061-1107, 1149-1171) exactly: q8_0 or q4_0 weights against the
+ * q8_0 activation of charsiu_act_set, int32 block dots, and the fp32 sum of
+ * (d_w * d_a) * dot in block order, so y is bit-identical to gguf_matvec.
+ * Weights are repacked once, at add time, into a coalesced device layout.
+ *
+ * The struct types are charsiu's own (include/charsiu_llm.h:51-59, 100-119;
+ * include/charsiu.h:113-119, 194-225); this header only names them. Callers
+ * without those headers use the flat forms (plain pointers and sizes).
+ */
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CHARSIU_GPU_API __attribute__((visibility("default")))
+#else
+#define CHARSIU_GPU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct gguf_tensor;
+struct charsiu_act;
+struct charsiu_job;
+struct charsiu_gpu;
+
+/* ---- lifetime ------------------------------------------------------------ */
+
+/* charsiu_npu_open (include/charsiu_llm.h:188-189, src/npudev.c:140-233).
+ * Device 0, the whole of every tensor. NULL: no usable GPU; stay on the CPU. */
+CHARSIU_GPU_API struct charsiu_gpu *charsiu_gpu_open(unsigned max_k, unsigned max_n,
+				     unsigned max_tensors);
+
+/* The same on `device`, holding only column slab `rank` of `world` of every
+ * tensor added: rows [rank*N/world, (rank+1)*N/world) rounded to whole
+ * 8-row groups. No counterpart in the reference (one board, one NPU); it is
+ * the N-split the vendor runtime uses across NPU cores (docs/vendor-dispatch.md:43-58). */
+CHARSIU_GPU_API struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n,
+					unsigned max_tensors, int device,
+					unsigned rank, unsigned world);
+
+/* charsiu_npu_close (include/charsiu_llm.h:190). NULL-safe. */
+CHARSIU_GPU_API void charsiu_gpu_close(struct charsiu_gpu *g);
+
+/* ---- weights ------------------------------------------------------------- */
+
+/* charsiu_npu_add (include/charsiu_llm.h:191, src/npudev.c:389-461), for the
+ * GGUF tensor: q8_0 or q4_0, ne[0] = K a multiple of 32, ne[1] = N. The host
+ * tensor stays the caller's. Returns an id >= 0, or -1 (tensor stays on the
+ * CPU). Adding the same tensor again returns its existing id. */
+CHARSIU_GPU_API int charsiu_gpu_add(struct charsiu_gpu *g, const struct gguf_tensor *w);
+
+/* Flat form of charsiu_gpu_add: `blocks` is N rows of K/32 GGML blocks
+ * (34 bytes q8_0, 18 bytes q4_0), row major, as in a GGUF file. */
+CHARSIU_GPU_API int charsiu_gpu_add_blocks(struct charsiu_gpu *g, uint32_t type, uint64_t k,
+			   uint64_t n, const void *blocks, const char *name);
+
+/* Rows this GPU holds of tensor `id`: [*row0, *row0 + *nrows). */
+CHARSIU_GPU_API int charsiu_gpu_rows(const struct charsiu_gpu *g, int id, uint64_t *row0,
+		     uint64_t *nrows);
+
+/* ---- the matvec ---------------------------------------------------------- */
+
+/* charsiu_npu_matvec (include/charsiu_llm.h:192-193, src/npudev.c:463-607):
+ * y = W x from a->q and a->d (a->quantised must be set, a->n = K). y holds
+ * this GPU's rows of the output (all N on an unsharded layer). */
+CHARSIU_GPU_API int charsiu_gpu_matvec(struct charsiu_gpu *g, int id,
+		       const struct charsiu_act *a, float *y);
+
+/* charsiu_npu_matvec_group (include/charsiu_llm.h:195-196,
+ * src/npudev.c:621-716): up to 8 projections of one activation, one launch
+ * and one fence. -1: the caller falls back to single calls. */
+CHARSIU_GPU_API int charsiu_gpu_matvec_group(struct charsiu_gpu *g, const int *ids, unsigned n,
+			     const struct charsiu_act *a, float **ys);
+
+/* Flat form of the group call: q is K int8 (K/32 blocks), d K/32 fp32. */
+CHARSIU_GPU_API int charsiu_gpu_matvec_q(struct charsiu_gpu *g, const int *ids, unsigned n,
+			 const int8_t *q, const float *d, unsigned k,
+			 float **ys);
+
+/* Batched: m activations q[m][K], d[m][K/32] against tensor id; y[m][rows].
+ * Each y[i] is bit-identical to the single matvec of activation i. No
+ * counterpart in the reference, which decodes one token at a time. */
+CHARSIU_GPU_API int charsiu_gpu_matvec_batch(struct charsiu_gpu *g, int id, unsigned m,
+			     const int8_t *q, const float *d, unsigned k,
+			     float *y);
+
+/* ---- the int8 matmul with the NPU's output stage ------------------------- */
+
+/* What charsiu_emit_job + charsiu_submit compute for an int8 job
+ * (include/charsiu.h:194-235; arithmetic of tools/charsiu_matmul.c:41-81 and
+ * the output stage of src/job.c:137-177): a u8 [m][k], w u8 [n][k] (int8
+ * weights, job->mm.wdtype CHARSIU_INT8), bias i32 [n]; out i8 [m][n] row
+ * major, out = clamp(max(requant, 0) + offset, -128, 127). Byte-exact
+ * against cpu_reference. */
+CHARSIU_GPU_API int charsiu_gpu_matmul_i8(struct charsiu_gpu *g, const struct charsiu_job *job,
+			  const uint8_t *a, const uint8_t *w,
+			  const int32_t *bias, int8_t *out);
+
+/* Flat form of charsiu_gpu_matmul_i8. */
+CHARSIU_GPU_API int charsiu_gpu_matmul_i8_flat(struct charsiu_gpu *g, unsigned m, unsigned k,
+			       unsigned n, const uint8_t *a, const uint8_t *w,
+			       const int32_t *bias, float in_scale,
+			       float wt_scale, float out_scale, int in_zp,
+			       int wt_zp, int out_zp, int8_t *out);
+
+/* ---- device-resident forms ------------------------------------------------ */
+/*
+ * For callers that keep the activation in HBM (a decode loop on the device).
+ * All pointers are device pointers; the work is queued on `stream` (a
+ * cudaStream_t, NULL for the layer's own) with no host synchronisation, so a
+ * caller may capture it in a CUDA graph. Return 0 when queued.
+ */
+CHARSIU_GPU_API int charsiu_gpu_matvec_dev(struct charsiu_gpu *g, const int *ids, unsigned n,
+			   const int8_t *q, const float *d, float *const *ys,
+			   void *stream);
+CHARSIU_GPU_API int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m,
+				 const int8_t *q, const float *d, float *y,
+				 void *stream);
+/* charsiu_act_set (src/gguf.c:829-882) on the device, bit-exact: x fp32
+ * [m][k] -> q int8 [m][k rounded up to 32], d fp32 [m][k/32]. */
+CHARSIU_GPU_API int charsiu_gpu_act_quantise_dev(struct charsiu_gpu *g, const float *x,
+				 unsigned m, unsigned k, int8_t *q, float *d,
+				 void *stream);
+
+/* ---- accounting ----------------------------------------------------------- */
+
+/* charsiu_npu_submits (include/charsiu_llm.h:197): calls that ran. */
+CHARSIU_GPU_API unsigned long charsiu_gpu_calls(const struct charsiu_gpu *g);
+/* kernels this layer has launched */
+CHARSIU_GPU_API unsigned long charsiu_gpu_launches(const struct charsiu_gpu *g);
+/* charsiu_npu_report (include/charsiu_llm.h:198, src/npudev.c:272-295) */
+CHARSIU_GPU_API void charsiu_gpu_report(const struct charsiu_gpu *g);
+/* the last failure, in words ("" if none) */
+CHARSIU_GPU_API const char *charsiu_gpu_error(const struct charsiu_gpu *g);
+/* 1 once the layer has retired itself */
+CHARSIU_GPU_API int charsiu_gpu_dead(const struct charsiu_gpu *g);
+
+/* ---- test hooks ------------------------------------------------------------ */
+
+/* The integer block dots of tensor id against q: dots[r][K/32], int32, for
+ * this GPU's rows. Bit-exact against dotq_q8_0 / dotq_q4_0's t. */
+CHARSIU_GPU_API int charsiu_gpu_block_dots(struct charsiu_gpu *g, int id, const int8_t *q,
+			   int32_t *dots);
+
+/* Host-side fault injection (no GPU fault is ever made): from call number
+ * `at` on (1-based, counting matvec/group/batch/matmul calls), `count` calls
+ * fail as `kind` says: 1 = the launch reports an error, 2 = the call is slow
+ * (counts as a watchdog strike), 3 = the device allocation fails (at add).
+ * count 0 disarms. */
+CHARSIU_GPU_API int charsiu_gpu_inject(struct charsiu_gpu *g, unsigned long at,
+		       unsigned long count, int kind);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CHARSIU_GPU_H */

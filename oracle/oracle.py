@@ -1,0 +1,229 @@
+"""ctypes access to the checkers. TEST INFRASTRUCTURE ONLY.
+
+Two libraries, both built by oracle/Makefile:
+  liboracle.so            the restatement in charsiu_oracle.c (always built);
+  _ref/libcharsiu_ref.so  the reference compiled from its own sources plus
+                          ref_shim.c (built only where the reference tree is).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline and
+reference legs use this module, and only as the checker or the baseline.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "liboracle.so")
+REF_LIB = os.path.join(HERE, "_ref", "libcharsiu_ref.so")
+
+_i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            build()
+        L = C.CDLL(LIB)
+        L.orc_act_quantise.argtypes = [_f32p, C.c_int, _i8p, _f32p, C.c_void_p]
+        L.orc_matvec.argtypes = [C.c_uint32, C.c_void_p, C.c_uint64, _i8p, _f32p, _f32p,
+                                 C.c_uint64, C.c_uint64]
+        L.orc_matvec.restype = C.c_int
+        L.orc_block_dots.argtypes = [C.c_uint32, C.c_void_p, C.c_uint64, C.c_uint64, _i8p, _i32p]
+        L.orc_block_dots.restype = C.c_int
+        L.orc_matmul_i8.argtypes = [C.c_uint, C.c_uint, C.c_uint, _u8p, _u8p, _i32p, C.c_float,
+                                    C.c_float, C.c_float, C.c_int, C.c_int, C.c_int, _i8p]
+        L.orc_half_to_float.argtypes = [C.c_uint16]
+        L.orc_half_to_float.restype = C.c_float
+        L.orc_state_new.argtypes = [C.c_void_p, C.c_int]
+        L.orc_state_new.restype = C.c_void_p
+        L.orc_state_free.argtypes = [C.c_void_p]
+        L.orc_forward.argtypes = [C.c_void_p, C.c_int32, C.c_int]
+        L.orc_forward.restype = C.POINTER(C.c_float)
+        L.orc_greedy.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _i32p]
+        L.orc_greedy.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def have_ref() -> bool:
+    return os.path.exists(REF_LIB)
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        if not have_ref():
+            raise FileNotFoundError(REF_LIB)
+        R = C.CDLL(REF_LIB)
+        R.ref_matmul_i8.argtypes = [C.c_uint, C.c_uint, C.c_uint, _u8p, _u8p, _i32p, C.c_float,
+                                    C.c_float, C.c_float, C.c_int, C.c_int, C.c_int, _u8p]
+        R.ref_matmul_i8.restype = C.c_int
+        R.ref_matvec.argtypes = [C.c_uint32, C.c_void_p, C.c_uint64, C.c_uint64, _f32p, _f32p,
+                                 _i8p, _f32p]
+        R.ref_matvec.restype = C.c_int
+        R.ref_greedy.argtypes = [C.c_char_p, _i32p, C.c_int, C.c_int, C.c_int, _i32p,
+                                 C.POINTER(C.c_double), C.POINTER(C.c_double), C.c_void_p]
+        R.ref_greedy.restype = C.c_int
+        _ref = R
+    return _ref
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+# ---- the restatement ---------------------------------------------------------
+
+def act_quantise(x: np.ndarray):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    nb = (x.size + 31) // 32
+    q = np.zeros(nb * 32, dtype=np.int8)
+    d = np.zeros(nb, dtype=np.float32)
+    lib().orc_act_quantise(x, x.size, q, d, None)
+    return q, d
+
+
+def matvec(qtype: int, blocks: np.ndarray, k: int, n: int, q: np.ndarray, d: np.ndarray):
+    y = np.zeros(n, dtype=np.float32)
+    rc = lib().orc_matvec(qtype, _ptr(blocks), k, np.ascontiguousarray(q), np.ascontiguousarray(d),
+                          y, 0, n)
+    assert rc == 0
+    return y
+
+
+def block_dots(qtype: int, blocks: np.ndarray, k: int, n: int, q: np.ndarray):
+    out = np.zeros((n, k // 32), dtype=np.int32)
+    rc = lib().orc_block_dots(qtype, _ptr(blocks), k, n, np.ascontiguousarray(q), out)
+    assert rc == 0
+    return out
+
+
+def matmul_i8(a, w, bias, in_scale, wt_scale, out_scale, in_zp=128, wt_zp=128, out_zp=0):
+    m, k = a.shape
+    n = w.shape[0]
+    out = np.zeros((m, n), dtype=np.int8)
+    lib().orc_matmul_i8(m, k, n, np.ascontiguousarray(a), np.ascontiguousarray(w),
+                        np.ascontiguousarray(bias, dtype=np.int32), in_scale, wt_scale, out_scale,
+                        in_zp, wt_zp, out_zp, out)
+    return out
+
+
+class _Layer(C.Structure):
+    _fields_ = [("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p), ("w", C.c_void_p * 7),
+                ("type", C.c_uint32 * 7)]
+
+
+class _Model(C.Structure):
+    _fields_ = [("n_embd", C.c_uint32), ("n_layer", C.c_uint32), ("n_head", C.c_uint32),
+                ("n_head_kv", C.c_uint32), ("n_ff", C.c_uint32), ("n_vocab", C.c_uint32),
+                ("head_dim", C.c_uint32), ("rms_eps", C.c_float), ("rope_base", C.c_float),
+                ("tok_embd", C.c_void_p), ("tok_type", C.c_uint32), ("output", C.c_void_p),
+                ("out_type", C.c_uint32), ("out_norm", C.c_void_p), ("layers", C.c_void_p)]
+
+
+class OracleModel:
+    """The restated decode loop over a GGUF file's tensors (mapped, not copied)."""
+
+    def __init__(self, gguf, n_ctx: int = 64):
+        from charsiu_b200.gguf import PROJ_NAMES
+        s = gguf.shape()
+        self.gguf, self.shape = gguf, s
+        T = gguf.tensors
+        layers = (_Layer * s.n_layer)()
+        for l in range(s.n_layer):
+            L = layers[l]
+            L.attn_norm = _ptr(gguf.data(f"blk.{l}.attn_norm.weight"))
+            L.ffn_norm = _ptr(gguf.data(f"blk.{l}.ffn_norm.weight"))
+            for i, nm in enumerate(PROJ_NAMES):
+                L.w[i] = _ptr(gguf.data(f"blk.{l}.{nm}.weight"))
+                L.type[i] = T[f"blk.{l}.{nm}.weight"].type
+        out = "output.weight" if "output.weight" in T else "token_embd.weight"
+        self._layers = layers
+        self.m = _Model(s.n_embd, s.n_layer, s.n_head, s.n_head_kv, s.n_ff, s.n_vocab, s.head_dim,
+                        s.rms_eps, s.rope_base, _ptr(gguf.data("token_embd.weight")),
+                        T["token_embd.weight"].type, _ptr(gguf.data(out)), T[out].type,
+                        _ptr(gguf.data("output_norm.weight")), C.addressof(layers))
+        self.n_ctx = n_ctx
+
+    def greedy(self, prompt, n_gen: int) -> np.ndarray:
+        L = lib()
+        st = L.orc_state_new(C.byref(self.m), self.n_ctx)
+        assert st
+        try:
+            out = np.zeros(n_gen, dtype=np.int32)
+            p = np.ascontiguousarray(prompt, dtype=np.int32)
+            rc = L.orc_greedy(st, p, p.size, n_gen, out)
+            assert rc == n_gen, rc
+            return out
+        finally:
+            L.orc_state_free(st)
+
+    def logits_after(self, prompt) -> np.ndarray:
+        L = lib()
+        st = L.orc_state_new(C.byref(self.m), self.n_ctx)
+        try:
+            lp = None
+            for i, t in enumerate(prompt):
+                lp = L.orc_forward(st, int(t), i)
+            return np.ctypeslib.as_array(lp, shape=(self.shape.n_vocab,)).copy()
+        finally:
+            L.orc_state_free(st)
+
+
+# ---- the reference itself ----------------------------------------------------
+
+def ref_matmul_i8(a, w, bias, in_scale, wt_scale, out_scale, in_zp=128, wt_zp=128, out_zp=0):
+    m, k = a.shape
+    n = w.shape[0]
+    out = np.zeros((m, n), dtype=np.uint8)
+    ref().ref_matmul_i8(m, k, n, np.ascontiguousarray(a), np.ascontiguousarray(w),
+                        np.ascontiguousarray(bias, dtype=np.int32), in_scale, wt_scale, out_scale,
+                        in_zp, wt_zp, out_zp, out)
+    return out.view(np.int8)
+
+
+def ref_matvec(qtype: int, blocks: np.ndarray, k: int, n: int, x: np.ndarray):
+    """charsiu_act_set + gguf_matvec of the reference: (y, q, d)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(n, dtype=np.float32)
+    q = np.zeros((k + 31) // 32 * 32, dtype=np.int8)
+    d = np.zeros((k + 31) // 32, dtype=np.float32)
+    rc = ref().ref_matvec(qtype, _ptr(blocks), k, n, x, y, q, d)
+    assert rc == 0
+    return y, q, d
+
+
+def ref_greedy(path: str, prompt, n_gen: int, n_ctx: int = 0, threads: int | None = None,
+               want_logits: int = 0):
+    """Greedy decode by the reference's own llama_forward.
+
+    Returns (tokens, prompt_ms, gen_ms[, logits after the prompt]). The
+    reference's pool reads CHARSIU_THREADS once per process."""
+    if threads is not None:
+        os.environ["CHARSIU_THREADS"] = str(threads)
+    out = np.zeros(n_gen, dtype=np.int32)
+    p = np.ascontiguousarray(prompt, dtype=np.int32)
+    pm, gm = C.c_double(), C.c_double()
+    lg = np.zeros(want_logits, dtype=np.float32) if want_logits else None
+    n = ref().ref_greedy(path.encode(), p, p.size, n_gen, n_ctx, out, C.byref(pm), C.byref(gm),
+                         _ptr(lg) if lg is not None else None)
+    if n < 0:
+        raise RuntimeError(f"reference could not load {path}")
+    res = (out[:n], pm.value, gm.value)
+    return res + (lg,) if want_logits else res

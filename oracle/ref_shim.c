@@ -1,0 +1,140 @@
+// SPDX-License-Identifier: GPL-2.0-or-later
+/*
+ * A thin shim over the reference itself, compiled by oracle/Makefile from
+ * the reference's own sources where they lie (nothing of them is copied into
+ * this repository). The result, oracle/_ref/libcharsiu_ref.so, is TEST
+ * INFRASTRUCTURE: it pins the restatement in charsiu_oracle.c and serves as
+ * the CPU baseline. It is never part of the product.
+ *
+ * It adds two things the reference does not export:
+ *  - cpu_reference() of tools/charsiu_matmul.c:41-81 is `static`, so that
+ *    file is included here with its main() renamed, and a wrapper exports it;
+ *  - a charsiu_run-style greedy driver (tools/charsiu_run.c:220-317) that
+ *    takes token ids instead of text, because the workload's prompt is a list
+ *    of seeded ids.
+ */
+#define _POSIX_C_SOURCE 200809L
+
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#include "charsiu.h"
+#include "charsiu_llm.h"
+
+#define main charsiu_matmul_tool_main
+#include "charsiu_matmul.c"
+#undef main
+
+int ref_cpu_reference(const struct charsiu_job *job, const uint8_t *a,
+		      const uint8_t *b, const int32_t *bias, uint8_t *out)
+{
+	return cpu_reference(job, a, b, bias, out);
+}
+
+/* flat arguments, so a ctypes caller needs no struct layout */
+int ref_matmul_i8(unsigned m, unsigned k, unsigned n, const uint8_t *a,
+		  const uint8_t *w, const int32_t *bias, float in_scale,
+		  float wt_scale, float out_scale, int in_zp, int wt_zp,
+		  int out_zp, uint8_t *out)
+{
+	struct charsiu_job job;
+
+	memset(&job, 0, sizeof(job));
+	job.mm.m = m;
+	job.mm.k = k;
+	job.mm.n = n;
+	job.mm.wdtype = CHARSIU_INT8;
+	job.mm.adtype = CHARSIU_INT8;
+	job.input_scale = in_scale;
+	job.weight_scale = wt_scale;
+	job.output_scale = out_scale;
+	job.input_zero_point = in_zp;
+	job.weight_zero_point = wt_zp;
+	job.output_zero_point = out_zp;
+	return cpu_reference(&job, a, w, bias, out);
+}
+
+size_t ref_sizeof_act(void)
+{
+	return sizeof(struct charsiu_act);
+}
+
+/* charsiu_act_set + gguf_matvec over all rows, on a caller's raw blocks */
+int ref_matvec(uint32_t type, const void *blocks, uint64_t k, uint64_t n,
+	       const float *x, float *y, int8_t *q_out, float *d_out)
+{
+	struct gguf_tensor w;
+	struct charsiu_act a;
+
+	memset(&w, 0, sizeof(w));
+	w.n_dims = 2;
+	w.ne[0] = k;
+	w.ne[1] = n;
+	w.ne[2] = w.ne[3] = 1;
+	w.type = type;
+	w.data = blocks;
+	if (charsiu_act_alloc(&a, (int)k) < 0)
+		return -1;
+	charsiu_act_set(&a, x, (int)k);
+	gguf_matvec(&w, &a, y, 0, n);
+	if (q_out)
+		memcpy(q_out, a.q, (size_t)a.nb * 32);
+	if (d_out)
+		memcpy(d_out, a.d, (size_t)a.nb * sizeof(float));
+	charsiu_act_free(&a);
+	return 0;
+}
+
+static double now_ms(void)
+{
+	struct timespec t;
+
+	clock_gettime(CLOCK_MONOTONIC, &t);
+	return (double)t.tv_sec * 1e3 + (double)t.tv_nsec / 1e6;
+}
+
+/*
+ * Greedy decode through the reference's own llama_load / llama_forward /
+ * llama_argmax. Returns the number of tokens written to out, or -1.
+ * *gen_ms is the generation time (tools/charsiu_run.c:295-339), and, when
+ * logits_out is given, the logits after the prompt are copied into it.
+ */
+int ref_greedy(const char *path, const int32_t *prompt, int n_prompt,
+	       int n_gen, int n_ctx, int32_t *out, double *prompt_ms,
+	       double *gen_ms, float *logits_out)
+{
+	struct llama_model m;
+	struct llama_state *st;
+	const float *logits = NULL;
+	double t0;
+	int i;
+
+	if (llama_load(&m, path) < 0)
+		return -1;
+	st = llama_state_new(&m, n_ctx);
+	if (!st) {
+		llama_free(&m);
+		return -1;
+	}
+	t0 = now_ms();
+	for (i = 0; i < n_prompt; i++)
+		logits = llama_forward(st, prompt[i], i);
+	if (prompt_ms)
+		*prompt_ms = now_ms() - t0;
+	if (logits_out && logits)
+		memcpy(logits_out, logits, (size_t)m.n_vocab * sizeof(float));
+	t0 = now_ms();
+	for (i = 0; i < n_gen && logits; i++) {
+		out[i] = llama_argmax(logits, m.n_vocab);
+		if (st->pos >= st->n_ctx)
+			break;
+		logits = llama_forward(st, out[i], st->pos);
+	}
+	if (gen_ms)
+		*gen_ms = now_ms() - t0;
+	llama_state_free(st);
+	llama_free(&m);
+	return i;
+}

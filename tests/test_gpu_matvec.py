@@ -1,0 +1,144 @@
+"""The block-quant matvec on the GPU, through the C ABI, against the oracle and
+the reference's golden vectors: y must be bit-identical (the CUDA path sums
+blocks in the reference's order), the integer block dots exact."""
+import os
+
+import numpy as np
+import pytest
+
+from charsiu_b200 import gguf as G
+from charsiu_b200 import workloads as W
+from charsiu_b200.lib import Layer
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLD = np.load(os.path.join(HERE, "golden", "golden.npz"))
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def same(a, b):
+    return np.array_equal(bits(a), bits(b))
+
+
+@pytest.fixture(scope="module")
+def layer():
+    with Layer(max_k=8192, max_n=128256, max_tensors=64) as L:
+        yield L
+
+
+@pytest.mark.parametrize("name", list(W.MATVEC_GOLDEN))
+def test_golden_small_shapes(layer, name):
+    qt, k, n, _ = W.MATVEC_GOLDEN[name]
+    tid = layer.add_blocks(qt, k, n, GOLD[f"{name}_blocks"], name)
+    q, d = GOLD[f"{name}_q"], GOLD[f"{name}_d"]
+    (y,) = layer.matvec([tid], q, d, k)
+    assert same(y, GOLD[f"{name}_y"])
+    assert np.array_equal(layer.block_dots(tid, q), GOLD[f"{name}_dots"])
+
+
+@pytest.mark.parametrize("name", list(W.MATVEC_SEEDED))
+def test_workload_shapes_bit_exact(layer, name):
+    qt, k, n, seed = W.MATVEC_SEEDED[name]
+    blk, x = W.matvec_inputs(qt, k, n, seed)
+    tid = layer.add_blocks(qt, k, n, blk, name)
+    q, d = O.act_quantise(x)
+    (y,) = layer.matvec([tid], q, d, k)
+    assert same(y, GOLD[f"{name}_y"])
+    # twice: the second call reuses every staging buffer
+    (y2,) = layer.matvec([tid], q, d, k)
+    assert same(y2, y)
+
+
+@pytest.mark.parametrize("qt", [G.GGML_Q8_0, G.GGML_Q4_0])
+@pytest.mark.parametrize("k,n", [(32, 1), (32, 7), (64, 9), (96, 40), (544, 31), (2080, 17),
+                                 (8192, 8), (8224, 3), (2048, 1000)])
+def test_ragged_shapes_vs_oracle(layer, qt, k, n):
+    blk, x = W.matvec_inputs(qt, k, n, seed=k * 7 + n)
+    x[: min(k, 64)] = 0.0            # all-zero activation blocks (d = 0)
+    tid = layer.add_blocks(qt, k, n, blk)
+    q, d = O.act_quantise(x)
+    (y,) = layer.matvec([tid], q, d, k)
+    assert same(y, O.matvec(qt, blk, k, n, q, d))
+    assert np.array_equal(layer.block_dots(tid, q), O.block_dots(qt, blk, k, n, q))
+
+
+def test_group_equals_singles(layer):
+    k = 2048
+    shapes = [(G.GGML_Q8_0, 2048), (G.GGML_Q8_0, 512), (G.GGML_Q4_0, 512), (G.GGML_Q8_0, 8192),
+              (G.GGML_Q4_0, 40)]
+    ids, blks = [], []
+    for i, (qt, n) in enumerate(shapes):
+        blk, _ = W.matvec_inputs(qt, k, n, seed=100 + i)
+        ids.append(layer.add_blocks(qt, k, n, blk, f"g{i}"))
+        blks.append((qt, blk, n))
+    x = np.random.default_rng(5).normal(size=k).astype(np.float32)
+    q, d = O.act_quantise(x)
+    ys = layer.matvec(ids, q, d, k)
+    for (qt, blk, n), y in zip(blks, ys):
+        assert same(y, O.matvec(qt, blk, k, n, q, d))
+
+
+def test_output_head_shape(layer):
+    """The 2048 -> 128256 tied head, q8_0: 16032 row groups in one launch."""
+    k, n = 2048, 128256
+    blk, x = W.matvec_inputs(G.GGML_Q8_0, k, n, seed=77)
+    tid = layer.add_blocks(G.GGML_Q8_0, k, n, blk, "output")
+    q, d = O.act_quantise(x)
+    (y,) = layer.matvec([tid], q, d, k)
+    assert same(y, O.matvec(G.GGML_Q8_0, blk, k, n, q, d))
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 13])
+@pytest.mark.parametrize("qt", [G.GGML_Q8_0, G.GGML_Q4_0])
+def test_batch_rows_match_single_matvec(layer, m, qt):
+    k, n = 2048, 520
+    blk, xs = W.batch_inputs(qt, k, n, m, seed=3)
+    tid = layer.add_blocks(qt, k, n, blk)
+    qs, ds = zip(*(O.act_quantise(x) for x in xs))
+    y = layer.batch(tid, np.stack(qs), np.stack(ds))
+    for i in range(m):
+        assert same(y[i], O.matvec(qt, blk, k, n, qs[i], ds[i])), f"row {i}"
+
+
+def test_device_forms_and_quantiser(layer):
+    torch = pytest.importorskip("torch")
+    k, n, m = 8192, 2048, 4
+    blk, xs = W.batch_inputs(G.GGML_Q4_0, k, n, m, seed=21)
+    xs[1, :96] = 0.0
+    tid = layer.add_blocks(G.GGML_Q4_0, k, n, blk)
+    dev = torch.device("cuda:0")
+    x_t = torch.from_numpy(xs).to(dev)
+    q_t = torch.empty((m, k), dtype=torch.int8, device=dev)
+    d_t = torch.empty((m, k // 32), dtype=torch.float32, device=dev)
+    y_t = torch.full((m, n), float("nan"), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert layer.act_quantise_dev(x_t.data_ptr(), m, k, q_t.data_ptr(), d_t.data_ptr(), stream) == 0
+    assert layer.batch_dev(tid, m, q_t.data_ptr(), d_t.data_ptr(), y_t.data_ptr(), stream) == 0
+    y1 = torch.full((n,), float("nan"), dtype=torch.float32, device=dev)
+    assert layer.matvec_dev([tid], q_t[2].data_ptr(), d_t[2].data_ptr(), [y1.data_ptr()],
+                            stream) == 0
+    torch.cuda.synchronize()
+    qg, dg, yg = q_t.cpu().numpy(), d_t.cpu().numpy(), y_t.cpu().numpy()
+    for i in range(m):
+        q, d = O.act_quantise(xs[i])
+        assert np.array_equal(qg[i], q) and same(dg[i], d), f"quantiser row {i}"
+        assert same(yg[i], O.matvec(G.GGML_Q4_0, blk, k, n, q, d)), f"row {i}"
+    assert same(y1.cpu().numpy(), yg[2])
+
+
+def test_rejects_bad_input(layer):
+    blk, _ = W.matvec_inputs(G.GGML_Q8_0, 64, 8, seed=1)
+    assert layer.try_add_blocks(G.GGML_F32, 64, 8, blk) == -1
+    assert layer.try_add_blocks(G.GGML_Q8_0, 48, 8, blk) == -1          # K not a multiple of 32
+    assert layer.try_add_blocks(G.GGML_Q8_0, 64, 10 ** 7, blk) == -1    # wider than opened
+    tid = layer.add_blocks(G.GGML_Q8_0, 64, 8, blk)
+    q = np.zeros(128, np.int8)
+    d = np.zeros(4, np.float32)
+    y = np.zeros(8, np.float32)
+    assert layer.try_matvec([tid], q, d, 128, [y]) == -1                # K mismatch
+    assert not layer.dead
