@@ -1,0 +1,404 @@
+#!/usr/bin/env python
+"""Benchmark: Llama-3.2-1B-shaped q8_0 decode, tokens per second.
+
+A step is one decode token's pass through the hot path: the 112 projections
+and the 128256-wide tied output head, issued as the decode loop issues them
+(q/k/v as one group launch, o, gate/up as one group launch, down, per layer;
+then the head): 65 launches of the block-quant matvec, 1.31 GB of q8_0
+weights. Synthetic seeded weights with the workload's distributions (no real
+checkpoint exists on these machines), random activations quantised on the
+device.
+
+  value   tokens/s of that chain with weights and activations resident in
+          HBM, replayed as one CUDA graph per token, timed with CUDA events.
+          1.31 GB a token is far larger than the 126 MB L2, so every token
+          streams its weights from HBM.
+  e2e     tokens/s of the real greedy decode through the public C ABI
+          (charsiu_gpu_llama_*): CPU rmsnorm/rope/attention/SwiGLU as
+          charsiu does them, every projection a host-buffer call with its
+          host->device and device->host copies inside the timed region.
+  roofline the matvec kernel's algorithmic bytes per launch over its average
+          launch time in the timed region, against the measured HBM copy peak.
+  cpu_baseline charsiu's own CPU decode (the reference compiled from its
+          sources, oracle/_ref) on this box's host cores.
+
+At N GPUs every tensor is column-split across the ranks and each launch
+group's output slabs are all-gathered (NCCL) into the full vector, so one
+decode stream runs on N GPUs: strong scaling.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+from charsiu_b200 import gguf as G  # noqa: E402
+from charsiu_b200 import workloads as W  # noqa: E402
+
+METRIC = "Llama-3.2-1B q8_0 decode tok/s"
+UNIT = "tok/s"
+SPEC = W.DECODE["llama1b_q8"]
+SHAPE = SPEC["shape"]
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return PEAKS_FALLBACK["hbm_gbs"], "fallback"
+
+
+def model_path(rank: int, barrier) -> str:
+    d = os.path.join(tempfile.gettempdir(), "charsiu_bench")
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, f"llama1b_q8_seed{SPEC['seed']}.gguf")
+    if rank == 0 and not os.path.exists(path):
+        G.write_llama(path, SHAPE, SPEC["qtype"], SPEC["seed"])
+    barrier()
+    return path
+
+
+# ---- clocks during the timed region ------------------------------------------
+
+CLOCK_Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+           "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+           "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class Clocks:
+    def __init__(self, index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={CLOCK_Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.2)
+
+    def stop(self):
+        if self.p:
+            self.p.terminate()
+            self.p.wait()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [ln.split(",") for ln in self.f.read().splitlines() if ln.strip()]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4)
+                          if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(sm)}
+
+
+# ---- the launch plan of one token --------------------------------------------
+
+def launch_groups(shape):
+    """[(tensor names, K)] in decode order: 4 launches a layer, then the head."""
+    out = []
+    for l in range(shape.n_layer):
+        b = f"blk.{l}."
+        out.append(([b + "attn_q.weight", b + "attn_k.weight", b + "attn_v.weight"], shape.n_embd))
+        out.append(([b + "attn_output.weight"], shape.n_embd))
+        out.append(([b + "ffn_gate.weight", b + "ffn_up.weight"], shape.n_embd))
+        out.append(([b + "ffn_down.weight"], shape.n_ff))
+    out.append((["token_embd.weight"], shape.n_embd))
+    return out
+
+
+def algorithmic_bytes(gguf, names, k, rows_of):
+    """weights streamed + the q8_0 activation (K + 4K/32) + fp32 outputs."""
+    w = sum(rows_of(nm) * (k // 32) * 34 for nm in names)
+    return w + k + 4 * (k // 32) + 4 * sum(rows_of(nm) for nm in names)
+
+
+# ---- our arm -------------------------------------------------------------------
+
+def run_ours(args, rank, world, dist):
+    import torch
+    from charsiu_b200.lib import Layer, Llama, lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
+    path = model_path(rank, barrier)
+    gg = G.GGUFFile(path)
+    groups = launch_groups(SHAPE)
+    names = sorted({nm for g, _ in groups for nm in g})
+
+    layer = Layer(max_k=max(SHAPE.n_embd, SHAPE.n_ff), max_n=SHAPE.n_vocab,
+                  max_tensors=len(names) + 1, device=dev.index, rank=rank, world=world)
+    ids, rows = {}, {}
+    for nm in names:
+        t = gg.tensors[nm]
+        ids[nm] = layer.add_blocks(t.type, t.k, t.n, np.asarray(gg.data(nm)), nm)
+        rows[nm] = layer.rows(ids[nm])[1]
+    full_rows = {nm: gg.tensors[nm].n for nm in names}
+
+    # device activations: seeded normal vectors, quantised by the device quantiser
+    gen = torch.Generator(device="cpu").manual_seed(1234)
+    acts = {}
+    for k in (SHAPE.n_embd, SHAPE.n_ff):
+        x = torch.randn(k, generator=gen).to(dev)
+        q = torch.empty(k, dtype=torch.int8, device=dev)
+        d = torch.empty(k // 32, dtype=torch.float32, device=dev)
+        assert layer.act_quantise_dev(x.data_ptr(), 1, k, q.data_ptr(), d.data_ptr(),
+                                      torch.cuda.current_stream().cuda_stream) == 0
+        acts[k] = (q, d)
+    # output slabs, padded to the widest rank's slab so NCCL gathers equal pieces
+    per = {}
+    for nm in names:
+        ngroups = -(-full_rows[nm] // 8)
+        per[nm] = -(-ngroups // world) * 8
+    ys = {nm: torch.zeros(per[nm], dtype=torch.float32, device=dev) for nm in names}
+    full = {nm: torch.zeros(per[nm] * world, dtype=torch.float32, device=dev) for nm in names} \
+        if world > 1 else None
+
+    def token(stream):
+        for g, k in groups:
+            q, d = acts[k]
+            rc = layer.matvec_dev([ids[nm] for nm in g], q.data_ptr(), d.data_ptr(),
+                                  [ys[nm].data_ptr() for nm in g], stream.cuda_stream)
+            assert rc == 0, layer.error()
+            if world > 1:
+                for nm in g:
+                    dist.all_gather_into_tensor(full[nm], ys[nm])
+
+    stream = torch.cuda.Stream(device=dev)
+    graph = None
+    launches0 = layer.launches
+    if world == 1:
+        with torch.cuda.stream(stream):
+            token(stream)                       # warm the kernels before capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            token(stream)
+        torch.cuda.synchronize()
+    per_token_launches = len(groups)
+    run = (lambda: graph.replay()) if graph else (lambda: token(stream))
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = Clocks(dev.index) if rank == 0 else None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            run()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop() if clocks else None
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = 1000.0 / ms_per_step
+
+    tok_bytes = sum(algorithmic_bytes(gg, g, k, lambda nm: rows[nm]) for g, k in groups)
+    peak, peak_kind = peaks()
+    achieved = tok_bytes / (ms_per_step * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
+                "kernel": "cgpu::qmv_kernel<1>", "peak_kind": peak_kind,
+                "bytes_per_launch": round(tok_bytes / per_token_launches),
+                "avg_launch_us": round(ms_per_step * 1e3 / per_token_launches, 3)}
+    del graph
+    layer.close()
+
+    e2e = None
+    if world == 1:
+        e2e = run_e2e(path, args, lib)
+    else:
+        e2e = {"value": None, "unit": UNIT, "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+               "note": "the host-ABI decode loop is single-GPU; N>1 e2e not measured"}
+
+    out = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+           "data": "synthetic (seeded random-init Llama-3.2-1B-shaped q8_0 GGUF; no checkpoint)",
+           "config": {"workload": "Llama-3.2-1B q8_0 greedy decode, hot path per token: 112 "
+                                  "projections + 128256 tied head in 65 matvec launches",
+                      "model": "Llama-3.2-1B architecture (16x2048, ffn 8192, 32/8 heads, "
+                               "vocab 128256)",
+                      "weights_bytes_per_token": tok_bytes, "global_batch": 1, "seq_len": 1,
+                      "parallelism": f"column-split x{world}" if world > 1 else "single GPU",
+                      "l2": "inputs larger than L2 (1.31 GB of weights per step vs 126 MB)"},
+           "roofline": roofline, "e2e": e2e, "gpu_launches": per_token_launches * args.steps,
+           "clocks": clk}
+    if rank == 0 and world == 1:
+        out["cpu_baseline"] = cpu_baseline(path)
+    return out
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the matvec from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "qmv_decode_llama1b.md")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for ln in f:
+            if ln.startswith("traffic_bytes_per_launch:"):
+                return int(ln.split(":")[1].strip().split()[0])
+    return None
+
+
+def run_e2e(path, args, lib):
+    """The public C ABI decode: host buffers in and out on every call."""
+    import ctypes as C
+    from charsiu_b200.lib import Llama
+
+    n_gen_timed = min(args.steps, SPEC["n_gen"])
+    n_warm = max(3, min(args.warmup, 8))
+    prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
+    n_ctx = len(prompt) + n_warm + n_gen_timed + 1
+    L = lib()
+    with Llama(path, n_ctx=n_ctx) as m:
+        lp = None
+        pos = 0
+        for t in prompt:
+            lp = L.charsiu_gpu_llama_forward(m.h, int(t), pos)
+            pos += 1
+        tok = L.charsiu_gpu_llama_argmax(lp, m.n_vocab)
+        for _ in range(n_warm):
+            lp = L.charsiu_gpu_llama_forward(m.h, tok, pos)
+            pos += 1
+            tok = L.charsiu_gpu_llama_argmax(lp, m.n_vocab)
+        calls0 = m.calls
+        t0 = time.perf_counter()
+        for _ in range(n_gen_timed):
+            lp = L.charsiu_gpu_llama_forward(m.h, tok, pos)
+            if not lp:
+                raise RuntimeError("e2e forward failed")
+            pos += 1
+            tok = L.charsiu_gpu_llama_argmax(lp, m.n_vocab)
+        dt = time.perf_counter() - t0
+        calls = (m.calls - calls0) / n_gen_timed
+    groups = launch_groups(SHAPE)
+    h2d = sum(k + 4 * (k // 32) for _, k in groups)
+    d2h = 4 * (SHAPE.n_layer * (SHAPE.n_embd * 2 + 2 * SHAPE.n_head_kv * SHAPE.head_dim
+                                + 3 * SHAPE.n_ff) + SHAPE.n_vocab)
+    return {"value": round(n_gen_timed / dt, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": n_gen_timed, "warmup": n_warm,
+            "calls_per_step": calls, "ms_per_step": round(dt * 1e3 / n_gen_timed, 4),
+            "api": "charsiu_gpu_llama_forward (C ABI, host buffers), positions "
+                   f"{len(prompt) + n_warm}..{len(prompt) + n_warm + n_gen_timed - 1}"}
+
+
+def cpu_baseline(path):
+    """charsiu's own CPU decode on this box's cores: the reference compiled from
+    its sources when present (oracle/_ref), else the oracle's restatement."""
+    from oracle import oracle as O
+    prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
+    n = 8
+    if O.have_ref():
+        cores = os.cpu_count()
+        toks, stamps = O.ref_greedy_timed(path, prompt, n, n_ctx=64, threads=cores)
+        kind = "reference"
+    else:
+        cores = 1
+        toks, stamps = O.port_greedy_timed(G.GGUFFile(path), prompt, n)
+        kind = "port"
+    rate = (len(stamps) - 1) / ((stamps[-1] - stamps[0]) / 1e3)
+    return {"value": round(rate, 3), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"6-token prompt then {n} greedy tokens of the same model; rate over "
+                      f"tokens 2..{n} (the first is warm-up)"}
+
+
+# ---- the reference arm --------------------------------------------------------
+
+def run_reference(args, rank, world, dist):
+    barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
+    path = model_path(rank, barrier)
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+    prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
+    n = args.warmup + args.steps
+    if O.have_ref():
+        cores, kind = os.cpu_count(), "reference"
+        toks, stamps = O.ref_greedy_timed(path, prompt, n, n_ctx=len(prompt) + n + 1,
+                                          threads=cores)
+    else:
+        cores, kind = 1, "port"
+        toks, stamps = O.port_greedy_timed(G.GGUFFile(path), prompt, n,
+                                           n_ctx=len(prompt) + n + 1)
+    t_warm = stamps[args.warmup - 1] if args.warmup else 0.0
+    ms = (stamps[-1] - t_warm) / args.steps
+    value = 1000.0 / ms
+    sample = (f"6-token prompt, {args.warmup} warm-up then {args.steps} timed greedy tokens of "
+              "the Llama-3.2-1B-shaped q8_0 model, charsiu's llama_forward")
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "Llama-3.2-1B q8_0 greedy decode", "global_batch": 1,
+                       "seq_len": 1, "parallelism": f"{cores} host threads"},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores,
+                             "kind": kind, "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        if args.impl == "ours":
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
+                                timeout=datetime.timedelta(seconds=600))
+    try:
+        if args.impl == "reference":
+            out = run_reference(args, rank, world, dist)
+        else:
+            out = run_ours(args, rank, world, dist)
+        if rank == 0 and out is not None:
+            print(json.dumps(out), flush=True)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

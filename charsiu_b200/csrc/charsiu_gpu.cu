@@ -20,11 +20,14 @@
 
 #include "aux_kernels.cuh"
 #include "qmv.cuh"
+#include "qmv1.cuh"
 #include "ref_abi.h"
 
 using namespace cgpu;
 
 namespace {
+
+constexpr unsigned MAX_K = 14336;
 
 double now_us()
 {
@@ -99,7 +102,9 @@ struct charsiu_gpu {
 	int32_t *d_dots = nullptr;
 	size_t cap_dots = 0;
 	int *d_err = nullptr;
-	bool smem_set[QMV_MAX_M + 1] = {};
+	bool smem_set[24] = {};
+	// CTAs per SM for (m, nb): asked of the driver once, never during capture
+	std::vector<std::pair<uint64_t, int>> occ;
 
 	unsigned long calls = 0, launches = 0, call_no = 0;
 	double busy_us = 0, h2d_us = 0, kern_ms = 0, d2h_us = 0, weight_mb = 0;
@@ -188,71 +193,6 @@ int finish(charsiu_gpu *g, double t0, double mb, unsigned k, unsigned n)
 	return 0;
 }
 
-int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st)
-{
-	const size_t smem = qmv_smem_bytes(m, p.nb);
-	const void *fn = nullptr;
-
-	switch (m) {
-	case 1: fn = (const void *)qmv_kernel<1>; break;
-	case 2: fn = (const void *)qmv_kernel<2>; break;
-	case 4: fn = (const void *)qmv_kernel<4>; break;
-	case 8: fn = (const void *)qmv_kernel<8>; break;
-	default: return -1;
-	}
-	if (!g->smem_set[m]) {
-		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-					 227 * 1024) != cudaSuccess)
-			return -1;
-		g->smem_set[m] = true;
-	}
-	int occ = 0;
-	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, QMV_WARPS * 32, smem) !=
-		    cudaSuccess || occ < 1)
-		return -1;
-	unsigned grid = (unsigned)occ * g->sm_count;
-	if (p.total_groups < grid)
-		grid = p.total_groups ? p.total_groups : 1;
-
-	cudaLaunchConfig_t cfg = {};
-	cfg.gridDim = dim3(grid);
-	cfg.blockDim = dim3(QMV_WARPS * 32);
-	cfg.dynamicSmemBytes = smem;
-	cfg.stream = st;
-	cudaLaunchAttribute attr[1];
-	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-	attr[0].val.programmaticStreamSerializationAllowed = 1;
-	cfg.attrs = attr;
-	cfg.numAttrs = 1;
-	cudaError_t e;
-	switch (m) {
-	case 1: e = cudaLaunchKernelEx(&cfg, qmv_kernel<1>, p); break;
-	case 2: e = cudaLaunchKernelEx(&cfg, qmv_kernel<2>, p); break;
-	case 4: e = cudaLaunchKernelEx(&cfg, qmv_kernel<4>, p); break;
-	default: e = cudaLaunchKernelEx(&cfg, qmv_kernel<8>, p); break;
-	}
-	if (e != cudaSuccess)
-		return -1;
-	g->launches++;
-	return 0;
-}
-
-int check_ids(charsiu_gpu *g, const int *ids, unsigned n, unsigned k)
-{
-	if (!n || n > QMV_MAX_TENSORS)
-		return -1;
-	for (unsigned i = 0; i < n; i++) {
-		if (ids[i] < 0 || (unsigned)ids[i] >= g->ent.size())
-			return -1;
-		if (g->ent[ids[i]].k != k) {
-			whine(g, "the activation is not this tensor's K (%u vs %llu)", k,
-			      (unsigned long long)g->ent[ids[i]].k);
-			return -1;
-		}
-	}
-	return 0;
-}
-
 // Fill QmvParams for tensors ids[0..n) with outputs at ys[i] (device).
 void fill_params(charsiu_gpu *g, QmvParams &p, const int *ids, unsigned n, float *const *ys,
 		 uint32_t k, const int8_t *q, const float *d)
@@ -278,6 +218,121 @@ void fill_params(charsiu_gpu *g, QmvParams &p, const int *ids, unsigned n, float
 	p.q = q;
 	p.d = d;
 	p.err = g->d_err;
+}
+
+// M = 1 runs qmv1_kernel<W, Q8, TWO> (W warps share one 8-row group, one or
+// two segments a warp; every tensor of the launch has the same quant type);
+// M = 2, 4, 8 run qmv_kernel<M> (a warp a group). Both sum blocks in the
+// reference's order.
+int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st)
+{
+	static const void *const qmv1_fns[4][2] = {
+		{(const void *)qmv1_kernel<4, false, false>, (const void *)qmv1_kernel<4, true, false>},
+		{(const void *)qmv1_kernel<8, false, false>, (const void *)qmv1_kernel<8, true, false>},
+		{(const void *)qmv1_kernel<8, false, true>, (const void *)qmv1_kernel<8, true, true>},
+		{(const void *)qmv1_kernel<16, false, true>, (const void *)qmv1_kernel<16, true, true>},
+	};
+	static const int qmv1_warps[4] = {4, 8, 8, 16};
+	const void *fn = nullptr;
+	size_t smem = 0;
+	int threads = QMV_WARPS * 32, slot = 0;
+	const bool q8 = p.t[0].type == TYPE_Q8_0;
+	const uint32_t nseg = nsegments(p.nb);
+	const int shape = nseg <= 4 ? 0 : nseg <= 8 ? 1 : nseg <= 16 ? 2 : 3;
+
+	if (m == 1) {
+		threads = qmv1_warps[shape] * 32;
+		smem = qmv1_smem_bytes(p.nb);
+		slot = 10 + 2 * shape + (q8 ? 1 : 0);   // 10..17; M > 1 uses slots 2, 4, 8
+		fn = qmv1_fns[shape][q8 ? 1 : 0];
+	} else {
+		smem = qmv_smem_bytes(m, p.nb);
+		slot = m;
+		switch (m) {
+		case 2: fn = (const void *)qmv_kernel<2>; break;
+		case 4: fn = (const void *)qmv_kernel<4>; break;
+		case 8: fn = (const void *)qmv_kernel<8>; break;
+		default: return -1;
+		}
+	}
+	if (!g->smem_set[slot]) {
+		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+					 227 * 1024) != cudaSuccess)
+			return -1;
+		g->smem_set[slot] = true;
+	}
+	const uint64_t key = (uint64_t)slot << 32 | p.nb;
+	int occ = 0;
+	for (const auto &kv : g->occ)
+		if (kv.first == key)
+			occ = kv.second;
+	if (!occ) {
+		if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem) !=
+			    cudaSuccess || occ < 1)
+			return -1;
+		g->occ.emplace_back(key, occ);
+	}
+	unsigned grid = (unsigned)occ * g->sm_count;
+	if (p.total_groups < grid)
+		grid = p.total_groups ? p.total_groups : 1;
+
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = dim3(grid);
+	cfg.blockDim = dim3(threads);
+	cfg.dynamicSmemBytes = smem;
+	cfg.stream = st;
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = attr;
+	cfg.numAttrs = 1;
+	QmvParams arg = p;
+	void *args[1] = {&arg};
+	const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+	if (e != cudaSuccess)
+		return -1;
+	g->launches++;
+	return 0;
+}
+
+// One launch per quant type present among ids (the M = 1 kernel takes one
+// type a launch; a decode's groups are always a single type).
+int launch_matvec1(charsiu_gpu *g, const int *ids, unsigned n, float *const *ys, uint32_t k,
+		   const int8_t *q, const float *d, cudaStream_t st)
+{
+	for (uint32_t type : {TYPE_Q8_0, TYPE_Q4_0}) {
+		int sub[QMV_MAX_TENSORS];
+		float *sy[QMV_MAX_TENSORS];
+		unsigned ns = 0;
+		for (unsigned i = 0; i < n; i++)
+			if (g->ent[ids[i]].type == type) {
+				sub[ns] = ids[i];
+				sy[ns++] = ys[i];
+			}
+		if (!ns)
+			continue;
+		QmvParams p;
+		fill_params(g, p, sub, ns, sy, k, q, d);
+		if (launch_qmv(g, 1, p, st))
+			return -1;
+	}
+	return 0;
+}
+
+int check_ids(charsiu_gpu *g, const int *ids, unsigned n, unsigned k)
+{
+	if (!n || n > QMV_MAX_TENSORS)
+		return -1;
+	for (unsigned i = 0; i < n; i++) {
+		if (ids[i] < 0 || (unsigned)ids[i] >= g->ent.size())
+			return -1;
+		if (g->ent[ids[i]].k != k) {
+			whine(g, "the activation is not this tensor's K (%u vs %llu)", k,
+			      (unsigned long long)g->ent[ids[i]].k);
+			return -1;
+		}
+	}
+	return 0;
 }
 
 // The host-pointer matvec: H2D of the activation, one launch per chunk of at
@@ -335,7 +390,9 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 		QmvParams p;
 		fill_params(g, p, ids, n, yd, k, g->d_q + (size_t)m0 * nb * 32,
 			    g->d_d + (size_t)m0 * nb);
-		if (launch_qmv(g, (int)mc, p, g->stream)) {
+		const int rc = mc == 1 ? launch_matvec1(g, ids, n, yd, k, p.q, p.d, g->stream)
+				       : launch_qmv(g, (int)mc, p, g->stream);
+		if (rc) {
 			whine(g, "the launch failed: %s", cudaGetErrorString(cudaGetLastError()));
 			retire(g, "a launch failed");
 			return -1;
@@ -377,7 +434,8 @@ struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned
 		fprintf(stderr, "charsiu: no CUDA device %d\n", device);
 		return nullptr;
 	}
-	if (!world || rank >= world || !max_k || max_k % 32 || !max_tensors)
+	// the widest activation every kernel's shared-memory plan holds
+	if (!world || rank >= world || !max_k || max_k % 32 || max_k > MAX_K || !max_tensors)
 		return nullptr;
 	cudaDeviceProp prop;
 	if (cudaSetDevice(device) != cudaSuccess ||
@@ -618,9 +676,7 @@ int charsiu_gpu_matvec_dev(struct charsiu_gpu *g, const int *ids, unsigned n, co
 	if (check_ids(g, ids, n, k))
 		return -1;
 	cudaSetDevice(g->device);
-	QmvParams p;
-	fill_params(g, p, ids, n, ys, k, q, d);
-	return launch_qmv(g, 1, p, stream ? (cudaStream_t)stream : g->stream);
+	return launch_matvec1(g, ids, n, ys, k, q, d, stream ? (cudaStream_t)stream : g->stream);
 }
 
 int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m, const int8_t *q,
@@ -641,7 +697,8 @@ int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m, cons
 		QmvParams p;
 		fill_params(g, p, &id, 1, yd, (uint32_t)e.k, q + (size_t)m0 * nb * 32,
 			    d + (size_t)m0 * nb);
-		if (launch_qmv(g, (int)mc, p, st))
+		if (mc == 1 ? launch_matvec1(g, &id, 1, yd, (uint32_t)e.k, p.q, p.d, st)
+			    : launch_qmv(g, (int)mc, p, st))
 			return -1;
 		m0 += mc;
 	}

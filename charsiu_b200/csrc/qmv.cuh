@@ -53,84 +53,91 @@ inline size_t qmv_smem_bytes(int m, uint32_t nb)
 	       (size_t)m * nb * (32 + sizeof(float) + sizeof(int32_t));
 }
 
-// One q8_0 segment. Lane l reads 16 bytes at l*16 of each 512-byte pair of
-// blocks: block pair half p = l>>4, row r = (l>>1)&7, 16-byte half h = l&1.
-// Lane 2r ends up holding row r's running sum.
-template <int M>
-__device__ __forceinline__ void seg_q8(const uint8_t *st, uint32_t sb, uint32_t b0,
-				       const int8_t *aq, const float *ad, uint32_t nb,
-				       int lane, float (&s)[M])
+// One segment (sb <= 16 blocks of 8 rows), in two phases. Lane l owns block
+// p = l>>3 of every 4-block step and row r = l&7; it computes the terms
+// (d_w * d_a) * t of its blocks with no dependence between them, so the
+// loads, dp4a and multiplies of all steps overlap. Then lane r adds row r's
+// terms in block order (step by step, blocks p = 0..3 fetched by shuffle),
+// which is the only serial part: one fadd per block.
+//
+// q8_0: a block row is 32 bytes, read as two 16-byte halves; rows 4-7 read
+// their halves in the other order so each quarter-warp's 16-byte loads hit
+// distinct banks. q4_0: a block row is 16 bytes of nibbles;
+// (q - 8) . a = q . a - 8 * sum(a).
+template <int M, bool Q8>
+__device__ __forceinline__ void seg_terms(const uint8_t *st, uint32_t sb, uint32_t b0,
+					  const int8_t *aq, const float *ad, const int32_t *asum,
+					  uint32_t nb, int lane, float (&s)[M])
 {
-	const uint16_t *dl = reinterpret_cast<const uint16_t *>(st + sb * RG * 32);
-	const int p = lane >> 4, r = (lane >> 1) & 7, h = lane & 1;
+	constexpr uint32_t QB = Q8 ? 32 : 16;
+	const uint16_t *dl = reinterpret_cast<const uint16_t *>(st + sb * RG * QB);
+	const int p = lane >> 3, r = lane & 7;
+	const int hf = (r >> 2) & 1;
+	float term[SB / 4][M];
 
-	for (uint32_t bb = 0; bb < sb; bb += 2) {
-		const uint32_t bl = bb + p;
-		const uint32_t blk = min(b0 + bl, nb - 1);
-		const uint4 w = *reinterpret_cast<const uint4 *>(st + bb * (RG * 32) + lane * 16);
-		const float dw = half_bits_to_float(dl[min(bl, sb - 1) * RG + r]);
-		const bool two = bb + 1 < sb;
 #pragma unroll
-		for (int m = 0; m < M; m++) {
-			const uint4 a = *reinterpret_cast<const uint4 *>(
-				aq + ((size_t)m * nb + blk) * 32 + h * 16);
-			int t = dp4a_ss(w.x, a.x, 0);
-			t = dp4a_ss(w.y, a.y, t);
-			t = dp4a_ss(w.z, a.z, t);
-			t = dp4a_ss(w.w, a.w, t);
-			t += __shfl_xor_sync(0xffffffffu, t, 1);
-			const float term = __fmul_rn(__fmul_rn(dw, ad[m * nb + blk]), __int2float_rn(t));
-			const float odd = __shfl_xor_sync(0xffffffffu, term, 16);
-			s[m] = __fadd_rn(s[m], term);
-			if (two)
-				s[m] = __fadd_rn(s[m], odd);
+	for (int j = 0; j < SB / 4; j++) {
+		if ((uint32_t)j * 4 >= sb)
+			break;
+		const uint32_t bl = min((uint32_t)(j * 4 + p), sb - 1);
+		const uint32_t blk = b0 + bl;
+		const uint8_t *wp = st + (bl * RG + r) * QB;
+		const float dw = half_bits_to_float(dl[bl * RG + r]);
+		if (Q8) {
+			const uint4 w0 = *reinterpret_cast<const uint4 *>(wp + hf * 16);
+			const uint4 w1 = *reinterpret_cast<const uint4 *>(wp + (hf ^ 1) * 16);
+#pragma unroll
+			for (int m = 0; m < M; m++) {
+				const int8_t *a = aq + ((size_t)m * nb + blk) * 32;
+				const uint4 a0 = *reinterpret_cast<const uint4 *>(a + hf * 16);
+				const uint4 a1 = *reinterpret_cast<const uint4 *>(a + (hf ^ 1) * 16);
+				int t0 = dp4a_ss(w0.x, a0.x, 0), t1 = dp4a_ss(w1.x, a1.x, 0);
+				t0 = dp4a_ss(w0.y, a0.y, t0);
+				t1 = dp4a_ss(w1.y, a1.y, t1);
+				t0 = dp4a_ss(w0.z, a0.z, t0);
+				t1 = dp4a_ss(w1.z, a1.z, t1);
+				t0 = dp4a_ss(w0.w, a0.w, t0);
+				t1 = dp4a_ss(w1.w, a1.w, t1);
+				term[j][m] = __fmul_rn(__fmul_rn(dw, ad[m * nb + blk]),
+						       __int2float_rn(t0 + t1));
+			}
+		} else {
+			const uint4 w = *reinterpret_cast<const uint4 *>(wp);
+			const uint32_t l0 = w.x & 0x0f0f0f0fu, l1 = w.y & 0x0f0f0f0fu;
+			const uint32_t l2 = w.z & 0x0f0f0f0fu, l3 = w.w & 0x0f0f0f0fu;
+			const uint32_t h0 = (w.x >> 4) & 0x0f0f0f0fu, h1 = (w.y >> 4) & 0x0f0f0f0fu;
+			const uint32_t h2 = (w.z >> 4) & 0x0f0f0f0fu, h3 = (w.w >> 4) & 0x0f0f0f0fu;
+#pragma unroll
+			for (int m = 0; m < M; m++) {
+				const uint4 *ap = reinterpret_cast<const uint4 *>(aq + ((size_t)m * nb + blk) * 32);
+				const uint4 a0 = ap[0], a1 = ap[1];
+				int t0 = dp4a_us(l0, a0.x, 0), t1 = dp4a_us(h0, a1.x, 0);
+				t0 = dp4a_us(l1, a0.y, t0);
+				t1 = dp4a_us(h1, a1.y, t1);
+				t0 = dp4a_us(l2, a0.z, t0);
+				t1 = dp4a_us(h2, a1.z, t1);
+				t0 = dp4a_us(l3, a0.w, t0);
+				t1 = dp4a_us(h3, a1.w, t1);
+				term[j][m] = __fmul_rn(__fmul_rn(dw, ad[m * nb + blk]),
+						       __int2float_rn(t0 + t1 - 8 * asum[m * nb + blk]));
+			}
 		}
 	}
-}
-
-// One q4_0 segment. Lane l reads 16 bytes (one block of one row) at l*16 of
-// each 512-byte run of four blocks: block p = l>>3, row r = l&7. Lane r ends
-// up holding row r's running sum. (q - 8) . a = q . a - 8 * sum(a).
-template <int M>
-__device__ __forceinline__ void seg_q4(const uint8_t *st, uint32_t sb, uint32_t b0,
-				       const int8_t *aq, const float *ad, const int32_t *asum,
-				       uint32_t nb, int lane, float (&s)[M])
-{
-	const uint16_t *dl = reinterpret_cast<const uint16_t *>(st + sb * RG * 16);
-	const int p = lane >> 3, r = lane & 7;
-
-	for (uint32_t bb = 0; bb < sb; bb += 4) {
-		const uint32_t bl = bb + p;
-		const uint32_t blk = min(b0 + bl, nb - 1);
-		const uint4 w = *reinterpret_cast<const uint4 *>(st + bb * (RG * 16) + lane * 16);
-		const float dw = half_bits_to_float(dl[min(bl, sb - 1) * RG + r]);
-		const uint32_t l0 = w.x & 0x0f0f0f0fu, l1 = w.y & 0x0f0f0f0fu;
-		const uint32_t l2 = w.z & 0x0f0f0f0fu, l3 = w.w & 0x0f0f0f0fu;
-		const uint32_t h0 = (w.x >> 4) & 0x0f0f0f0fu, h1 = (w.y >> 4) & 0x0f0f0f0fu;
-		const uint32_t h2 = (w.z >> 4) & 0x0f0f0f0fu, h3 = (w.w >> 4) & 0x0f0f0f0fu;
+#pragma unroll
+	for (int j = 0; j < SB / 4; j++) {
+		if ((uint32_t)j * 4 >= sb)
+			break;
 #pragma unroll
 		for (int m = 0; m < M; m++) {
-			const uint4 *ap = reinterpret_cast<const uint4 *>(aq + ((size_t)m * nb + blk) * 32);
-			const uint4 a0 = ap[0], a1 = ap[1];
-			int t = dp4a_us(l0, a0.x, 0);
-			t = dp4a_us(l1, a0.y, t);
-			t = dp4a_us(l2, a0.z, t);
-			t = dp4a_us(l3, a0.w, t);
-			t = dp4a_us(h0, a1.x, t);
-			t = dp4a_us(h1, a1.y, t);
-			t = dp4a_us(h2, a1.z, t);
-			t = dp4a_us(h3, a1.w, t);
-			t -= 8 * asum[m * nb + blk];
-			const float term = __fmul_rn(__fmul_rn(dw, ad[m * nb + blk]), __int2float_rn(t));
-			const float t1 = __shfl_sync(0xffffffffu, term, r + 8);
-			const float t2 = __shfl_sync(0xffffffffu, term, r + 16);
-			const float t3 = __shfl_sync(0xffffffffu, term, r + 24);
-			s[m] = __fadd_rn(s[m], term);
-			if (bb + 1 < sb)
+			const float t1 = __shfl_sync(0xffffffffu, term[j][m], r + 8);
+			const float t2 = __shfl_sync(0xffffffffu, term[j][m], r + 16);
+			const float t3 = __shfl_sync(0xffffffffu, term[j][m], r + 24);
+			s[m] = __fadd_rn(s[m], term[j][m]);
+			if ((uint32_t)j * 4 + 1 < sb)
 				s[m] = __fadd_rn(s[m], t1);
-			if (bb + 2 < sb)
+			if ((uint32_t)j * 4 + 2 < sb)
 				s[m] = __fadd_rn(s[m], t2);
-			if (bb + 3 < sb)
+			if ((uint32_t)j * 4 + 3 < sb)
 				s[m] = __fadd_rn(s[m], t3);
 		}
 	}
@@ -201,10 +208,16 @@ qmv_kernel(const __grid_constant__ QmvParams p)
 	}
 	__syncthreads();
 	for (uint32_t i = threadIdx.x; i < M * nb; i += blockDim.x) {
-		const int8_t *b = aq + (size_t)i * 32;
-		int sum = 0;
-		for (int j = 0; j < 32; j++)
-			sum += b[j];
+		const uint4 *b = reinterpret_cast<const uint4 *>(aq + (size_t)i * 32);
+		const uint4 u = b[0], v = b[1];
+		int sum = dp4a_ss(u.x, 0x01010101u, 0);
+		sum = dp4a_ss(u.y, 0x01010101u, sum);
+		sum = dp4a_ss(u.z, 0x01010101u, sum);
+		sum = dp4a_ss(u.w, 0x01010101u, sum);
+		sum = dp4a_ss(v.x, 0x01010101u, sum);
+		sum = dp4a_ss(v.y, 0x01010101u, sum);
+		sum = dp4a_ss(v.z, 0x01010101u, sum);
+		sum = dp4a_ss(v.w, 0x01010101u, sum);
 		asum[i] = sum;
 	}
 	__syncthreads();
@@ -237,19 +250,17 @@ qmv_kernel(const __grid_constant__ QmvParams p)
 		const uint8_t *st = ring + stage * MAX_SEG_BYTES;
 		const uint32_t sb = seg_blocks(nb, seg);
 		if (T.type == TYPE_Q8_0)
-			seg_q8<M>(st, sb, seg * SB, aq, ad, nb, lane, s);
+			seg_terms<M, true>(st, sb, seg * SB, aq, ad, asum, nb, lane, s);
 		else
-			seg_q4<M>(st, sb, seg * SB, aq, ad, asum, nb, lane, s);
+			seg_terms<M, false>(st, sb, seg * SB, aq, ad, asum, nb, lane, s);
 		__syncwarp();
 		if (lane == 0 && i + QMV_STAGES < nitems) {
 			fence_proxy_async_smem();
 			issue(i + QMV_STAGES);
 		}
 		if (seg == nseg - 1) {
-			const bool q8 = T.type == TYPE_Q8_0;
-			const bool owner = q8 ? (lane < 16 && !(lane & 1)) : lane < 8;
-			const uint32_t row = lg * RG + (q8 ? (lane >> 1) : lane);
-			if (owner && row < T.rows) {
+			const uint32_t row = lg * RG + lane;
+			if (lane < RG && row < T.rows) {
 #pragma unroll
 				for (int m = 0; m < M; m++)
 					T.y[(size_t)m * T.y_stride + row] = s[m];

@@ -52,7 +52,7 @@ SIGNATURES = [
     ("charsiu_gpu_llama_open", _vp, [C.c_char_p, C.c_int, C.c_int]),
     ("charsiu_gpu_llama_close", None, [_vp]),
     ("charsiu_gpu_llama_forward", C.POINTER(C.c_float), [_vp, C.c_int32, C.c_int]),
-    ("charsiu_gpu_llama_argmax", C.c_int32, [_vp, C.c_uint32]),
+    ("charsiu_gpu_llama_argmax", C.c_int32, [C.POINTER(C.c_float), C.c_uint32]),
     ("charsiu_gpu_llama_greedy", C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp, _vp,
                                            C.POINTER(C.c_double)]),
     ("charsiu_gpu_llama_vocab", C.c_uint32, [_vp]),

@@ -52,7 +52,8 @@ struct charsiu_gpu;
 /* ---- lifetime ------------------------------------------------------------ */
 
 /* charsiu_npu_open (include/charsiu_llm.h:188-189, src/npudev.c:140-233).
- * Device 0, the whole of every tensor. NULL: no usable GPU; stay on the CPU. */
+ * Device 0, the whole of every tensor. max_k: a multiple of 32, at most
+ * 14336. NULL: no usable GPU; stay on the CPU. */
 CHARSIU_GPU_API struct charsiu_gpu *charsiu_gpu_open(unsigned max_k, unsigned max_n,
 				     unsigned max_tensors);
 

@@ -57,6 +57,8 @@ def lib():
         L.orc_forward.restype = C.POINTER(C.c_float)
         L.orc_greedy.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _i32p]
         L.orc_greedy.restype = C.c_int
+        L.orc_argmax.argtypes = [C.POINTER(C.c_float), C.c_uint32]
+        L.orc_argmax.restype = C.c_int32
         _lib = L
     return _lib
 
@@ -80,6 +82,10 @@ def ref():
         R.ref_greedy.argtypes = [C.c_char_p, _i32p, C.c_int, C.c_int, C.c_int, _i32p,
                                  C.POINTER(C.c_double), C.POINTER(C.c_double), C.c_void_p]
         R.ref_greedy.restype = C.c_int
+        R.ref_greedy_timed.argtypes = [C.c_char_p, _i32p, C.c_int, C.c_int, C.c_int, _i32p,
+                                       C.POINTER(C.c_double), C.POINTER(C.c_double), C.c_void_p,
+                                       C.c_void_p]
+        R.ref_greedy_timed.restype = C.c_int
         _ref = R
     return _ref
 
@@ -227,3 +233,42 @@ def ref_greedy(path: str, prompt, n_gen: int, n_ctx: int = 0, threads: int | Non
         raise RuntimeError(f"reference could not load {path}")
     res = (out[:n], pm.value, gm.value)
     return res + (lg,) if want_logits else res
+
+
+def ref_greedy_timed(path: str, prompt, n_gen: int, n_ctx: int = 0, threads: int | None = None):
+    """(tokens, ms stamps after each generated token's forward pass)."""
+    if threads is not None:
+        os.environ["CHARSIU_THREADS"] = str(threads)
+    out = np.zeros(n_gen, dtype=np.int32)
+    stamps = np.zeros(n_gen, dtype=np.float64)
+    p = np.ascontiguousarray(prompt, dtype=np.int32)
+    pm, gm = C.c_double(), C.c_double()
+    n = ref().ref_greedy_timed(path.encode(), p, p.size, n_gen, n_ctx, out, C.byref(pm),
+                               C.byref(gm), None, _ptr(stamps))
+    if n < 0:
+        raise RuntimeError(f"reference could not load {path}")
+    return out[:n], stamps[:n]
+
+
+def port_greedy_timed(gguf, prompt, n_gen: int, n_ctx: int = 64):
+    """The restated decode loop, one thread: (tokens, ms stamps)."""
+    import time
+    om = OracleModel(gguf, n_ctx=n_ctx)
+    L = lib()
+    st = L.orc_state_new(C.byref(om.m), n_ctx)
+    try:
+        lp = None
+        for i, t in enumerate(prompt):
+            lp = L.orc_forward(st, int(t), i)
+        pos = len(prompt)
+        out = np.zeros(n_gen, dtype=np.int32)
+        stamps = np.zeros(n_gen, dtype=np.float64)
+        t0 = time.perf_counter()
+        for i in range(n_gen):
+            out[i] = L.orc_argmax(lp, om.shape.n_vocab)
+            lp = L.orc_forward(st, int(out[i]), pos)
+            pos += 1
+            stamps[i] = (time.perf_counter() - t0) * 1e3
+        return out, stamps
+    finally:
+        L.orc_state_free(st)

@@ -101,9 +101,23 @@ static double now_ms(void)
  * *gen_ms is the generation time (tools/charsiu_run.c:295-339), and, when
  * logits_out is given, the logits after the prompt are copied into it.
  */
+int ref_greedy_timed(const char *path, const int32_t *prompt, int n_prompt,
+		     int n_gen, int n_ctx, int32_t *out, double *prompt_ms,
+		     double *gen_ms, float *logits_out, double *tok_ms);
+
 int ref_greedy(const char *path, const int32_t *prompt, int n_prompt,
 	       int n_gen, int n_ctx, int32_t *out, double *prompt_ms,
 	       double *gen_ms, float *logits_out)
+{
+	return ref_greedy_timed(path, prompt, n_prompt, n_gen, n_ctx, out,
+				prompt_ms, gen_ms, logits_out, NULL);
+}
+
+/* The same, also stamping tok_ms[i]: ms since the generation loop began when
+ * token i's forward pass had finished. */
+int ref_greedy_timed(const char *path, const int32_t *prompt, int n_prompt,
+		     int n_gen, int n_ctx, int32_t *out, double *prompt_ms,
+		     double *gen_ms, float *logits_out, double *tok_ms)
 {
 	struct llama_model m;
 	struct llama_state *st;
@@ -131,6 +145,8 @@ int ref_greedy(const char *path, const int32_t *prompt, int n_prompt,
 		if (st->pos >= st->n_ctx)
 			break;
 		logits = llama_forward(st, out[i], st->pos);
+		if (tok_ms)
+			tok_ms[i] = now_ms() - t0;
 	}
 	if (gen_ms)
 		*gen_ms = now_ms() - t0;

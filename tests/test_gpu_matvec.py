@@ -27,7 +27,7 @@ def same(a, b):
 
 @pytest.fixture(scope="module")
 def layer():
-    with Layer(max_k=8192, max_n=128256, max_tensors=64) as L:
+    with Layer(max_k=8256, max_n=128256, max_tensors=64) as L:
         yield L
 
 
