@@ -226,7 +226,7 @@ def run_ours(args, rank, world, dist):
     achieved = tok_bytes / (ms_per_step * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
-                "kernel": "cgpu::qmv_kernel<1>", "peak_kind": peak_kind,
+                "kernel": "cgpu::qmv1_kernel (M=1 block-quant matvec)", "peak_kind": peak_kind,
                 "bytes_per_launch": round(tok_bytes / per_token_launches),
                 "avg_launch_us": round(ms_per_step * 1e3 / per_token_launches, 3)}
     del graph
@@ -291,6 +291,7 @@ def run_e2e(path, args, lib):
             pos += 1
             tok = L.charsiu_gpu_llama_argmax(lp, m.n_vocab)
         calls0 = m.calls
+        m.stages(reset=True)
         t0 = time.perf_counter()
         for _ in range(n_gen_timed):
             lp = L.charsiu_gpu_llama_forward(m.h, tok, pos)
@@ -300,6 +301,7 @@ def run_e2e(path, args, lib):
             tok = L.charsiu_gpu_llama_argmax(lp, m.n_vocab)
         dt = time.perf_counter() - t0
         calls = (m.calls - calls0) / n_gen_timed
+        stages = {k: round(v, 4) for k, v in m.stages().items()}
     groups = launch_groups(SHAPE)
     h2d = sum(k + 4 * (k // 32) for _, k in groups)
     d2h = 4 * (SHAPE.n_layer * (SHAPE.n_embd * 2 + 2 * SHAPE.n_head_kv * SHAPE.head_dim
@@ -307,6 +309,7 @@ def run_e2e(path, args, lib):
     return {"value": round(n_gen_timed / dt, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": n_gen_timed, "warmup": n_warm,
             "calls_per_step": calls, "ms_per_step": round(dt * 1e3 / n_gen_timed, 4),
+            "stages_ms_per_step": stages,
             "api": "charsiu_gpu_llama_forward (C ABI, host buffers), positions "
                    f"{len(prompt) + n_warm}..{len(prompt) + n_warm + n_gen_timed - 1}"}
 
@@ -329,6 +332,71 @@ def cpu_baseline(path):
     return {"value": round(rate, 3), "unit": UNIT, "cores": cores, "kind": kind,
             "sample": f"6-token prompt then {n} greedy tokens of the same model; rate over "
                       f"tokens 2..{n} (the first is warm-up)"}
+
+
+# ---- one matvec on its own -------------------------------------------------------
+
+def run_matvec_case(args):
+    """--matvec q8_0:2048:8192: one block-quant matvec shape (M = 1), enough
+    copies of the weights rotated that every launch streams from HBM (their
+    total is at least twice the 126 MB L2), launches replayed as a CUDA graph."""
+    import torch
+    from charsiu_b200.lib import Layer
+
+    qname, k, n = args.matvec.split(":")
+    k, n = int(k), int(n)
+    qtype = {"q8_0": G.GGML_Q8_0, "q4_0": G.GGML_Q4_0}[qname]
+    blk, _ = W.matvec_inputs(qtype, k, n, seed=1)
+    wbytes = blk.nbytes
+    copies = max(2, -(-2 * 126 * 2 ** 20 // wbytes))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    with Layer(max_k=k, max_n=n, max_tensors=copies) as L:
+        ids = [L.add_blocks(qtype, k, n, blk, f"copy{i}") for i in range(copies)]
+        x = torch.randn(k, generator=torch.Generator().manual_seed(7)).to(dev)
+        q = torch.empty(k, dtype=torch.int8, device=dev)
+        d = torch.empty(k // 32, dtype=torch.float32, device=dev)
+        y = torch.empty(n, dtype=torch.float32, device=dev)
+        stream = torch.cuda.Stream(device=dev)
+        assert L.act_quantise_dev(x.data_ptr(), 1, k, q.data_ptr(), d.data_ptr(),
+                                  stream.cuda_stream) == 0
+
+        def launch(i):
+            assert L.matvec_dev([ids[i % copies]], q.data_ptr(), d.data_ptr(), [y.data_ptr()],
+                                stream.cuda_stream) == 0
+        for i in range(args.warmup):
+            launch(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(args.steps):
+                launch(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        clocks = Clocks(0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        del graph
+    algo = wbytes + k + 4 * (k // 32) + 4 * n
+    peak, peak_kind = peaks()
+    gbs = algo / (us * 1e-6) / 1e9
+    return {"metric": "quant matvec HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(us / 1e3, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"{qname} matvec M=1 K={k} N={n}", "weight_copies": copies,
+                       "l2": f"{copies} weight copies rotated ({copies * wbytes / 1e6:.0f} MB "
+                             "> 2x L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "bytes_per_launch": algo, "avg_launch_us": round(us, 3)},
+            "gpu_launches": args.steps, "clocks": clk}
 
 
 # ---- the reference arm --------------------------------------------------------
@@ -372,6 +440,8 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N",
+                    help="time one matvec shape instead of the decode (e.g. q8_0:2048:8192)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -389,6 +459,9 @@ def main():
         dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
                                 timeout=datetime.timedelta(seconds=600))
     try:
+        if args.matvec:
+            print(json.dumps(run_matvec_case(args)), flush=True)
+            return
         if args.impl == "reference":
             out = run_reference(args, rank, world, dist)
         else:

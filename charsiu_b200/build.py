@@ -28,7 +28,9 @@ C_SOURCES = [os.path.join(HOST, f) for f in sorted(os.listdir(HOST)) if f.endswi
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-fmad=false", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               f"-I{INCLUDE}", f"-I{CSRC}"]
-CC_FLAGS = ["-O2", "-std=c11", "-fPIC", "-ffp-contract=off", "-Wall", "-Wextra",
+# -fno-math-errno only lets lrintf / sqrtf compile to their single instructions
+# (cvtss2si in the default round-to-nearest-even mode, sqrtss): same values.
+CC_FLAGS = ["-O2", "-std=c11", "-fPIC", "-ffp-contract=off", "-fno-math-errno", "-Wall", "-Wextra",
             "-fvisibility=hidden", f"-I{INCLUDE}"]
 
 

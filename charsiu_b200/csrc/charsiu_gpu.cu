@@ -84,6 +84,13 @@ bool grow_host(T *&p, size_t &cap, size_t want)
 	return true;
 }
 
+// One host call captured as a CUDA graph: tensors ids[0..n) at K = k.
+struct CallGraph {
+	int ids[8];
+	unsigned n, k;
+	cudaGraphExec_t exec;
+};
+
 } // namespace
 
 struct charsiu_gpu {
@@ -94,13 +101,20 @@ struct charsiu_gpu {
 	cudaEvent_t ev_k0 = nullptr, ev_k1 = nullptr, ev_done = nullptr;
 	std::vector<Ent> ent;
 
-	int8_t *d_q = nullptr, *h_q = nullptr;
-	float *d_d = nullptr, *h_d = nullptr, *d_y = nullptr, *h_y = nullptr;
-	size_t cap_dq = 0, cap_hq = 0, cap_dd = 0, cap_hd = 0, cap_dy = 0, cap_hy = 0;
+	// host-call staging: the activation as one [q | d] block, and every y
+	uint8_t *d_act = nullptr, *h_act = nullptr;
+	float *d_y = nullptr, *h_y = nullptr;
+	size_t cap_dact = 0, cap_hact = 0, cap_dy = 0, cap_hy = 0;
+	int8_t *d_q = nullptr;              // block-dot test hook
+	size_t cap_dq = 0;
+	std::vector<CallGraph> graphs;
 	uint8_t *d_i8 = nullptr, *h_i8 = nullptr;
 	size_t cap_di8 = 0, cap_hi8 = 0;
 	int32_t *d_dots = nullptr;
 	size_t cap_dots = 0;
+	// a kernel whose wait gave up writes here: mapped host memory, read after
+	// the call's event without another copy
+	volatile int *h_err = nullptr;
 	int *d_err = nullptr;
 	bool smem_set[24] = {};
 	// CTAs per SM for (m, nb): asked of the driver once, never during capture
@@ -116,6 +130,14 @@ struct charsiu_gpu {
 };
 
 namespace {
+
+void drop_graphs(charsiu_gpu *g)
+{
+	for (CallGraph &c : g->graphs)
+		if (c.exec)
+			cudaGraphExecDestroy(c.exec);
+	g->graphs.clear();
+}
 
 // Say why, once (the reference's whine(), src/npudev.c:124-138): a silent
 // fallback to the CPU produces results that look like GPU evidence.
@@ -170,10 +192,8 @@ int finish(charsiu_gpu *g, double t0, double mb, unsigned k, unsigned n)
 		retire(g, "a CUDA error");
 		return -1;
 	}
-	int derr = 0;
-	cudaMemcpy(&derr, g->d_err, sizeof(int), cudaMemcpyDeviceToHost);
-	if (derr) {
-		cudaMemset(g->d_err, 0, sizeof(int));
+	if (*g->h_err) {
+		*g->h_err = 0;
 		whine(g, "a kernel wait gave up (K=%u N=%u)", k, n);
 		retire(g, "a kernel wait gave up");
 		return -1;
@@ -335,8 +355,37 @@ int check_ids(charsiu_gpu *g, const int *ids, unsigned n, unsigned k)
 	return 0;
 }
 
-// The host-pointer matvec: H2D of the activation, one launch per chunk of at
-// most QMV_MAX_M activation rows, D2H of every y, one fence.
+// Queue the kernels of one host call: one launch per chunk of at most
+// QMV_MAX_M activation rows (the M = 1 path one launch per quant type).
+int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k, unsigned m)
+{
+	const uint32_t nb = k / 32;
+	const int8_t *dq = reinterpret_cast<const int8_t *>(g->d_act);
+	const float *dd = reinterpret_cast<const float *>(g->d_act + (size_t)m * nb * 32);
+	for (unsigned m0 = 0, mc = 0; m0 < m; m0 += mc) {
+		const unsigned left = m - m0;
+		mc = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+		float *yd[QMV_MAX_TENSORS];
+		size_t off = 0;
+		for (unsigned i = 0; i < n; i++) {
+			yd[i] = g->d_y + off + (size_t)m0 * g->ent[ids[i]].rows;
+			off += (size_t)m * g->ent[ids[i]].rows;
+		}
+		QmvParams p;
+		fill_params(g, p, ids, n, yd, k, dq + (size_t)m0 * nb * 32, dd + (size_t)m0 * nb);
+		const int rc = mc == 1 ? launch_matvec1(g, ids, n, yd, k, p.q, p.d, g->stream)
+				       : launch_qmv(g, (int)mc, p, g->stream);
+		if (rc)
+			return -1;
+	}
+	return 0;
+}
+
+// The host-pointer matvec (charsiu_gpu_matvec / _group / _batch): the
+// activation copied in as one [q | d] block, the kernels, every y copied
+// back, one fence. From its second call on, a given single-activation call
+// (same tensors) replays a CUDA graph of the whole sequence, so a call costs
+// one graph launch and one event wait.
 int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, const float *d,
 	       unsigned k, unsigned m, float **ys)
 {
@@ -353,54 +402,75 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 		return -1;
 	}
 	const uint32_t nb = k / 32;
+	const size_t qbytes = (size_t)m * nb * 32, abytes = qbytes + (size_t)m * nb * sizeof(float);
 	size_t ytot = 0;
 	double mb = 0;
 	for (unsigned i = 0; i < n; i++) {
 		ytot += (size_t)m * g->ent[ids[i]].rows;
 		mb += g->ent[ids[i]].weight_mb;
 	}
-	if (!grow_dev(g->d_q, g->cap_dq, (size_t)m * nb * 32) ||
-	    !grow_dev(g->d_d, g->cap_dd, (size_t)m * nb) ||
-	    !grow_dev(g->d_y, g->cap_dy, ytot) ||
-	    !grow_host(g->h_q, g->cap_hq, (size_t)m * nb * 32) ||
-	    !grow_host(g->h_d, g->cap_hd, (size_t)m * nb) ||
-	    !grow_host(g->h_y, g->cap_hy, ytot)) {
+	const size_t caps[4] = {g->cap_dact, g->cap_hact, g->cap_dy, g->cap_hy};
+	if (!grow_dev(g->d_act, g->cap_dact, abytes) || !grow_host(g->h_act, g->cap_hact, abytes) ||
+	    !grow_dev(g->d_y, g->cap_dy, ytot) || !grow_host(g->h_y, g->cap_hy, ytot)) {
 		whine(g, "a staging buffer would not allocate");
 		return -1;
 	}
+	if (caps[0] != g->cap_dact || caps[1] != g->cap_hact || caps[2] != g->cap_dy ||
+	    caps[3] != g->cap_hy)
+		drop_graphs(g);         // they name the old staging buffers
 
 	const double t0 = now_us();
-	memcpy(g->h_q, q, (size_t)m * nb * 32);
-	memcpy(g->h_d, d, (size_t)m * nb * sizeof(float));
-	cudaMemcpyAsync(g->d_q, g->h_q, (size_t)m * nb * 32, cudaMemcpyHostToDevice, g->stream);
-	cudaMemcpyAsync(g->d_d, g->h_d, (size_t)m * nb * sizeof(float), cudaMemcpyHostToDevice,
-			g->stream);
-	const double t1 = now_us();
+	memcpy(g->h_act, q, qbytes);
+	memcpy(g->h_act + qbytes, d, (size_t)m * nb * sizeof(float));
 
-	cudaEventRecord(g->ev_k0, g->stream);
-	for (unsigned m0 = 0, mc = 0; m0 < m; m0 += mc) {
-		const unsigned left = m - m0;
-		mc = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
-		float *yd[QMV_MAX_TENSORS];
-		size_t off = 0;
-		for (unsigned i = 0; i < n; i++) {
-			yd[i] = g->d_y + off + (size_t)m0 * g->ent[ids[i]].rows;
-			off += (size_t)m * g->ent[ids[i]].rows;
-		}
-		QmvParams p;
-		fill_params(g, p, ids, n, yd, k, g->d_q + (size_t)m0 * nb * 32,
-			    g->d_d + (size_t)m0 * nb);
-		const int rc = mc == 1 ? launch_matvec1(g, ids, n, yd, k, p.q, p.d, g->stream)
-				       : launch_qmv(g, (int)mc, p, g->stream);
-		if (rc) {
-			whine(g, "the launch failed: %s", cudaGetErrorString(cudaGetLastError()));
-			retire(g, "a launch failed");
-			return -1;
+	CallGraph *cg = nullptr;
+	if (m == 1) {
+		for (CallGraph &c : g->graphs)
+			if (c.n == n && c.k == k && !memcmp(c.ids, ids, n * sizeof(int)))
+				cg = &c;
+	}
+	bool ok = true;
+	if (cg && cg->exec) {
+		ok = cudaGraphLaunch(cg->exec, g->stream) == cudaSuccess;
+	} else {
+		// the first call of a set runs eagerly (warming every launch cache)
+		// and records the set; the second captures it
+		cudaGraph_t graph = nullptr;
+		const bool capture = cg != nullptr;
+		if (capture)
+			ok = cudaStreamBeginCapture(g->stream, cudaStreamCaptureModeThreadLocal) ==
+			     cudaSuccess;
+		ok = ok && cudaMemcpyAsync(g->d_act, g->h_act, abytes, cudaMemcpyHostToDevice,
+					   g->stream) == cudaSuccess;
+		// while capturing, external records, so the graph holds real event
+		// nodes (a plain record there is only a dependency edge)
+		const unsigned rf = capture ? cudaEventRecordExternal : cudaEventRecordDefault;
+		ok = ok && cudaEventRecordWithFlags(g->ev_k0, g->stream, rf) == cudaSuccess;
+		ok = ok && !queue_matvec_kernels(g, ids, n, k, m);
+		ok = ok && cudaEventRecordWithFlags(g->ev_k1, g->stream, rf) == cudaSuccess;
+		ok = ok && cudaMemcpyAsync(g->h_y, g->d_y, ytot * sizeof(float),
+					   cudaMemcpyDeviceToHost, g->stream) == cudaSuccess;
+		if (capture) {
+			ok = cudaStreamEndCapture(g->stream, &graph) == cudaSuccess && ok;
+			ok = ok && cudaGraphInstantiate(&cg->exec, graph, 0) == cudaSuccess;
+			if (graph)
+				cudaGraphDestroy(graph);
+			ok = ok && cudaGraphLaunch(cg->exec, g->stream) == cudaSuccess;
+		} else if (m == 1 && n <= QMV_MAX_TENSORS && g->graphs.size() < 4 * g->max_tensors) {
+			CallGraph c = {};
+			c.n = n;
+			c.k = k;
+			memcpy(c.ids, ids, n * sizeof(int));
+			g->graphs.push_back(c);
 		}
 	}
-	cudaEventRecord(g->ev_k1, g->stream);
-	cudaMemcpyAsync(g->h_y, g->d_y, ytot * sizeof(float), cudaMemcpyDeviceToHost, g->stream);
+	if (!ok) {
+		whine(g, "the launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+		retire(g, "a launch failed");
+		return -1;
+	}
 	cudaEventRecord(g->ev_done, g->stream);
+	const double t1 = now_us();
 	if (finish(g, t0, mb, k, (unsigned)g->ent[ids[0]].n))
 		return -1;
 	const double t2 = now_us();
@@ -411,7 +481,10 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 		off += cnt;
 	}
 	float kms = 0;
-	cudaEventElapsedTime(&kms, g->ev_k0, g->ev_k1);
+	if (cudaEventElapsedTime(&kms, g->ev_k0, g->ev_k1) != cudaSuccess) {
+		kms = 0;
+		cudaGetLastError();      // timing is best effort; clear it
+	}
 	const double t3 = now_us();
 	g->calls++;
 	g->weight_mb += mb;
@@ -459,15 +532,15 @@ struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	if (cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking) != cudaSuccess ||
 	    cudaEventCreate(&g->ev_k0) != cudaSuccess || cudaEventCreate(&g->ev_k1) != cudaSuccess ||
 	    cudaEventCreateWithFlags(&g->ev_done, cudaEventDisableTiming) != cudaSuccess ||
-	    cudaMalloc(&g->d_err, sizeof(int)) != cudaSuccess ||
-	    cudaMemset(g->d_err, 0, sizeof(int)) != cudaSuccess) {
+	    cudaHostAlloc((void **)&g->h_err, sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
+	    cudaHostGetDevicePointer((void **)&g->d_err, (void *)g->h_err, 0) != cudaSuccess) {
 		charsiu_gpu_close(g);
 		return nullptr;
 	}
 	const size_t nb = max_k / 32;
-	if (!grow_dev(g->d_q, g->cap_dq, nb * 32) || !grow_dev(g->d_d, g->cap_dd, nb) ||
+	*g->h_err = 0;
+	if (!grow_dev(g->d_act, g->cap_dact, nb * 36) || !grow_host(g->h_act, g->cap_hact, nb * 36) ||
 	    !grow_dev(g->d_y, g->cap_dy, (size_t)max_n + 64) ||
-	    !grow_host(g->h_q, g->cap_hq, nb * 32) || !grow_host(g->h_d, g->cap_hd, nb) ||
 	    !grow_host(g->h_y, g->cap_hy, (size_t)max_n + 64)) {
 		charsiu_gpu_close(g);
 		return nullptr;
@@ -490,14 +563,15 @@ void charsiu_gpu_close(struct charsiu_gpu *g)
 	for (Ent &e : g->ent)
 		if (e.data)
 			cudaFree(e.data);
+	drop_graphs(g);
+	cudaFree(g->d_act);
 	cudaFree(g->d_q);
-	cudaFree(g->d_d);
 	cudaFree(g->d_y);
 	cudaFree(g->d_i8);
 	cudaFree(g->d_dots);
-	cudaFree(g->d_err);
-	cudaFreeHost(g->h_q);
-	cudaFreeHost(g->h_d);
+	if (g->h_err)
+		cudaFreeHost((void *)g->h_err);
+	cudaFreeHost(g->h_act);
 	cudaFreeHost(g->h_y);
 	cudaFreeHost(g->h_i8);
 	if (g->ev_k0)
@@ -540,6 +614,7 @@ int charsiu_gpu_add_blocks(struct charsiu_gpu *g, uint32_t type, uint64_t k, uin
 		return -1;
 	}
 	cudaSetDevice(g->device);
+	cudaGetLastError();              // a stale error must not be read as this upload's
 
 	Ent e;
 	memset(&e, 0, sizeof(e));
@@ -785,7 +860,10 @@ int charsiu_gpu_matmul_i8_flat(struct charsiu_gpu *g, unsigned m, unsigned k, un
 	const double t2 = now_us();
 	memcpy(out, g->h_i8 + oo, (size_t)m * n);
 	float kms = 0;
-	cudaEventElapsedTime(&kms, g->ev_k0, g->ev_k1);
+	if (cudaEventElapsedTime(&kms, g->ev_k0, g->ev_k1) != cudaSuccess) {
+		kms = 0;
+		cudaGetLastError();
+	}
 	const double t3 = now_us();
 	g->calls++;
 	g->weight_mb += mb;

@@ -43,7 +43,7 @@ struct QmvParams {
 	uint32_t ntensor, total_groups, k, nb;
 	const int8_t *q;         // activation quants [M][nb * 32]
 	const float *d;          // activation deltas [M][nb]
-	int *err;                // set nonzero if a wait gave up
+	int *err;                // set nonzero if a wait gave up (mapped host memory)
 };
 
 inline size_t qmv_smem_bytes(int m, uint32_t nb)
@@ -232,7 +232,7 @@ qmv_kernel(const __grid_constant__ QmvParams p)
 		const uint32_t stage = i % QMV_STAGES;
 		if (!mbar_wait_bounded(&bar[stage], (i / QMV_STAGES) & 1, WAIT_LIMIT_NS)) {
 			if (lane == 0)
-				atomicExch(p.err, 1);
+				*(volatile int *)p.err = 1;
 			// let the copies already issued land before this CTA leaves
 			const uint32_t issued = min(nitems, i + QMV_STAGES);
 			for (uint32_t j = i + 1; j < issued; j++)

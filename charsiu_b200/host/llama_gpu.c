@@ -317,8 +317,23 @@ struct layer {
 	int id[P_N];
 };
 
+/* where the token's time goes: the stages of src/llama.c:695-705 */
+enum {
+	ST_EMBD, ST_NORM1, ST_QKV, ST_ROPE, ST_ATTN, ST_WO, ST_RES1,
+	ST_NORM2, ST_GATEUP, ST_SILU, ST_DOWN, ST_RES2, ST_NORMF, ST_HEAD,
+	ST_N
+};
+
+static const char *stage_name[ST_N] = {
+	"token embedding", "attn rmsnorm", "q k v", "rope + kv copy",
+	"attention", "o proj", "residual", "ffn rmsnorm", "gate + up",
+	"silu * up", "down", "residual", "final rmsnorm", "output head",
+};
+
 struct charsiu_gpu_llama {
 	struct gfile g;
+	double stage_ms[ST_N];
+	unsigned stage_tok;
 	struct charsiu_gpu *dev;
 	uint32_t n_embd, n_layer, n_head, n_head_kv, n_ff, n_vocab, hd;
 	float eps, base;
@@ -328,6 +343,7 @@ struct charsiu_gpu_llama {
 	struct layer *L;
 	int n_ctx, nogroup;
 	float *kcache, *vcache, *x, *xb, *xb2, *hb, *hb2, *q, *k, *v, *att, *logits;
+	float *rope_cs;           /* cos, sin of each pair at the current pos */
 	int8_t *aq;
 	float *ad;
 };
@@ -443,14 +459,27 @@ static void softmax(float *x, int n)
 		x[i] /= sum;
 }
 
-static void rope(float *v, uint32_t nheads, uint32_t hd, int pos, float base)
+/* The rotation of pair i at `pos` depends on neither the head nor the layer,
+ * so its cos and sin are computed once a token (the same libm calls on the
+ * same arguments as src/llama.c:373-379, hence the same values) and applied
+ * to every head of every layer. */
+static void rope_angles(float *cs, uint32_t hd, int pos, float base)
+{
+	for (uint32_t i = 0; i < hd / 2; i++) {
+		float theta = (float)pos * powf(base, -2.0f * (float)i / (float)hd);
+
+		cs[2 * i] = cosf(theta);
+		cs[2 * i + 1] = sinf(theta);
+	}
+}
+
+static void rope(float *v, uint32_t nheads, uint32_t hd, const float *cs)
 {
 	for (uint32_t h = 0; h < nheads; h++) {
 		float *p = v + h * hd;
 
 		for (uint32_t i = 0; i < hd / 2; i++) {
-			float theta = (float)pos * powf(base, -2.0f * (float)i / (float)hd);
-			float c = cosf(theta), s = sinf(theta);
+			float c = cs[2 * i], s = cs[2 * i + 1];
 			float x0 = p[2 * i], x1 = p[2 * i + 1];
 
 			p[2 * i] = x0 * c - x1 * s;
@@ -477,12 +506,25 @@ API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m)
 {
 	if (!m)
 		return;
+	if (getenv("CHARSIU_STAGES") && m->stage_tok) {
+		double tot = 0;
+
+		for (int i = 0; i < ST_N; i++)
+			tot += m->stage_ms[i];
+		fprintf(stderr, "charsiu stages: %u tokens, %.3f ms a token\n", m->stage_tok,
+			tot / m->stage_tok);
+		for (int i = 0; i < ST_N; i++)
+			fprintf(stderr, "  %-16s %8.3f ms a token   %5.1f%%\n", stage_name[i],
+				m->stage_ms[i] / m->stage_tok, 100.0 * m->stage_ms[i] / tot);
+	}
+	if (m->dev && getenv("CHARSIU_GPU_REPORT"))
+		charsiu_gpu_report(m->dev);
 	charsiu_gpu_close(m->dev);
 	free(m->L);
 	free(m->kcache); free(m->vcache);
 	free(m->x); free(m->xb); free(m->xb2); free(m->hb); free(m->hb2);
 	free(m->q); free(m->k); free(m->v); free(m->att); free(m->logits);
-	free(m->aq); free(m->ad);
+	free(m->aq); free(m->ad); free(m->rope_cs);
 	gclose(&m->g);
 	free(m);
 }
@@ -596,7 +638,8 @@ API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *path, int n_ctx
 	m->logits = calloc(m->n_vocab, sizeof(float));
 	m->aq = calloc((size_t)(widest + 31) / 32 * 32, 1);
 	m->ad = calloc((size_t)(widest + 31) / 32, sizeof(float));
-	if (!m->kcache || !m->vcache || !m->x || !m->xb || !m->xb2 || !m->hb || !m->hb2 ||
+	m->rope_cs = calloc(m->hd, sizeof(float));
+	if (!m->rope_cs || !m->kcache || !m->vcache || !m->x || !m->xb || !m->xb2 || !m->hb || !m->hb2 ||
 	    !m->q || !m->k || !m->v || !m->att || !m->logits || !m->aq || !m->ad)
 		goto fail;
 	return m;
@@ -605,15 +648,28 @@ fail:
 	return NULL;
 }
 
+static double now_ms(void)
+{
+	struct timespec t;
+
+	clock_gettime(CLOCK_MONOTONIC, &t);
+	return (double)t.tv_sec * 1e3 + (double)t.tv_nsec / 1e6;
+}
+
 API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t token, int pos)
 {
 	uint32_t hd = m->hd, kvdim = m->n_head_kv * hd, gqa = m->n_head / m->n_head_kv;
 	float scale = 1.0f / sqrtf((float)hd);
+	double t0 = now_ms(), t1;
+
+#define STAGE(i) do { t1 = now_ms(); m->stage_ms[i] += t1 - t0; t0 = t1; } while (0)
 
 	if (pos < 0 || pos >= m->n_ctx || token < 0 || (uint32_t)token >= m->tok->ne[1])
 		return NULL;
 	if (row_f32(m->tok, (uint64_t)token, m->x))
 		return NULL;
+	rope_angles(m->rope_cs, hd, pos, m->base);
+	STAGE(ST_EMBD);
 
 	for (uint32_t l = 0; l < m->n_layer; l++) {
 		const struct layer *L = &m->L[l];
@@ -621,6 +677,7 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 		float *vc = m->vcache + ((size_t)l * m->n_ctx + pos) * kvdim;
 
 		rmsnorm(m->xb, m->x, L->attn_norm, m->n_embd, m->eps);
+		STAGE(ST_NORM1);
 		{
 			int ids[3] = { L->id[P_Q], L->id[P_K], L->id[P_V] };
 			float *ys[3] = { m->q, m->k, m->v };
@@ -628,10 +685,12 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 			if (project(m, m->xb, m->n_embd, ids, ys, 3))
 				return NULL;
 		}
-		rope(m->q, m->n_head, hd, pos, m->base);
-		rope(m->k, m->n_head_kv, hd, pos, m->base);
+		STAGE(ST_QKV);
+		rope(m->q, m->n_head, hd, m->rope_cs);
+		rope(m->k, m->n_head_kv, hd, m->rope_cs);
 		memcpy(kc, m->k, kvdim * sizeof(float));
 		memcpy(vc, m->v, kvdim * sizeof(float));
+		STAGE(ST_ROPE);
 
 		for (uint32_t h = 0; h < m->n_head; h++) {
 			const float *qh = m->q + h * hd;
@@ -657,6 +716,7 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 					out[i] += a * vt[i];
 			}
 		}
+		STAGE(ST_ATTN);
 		{
 			int id = L->id[P_O];
 			float *ys[1] = { m->xb2 };
@@ -664,10 +724,13 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 			if (project(m, m->xb, m->n_embd, &id, ys, 1))
 				return NULL;
 		}
+		STAGE(ST_WO);
 		for (uint32_t i = 0; i < m->n_embd; i++)
 			m->x[i] += m->xb2[i];
+		STAGE(ST_RES1);
 
 		rmsnorm(m->xb, m->x, L->ffn_norm, m->n_embd, m->eps);
+		STAGE(ST_NORM2);
 		{
 			int ids[2] = { L->id[P_GATE], L->id[P_UP] };
 			float *ys[2] = { m->hb, m->hb2 };
@@ -675,12 +738,14 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 			if (project(m, m->xb, m->n_embd, ids, ys, 2))
 				return NULL;
 		}
+		STAGE(ST_GATEUP);
 		for (uint32_t i = 0; i < m->n_ff; i++) {
 			float g = m->hb[i];
 
 			g *= 1.0f / (1.0f + expf(-g));
 			m->hb[i] = g * m->hb2[i];
 		}
+		STAGE(ST_SILU);
 		{
 			int id = L->id[P_DOWN];
 			float *ys[1] = { m->xb2 };
@@ -688,17 +753,43 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 			if (project(m, m->hb, m->n_ff, &id, ys, 1))
 				return NULL;
 		}
+		STAGE(ST_DOWN);
 		for (uint32_t i = 0; i < m->n_embd; i++)
 			m->x[i] += m->xb2[i];
+		STAGE(ST_RES2);
 	}
 	rmsnorm(m->xb, m->x, m->out_norm, m->n_embd, m->eps);
+	STAGE(ST_NORMF);
 	{
 		float *ys[1] = { m->logits };
 
 		if (project(m, m->xb, m->n_embd, &m->out_id, ys, 1))
 			return NULL;
 	}
+	STAGE(ST_HEAD);
+#undef STAGE
+	m->stage_tok++;
 	return m->logits;
+}
+
+/* llama_stages_report / reset (src/llama.c:719-739) */
+API int charsiu_gpu_llama_stages(struct charsiu_gpu_llama *m, double *ms_per_token, int n,
+				 int reset)
+{
+	if (!m)
+		return -1;
+	for (int i = 0; i < n && i < ST_N; i++)
+		ms_per_token[i] = m->stage_tok ? m->stage_ms[i] / m->stage_tok : 0.0;
+	if (reset) {
+		memset(m->stage_ms, 0, sizeof(m->stage_ms));
+		m->stage_tok = 0;
+	}
+	return ST_N;
+}
+
+API const char *charsiu_gpu_llama_stage_name(int i)
+{
+	return i >= 0 && i < ST_N ? stage_name[i] : "";
 }
 
 API int32_t charsiu_gpu_llama_argmax(const float *logits, uint32_t n)
@@ -709,14 +800,6 @@ API int32_t charsiu_gpu_llama_argmax(const float *logits, uint32_t n)
 		if (logits[i] > logits[best])
 			best = (int32_t)i;
 	return best;
-}
-
-static double now_ms(void)
-{
-	struct timespec t;
-
-	clock_gettime(CLOCK_MONOTONIC, &t);
-	return (double)t.tv_sec * 1e3 + (double)t.tv_nsec / 1e6;
 }
 
 API int charsiu_gpu_llama_greedy(struct charsiu_gpu_llama *m, const int32_t *prompt,

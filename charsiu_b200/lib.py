@@ -55,6 +55,8 @@ SIGNATURES = [
     ("charsiu_gpu_llama_argmax", C.c_int32, [C.POINTER(C.c_float), C.c_uint32]),
     ("charsiu_gpu_llama_greedy", C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp, _vp,
                                            C.POINTER(C.c_double)]),
+    ("charsiu_gpu_llama_stages", C.c_int, [_vp, _vp, C.c_int, C.c_int]),
+    ("charsiu_gpu_llama_stage_name", C.c_char_p, [C.c_int]),
     ("charsiu_gpu_llama_vocab", C.c_uint32, [_vp]),
     ("charsiu_gpu_llama_layer", _vp, [_vp]),
 ]
@@ -249,6 +251,12 @@ class Llama:
     @property
     def calls(self) -> int:
         return self.L.charsiu_gpu_calls(self.layer_handle)
+
+    def stages(self, reset: bool = False) -> dict:
+        """Mean ms a token of each forward-pass stage (reference llama.c:695-705)."""
+        ms = np.zeros(32, dtype=np.float64)
+        n = self.L.charsiu_gpu_llama_stages(self.h, _p(ms), 32, int(reset))
+        return {self.L.charsiu_gpu_llama_stage_name(i).decode(): float(ms[i]) for i in range(n)}
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         p = self.L.charsiu_gpu_llama_forward(self.h, token, pos)

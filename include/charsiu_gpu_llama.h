@@ -47,6 +47,14 @@ CHARSIU_GPU_API int32_t charsiu_gpu_llama_argmax(const float *logits, uint32_t n
 CHARSIU_GPU_API int charsiu_gpu_llama_greedy(struct charsiu_gpu_llama *m, const int32_t *prompt, int n_prompt,
 			     int n_gen, int32_t *out, float *logits, double *gen_ms);
 
+/* llama_stages_report (src/llama.c:684-739): the mean ms a token of each
+ * of the forward pass's 14 stages into ms_per_token[0..n), since open or the
+ * last reset. Returns the number of stages. CHARSIU_STAGES=1 also prints the
+ * table at close. */
+CHARSIU_GPU_API int charsiu_gpu_llama_stages(struct charsiu_gpu_llama *m, double *ms_per_token,
+					     int n, int reset);
+CHARSIU_GPU_API const char *charsiu_gpu_llama_stage_name(int i);
+
 CHARSIU_GPU_API uint32_t charsiu_gpu_llama_vocab(const struct charsiu_gpu_llama *m);
 /* the device layer the model runs on (for its report and counters) */
 CHARSIU_GPU_API struct charsiu_gpu *charsiu_gpu_llama_layer(struct charsiu_gpu_llama *m);
