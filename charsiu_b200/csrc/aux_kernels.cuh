@@ -23,11 +23,10 @@ __global__ void repack_kernel(const uint8_t *__restrict__ raw, uint32_t type, ui
 	const uint32_t qb = quant_bytes(type), bsz = qb + 2;
 	const uint8_t *src = raw + ((uint64_t)rl * nb + b) * bsz;
 	uint8_t *segp = dst + (uint64_t)g * group_bytes(type, nb) + seg_offset(type, seg);
-	uint8_t *qd = segp + ((uint64_t)bi * RG + rr) * qb;
 	uint8_t *dd = segp + (uint64_t)sb * RG * qb + ((uint64_t)bi * RG + rr) * 2;
 
 	for (uint32_t j = 0; j < qb; j++)
-		qd[j] = src[2 + j];
+		segp[quant_offset(type, bi, j / 16, rr) + j % 16] = src[2 + j];
 	dd[0] = src[0];
 	dd[1] = src[1];
 }
@@ -44,14 +43,15 @@ __global__ void block_dots_kernel(const uint8_t *__restrict__ data, uint32_t typ
 	const uint32_t r = (uint32_t)(idx / nb), b = (uint32_t)(idx % nb);
 	const uint32_t g = r / RG, rr = r % RG, seg = b / SB, bi = b % SB;
 	const uint32_t qb = quant_bytes(type);
-	const uint8_t *qp = data + (uint64_t)g * group_bytes(type, nb) + seg_offset(type, seg) +
-			    ((uint64_t)bi * RG + rr) * qb;
+	const uint8_t *segp = data + (uint64_t)g * group_bytes(type, nb) + seg_offset(type, seg);
+	const uint8_t *qp = segp + quant_offset(type, bi, 0, rr);
 	const int8_t *x = q + (uint64_t)b * 32;
 	int t = 0;
 
+	(void)qb;
 	if (type == TYPE_Q8_0) {
 		for (int j = 0; j < 32; j++)
-			t += (int)(int8_t)qp[j] * x[j];
+			t += (int)(int8_t)segp[quant_offset(type, bi, j / 16, rr) + j % 16] * x[j];
 	} else {
 		for (int j = 0; j < 16; j++) {
 			t += ((qp[j] & 0x0f) - 8) * x[j];

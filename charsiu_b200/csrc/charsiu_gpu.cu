@@ -19,6 +19,7 @@
 #include "charsiu_gpu.h"
 
 #include "aux_kernels.cuh"
+#include "i8mm_tc.cuh"
 #include "qmv.cuh"
 #include "qmv1.cuh"
 #include "ref_abi.h"
@@ -843,7 +844,15 @@ int charsiu_gpu_matmul_i8_flat(struct charsiu_gpu *g, unsigned m, unsigned k, un
 	p.zp_a = in_zp;
 	p.zp_w = wt_zp;
 	cudaEventRecord(g->ev_k0, g->stream);
-	i8mm_simt_kernel<<<dim3((n + 31) / 32, (m + 31) / 32), 256, 0, g->stream>>>(p);
+	// M = 1 (a matvec): dp4a on the CUDA cores; M > 1: the tensor cores
+	if (m == 1)
+		i8mm_simt_kernel<<<dim3((n + 31) / 32, (m + 31) / 32), 256, 0, g->stream>>>(p);
+	else if (n <= 64)
+		i8mm_tc_kernel<64><<<dim3((n + 63) / 64, (m + I8TC_M - 1) / I8TC_M), 128, 0,
+				    g->stream>>>(p, g->d_err);
+	else
+		i8mm_tc_kernel<128><<<dim3((n + 127) / 128, (m + I8TC_M - 1) / I8TC_M), 128, 0,
+				     g->stream>>>(p, g->d_err);
 	if (cudaGetLastError() != cudaSuccess) {
 		whine(g, "the int8 launch failed");
 		retire(g, "a launch failed");

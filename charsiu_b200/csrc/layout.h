@@ -9,15 +9,17 @@
 //   rows in GROUPS of RG = 8; a group's K in SEGMENTS of SB = 16 blocks;
 //   a segment of sb blocks (sb = SB, or fewer for the last) is one contiguous
 //   run of bytes:
-//       quants  [sb][RG rows][QB]   QB = 32 bytes (q8_0) or 16 (q4_0)
-//       deltas  [sb][RG rows]       fp16, unchanged bits
+//       quants  [sb][QB / 16 chunks][RG rows][16 B]   QB = 32 (q8_0), 16 (q4_0)
+//       deltas  [sb][RG rows]                          fp16, unchanged bits
 //   a group is its segments back to back, a tensor its groups back to back.
 //
-// So one segment is one bulk copy into shared memory, and inside it the RG
-// rows of one block sit side by side: a warp's 16-byte reads cover 512
-// contiguous bytes. Rows past N in the last group are zero (delta 0, quants
-// 0) and are never written out. q4_0 nibbles keep GGUF order (byte j: low
-// nibble element j, high nibble element j + 16).
+// So one segment is one bulk copy, 8 lanes reading 16 bytes each of one chunk
+// cover 128 contiguous bytes, and each (group, block, chunk) is an 8-row x
+// 16-byte core matrix of the tensor cores' K-major no-swizzle operand layout:
+// a 128-row MMA tile of one block is 16 groups' core-matrix pairs, K-chunk
+// stride 128 B, 8-row stride one segment. Rows past N in the last group are
+// zero (delta 0, quants 0) and are never written out. q4_0 nibbles keep GGUF
+// order (byte j: low nibble element j, high nibble element j + 16).
 #pragma once
 
 #include <cstdint>
@@ -63,5 +65,12 @@ __host__ __device__ inline uint64_t seg_offset(uint32_t type, uint32_t seg)
 }
 
 constexpr uint32_t MAX_SEG_BYTES = SB * RG * (32u + 2u);   // 4352
+
+// byte offset, within its segment, of 16-byte chunk c of row r of block bi
+__host__ __device__ constexpr uint32_t quant_offset(uint32_t type, uint32_t bi, uint32_t c,
+						    uint32_t r)
+{
+	return bi * RG * quant_bytes(type) + c * RG * 16 + r * 16;
+}
 
 } // namespace cgpu

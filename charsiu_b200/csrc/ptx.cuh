@@ -8,6 +8,9 @@
 
 namespace cgpu {
 
+// every bounded wait in this library gives up after this long
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;   // one second
+
 __device__ __forceinline__ uint32_t smem_addr(const void *p)
 {
 	return static_cast<uint32_t>(__cvta_generic_to_shared(p));

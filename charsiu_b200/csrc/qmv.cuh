@@ -28,7 +28,6 @@ constexpr int QMV_WARPS = 4;
 constexpr int QMV_STAGES = 5;
 constexpr int QMV_MAX_TENSORS = 8;
 constexpr int QMV_MAX_M = 8;
-constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;   // one second
 
 struct QmvTensor {
 	const uint8_t *data;     // the device layout of layout.h
@@ -60,9 +59,8 @@ inline size_t qmv_smem_bytes(int m, uint32_t nb)
 // terms in block order (step by step, blocks p = 0..3 fetched by shuffle),
 // which is the only serial part: one fadd per block.
 //
-// q8_0: a block row is 32 bytes, read as two 16-byte halves; rows 4-7 read
-// their halves in the other order so each quarter-warp's 16-byte loads hit
-// distinct banks. q4_0: a block row is 16 bytes of nibbles;
+// q8_0: a block row is two 16-byte chunks (layout.h), 8 lanes of one chunk
+// reading 128 contiguous bytes. q4_0: a block row is 16 bytes of nibbles;
 // (q - 8) . a = q . a - 8 * sum(a).
 template <int M, bool Q8>
 __device__ __forceinline__ void seg_terms(const uint8_t *st, uint32_t sb, uint32_t b0,
@@ -72,7 +70,6 @@ __device__ __forceinline__ void seg_terms(const uint8_t *st, uint32_t sb, uint32
 	constexpr uint32_t QB = Q8 ? 32 : 16;
 	const uint16_t *dl = reinterpret_cast<const uint16_t *>(st + sb * RG * QB);
 	const int p = lane >> 3, r = lane & 7;
-	const int hf = (r >> 2) & 1;
 	float term[SB / 4][M];
 
 #pragma unroll
@@ -81,16 +78,16 @@ __device__ __forceinline__ void seg_terms(const uint8_t *st, uint32_t sb, uint32
 			break;
 		const uint32_t bl = min((uint32_t)(j * 4 + p), sb - 1);
 		const uint32_t blk = b0 + bl;
-		const uint8_t *wp = st + (bl * RG + r) * QB;
+		const uint8_t *wp = st + bl * RG * QB + r * 16;
 		const float dw = half_bits_to_float(dl[bl * RG + r]);
 		if (Q8) {
-			const uint4 w0 = *reinterpret_cast<const uint4 *>(wp + hf * 16);
-			const uint4 w1 = *reinterpret_cast<const uint4 *>(wp + (hf ^ 1) * 16);
+			const uint4 w0 = *reinterpret_cast<const uint4 *>(wp);
+			const uint4 w1 = *reinterpret_cast<const uint4 *>(wp + RG * 16);
 #pragma unroll
 			for (int m = 0; m < M; m++) {
 				const int8_t *a = aq + ((size_t)m * nb + blk) * 32;
-				const uint4 a0 = *reinterpret_cast<const uint4 *>(a + hf * 16);
-				const uint4 a1 = *reinterpret_cast<const uint4 *>(a + (hf ^ 1) * 16);
+				const uint4 a0 = *reinterpret_cast<const uint4 *>(a);
+				const uint4 a1 = *reinterpret_cast<const uint4 *>(a + 16);
 				int t0 = dp4a_ss(w0.x, a0.x, 0), t1 = dp4a_ss(w1.x, a1.x, 0);
 				t0 = dp4a_ss(w0.y, a0.y, t0);
 				t1 = dp4a_ss(w1.y, a1.y, t1);

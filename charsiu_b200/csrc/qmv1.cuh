@@ -52,8 +52,8 @@ __device__ __forceinline__ uint16_t ldg_stream_u16(const uint8_t *p)
 }
 
 // One segment's raw bytes for this lane: step j covers blocks 4j..4j+3; lane
-// l reads block p = l>>3, row r = l&7 (32 bytes q8_0 as two loads, 16 bytes
-// q4_0) and that block-row's fp16 delta.
+// l reads block p = l>>3, row r = l&7 (q8_0: its two 16-byte chunks; q4_0:
+// its one) and that block-row's fp16 delta.
 template <bool Q8>
 struct SegRegs {
 	uint4 w[SB / 4][Q8 ? 2 : 1];
@@ -69,10 +69,10 @@ __device__ __forceinline__ void seg_load(SegRegs<Q8> &R, const uint8_t *seg, uin
 	for (int j = 0; j < SB / 4; j++) {
 		const uint32_t bl = min((uint32_t)(j * 4 + p), sb - 1);
 		if ((uint32_t)j * 4 < sb) {
-			const uint8_t *wp = seg + (bl * RG + r) * QB;
+			const uint8_t *wp = seg + bl * RG * QB + r * 16;
 			R.w[j][0] = ldg_stream(wp);
 			if (Q8)
-				R.w[j][Q8 ? 1 : 0] = ldg_stream(wp + 16);
+				R.w[j][Q8 ? 1 : 0] = ldg_stream(wp + RG * 16);
 			R.dl[j] = ldg_stream_u16(seg + (size_t)sb * RG * QB + (bl * RG + r) * 2);
 		}
 	}

@@ -1,0 +1,117 @@
+// SPDX-License-Identifier: GPL-2.0-or-later
+// Inline-PTX helpers for the sm_100a tensor cores (tcgen05): tensor-memory
+// allocation, the kind::i8 MMA (signed int8 x signed int8 -> int32), its
+// commit to an mbarrier, loads of the accumulator out of tensor memory, and
+// the two 64-bit descriptors. cta_group::1 throughout; nothing here multicasts.
+#pragma once
+
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace cgpu {
+
+// ---- tensor memory ---------------------------------------------------------
+
+// Allocate `ncols` columns (a power of two, >= 32) of this CTA's tensor memory;
+// the base address lands in *dst (shared memory). One whole warp executes it.
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols)
+{
+	asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+		     :: "r"(smem_addr(dst)), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish()
+{
+	asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
+{
+	asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+		     :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before()
+{
+	asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after()
+{
+	asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// ---- descriptors -------------------------------------------------------------
+
+// Shared-memory matrix descriptor, K-major, no swizzle: the operand is made
+// of 8-row x 16-byte core matrices (rows 16 bytes apart); `lbo` is the byte
+// distance between the two 16-byte K chunks of one K = 32 step, `sbo` the
+// distance between consecutive 8-row groups. Version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc_k_nosw(const void *base, uint32_t lbo, uint32_t sbo)
+{
+	const uint64_t a = smem_addr(base);
+	return ((a >> 4) & 0x3fffull) | (((uint64_t)(lbo >> 4) & 0x3fffull) << 16) |
+	       (((uint64_t)(sbo >> 4) & 0x3fffull) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor of a dense kind::i8 MMA: D int32, A and B signed
+// int8, both K-major, M = m rows (64 or 128), N = n columns (multiple of 16
+// for M = 128, 16..256).
+__host__ __device__ constexpr uint32_t idesc_i8(uint32_t m, uint32_t n)
+{
+	return (2u << 4)               // D format: s32
+	     | (1u << 7)               // A format: signed 8 bit
+	     | (1u << 10)              // B format: signed 8 bit
+	     | ((n >> 3) << 17)        // N >> 3
+	     | ((m >> 4) << 24);       // M >> 4
+}
+
+// ---- the MMA -----------------------------------------------------------------
+
+// D[tmem] (+)= A[smem] . B[smem]^T for one K = 32 step. One thread issues it.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+				       uint32_t idesc, bool accumulate)
+{
+	asm volatile("{\n\t.reg .pred p;\n\t"
+		     "setp.ne.b32 p, %4, 0;\n\t"
+		     "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+		     :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc),
+			"r"((uint32_t)accumulate)
+		     : "memory");
+}
+
+// Arrive (once) on `bar` when every tcgen05 op this thread issued before has
+// completed.
+__device__ __forceinline__ void mma_commit(uint64_t *bar)
+{
+	asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+		     :: "r"(smem_addr(bar)) : "memory");
+}
+
+// ---- accumulator out of tensor memory -----------------------------------------
+
+// 32 lanes x 32 bits, 16 consecutive columns: lane i of the warp gets row
+// (its warp's lane quarter base + i), columns col..col+15.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
+{
+	asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+		     "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+		     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+		       "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+		       "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+		     : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld()
+{
+	asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// |t| < 2^22 to fp32, exactly: two full-rate ops instead of a conversion.
+__device__ __forceinline__ float small_int_to_float(int32_t t)
+{
+	return __fsub_rn(__int_as_float(0x4b400000 + t), 12582912.0f);
+}
+
+} // namespace cgpu
