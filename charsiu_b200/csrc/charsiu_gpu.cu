@@ -22,6 +22,7 @@
 #include "i8mm_tc.cuh"
 #include "qmv.cuh"
 #include "qmv1.cuh"
+#include "qmm_tc.cuh"
 #include "ref_abi.h"
 
 using namespace cgpu;
@@ -108,6 +109,8 @@ struct charsiu_gpu {
 	size_t cap_dact = 0, cap_hact = 0, cap_dy = 0, cap_hy = 0;
 	int8_t *d_q = nullptr;              // block-dot test hook
 	size_t cap_dq = 0;
+	uint8_t *d_pack = nullptr;          // packed activation tiles of the batched path
+	size_t cap_pack = 0;
 	std::vector<CallGraph> graphs;
 	uint8_t *d_i8 = nullptr, *h_i8 = nullptr;
 	size_t cap_di8 = 0, cap_hi8 = 0;
@@ -316,6 +319,55 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st)
 	return 0;
 }
 
+// The batched q8_0 path on the tensor cores: pack the m activations into MMA
+// tiles of NA (16, 32 or 64) rows, then one CTA per 128 weight rows and NA
+// activations. `pack` (device) holds at least qmm_pack_bytes(m, nb).
+size_t qmm_pack_bytes(uint32_t m, uint32_t nb)
+{
+	const uint32_t na = m <= 16 ? 16 : m <= 32 ? 32 : 64;
+	return (size_t)((m + na - 1) / na) * nsegments(nb) * qmm_act_seg_bytes(na);
+}
+
+int launch_qmm(charsiu_gpu *g, const Ent &e, const int8_t *q, const float *d, uint32_t m,
+	       float *y, uint8_t *pack, cudaStream_t st)
+{
+	const uint32_t na = m <= 16 ? 16 : m <= 32 ? 32 : 64;
+	const uint32_t mt = (m + na - 1) / na, nseg = nsegments(e.nb);
+	const uint64_t items = (uint64_t)mt * nseg * (SB * 2 * na + SB * na);
+	qmm_pack_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(q, d, m, e.nb, na, pack);
+	if (cudaGetLastError() != cudaSuccess)
+		return -1;
+	g->launches++;
+	QmmParams p;
+	p.w = e.data;
+	p.act = pack;
+	p.y = y;
+	p.rows = (uint32_t)e.rows;
+	p.groups = e.groups;
+	p.nb = e.nb;
+	p.m = m;
+	p.err = g->d_err;
+	const void *fn = na == 16 ? (const void *)qmm_tc_kernel<16>
+		       : na == 32 ? (const void *)qmm_tc_kernel<32> : (const void *)qmm_tc_kernel<64>;
+	const int slot = na == 16 ? 20 : na == 32 ? 21 : 22;
+	const size_t smem = qmm_smem_bytes(na);
+	if (!g->smem_set[slot]) {
+		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+					 (int)smem) != cudaSuccess)
+			return -1;
+		g->smem_set[slot] = true;
+	}
+	const int threads = (2 + 4 * (na > 32 ? na / 32 : 1)) * 32;
+	dim3 grid((e.groups + QMM_TILE_GROUPS - 1) / QMM_TILE_GROUPS, mt);
+	void *args[1] = {&p};
+	if (!e.groups)
+		return 0;
+	if (cudaLaunchKernel(fn, grid, dim3(threads), args, smem, st) != cudaSuccess)
+		return -1;
+	g->launches++;
+	return 0;
+}
+
 // One launch per quant type present among ids (the M = 1 kernel takes one
 // type a launch; a decode's groups are always a single type).
 int launch_matvec1(charsiu_gpu *g, const int *ids, unsigned n, float *const *ys, uint32_t k,
@@ -363,6 +415,22 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 	const uint32_t nb = k / 32;
 	const int8_t *dq = reinterpret_cast<const int8_t *>(g->d_act);
 	const float *dd = reinterpret_cast<const float *>(g->d_act + (size_t)m * nb * 32);
+	if (m > 1) {
+		// q8_0 on the tensor cores; q4_0 on the CUDA cores below
+		bool all_q8 = true;
+		for (unsigned i = 0; i < n; i++)
+			all_q8 = all_q8 && g->ent[ids[i]].type == TYPE_Q8_0;
+		if (all_q8) {
+			size_t off = 0;
+			for (unsigned i = 0; i < n; i++) {
+				if (launch_qmm(g, g->ent[ids[i]], dq, dd, m, g->d_y + off, g->d_pack,
+					       g->stream))
+					return -1;
+				off += (size_t)m * g->ent[ids[i]].rows;
+			}
+			return 0;
+		}
+	}
 	for (unsigned m0 = 0, mc = 0; m0 < m; m0 += mc) {
 		const unsigned left = m - m0;
 		mc = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
@@ -419,6 +487,10 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	if (caps[0] != g->cap_dact || caps[1] != g->cap_hact || caps[2] != g->cap_dy ||
 	    caps[3] != g->cap_hy)
 		drop_graphs(g);         // they name the old staging buffers
+	if (m > 1 && !grow_dev(g->d_pack, g->cap_pack, qmm_pack_bytes(m, nb))) {
+		whine(g, "a staging buffer would not allocate");
+		return -1;
+	}
 
 	const double t0 = now_us();
 	memcpy(g->h_act, q, qbytes);
@@ -567,6 +639,7 @@ void charsiu_gpu_close(struct charsiu_gpu *g)
 	drop_graphs(g);
 	cudaFree(g->d_act);
 	cudaFree(g->d_q);
+	cudaFree(g->d_pack);
 	cudaFree(g->d_y);
 	cudaFree(g->d_i8);
 	cudaFree(g->d_dots);
@@ -766,6 +839,11 @@ int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m, cons
 	const Ent &e = g->ent[id];
 	const uint32_t nb = e.nb;
 	cudaStream_t st = stream ? (cudaStream_t)stream : g->stream;
+	if (m > 1 && e.type == TYPE_Q8_0) {
+		if (!grow_dev(g->d_pack, g->cap_pack, qmm_pack_bytes(m, nb)))
+			return -1;
+		return launch_qmm(g, e, q, d, m, y, g->d_pack, st);
+	}
 	for (unsigned m0 = 0; m0 < m;) {
 		const unsigned left = m - m0;
 		const unsigned mc = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;

@@ -27,7 +27,7 @@ def same(a, b):
 
 @pytest.fixture(scope="module")
 def layer():
-    with Layer(max_k=8256, max_n=128256, max_tensors=64) as L:
+    with Layer(max_k=8256, max_n=128256, max_tensors=96) as L:
         yield L
 
 
@@ -93,10 +93,12 @@ def test_output_head_shape(layer):
     assert same(y, O.matvec(G.GGML_Q8_0, blk, k, n, q, d))
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 13])
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 13, 32, 64, 100])
 @pytest.mark.parametrize("qt", [G.GGML_Q8_0, G.GGML_Q4_0])
-def test_batch_rows_match_single_matvec(layer, m, qt):
-    k, n = 2048, 520
+@pytest.mark.parametrize("k,n", [(2048, 520), (8192, 136)])
+def test_batch_rows_match_single_matvec(layer, m, qt, k, n):
+    """M > 1: q8_0 runs on the tensor cores (tcgen05 kind::i8, tiles of 16,
+    32 or 64 activations), q4_0 on the CUDA cores; every row bit-exact."""
     blk, xs = W.batch_inputs(qt, k, n, m, seed=3)
     tid = layer.add_blocks(qt, k, n, blk)
     qs, ds = zip(*(O.act_quantise(x) for x in xs))
