@@ -570,6 +570,35 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 
 } // namespace
 
+// ---- scratch for charsiu_gpu_matvec_batch_noalloc -----------------------------
+//
+// For callers that cannot allocate device memory while they run, the batched
+// tensor-core matvec can keep its packed activation tiles here instead of in
+// the layer's staging buffer (which is grown with cudaMalloc on first use).
+// A fixed 1 MiB: every GPU that loads this library holds it until exit.
+static constexpr size_t NOALLOC_SCRATCH_BYTES = (size_t)1 << 20;
+static __device__ __align__(256) uint8_t noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+// In host code `noalloc_scratch` is only a stand-in for the device array, so
+// its device address is looked up once per device (with that device current)
+// and passed to the kernels.
+static uint8_t *noalloc_scratch_addr[256];
+
+static uint8_t *noalloc_scratch_on(int device)
+{
+	if (device < 0 || device >= 256)
+		return nullptr;
+	if (!noalloc_scratch_addr[device]) {
+		void *ptr = nullptr;
+		if (cudaGetSymbolAddress(&ptr, noalloc_scratch) != cudaSuccess) {
+			cudaGetLastError();
+			return nullptr;
+		}
+		noalloc_scratch_addr[device] = static_cast<uint8_t *>(ptr);
+	}
+	return noalloc_scratch_addr[device];
+}
+
 extern "C" {
 
 struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned max_tensors,
@@ -857,6 +886,39 @@ int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m, cons
 		m0 += mc;
 	}
 	return 0;
+}
+
+// The batched q8_0 matvec with nothing allocated: the same pack and
+// tensor-core kernels as charsiu_gpu_matvec_batch_dev, with the packed
+// activations in noalloc_scratch. The pack step writes every byte the matmul
+// then reads (padding zeroed), so no clearing is needed between calls; calls
+// that overlap on one GPU share the array and race.
+int charsiu_gpu_matvec_batch_noalloc(struct charsiu_gpu *g, int id, unsigned m, const int8_t *q,
+				     const float *d, float *y, void *stream)
+{
+	if (!g || g->dead || !q || !d || !y || !m || ((uintptr_t)q & 15) || ((uintptr_t)d & 3))
+		return -1;
+	if (id < 0 || (size_t)id >= g->ent.size())
+		return -1;
+	const Ent &e = g->ent[id];
+	if (e.type != TYPE_Q8_0) {
+		whine(g, "the allocation-free batched matvec takes q8_0 tensors only (%s)", e.name);
+		return -1;
+	}
+	const size_t need = qmm_pack_bytes(m, e.nb);
+	if (need > NOALLOC_SCRATCH_BYTES) {
+		whine(g, "the allocation-free batched matvec holds %zu bytes of packed activations; "
+			 "m=%u at K=%llu needs %zu", NOALLOC_SCRATCH_BYTES, m,
+		      (unsigned long long)e.k, need);
+		return -1;
+	}
+	cudaSetDevice(g->device);
+	uint8_t *scratch = noalloc_scratch_on(g->device);
+	if (!scratch) {
+		whine(g, "the allocation-free scratch has no device address on device %d", g->device);
+		return -1;
+	}
+	return launch_qmm(g, e, q, d, m, y, scratch, stream ? (cudaStream_t)stream : g->stream);
 }
 
 int charsiu_gpu_act_quantise_dev(struct charsiu_gpu *g, const float *x, unsigned m, unsigned k,

@@ -41,6 +41,7 @@ SIGNATURES = [
                                              C.c_int, _vp]),
     ("charsiu_gpu_matvec_dev", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp, _vp, _vp]),
     ("charsiu_gpu_matvec_batch_dev", C.c_int, [_vp, C.c_int, C.c_uint, _vp, _vp, _vp, _vp]),
+    ("charsiu_gpu_matvec_batch_noalloc", C.c_int, [_vp, C.c_int, C.c_uint, _vp, _vp, _vp, _vp]),
     ("charsiu_gpu_act_quantise_dev", C.c_int, [_vp, _vp, C.c_uint, C.c_uint, _vp, _vp, _vp]),
     ("charsiu_gpu_calls", C.c_ulong, [_vp]),
     ("charsiu_gpu_launches", C.c_ulong, [_vp]),
@@ -209,6 +210,12 @@ class Layer:
                   stream: int = 0) -> int:
         return self.L.charsiu_gpu_matvec_batch_dev(self.h, tid, m, q_ptr, d_ptr, y_ptr,
                                                    stream or None)
+
+    def batch_noalloc(self, tid: int, m: int, q_ptr: int, d_ptr: int, y_ptr: int,
+                      stream: int = 0) -> int:
+        """The batched matvec with no device allocation (fixed 1 MiB scratch)."""
+        return self.L.charsiu_gpu_matvec_batch_noalloc(self.h, tid, m, q_ptr, d_ptr, y_ptr,
+                                                       stream or None)
 
     def act_quantise_dev(self, x_ptr: int, m: int, k: int, q_ptr: int, d_ptr: int,
                          stream: int = 0) -> int:

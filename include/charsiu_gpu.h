@@ -143,6 +143,22 @@ CHARSIU_GPU_API int charsiu_gpu_matvec_dev(struct charsiu_gpu *g, const int *ids
 CHARSIU_GPU_API int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m,
 				 const int8_t *q, const float *d, float *y,
 				 void *stream);
+/* The batched matvec of charsiu_gpu_matvec_batch_dev, for callers that
+ * cannot allocate GPU memory while they run -- a server whose own memory
+ * pool already owns the GPU's free memory, or a latency-bound loop that must
+ * not take cudaMalloc's implicit device synchronisation (the _dev form grows
+ * a staging buffer with cudaMalloc on first use). This call allocates
+ * nothing: its scratch is a fixed 1 MiB array inside the library, held on
+ * every GPU that loads it until exit. q8_0 tensors only; the m activations
+ * are packed in tiles of 16, 32 or 64 and must fit that array (m <= 64 up to
+ * K = 14336), else -1 with the reason in charsiu_gpu_error. All calls on a GPU
+ * share the array, so two calls running on it at the same time race. The
+ * first call on each GPU looks up the array's device address; make it before
+ * any stream capture. Same results as charsiu_gpu_matvec_batch_dev, bit for
+ * bit. No counterpart in the reference. */
+CHARSIU_GPU_API int charsiu_gpu_matvec_batch_noalloc(struct charsiu_gpu *g, int id, unsigned m,
+						     const int8_t *q, const float *d, float *y,
+						     void *stream);
 /* charsiu_act_set (src/gguf.c:829-882) on the device, bit-exact: x fp32
  * [m][k] -> q int8 [m][k rounded up to 32], d fp32 [m][k/32]. */
 CHARSIU_GPU_API int charsiu_gpu_act_quantise_dev(struct charsiu_gpu *g, const float *x,
