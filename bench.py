@@ -45,6 +45,7 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 from charsiu_b200 import gguf as G  # noqa: E402
+from charsiu_b200 import shard  # noqa: E402
 from charsiu_b200 import workloads as W  # noqa: E402
 
 METRIC = "Llama-3.2-1B q8_0 decode tok/s"
@@ -132,82 +133,91 @@ def algorithmic_bytes(gguf, names, k, rows_of):
 
 # ---- our arm -------------------------------------------------------------------
 
-def run_ours(args, rank, world, dist):
-    import torch
-    from charsiu_b200.lib import Layer, Llama, lib
+class TokenChain:
+    """The 65 launches of one decode token on this GPU, weights resident.
 
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
-    torch.cuda.set_device(dev)
-    barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
-    path = model_path(rank, barrier)
-    gg = G.GGUFFile(path)
-    groups = launch_groups(SHAPE)
-    names = sorted({nm for g, _ in groups for nm in g})
+    world == 1: the whole model here. world > 1 (column split): this rank holds
+    its slab of every tensor, and each launch group's slabs (one contiguous
+    buffer a group) are all-gathered with one NCCL collective."""
 
-    layer = Layer(max_k=max(SHAPE.n_embd, SHAPE.n_ff), max_n=SHAPE.n_vocab,
-                  max_tensors=len(names) + 1, device=dev.index, rank=rank, world=world)
-    ids, rows = {}, {}
-    for nm in names:
-        t = gg.tensors[nm]
-        ids[nm] = layer.add_blocks(t.type, t.k, t.n, np.asarray(gg.data(nm)), nm)
-        rows[nm] = layer.rows(ids[nm])[1]
-    full_rows = {nm: gg.tensors[nm].n for nm in names}
+    def __init__(self, gg, dev, rank=0, world=1, dist=None):
+        import torch
+        from charsiu_b200.lib import Layer
 
-    # device activations: seeded normal vectors, quantised by the device quantiser
-    gen = torch.Generator(device="cpu").manual_seed(1234)
-    acts = {}
-    for k in (SHAPE.n_embd, SHAPE.n_ff):
-        x = torch.randn(k, generator=gen).to(dev)
-        q = torch.empty(k, dtype=torch.int8, device=dev)
-        d = torch.empty(k // 32, dtype=torch.float32, device=dev)
-        assert layer.act_quantise_dev(x.data_ptr(), 1, k, q.data_ptr(), d.data_ptr(),
-                                      torch.cuda.current_stream().cuda_stream) == 0
-        acts[k] = (q, d)
-    # output slabs, padded to the widest rank's slab so NCCL gathers equal pieces
-    per = {}
-    for nm in names:
-        ngroups = -(-full_rows[nm] // 8)
-        per[nm] = -(-ngroups // world) * 8
-    ys = {nm: torch.zeros(per[nm], dtype=torch.float32, device=dev) for nm in names}
-    full = {nm: torch.zeros(per[nm] * world, dtype=torch.float32, device=dev) for nm in names} \
-        if world > 1 else None
+        self.torch, self.dev, self.world, self.dist = torch, dev, world, dist
+        self.groups = launch_groups(SHAPE)
+        names = [nm for g, _ in self.groups for nm in g]
+        self.layer = Layer(max_k=max(SHAPE.n_embd, SHAPE.n_ff), max_n=SHAPE.n_vocab,
+                           max_tensors=len(names) + 1, device=dev.index, rank=rank, world=world)
+        self.ids, self.rows = {}, {}
+        for nm in names:
+            t = gg.tensors[nm]
+            self.ids[nm] = self.layer.add_blocks(t.type, t.k, t.n, np.asarray(gg.data(nm)), nm)
+            self.rows[nm] = self.layer.rows(self.ids[nm])[1]
+        gen = torch.Generator(device="cpu").manual_seed(1234)
+        self.acts = {}
+        for k in (SHAPE.n_embd, SHAPE.n_ff):
+            x = torch.randn(k, generator=gen).to(dev)
+            q = torch.empty(k, dtype=torch.int8, device=dev)
+            d = torch.empty(k // 32, dtype=torch.float32, device=dev)
+            assert self.layer.act_quantise_dev(x.data_ptr(), 1, k, q.data_ptr(), d.data_ptr(),
+                                               torch.cuda.current_stream().cuda_stream) == 0
+            self.acts[k] = (q, d)
+        # one output buffer a launch group: its tensors' slabs back to back,
+        # each padded to the widest rank's slab so a gather moves equal pieces
+        self.bufs, self.full = [], []
+        for g, _ in self.groups:
+            slabs = [shard.slab_rows(gg.tensors[nm].n, world) for nm in g]
+            buf = torch.zeros(sum(slabs), dtype=torch.float32, device=dev)
+            ptrs, off = [], 0
+            for sl in slabs:
+                ptrs.append(buf[off:].data_ptr())
+                off += sl
+            self.bufs.append((buf, ptrs))
+            self.full.append(torch.zeros(world * sum(slabs), dtype=torch.float32, device=dev)
+                             if world > 1 else None)
+        self.bytes_per_token = sum(algorithmic_bytes(gg, g, k, lambda nm: self.rows[nm])
+                                   for g, k in self.groups)
 
-    def token(stream):
-        for g, k in groups:
-            q, d = acts[k]
-            rc = layer.matvec_dev([ids[nm] for nm in g], q.data_ptr(), d.data_ptr(),
-                                  [ys[nm].data_ptr() for nm in g], stream.cuda_stream)
-            assert rc == 0, layer.error()
-            if world > 1:
-                for nm in g:
-                    dist.all_gather_into_tensor(full[nm], ys[nm])
+    def token(self, stream):
+        for (g, k), (buf, ptrs), full in zip(self.groups, self.bufs, self.full):
+            q, d = self.acts[k]
+            rc = self.layer.matvec_dev([self.ids[nm] for nm in g], q.data_ptr(), d.data_ptr(),
+                                       ptrs, stream.cuda_stream)
+            assert rc == 0, self.layer.error()
+            if full is not None:
+                self.dist.all_gather_into_tensor(full, buf)
 
+    def close(self):
+        self.layer.close()
+
+
+def time_chain(chain, steps, warmup, barrier, dist, world, dev, graph_ok, sample_clocks):
+    """ms a token, the max over ranks; the chain as one CUDA graph when graph_ok."""
+    torch = chain.torch
     stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        chain.token(stream)                     # warm every launch cache first
+    torch.cuda.synchronize()
     graph = None
-    launches0 = layer.launches
-    if world == 1:
-        with torch.cuda.stream(stream):
-            token(stream)                       # warm the kernels before capture
-        torch.cuda.synchronize()
+    if graph_ok:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            token(stream)
+            chain.token(stream)
         torch.cuda.synchronize()
-    per_token_launches = len(groups)
-    run = (lambda: graph.replay()) if graph else (lambda: token(stream))
-
+    run = (lambda: graph.replay()) if graph else (lambda: chain.token(stream))
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             run()
     torch.cuda.synchronize()
     barrier()
-    clocks = Clocks(dev.index) if rank == 0 else None
+    clocks = Clocks(dev.index) if sample_clocks else None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     barrier()
     with torch.cuda.stream(stream):
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             run()
         e1.record(stream)
     torch.cuda.synchronize()
@@ -218,40 +228,67 @@ def run_ours(args, rank, world, dist):
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    ms_per_step = ms / args.steps
-    value = 1000.0 / ms_per_step
+    del graph
+    return ms / steps, clk
 
-    tok_bytes = sum(algorithmic_bytes(gg, g, k, lambda nm: rows[nm]) for g, k in groups)
+
+def run_ours(args, rank, world, dist):
+    import torch
+    from charsiu_b200.lib import lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
+    path = model_path(rank, barrier)
+    gg = G.GGUFFile(path)
+
+    # every GPU decodes its own stream with the whole model: no collective
+    chain = TokenChain(gg, dev)
+    ms_per_step, clk = time_chain(chain, args.steps, args.warmup, barrier, dist, world, dev,
+                                  True, rank == 0)
+    per_token_launches = len(chain.groups)
+    tok_bytes = chain.bytes_per_token
+    chain.close()
+    value = world * 1000.0 / ms_per_step
     peak, peak_kind = peaks()
     achieved = tok_bytes / (ms_per_step * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
                 "kernel": "cgpu::qmv1_kernel (M=1 block-quant matvec)", "peak_kind": peak_kind,
                 "bytes_per_launch": round(tok_bytes / per_token_launches),
-                "avg_launch_us": round(ms_per_step * 1e3 / per_token_launches, 3)}
-    del graph
-    layer.close()
+                "avg_launch_us": round(ms_per_step * 1e3 / per_token_launches, 3),
+                "per_gpu": True}
 
-    e2e = None
-    if world == 1:
-        e2e = run_e2e(path, args, lib)
-    else:
-        e2e = {"value": None, "unit": UNIT, "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
-               "note": "the host-ABI decode loop is single-GPU; N>1 e2e not measured"}
+    split = None
+    if world > 1:
+        # the north star's sharded form: ONE stream, every tensor column-split
+        cs = TokenChain(gg, dev, rank, world, dist)
+        ms_split, _ = time_chain(cs, max(1, min(args.steps, 200)), 3, barrier, dist, world, dev,
+                                 False, False)
+        cs.close()
+        split = {"value": round(1000.0 / ms_split, 2), "unit": UNIT,
+                 "ms_per_step": round(ms_split, 5),
+                 "workload": f"one decode stream, every tensor column-split over {world} GPUs, "
+                             "one NCCL all-gather per launch group (65 a token)"}
+
+    e2e = run_e2e(path, args, lib, world, dist, dev)
 
     out = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
            "data": "synthetic (seeded random-init Llama-3.2-1B-shaped q8_0 GGUF; no checkpoint)",
            "config": {"workload": "Llama-3.2-1B q8_0 greedy decode, hot path per token: 112 "
                                   "projections + 128256 tied head in 65 matvec launches",
                       "model": "Llama-3.2-1B architecture (16x2048, ffn 8192, 32/8 heads, "
                                "vocab 128256)",
-                      "weights_bytes_per_token": tok_bytes, "global_batch": 1, "seq_len": 1,
-                      "parallelism": f"column-split x{world}" if world > 1 else "single GPU",
+                      "weights_bytes_per_token": tok_bytes, "global_batch": world, "seq_len": 1,
+                      "parallelism": f"data-parallel x{world}: one decode stream a GPU, "
+                                     "no collective" if world > 1 else "single GPU",
                       "l2": "inputs larger than L2 (1.31 GB of weights per step vs 126 MB)"},
            "roofline": roofline, "e2e": e2e, "gpu_launches": per_token_launches * args.steps,
            "clocks": clk}
+    if split:
+        out["column_split"] = split
     if rank == 0 and world == 1:
         out["cpu_baseline"] = cpu_baseline(path)
     return out
@@ -269,9 +306,10 @@ def profile_traffic():
     return None
 
 
-def run_e2e(path, args, lib):
-    """The public C ABI decode: host buffers in and out on every call."""
-    import ctypes as C
+def run_e2e(path, args, lib, world=1, dist=None, dev=None):
+    """The public C ABI decode: host buffers in and out on every call. At N GPUs
+    every rank decodes its own stream on its own GPU; the rate is the sum over
+    ranks, from the slowest rank's time."""
     from charsiu_b200.lib import Llama
 
     n_gen_timed = min(args.steps, SPEC["n_gen"])
@@ -279,7 +317,9 @@ def run_e2e(path, args, lib):
     prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
     n_ctx = len(prompt) + n_warm + n_gen_timed + 1
     L = lib()
-    with Llama(path, n_ctx=n_ctx) as m:
+    if world > 1:
+        dist.barrier()
+    with Llama(path, n_ctx=n_ctx, device=dev.index if dev is not None else 0) as m:
         lp = None
         pos = 0
         for t in prompt:
@@ -302,11 +342,16 @@ def run_e2e(path, args, lib):
         dt = time.perf_counter() - t0
         calls = (m.calls - calls0) / n_gen_timed
         stages = {k: round(v, 4) for k, v in m.stages().items()}
+    if world > 1:
+        import torch
+        t = torch.tensor([dt], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
     groups = launch_groups(SHAPE)
     h2d = sum(k + 4 * (k // 32) for _, k in groups)
     d2h = 4 * (SHAPE.n_layer * (SHAPE.n_embd * 2 + 2 * SHAPE.n_head_kv * SHAPE.head_dim
                                 + 3 * SHAPE.n_ff) + SHAPE.n_vocab)
-    return {"value": round(n_gen_timed / dt, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+    return {"value": round(world * n_gen_timed / dt, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": n_gen_timed, "warmup": n_warm,
             "calls_per_step": calls, "ms_per_step": round(dt * 1e3 / n_gen_timed, 4),
             "stages_ms_per_step": stages,
@@ -399,6 +444,84 @@ def run_matvec_case(args):
             "gpu_launches": args.steps, "clocks": clk}
 
 
+# ---- the batched decode step ------------------------------------------------------
+
+def run_batch_case(args):
+    """--batch M: one decode step of M sequences through every projection and
+    the head (113 q8_0 tensors), each tensor one batched matvec of M
+    activations on the tensor cores (tcgen05 kind::i8), as a CUDA graph."""
+    import torch
+    from charsiu_b200.lib import Layer
+
+    m = args.batch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    path = model_path(0, lambda: None)
+    gg = G.GGUFFile(path)
+    names = [nm for g, _ in launch_groups(SHAPE) for nm in g]
+    with Layer(max_k=max(SHAPE.n_embd, SHAPE.n_ff), max_n=SHAPE.n_vocab,
+               max_tensors=len(names) + 1, device=0) as L:
+        ids = {}
+        for nm in dict.fromkeys(names):
+            t = gg.tensors[nm]
+            ids[nm] = L.add_blocks(t.type, t.k, t.n, np.asarray(gg.data(nm)), nm)
+        stream = torch.cuda.Stream(device=dev)
+        acts = {}
+        for k in (SHAPE.n_embd, SHAPE.n_ff):
+            x = torch.randn(m, k, generator=torch.Generator().manual_seed(k)).to(dev)
+            q = torch.empty((m, k), dtype=torch.int8, device=dev)
+            d = torch.empty((m, k // 32), dtype=torch.float32, device=dev)
+            assert L.act_quantise_dev(x.data_ptr(), m, k, q.data_ptr(), d.data_ptr(),
+                                      stream.cuda_stream) == 0
+            acts[k] = (q, d)
+        ys = {nm: torch.empty((m, gg.tensors[nm].n), dtype=torch.float32, device=dev)
+              for nm in dict.fromkeys(names)}
+
+        def step():
+            for nm in names:
+                q, d = acts[gg.tensors[nm].k]
+                assert L.batch_dev(ids[nm], m, q.data_ptr(), d.data_ptr(), ys[nm].data_ptr(),
+                                   stream.cuda_stream) == 0, L.error()
+        launches0 = L.launches
+        step()
+        torch.cuda.synchronize()
+        per_step = L.launches - launches0
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        clocks = Clocks(0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        ms = e0.elapsed_time(e1) / args.steps
+        del graph
+    wbytes = sum(gg.tensors[nm].nbytes for nm in names)
+    abytes = sum(m * (gg.tensors[nm].k + gg.tensors[nm].k // 8) + 4 * m * gg.tensors[nm].n
+                 for nm in names)
+    peak, peak_kind = peaks()
+    gbs = (wbytes + abytes) / (ms * 1e-3) / 1e9
+    return {"metric": f"Llama-3.2-1B q8_0 batched decode tok/s (M={m})",
+            "value": round(m * 1000.0 / ms, 1), "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": f"one decode step of {m} sequences: 112 projections + head, "
+                                   "each a tcgen05 kind::i8 batched matvec", "global_batch": m,
+                       "l2": "1.31 GB of weights a step (> L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "bytes_per_step": wbytes + abytes},
+            "gpu_launches": per_step * args.steps, "clocks": clk}
+
+
 # ---- the reference arm --------------------------------------------------------
 
 def run_reference(args, rank, world, dist):
@@ -424,7 +547,7 @@ def run_reference(args, rank, world, dist):
               "the Llama-3.2-1B-shaped q8_0 model, charsiu's llama_forward")
     return {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "Llama-3.2-1B q8_0 greedy decode", "global_batch": 1,
                        "seq_len": 1, "parallelism": f"{cores} host threads"},
@@ -440,6 +563,8 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=0, metavar="M",
+                    help="time one batched decode step of M sequences instead")
     ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N",
                     help="time one matvec shape instead of the decode (e.g. q8_0:2048:8192)")
     args = ap.parse_args()
@@ -461,6 +586,9 @@ def main():
     try:
         if args.matvec:
             print(json.dumps(run_matvec_case(args)), flush=True)
+            return
+        if args.batch:
+            print(json.dumps(run_batch_case(args)), flush=True)
             return
         if args.impl == "reference":
             out = run_reference(args, rank, world, dist)

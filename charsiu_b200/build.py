@@ -30,7 +30,8 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", 
               f"-I{INCLUDE}", f"-I{CSRC}"]
 # -fno-math-errno only lets lrintf / sqrtf compile to their single instructions
 # (cvtss2si in the default round-to-nearest-even mode, sqrtss): same values.
-CC_FLAGS = ["-O2", "-std=c11", "-fPIC", "-ffp-contract=off", "-fno-math-errno", "-Wall", "-Wextra",
+# -O3 vectorises elementwise loops only; without fast-math nothing reassociates.
+CC_FLAGS = ["-O3", "-std=c11", "-fPIC", "-ffp-contract=off", "-fno-math-errno", "-Wall", "-Wextra",
             "-fvisibility=hidden", f"-I{INCLUDE}"]
 
 

@@ -128,6 +128,7 @@ struct charsiu_gpu {
 	double busy_us = 0, h2d_us = 0, kern_ms = 0, d2h_us = 0, weight_mb = 0;
 	double slow_us = 100000;
 	int strikes = 0, dead = 0, whined = 0;
+	int no_pdl = 0;     // CHARSIU_GPU_NO_PDL: launch without programmatic dependence (control)
 	unsigned long inj_at = 0, inj_count = 0;
 	int inj_kind = 0;
 	std::string err;
@@ -309,7 +310,7 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st)
 	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 	cfg.attrs = attr;
-	cfg.numAttrs = 1;
+	cfg.numAttrs = g->no_pdl ? 0 : 1;
 	QmvParams arg = p;
 	void *args[1] = {&arg};
 	const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
@@ -630,6 +631,7 @@ struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	g->max_tensors = max_tensors;
 	g->sm_count = prop.multiProcessorCount;
 	g->slow_us = (double)env_u("CHARSIU_GPU_SLOW_US", 100000);
+	g->no_pdl = getenv("CHARSIU_GPU_NO_PDL") != nullptr;
 	g->ent.reserve(max_tensors);
 	if (cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking) != cudaSuccess ||
 	    cudaEventCreate(&g->ev_k0) != cudaSuccess || cudaEventCreate(&g->ev_k1) != cudaSuccess ||

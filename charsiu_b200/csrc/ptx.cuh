@@ -1,6 +1,6 @@
 // SPDX-License-Identifier: GPL-2.0-or-later
 // Inline-PTX helpers for sm_100a: mbarriers, the untiled bulk copy engine
-// (global -> this CTA's shared memory, never multicast), programmatic
+// (global -> this CTA's shared memory, one destination), programmatic
 // dependent launch, and the mixed-sign dp4a.
 #pragma once
 
@@ -73,7 +73,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 
 // Untiled bulk copy, global -> shared memory of this CTA, completing `bytes`
 // of transaction count on `bar`. dst and src 16-byte aligned, bytes a
-// multiple of 16. No .multicast form anywhere in this library.
+// multiple of 16. Every bulk copy in this library has this one destination.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
 					 uint64_t *bar)
 {

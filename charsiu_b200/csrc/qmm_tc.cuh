@@ -13,7 +13,7 @@
 // a fresh int32 tile per block into one of two tensor-memory buffers while
 // the epilogue drains the other.
 //
-// Warp roles: warp 0 lane 0 issues the bulk copies (no multicast) of one
+// Warp roles: warp 0 lane 0 issues the single-destination bulk copies of one
 // K segment (16 blocks) a stage -- the 16 groups' weight segments as they lie
 // in the device layout (layout.h), already MMA core matrices, and the packed
 // activation tile (qmm_pack_kernel) -- into a double-buffered stage; warp 1

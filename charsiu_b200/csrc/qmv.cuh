@@ -12,7 +12,7 @@
 // comes from many groups (RG = 8 rows keeps even N = 512 at 64 groups).
 //
 // Data movement: each warp owns a ring of QMV_STAGES shared-memory stages; its
-// lane 0 issues one bulk copy (cp.async.bulk, no multicast) per segment of 16
+// lane 0 issues one single-destination bulk copy (cp.async.bulk) per segment of 16
 // blocks x 8 rows (4352 bytes q8_0, 2304 q4_0) and the warp consumes stages in
 // order, refilling each as soon as it is read. The weights do not depend on
 // the previous kernel, so the ring is filled before griddepcontrol.wait; only

@@ -2,7 +2,7 @@
 // Inline-PTX helpers for the sm_100a tensor cores (tcgen05): tensor-memory
 // allocation, the kind::i8 MMA (signed int8 x signed int8 -> int32), its
 // commit to an mbarrier, loads of the accumulator out of tensor memory, and
-// the two 64-bit descriptors. cta_group::1 throughout; nothing here multicasts.
+// the two 64-bit descriptors. cta_group::1 throughout; every copy has one destination CTA.
 #pragma once
 
 #include <cstdint>

@@ -407,12 +407,58 @@ static int row_f32(const struct gt *t, uint64_t row, float *dst)
 	}
 }
 
+#if defined(__SSE2__)
+#include <emmintrin.h>
+
+/*
+ * One full 32-block of act_set with SSE2, the same values as the scalar form:
+ * the block's max |x| is a max (maxps skips a NaN |x| exactly as `av > amax`
+ * does, and the order of a max does not matter), d and 1/d are the same
+ * scalar divisions, x * (1/d) is the same IEEE multiply, cvtps2dq rounds to
+ * nearest even as lrintf (cvtss2si) does, and the int8 is the low byte of the
+ * int32 as (int8_t) of lrintf's result is.
+ */
+static void act_block_sse(const float *x, int8_t *q, float *dout)
+{
+	const __m128 sign = _mm_set1_ps(-0.0f);
+	__m128 v[8], mx = _mm_setzero_ps();
+	int32_t iq[32];
+	float amax, d, id;
+
+	for (int i = 0; i < 8; i++) {
+		v[i] = _mm_loadu_ps(x + 4 * i);
+		mx = _mm_max_ps(_mm_andnot_ps(sign, v[i]), mx);
+	}
+	mx = _mm_max_ps(mx, _mm_shuffle_ps(mx, mx, _MM_SHUFFLE(2, 3, 0, 1)));
+	mx = _mm_max_ps(mx, _mm_shuffle_ps(mx, mx, _MM_SHUFFLE(1, 0, 3, 2)));
+	amax = _mm_cvtss_f32(mx);
+	d = amax / 127.0f;
+	id = d != 0.0f ? 1.0f / d : 0.0f;
+	*dout = d;
+	{
+		const __m128 vid = _mm_set1_ps(id);
+
+		for (int i = 0; i < 8; i++)
+			_mm_storeu_si128((__m128i *)(iq + 4 * i),
+					 _mm_cvtps_epi32(_mm_mul_ps(v[i], vid)));
+	}
+	for (int j = 0; j < 32; j++)
+		q[j] = (int8_t)iq[j];
+}
+#endif
+
 /* charsiu_act_set's q8_0 form (src/gguf.c:852-881) */
 static void act_set(struct charsiu_gpu_llama *m, const float *x, int n)
 {
 	int nb = (n + 31) / 32;
 
 	for (int b = 0; b < nb; b++) {
+#if defined(__SSE2__)
+		if (b * 32 + 32 <= n) {
+			act_block_sse(x + b * 32, m->aq + b * 32, &m->ad[b]);
+			continue;
+		}
+#endif
 		float amax = 0.0f, d, id;
 
 		for (int j = 0; j < 32; j++) {
@@ -698,7 +744,27 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 			uint32_t kvh = h / gqa;
 			float *out = m->xb + h * hd;
 
-			for (int t = 0; t <= pos; t++) {
+			/* four positions at a time: four independent chains, each
+			 * summed over i in order, as src/llama.c:798-806 sums one */
+			int t = 0;
+
+			for (; t + 3 <= pos; t += 4) {
+				const float *k0 = m->kcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
+				const float *k1 = k0 + kvdim, *k2 = k1 + kvdim, *k3 = k2 + kvdim;
+				float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+
+				for (uint32_t i = 0; i < hd; i++) {
+					a0 += qh[i] * k0[i];
+					a1 += qh[i] * k1[i];
+					a2 += qh[i] * k2[i];
+					a3 += qh[i] * k3[i];
+				}
+				att[t] = a0 * scale;
+				att[t + 1] = a1 * scale;
+				att[t + 2] = a2 * scale;
+				att[t + 3] = a3 * scale;
+			}
+			for (; t <= pos; t++) {
 				const float *kt = m->kcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
 				float a = 0.0f;
 
