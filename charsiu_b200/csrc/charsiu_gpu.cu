@@ -129,6 +129,8 @@ struct charsiu_gpu {
 	double slow_us = 100000;
 	int strikes = 0, dead = 0, whined = 0;
 	int no_pdl = 0;     // CHARSIU_GPU_NO_PDL: launch without programmatic dependence (control)
+	uint32_t qmm_na = 0;   // CHARSIU_GPU_QMM_NA: activations a tensor-core tile (16, 32; 0 = by m)
+	bool qmm_pre = false;  // CHARSIU_GPU_QMM_PRE=1: the MMA adds the float-bias constant (slower)
 	unsigned long inj_at = 0, inj_count = 0;
 	int inj_kind = 0;
 	std::string err;
@@ -321,36 +323,70 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st)
 }
 
 // The batched q8_0 path on the tensor cores: pack the m activations into MMA
-// tiles of NA (16, 32 or 64) rows, then one CTA per 128 weight rows and NA
-// activations. `pack` (device) holds at least qmm_pack_bytes(m, nb).
-size_t qmm_pack_bytes(uint32_t m, uint32_t nb)
+// tiles of NA (16 or 32) rows once, then one persistent launch over every
+// (128-row tile, NA activations) unit of the tensors `ids` (same K, at most
+// QMM_MAX_TENSORS). NA = 16 for m <= 16, else 32 (CHARSIU_GPU_QMM_NA picks
+// one for every m). `pack` (device) holds at least qmm_pack_bytes(na, m, nb).
+uint32_t qmm_na(const charsiu_gpu *g, uint32_t m)
 {
-	const uint32_t na = m <= 16 ? 16 : m <= 32 ? 32 : 64;
+	if (g->qmm_na)
+		return g->qmm_na;
+	return m <= 16 ? 16 : 32;
+}
+
+size_t qmm_pack_bytes(uint32_t na, uint32_t m, uint32_t nb)
+{
 	return (size_t)((m + na - 1) / na) * nsegments(nb) * qmm_act_seg_bytes(na);
 }
 
-int launch_qmm(charsiu_gpu *g, const Ent &e, const int8_t *q, const float *d, uint32_t m,
-	       float *y, uint8_t *pack, cudaStream_t st)
+int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, const float *d,
+	       uint32_t m, float *const *ys, uint8_t *pack, cudaStream_t st)
 {
-	const uint32_t na = m <= 16 ? 16 : m <= 32 ? 32 : 64;
-	const uint32_t mt = (m + na - 1) / na, nseg = nsegments(e.nb);
+	if (!n || n > (unsigned)QMM_MAX_TENSORS)
+		return -1;
+	const uint32_t na = qmm_na(g, m), nb = g->ent[ids[0]].nb;
+	const uint32_t mt = (m + na - 1) / na, nseg = nsegments(nb);
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[0].val.programmaticStreamSerializationAllowed = 1;
+
 	const uint64_t items = (uint64_t)mt * nseg * (SB * 2 * na + SB * na);
-	qmm_pack_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(q, d, m, e.nb, na, pack);
-	if (cudaGetLastError() != cudaSuccess)
+	cudaLaunchConfig_t pc = {};
+	pc.gridDim = dim3((unsigned)((items + 255) / 256));
+	pc.blockDim = dim3(256);
+	pc.stream = st;
+	pc.attrs = attr;
+	pc.numAttrs = g->no_pdl ? 0 : 1;
+	if (cudaLaunchKernelEx(&pc, qmm_pack_kernel, q, d, m, nb, na, pack) != cudaSuccess)
 		return -1;
 	g->launches++;
-	QmmParams p;
-	p.w = e.data;
+
+	QmmParams p = {};
+	uint32_t tiles = 0;
+	for (unsigned i = 0; i < n; i++) {
+		const Ent &e = g->ent[ids[i]];
+		p.t[i].w = e.data;
+		p.t[i].y = ys[i];
+		p.t[i].rows = (uint32_t)e.rows;
+		p.t[i].groups = e.groups;
+		tiles += (e.groups + QMM_TILE_GROUPS - 1) / QMM_TILE_GROUPS;
+		p.t[i].tile_end = tiles;
+	}
 	p.act = pack;
-	p.y = y;
-	p.rows = (uint32_t)e.rows;
-	p.groups = e.groups;
-	p.nb = e.nb;
+	p.ntensor = n;
+	p.tiles = tiles;
+	p.atiles = mt;
+	p.nb = nb;
 	p.m = m;
 	p.err = g->d_err;
-	const void *fn = na == 16 ? (const void *)qmm_tc_kernel<16>
-		       : na == 32 ? (const void *)qmm_tc_kernel<32> : (const void *)qmm_tc_kernel<64>;
-	const int slot = na == 16 ? 20 : na == 32 ? 21 : 22;
+	if (!tiles)
+		return 0;
+	const bool pre = g->qmm_pre;
+	const void *fn = na == 16 ? (pre ? (const void *)qmm_tc_kernel<16, true>
+					 : (const void *)qmm_tc_kernel<16, false>)
+				  : (pre ? (const void *)qmm_tc_kernel<32, true>
+					 : (const void *)qmm_tc_kernel<32, false>);
+	const int slot = 20 + (na == 32 ? 2 : 0) + (pre ? 1 : 0);
 	const size_t smem = qmm_smem_bytes(na);
 	if (!g->smem_set[slot]) {
 		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -358,12 +394,16 @@ int launch_qmm(charsiu_gpu *g, const Ent &e, const int8_t *q, const float *d, ui
 			return -1;
 		g->smem_set[slot] = true;
 	}
-	const int threads = (2 + 4 * (na > 32 ? na / 32 : 1)) * 32;
-	dim3 grid((e.groups + QMM_TILE_GROUPS - 1) / QMM_TILE_GROUPS, mt);
+	const uint32_t units = tiles * mt;
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = dim3(units < (uint32_t)g->sm_count ? units : (uint32_t)g->sm_count);
+	cfg.blockDim = dim3(qmm_threads((int)na));
+	cfg.dynamicSmemBytes = smem;
+	cfg.stream = st;
+	cfg.attrs = attr;
+	cfg.numAttrs = g->no_pdl ? 0 : 1;
 	void *args[1] = {&p};
-	if (!e.groups)
-		return 0;
-	if (cudaLaunchKernel(fn, grid, dim3(threads), args, smem, st) != cudaSuccess)
+	if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess)
 		return -1;
 	g->launches++;
 	return 0;
@@ -422,14 +462,13 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 		for (unsigned i = 0; i < n; i++)
 			all_q8 = all_q8 && g->ent[ids[i]].type == TYPE_Q8_0;
 		if (all_q8) {
+			float *yd[QMV_MAX_TENSORS];
 			size_t off = 0;
 			for (unsigned i = 0; i < n; i++) {
-				if (launch_qmm(g, g->ent[ids[i]], dq, dd, m, g->d_y + off, g->d_pack,
-					       g->stream))
-					return -1;
+				yd[i] = g->d_y + off;
 				off += (size_t)m * g->ent[ids[i]].rows;
 			}
-			return 0;
+			return launch_qmm(g, ids, n, dq, dd, m, yd, g->d_pack, g->stream);
 		}
 	}
 	for (unsigned m0 = 0, mc = 0; m0 < m; m0 += mc) {
@@ -488,7 +527,7 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	if (caps[0] != g->cap_dact || caps[1] != g->cap_hact || caps[2] != g->cap_dy ||
 	    caps[3] != g->cap_hy)
 		drop_graphs(g);         // they name the old staging buffers
-	if (m > 1 && !grow_dev(g->d_pack, g->cap_pack, qmm_pack_bytes(m, nb))) {
+	if (m > 1 && !grow_dev(g->d_pack, g->cap_pack, qmm_pack_bytes(qmm_na(g, m), m, nb))) {
 		whine(g, "a staging buffer would not allocate");
 		return -1;
 	}
@@ -632,6 +671,10 @@ struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	g->sm_count = prop.multiProcessorCount;
 	g->slow_us = (double)env_u("CHARSIU_GPU_SLOW_US", 100000);
 	g->no_pdl = getenv("CHARSIU_GPU_NO_PDL") != nullptr;
+	if (const char *na = getenv("CHARSIU_GPU_QMM_NA"))
+		g->qmm_na = !strcmp(na, "16") ? 16 : !strcmp(na, "32") ? 32 : 0;
+	if (const char *pre = getenv("CHARSIU_GPU_QMM_PRE"))
+		g->qmm_pre = !strcmp(pre, "1");
 	g->ent.reserve(max_tensors);
 	if (cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking) != cudaSuccess ||
 	    cudaEventCreate(&g->ev_k0) != cudaSuccess || cudaEventCreate(&g->ev_k1) != cudaSuccess ||
@@ -871,9 +914,9 @@ int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m, cons
 	const uint32_t nb = e.nb;
 	cudaStream_t st = stream ? (cudaStream_t)stream : g->stream;
 	if (m > 1 && e.type == TYPE_Q8_0) {
-		if (!grow_dev(g->d_pack, g->cap_pack, qmm_pack_bytes(m, nb)))
+		if (!grow_dev(g->d_pack, g->cap_pack, qmm_pack_bytes(qmm_na(g, m), m, nb)))
 			return -1;
-		return launch_qmm(g, e, q, d, m, y, g->d_pack, st);
+		return launch_qmm(g, &id, 1, q, d, m, &y, g->d_pack, st);
 	}
 	for (unsigned m0 = 0; m0 < m;) {
 		const unsigned left = m - m0;
@@ -887,6 +930,34 @@ int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m, cons
 			return -1;
 		m0 += mc;
 	}
+	return 0;
+}
+
+int charsiu_gpu_matvec_batch_group_dev(struct charsiu_gpu *g, const int *ids, unsigned n,
+				       unsigned m, const int8_t *q, const float *d, float *const *ys,
+				       void *stream)
+{
+	if (!g || g->dead || !ids || !q || !d || !ys || !m || ((uintptr_t)q & 15) ||
+	    !n || n > (unsigned)QMM_MAX_TENSORS)
+		return -1;
+	for (unsigned i = 0; i < n; i++)
+		if (ids[i] < 0 || (size_t)ids[i] >= g->ent.size() || !ys[i] ||
+		    g->ent[ids[i]].k != g->ent[ids[0]].k)
+			return -1;
+	cudaSetDevice(g->device);
+	bool all_q8 = m > 1;
+	for (unsigned i = 0; i < n; i++)
+		all_q8 = all_q8 && g->ent[ids[i]].type == TYPE_Q8_0;
+	if (all_q8) {
+		const uint32_t nb = g->ent[ids[0]].nb;
+		if (!grow_dev(g->d_pack, g->cap_pack, qmm_pack_bytes(qmm_na(g, m), m, nb)))
+			return -1;
+		return launch_qmm(g, ids, n, q, d, m, ys, g->d_pack,
+				  stream ? (cudaStream_t)stream : g->stream);
+	}
+	for (unsigned i = 0; i < n; i++)
+		if (charsiu_gpu_matvec_batch_dev(g, ids[i], m, q, d, ys[i], stream))
+			return -1;
 	return 0;
 }
 
@@ -907,7 +978,7 @@ int charsiu_gpu_matvec_batch_noalloc(struct charsiu_gpu *g, int id, unsigned m, 
 		whine(g, "the allocation-free batched matvec takes q8_0 tensors only (%s)", e.name);
 		return -1;
 	}
-	const size_t need = qmm_pack_bytes(m, e.nb);
+	const size_t need = qmm_pack_bytes(qmm_na(g, m), m, e.nb);
 	if (need > NOALLOC_SCRATCH_BYTES) {
 		whine(g, "the allocation-free batched matvec holds %zu bytes of packed activations; "
 			 "m=%u at K=%llu needs %zu", NOALLOC_SCRATCH_BYTES, m,
@@ -920,7 +991,8 @@ int charsiu_gpu_matvec_batch_noalloc(struct charsiu_gpu *g, int id, unsigned m, 
 		whine(g, "the allocation-free scratch has no device address on device %d", g->device);
 		return -1;
 	}
-	return launch_qmm(g, e, q, d, m, y, scratch, stream ? (cudaStream_t)stream : g->stream);
+	return launch_qmm(g, &id, 1, q, d, m, &y, scratch,
+			  stream ? (cudaStream_t)stream : g->stream);
 }
 
 int charsiu_gpu_act_quantise_dev(struct charsiu_gpu *g, const float *x, unsigned m, unsigned k,

@@ -115,6 +115,35 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c)
 	return __dp4a(static_cast<int>(a), static_cast<int>(b), c);
 }
 
+// Packed fp32 pairs (sm_100): each lane rounds to nearest as mul.rn.f32 /
+// add.rn.f32 do. Unlike the scalar forms, a mul.rn.f32x2 whose result feeds
+// an add.rn.f32x2 is contracted by the assembler into one fused
+// multiply-add (seen on sm_100a with CUDA 12.9), so code that needs the
+// product rounded before the sum must not pair these two.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b)
+{
+	float2 r;
+	asm("{\n\t.reg .b64 x, y, z;\n\t"
+	    "mov.b64 x, {%2, %3};\n\t"
+	    "mov.b64 y, {%4, %5};\n\t"
+	    "mul.rn.f32x2 z, x, y;\n\t"
+	    "mov.b64 {%0, %1}, z;\n\t}"
+	    : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+	return r;
+}
+
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b)
+{
+	float2 r;
+	asm("{\n\t.reg .b64 x, y, z;\n\t"
+	    "mov.b64 x, {%2, %3};\n\t"
+	    "mov.b64 y, {%4, %5};\n\t"
+	    "add.rn.f32x2 z, x, y;\n\t"
+	    "mov.b64 {%0, %1}, z;\n\t}"
+	    : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+	return r;
+}
+
 // fp16 bits -> fp32, exact for every finite value (subnormals included)
 __device__ __forceinline__ float half_bits_to_float(uint16_t h)
 {

@@ -1,7 +1,7 @@
 // SPDX-License-Identifier: GPL-2.0-or-later
 // The batched block-quant matvec on the tensor cores: m activations against
-// a q8_0 tensor, y[a][n] bit-identical to charsiu's gguf_matvec of each
-// activation (reference src/gguf.c:1098-1107, 1149-1171).
+// up to eight q8_0 tensors of one K, y[a][n] bit-identical to charsiu's
+// gguf_matvec of each activation (reference src/gguf.c:1098-1107, 1149-1171).
 //
 // One tcgen05.mma kind::i8 with K = 32 is exactly one GGML block: for block b
 // it gives t[n][a] = sum_j q_w[n][b][j] * q_a[a][b][j] for a 128-row weight
@@ -10,16 +10,29 @@
 //     s[n][a] = s[n][a] + (d_w[n][b] * d_a[a][b]) * (float)t[n][a]
 // in block order, so the fp32 sums are the reference's exactly. The MMA
 // cannot accumulate across blocks (each block has its own scales); it writes
-// a fresh int32 tile per block into one of two tensor-memory buffers while
-// the epilogue drains the other.
+// a fresh int32 tile per block. Tiles are grouped in CHUNKS of four blocks,
+// one commit a chunk, into two chunk buffers of tensor memory, so the
+// epilogue drains one chunk while the MMAs fill the other.
 //
-// Warp roles: warp 0 lane 0 issues the single-destination bulk copies of one
-// K segment (16 blocks) a stage -- the 16 groups' weight segments as they lie
-// in the device layout (layout.h), already MMA core matrices, and the packed
-// activation tile (qmm_pack_kernel) -- into a double-buffered stage; warp 1
-// owns tensor memory and lane 0 issues the MMAs; 4 * EP epilogue warps (a
-// lane quarter each, EP column slices of 32 when NA = 64) read the int32
-// tiles with tcgen05.ld and accumulate. Every wait is bounded.
+// Work units are (128-row tile of one tensor, NA activations); a persistent
+// grid deals them round robin, activation tile fastest so the CTAs sharing a
+// weight tile run together (the second and later reads of it hit L2). Warp
+// roles: warp 0 lane 0 issues the single-destination bulk copies of one K
+// segment (16 blocks) a stage -- the tile's 16 groups' weight segments as
+// they lie in the device layout (layout.h), already MMA core matrices, and
+// the packed activation tile (qmm_pack_kernel) -- into a double-buffered
+// stage; warp 1 owns tensor memory and lane 0 issues the MMAs; EW = 4 * NA/16
+// epilogue warps (a tensor-memory lane quarter and 16 activations each) read
+// the int32 tiles with tcgen05.ld and accumulate. The conversion, the scale
+// d_w * d_a and the product use the packed fp32x2 operations (two columns an
+// instruction, each lane rounded as the scalar operation rounds); the sum is
+// scalar.
+//
+// PRE: the tensor memory of every block slot holds 0x4b400000 before its MMA,
+// which then accumulates onto it, so the int32 comes out as the bits of the
+// float 1.5 * 2^23 + t and the epilogue's int-to-float is one subtraction
+// (|t| <= 32 * 127 * 128 < 2^22). The epilogue writes the constant back after
+// each read. Every wait is bounded.
 #pragma once
 
 #include "layout.h"
@@ -30,6 +43,8 @@ namespace cgpu {
 
 constexpr int QMM_TILE_GROUPS = 16;                       // 128 weight rows
 constexpr uint32_t QMM_WSTAGE = QMM_TILE_GROUPS * MAX_SEG_BYTES;   // 69632
+constexpr int QMM_CHUNK = 4;                              // blocks a commit
+constexpr int QMM_MAX_TENSORS = 8;
 
 // The packed activation tile of a NA-row slab of activations, per K segment:
 // quants [16 blocks][2 chunks][NA rows][16 B] then deltas [16 blocks][NA] f32.
@@ -44,11 +59,24 @@ __host__ inline size_t qmm_smem_bytes(uint32_t na)
 	return 2 * ((size_t)QMM_WSTAGE + qmm_act_seg_bytes(na)) + 16 * sizeof(uint64_t) + 16;
 }
 
+__host__ __device__ constexpr int qmm_threads(int na)
+{
+	return (2 + 4 * (na / 16)) * 32;
+}
+
+// tensor-memory columns: two chunk buffers of QMM_CHUNK blocks of NA columns
+__host__ __device__ constexpr uint32_t qmm_tmem_cols(int na)
+{
+	return 2 * QMM_CHUNK * na;
+}
+
 // q int8 [m][nb*32], d f32 [m][nb] -> packed [m tiles][nseg][qmm_act_seg_bytes]
 // One thread per 16-byte quant chunk or per delta.
 __global__ void qmm_pack_kernel(const int8_t *__restrict__ q, const float *__restrict__ d,
 				uint32_t m, uint32_t nb, uint32_t na, uint8_t *__restrict__ out)
 {
+	pdl_wait();                 // q and d may come from the kernel before
+	pdl_launch_dependents();
 	const uint32_t nseg = nsegments(nb), mt = (m + na - 1) / na;
 	const uint64_t per_seg = (uint64_t)SB * 2 * na + (uint64_t)SB * na;   // work items
 	const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -73,21 +101,28 @@ __global__ void qmm_pack_kernel(const int8_t *__restrict__ q, const float *__res
 	}
 }
 
-struct QmmParams {
+struct QmmTensor {
 	const uint8_t *w;          // the tensor's device layout (q8_0)
-	const uint8_t *act;        // qmm_pack_kernel output
 	float *y;                  // y[a][rows]
-	uint32_t rows, groups, nb, m;
+	uint32_t rows, groups;
+	uint32_t tile_end;         // running count of 128-row tiles through this tensor
+	uint32_t pad_;
+};
+
+struct QmmParams {
+	QmmTensor t[QMM_MAX_TENSORS];
+	const uint8_t *act;        // qmm_pack_kernel output
+	uint32_t ntensor, tiles, atiles, nb, m;
 	int *err;
 };
 
-template <int NA>
-__global__ void __launch_bounds__((2 + 4 * (NA > 32 ? NA / 32 : 1)) * 32, 1)
+template <int NA, bool PRE>
+__global__ void __launch_bounds__(qmm_threads(NA), 1)
 qmm_tc_kernel(const __grid_constant__ QmmParams p)
 {
-	constexpr int EP = NA > 32 ? NA / 32 : 1;          // column slices
-	constexpr int EC = NA / EP;                        // columns a slice
+	constexpr int EW = 4 * (NA / 16);                  // epilogue warps
 	constexpr uint32_t ASEG = qmm_act_seg_bytes(NA);
+	constexpr uint32_t NCOLS = qmm_tmem_cols(NA);
 	extern __shared__ __align__(128) uint8_t smem[];
 	auto stage_w = [&](uint32_t st) { return smem + st * QMM_WSTAGE; };
 	auto stage_a = [&](uint32_t st) { return smem + 2 * QMM_WSTAGE + st * ASEG; };
@@ -96,21 +131,19 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 	uint32_t *taddr_s = reinterpret_cast<uint32_t *>(bars + 8);
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const uint32_t g0 = blockIdx.x * QMM_TILE_GROUPS, a0 = blockIdx.y * NA;
 	const uint32_t nb = p.nb, nseg = nsegments(nb);
-	const uint32_t tgroups = min((uint32_t)QMM_TILE_GROUPS, p.groups - g0);
-	const uint8_t *act = p.act + (uint64_t)blockIdx.y * nseg * ASEG;
+	const uint32_t units = p.tiles * p.atiles;
 
 	if (warp == 1) {
-		tmem_alloc(taddr_s, 2 * NA < 32 ? 32 : 2 * NA);
+		tmem_alloc(taddr_s, NCOLS);
 		tmem_relinquish();
 	}
 	if (threadIdx.x == 0) {
 		for (int i = 0; i < 2; i++) {
 			mbar_init(&full[i], 1);
-			mbar_init(&freeb[i], 1 + 4 * EP);
+			mbar_init(&freeb[i], 1 + EW);
 			mbar_init(&mma_done[i], 1);
-			mbar_init(&tfree[i], 4 * EP);
+			mbar_init(&tfree[i], EW);
 		}
 		fence_mbar_init();
 	}
@@ -119,120 +152,235 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 	tc_fence_after();
 	const uint32_t taddr = *taddr_s;
 
+	// the tensor and row tile of unit u
+	auto locate = [&](uint32_t u, uint32_t &ti, uint32_t &tile) {
+		const uint32_t rt = u / p.atiles;
+		ti = 0;
+		while (ti + 1 < p.ntensor && rt >= p.t[ti].tile_end)
+			ti++;
+		tile = rt - (ti ? p.t[ti - 1].tile_end : 0);
+	};
+
 	if (warp == 0) {
 		// ---- producer ------------------------------------------------------
 		if (lane == 0) {
-			for (uint32_t s = 0; s < nseg; s++) {
-				const uint32_t st = s & 1, sb = seg_blocks(nb, s);
-				if (s >= 2 && !mbar_wait_bounded(&freeb[st], ((s >> 1) - 1) & 1, WAIT_LIMIT_NS)) {
-					*(volatile int *)p.err = 5;
-					break;
+			bool ok = true;
+			uint32_t s_cnt = 0, waited_act = 0;
+			for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+				uint32_t ti, tile;
+				locate(u, ti, tile);
+				const QmmTensor &T = p.t[ti];
+				const uint32_t g0 = tile * QMM_TILE_GROUPS;
+				const uint32_t tgroups = min((uint32_t)QMM_TILE_GROUPS, T.groups - g0);
+				const uint8_t *act = p.act + (uint64_t)(u % p.atiles) * nseg * ASEG;
+				for (uint32_t s = 0; s < nseg; s++, s_cnt++) {
+					const uint32_t st = s_cnt & 1, sb = seg_blocks(nb, s);
+					if (s_cnt >= 2 &&
+					    !mbar_wait_bounded(&freeb[st], ((s_cnt >> 1) - 1) & 1, WAIT_LIMIT_NS)) {
+						*(volatile int *)p.err = 5;
+						ok = false;
+						break;
+					}
+					const uint32_t wbytes = sb * block_group_bytes(TYPE_Q8_0);
+					mbar_arrive_expect_tx(&full[st], tgroups * wbytes + ASEG);
+					for (uint32_t g = 0; g < tgroups; g++)
+						bulk_g2s(stage_w(st) + g * MAX_SEG_BYTES,
+							 T.w + (uint64_t)(g0 + g) * group_bytes(TYPE_Q8_0, nb) +
+								 seg_offset(TYPE_Q8_0, s),
+							 wbytes, &full[st]);
+					if (!waited_act) {
+						// weights never depend on the kernel before; the
+						// packed activations do
+						pdl_wait();
+						waited_act = 1;
+					}
+					bulk_g2s(stage_a(st), act + (uint64_t)s * ASEG, ASEG, &full[st]);
 				}
-				const uint32_t wbytes = sb * block_group_bytes(TYPE_Q8_0);
-				mbar_arrive_expect_tx(&full[st], tgroups * wbytes + ASEG);
-				for (uint32_t g = 0; g < tgroups; g++)
-					bulk_g2s(stage_w(st) + g * MAX_SEG_BYTES,
-						 p.w + (uint64_t)(g0 + g) * group_bytes(TYPE_Q8_0, nb) +
-							 seg_offset(TYPE_Q8_0, s),
-						 wbytes, &full[st]);
-				bulk_g2s(stage_a(st), act + (uint64_t)s * ASEG, ASEG, &full[st]);
 			}
+			// before leaving, let every copy issued land (already true unless
+			// a wait above gave up)
+			for (uint32_t i = s_cnt > 2 ? s_cnt - 2 : 0; i < s_cnt; i++)
+				if (!mbar_wait_bounded(&full[i & 1], (i >> 1) & 1, WAIT_LIMIT_NS))
+					*(volatile int *)p.err = 10;
 		}
 	} else if (warp == 1) {
 		// ---- MMA issuer ------------------------------------------------------
 		if (lane == 0) {
 			constexpr uint32_t idesc = idesc_i8(128, NA);
 			bool ok = true;
-			for (uint32_t s = 0; s < nseg && ok; s++) {
-				const uint32_t st = s & 1, sb = seg_blocks(nb, s);
-				if (!mbar_wait_bounded(&full[st], (s >> 1) & 1, WAIT_LIMIT_NS)) {
-					*(volatile int *)p.err = 6;
-					break;
-				}
-				tc_fence_after();
-				for (uint32_t bi = 0; bi < sb; bi++) {
-					const uint32_t j = s * SB + bi, buf = j & 1;
-					if (j >= 2 && !mbar_wait_bounded(&tfree[buf], ((j >> 1) - 1) & 1,
-									 WAIT_LIMIT_NS)) {
-						*(volatile int *)p.err = 7;
+			uint32_t s_cnt = 0, c_cnt = 0;
+			for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+				for (uint32_t s = 0; s < nseg && ok; s++, s_cnt++) {
+					const uint32_t st = s_cnt & 1, sb = seg_blocks(nb, s);
+					if (!mbar_wait_bounded(&full[st], (s_cnt >> 1) & 1, WAIT_LIMIT_NS)) {
+						*(volatile int *)p.err = 6;
 						ok = false;
 						break;
 					}
 					tc_fence_after();
-					const uint64_t ad = smem_desc_k_nosw(stage_w(st) + bi * RG * 32, RG * 16,
-									     MAX_SEG_BYTES);
-					const uint64_t bd = smem_desc_k_nosw(stage_a(st) + bi * 2 * NA * 16,
-									     NA * 16, 128);
-					mma_i8(taddr + buf * NA, ad, bd, idesc, false);
-					mma_commit(&mma_done[buf]);
+					for (uint32_t b0 = 0; b0 < sb; b0 += QMM_CHUNK, c_cnt++) {
+						const uint32_t buf = c_cnt & 1;
+						// PRE: the epilogue's first release of each buffer is
+						// its fill with the constant
+						if ((PRE || c_cnt >= 2) &&
+						    !mbar_wait_bounded(&tfree[buf],
+								       ((c_cnt >> 1) - (PRE ? 0 : 1)) & 1,
+								       WAIT_LIMIT_NS)) {
+							*(volatile int *)p.err = 7;
+							ok = false;
+							break;
+						}
+						tc_fence_after();
+						const uint32_t nblk = min((uint32_t)QMM_CHUNK, sb - b0);
+						for (uint32_t j = 0; j < nblk; j++) {
+							const uint32_t bi = b0 + j;
+							const uint64_t ad = smem_desc_k_nosw(
+								stage_w(st) + bi * RG * 32, RG * 16, MAX_SEG_BYTES);
+							const uint64_t bd = smem_desc_k_nosw(
+								stage_a(st) + bi * 2 * NA * 16, NA * 16, 128);
+							mma_i8(taddr + buf * QMM_CHUNK * NA + j * NA, ad, bd, idesc,
+							       PRE);
+						}
+						mma_commit(&mma_done[buf]);
+					}
+					if (ok)
+						mma_commit(&freeb[st]);
 				}
-				mma_commit(&freeb[st]);
 			}
+			// the last chunk's MMAs must be done before tensor memory is freed
+			if (c_cnt && !mbar_wait_bounded(&mma_done[(c_cnt - 1) & 1], ((c_cnt - 1) >> 1) & 1,
+							WAIT_LIMIT_NS))
+				*(volatile int *)p.err = 11;
 		}
 	} else {
-		// ---- epilogue: TMEM lane quarter q, column slice e -------------------
+		// ---- epilogue: TMEM lane quarter q, activations e*16 .. e*16+15 -------
 		const int ew = warp - 2, q = warp % 4, e = ew / 4;
 		const uint32_t r = q * 32 + lane;                  // row of the tile
 		const uint32_t grp = r / RG, rr = r % RG;
-		float acc[EC];
-#pragma unroll
-		for (int c = 0; c < EC; c++)
-			acc[c] = 0.0f;
+		const uint32_t lane_base = (uint32_t)(q * 32) << 16;
 		bool ok = true;
-		for (uint32_t s = 0; s < nseg && ok; s++) {
-			const uint32_t st = s & 1, sb = seg_blocks(nb, s);
-			if (!mbar_wait_bounded(&full[st], (s >> 1) & 1, WAIT_LIMIT_NS)) {
-				if (lane == 0)
-					*(volatile int *)p.err = 8;
-				break;
+		if (PRE) {
+			for (uint32_t c = 0; c < NCOLS; c += NA)
+				tmem_fill16(taddr + lane_base + c + e * 16, INT_FLOAT_MAGIC);
+			tmem_wait_st();
+			tc_fence_before();
+			__syncwarp();
+			if (lane == 0) {
+				mbar_arrive(&tfree[0]);
+				mbar_arrive(&tfree[1]);
 			}
-			const uint16_t *dl = reinterpret_cast<const uint16_t *>(
-				stage_w(st) + grp * MAX_SEG_BYTES + sb * RG * 32);
-			const float *da = reinterpret_cast<const float *>(stage_a(st) + SB * 2 * NA * 16);
-			for (uint32_t bi = 0; bi < sb; bi++) {
-				const uint32_t j = s * SB + bi, buf = j & 1;
-				if (!mbar_wait_bounded(&mma_done[buf], (j >> 1) & 1, WAIT_LIMIT_NS)) {
+		}
+		pdl_wait();                  // y may still be read by the kernel before
+		pdl_launch_dependents();
+		const float2 neg_bias = make_float2(-INT_FLOAT_BIAS, -INT_FLOAT_BIAS);
+		uint32_t s_cnt = 0, c_cnt = 0;
+		for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+			uint32_t ti, tile;
+			locate(u, ti, tile);
+			float2 acc[8];
+#pragma unroll
+			for (int c = 0; c < 8; c++)
+				acc[c] = make_float2(0.0f, 0.0f);
+			for (uint32_t s = 0; s < nseg && ok; s++, s_cnt++) {
+				const uint32_t st = s_cnt & 1, sb = seg_blocks(nb, s);
+				if (!mbar_wait_bounded(&full[st], (s_cnt >> 1) & 1, WAIT_LIMIT_NS)) {
 					if (lane == 0)
-						*(volatile int *)p.err = 9;
+						*(volatile int *)p.err = 8;
 					ok = false;
 					break;
 				}
-				tc_fence_after();
-				uint32_t t[EC];
+				const uint16_t *dl = reinterpret_cast<const uint16_t *>(
+					stage_w(st) + grp * MAX_SEG_BYTES + sb * RG * 32);
+				const float *da = reinterpret_cast<const float *>(stage_a(st) + SB * 2 * NA * 16) +
+						  e * 16;
+				for (uint32_t b0 = 0; b0 < sb; b0 += QMM_CHUNK, c_cnt++) {
+					const uint32_t buf = c_cnt & 1, nblk = min((uint32_t)QMM_CHUNK, sb - b0);
+					if (!mbar_wait_bounded(&mma_done[buf], (c_cnt >> 1) & 1, WAIT_LIMIT_NS)) {
+						if (lane == 0)
+							*(volatile int *)p.err = 9;
+						ok = false;
+						break;
+					}
+					tc_fence_after();
+					uint32_t t[QMM_CHUNK][16];
+					const uint32_t col0 = taddr + lane_base + buf * QMM_CHUNK * NA + e * 16;
 #pragma unroll
-				for (int c = 0; c < EC; c += 16)
-					tmem_ld16(taddr + ((uint32_t)(q * 32) << 16) + buf * NA + e * EC + c,
-						  *reinterpret_cast<uint32_t(*)[16]>(&t[c]));
-				tmem_wait_ld();
-				tc_fence_before();
+					for (int j = 0; j < QMM_CHUNK; j++)
+						if (j < (int)nblk)
+							tmem_ld16(col0 + j * NA, t[j]);
+					tmem_wait_ld();
+					if (PRE) {
+#pragma unroll
+						for (int j = 0; j < QMM_CHUNK; j++)
+							if (j < (int)nblk)
+								tmem_fill16(col0 + j * NA, INT_FLOAT_MAGIC);
+						tmem_wait_st();
+					}
+					tc_fence_before();
+					__syncwarp();
+					if (lane == 0)
+						mbar_arrive(&tfree[buf]);
+#pragma unroll
+					for (int j = 0; j < QMM_CHUNK; j++) {
+						if (j >= (int)nblk)
+							break;
+						const uint32_t bi = b0 + j;
+						const float dw = half_bits_to_float(dl[bi * RG + rr]);
+						const float2 dw2 = make_float2(dw, dw);
+						const float4 *da4 = reinterpret_cast<const float4 *>(da + bi * NA);
+#pragma unroll
+						for (int c4 = 0; c4 < 4; c4++) {
+							const float4 a4 = da4[c4];
+							const float2 sc0 = mul2_rn(dw2, make_float2(a4.x, a4.y));
+							const float2 sc1 = mul2_rn(dw2, make_float2(a4.z, a4.w));
+							const uint32_t *tt = &t[j][4 * c4];
+							float2 f0, f1;
+							if (PRE) {
+								f0 = make_float2(__uint_as_float(tt[0]), __uint_as_float(tt[1]));
+								f1 = make_float2(__uint_as_float(tt[2]), __uint_as_float(tt[3]));
+							} else {
+								f0 = make_float2(__uint_as_float(INT_FLOAT_MAGIC + tt[0]),
+										 __uint_as_float(INT_FLOAT_MAGIC + tt[1]));
+								f1 = make_float2(__uint_as_float(INT_FLOAT_MAGIC + tt[2]),
+										 __uint_as_float(INT_FLOAT_MAGIC + tt[3]));
+							}
+							f0 = add2_rn(f0, neg_bias);
+							f1 = add2_rn(f1, neg_bias);
+							// the sum stays scalar: a packed product feeding a
+							// packed add is contracted into a fused multiply-add
+							// by the assembler (explicit .rn notwithstanding),
+							// which rounds once where the reference rounds twice
+							const float2 p0 = mul2_rn(sc0, f0), p1 = mul2_rn(sc1, f1);
+							acc[2 * c4].x = __fadd_rn(acc[2 * c4].x, p0.x);
+							acc[2 * c4].y = __fadd_rn(acc[2 * c4].y, p0.y);
+							acc[2 * c4 + 1].x = __fadd_rn(acc[2 * c4 + 1].x, p1.x);
+							acc[2 * c4 + 1].y = __fadd_rn(acc[2 * c4 + 1].y, p1.y);
+						}
+					}
+				}
 				__syncwarp();
 				if (lane == 0)
-					mbar_arrive(&tfree[buf]);
-				const float dw = half_bits_to_float(dl[bi * RG + rr]);
-				const float *dab = da + bi * NA + e * EC;
-#pragma unroll
-				for (int c = 0; c < EC; c++)
-					acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(dw, dab[c]),
-									     small_int_to_float((int32_t)t[c])));
+					mbar_arrive(&freeb[st]);
 			}
-			__syncwarp();
-			if (lane == 0)
-				mbar_arrive(&freeb[st]);
-		}
-		const uint32_t row = g0 * RG + r;
-		if (ok && row < p.rows) {
+			if (!ok)
+				break;
+			const QmmTensor &T = p.t[ti];
+			const uint32_t row = tile * QMM_TILE_GROUPS * RG + r;
+			const uint32_t a0 = (u % p.atiles) * NA + e * 16;
+			if (row < T.rows) {
 #pragma unroll
-			for (int c = 0; c < EC; c++) {
-				const uint32_t a = a0 + e * EC + c;
-				if (a < p.m)
-					p.y[(uint64_t)a * p.rows + row] = acc[c];
+				for (int c = 0; c < 16; c++) {
+					const uint32_t a = a0 + c;
+					if (a < p.m)
+						T.y[(uint64_t)a * T.rows + row] = c & 1 ? acc[c / 2].y : acc[c / 2].x;
+				}
 			}
 		}
 	}
 	tc_fence_before();
 	__syncthreads();
 	if (warp == 1)
-		tmem_dealloc(taddr, 2 * NA < 32 ? 32 : 2 * NA);
+		tmem_dealloc(taddr, NCOLS);
 }
 
 } // namespace cgpu

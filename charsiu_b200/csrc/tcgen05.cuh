@@ -108,10 +108,28 @@ __device__ __forceinline__ void tmem_wait_ld()
 	asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// |t| < 2^22 to fp32, exactly: two full-rate ops instead of a conversion.
+// The same 32 lanes x 16 columns, every word set to `v`.
+__device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t v)
+{
+	asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+		     "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};"
+		     :: "r"(taddr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st()
+{
+	asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// |t| < 2^22 to fp32, exactly: 0x4b400000 is 1.5 * 2^23, whose float spacing
+// is 1, so the bits 0x4b400000 + t are the float 1.5 * 2^23 + t, and taking
+// 1.5 * 2^23 away again is exact. Two full-rate ops instead of a conversion.
+constexpr uint32_t INT_FLOAT_MAGIC = 0x4b400000u;
+constexpr float INT_FLOAT_BIAS = 12582912.0f;
+
 __device__ __forceinline__ float small_int_to_float(int32_t t)
 {
-	return __fsub_rn(__int_as_float(0x4b400000 + t), 12582912.0f);
+	return __fsub_rn(__int_as_float((int32_t)INT_FLOAT_MAGIC + t), INT_FLOAT_BIAS);
 }
 
 } // namespace cgpu

@@ -41,6 +41,8 @@ SIGNATURES = [
                                              C.c_int, _vp]),
     ("charsiu_gpu_matvec_dev", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp, _vp, _vp]),
     ("charsiu_gpu_matvec_batch_dev", C.c_int, [_vp, C.c_int, C.c_uint, _vp, _vp, _vp, _vp]),
+    ("charsiu_gpu_matvec_batch_group_dev", C.c_int,
+     [_vp, _vp, C.c_uint, C.c_uint, _vp, _vp, _vp, _vp]),
     ("charsiu_gpu_matvec_batch_noalloc", C.c_int, [_vp, C.c_int, C.c_uint, _vp, _vp, _vp, _vp]),
     ("charsiu_gpu_act_quantise_dev", C.c_int, [_vp, _vp, C.c_uint, C.c_uint, _vp, _vp, _vp]),
     ("charsiu_gpu_calls", C.c_ulong, [_vp]),
@@ -210,6 +212,15 @@ class Layer:
                   stream: int = 0) -> int:
         return self.L.charsiu_gpu_matvec_batch_dev(self.h, tid, m, q_ptr, d_ptr, y_ptr,
                                                    stream or None)
+
+    def batch_group_dev(self, ids, m: int, q_ptr: int, d_ptr: int, y_ptrs,
+                        stream: int = 0) -> int:
+        ids = list(ids)
+        idarr = (C.c_int * len(ids))(*ids)
+        yarr = (C.c_void_p * len(ids))(*y_ptrs)
+        return self.L.charsiu_gpu_matvec_batch_group_dev(self.h, C.addressof(idarr), len(ids),
+                                                         m, q_ptr, d_ptr, C.addressof(yarr),
+                                                         stream or None)
 
     def batch_noalloc(self, tid: int, m: int, q_ptr: int, d_ptr: int, y_ptr: int,
                       stream: int = 0) -> int:

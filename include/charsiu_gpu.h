@@ -143,6 +143,14 @@ CHARSIU_GPU_API int charsiu_gpu_matvec_dev(struct charsiu_gpu *g, const int *ids
 CHARSIU_GPU_API int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m,
 				 const int8_t *q, const float *d, float *y,
 				 void *stream);
+/* The batched twin of charsiu_gpu_matvec_group (include/charsiu_llm.h:194-196
+ * for one activation): m activations (q [m][K] int8, d [m][K/32] fp32) against
+ * n <= 8 tensors of the same K, ys[i] = [m][rows of ids[i]]. q8_0 tensors share
+ * one packing of the activations and one tensor-core launch. */
+CHARSIU_GPU_API int charsiu_gpu_matvec_batch_group_dev(struct charsiu_gpu *g, const int *ids,
+						       unsigned n, unsigned m, const int8_t *q,
+						       const float *d, float *const *ys,
+						       void *stream);
 /* The batched matvec of charsiu_gpu_matvec_batch_dev, for callers that
  * cannot allocate GPU memory while they run -- a server whose own memory
  * pool already owns the GPU's free memory, or a latency-bound loop that must
@@ -150,7 +158,7 @@ CHARSIU_GPU_API int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, 
  * a staging buffer with cudaMalloc on first use). This call allocates
  * nothing: its scratch is a fixed 1 MiB array inside the library, held on
  * every GPU that loads it until exit. q8_0 tensors only; the m activations
- * are packed in tiles of 16, 32 or 64 and must fit that array (m <= 64 up to
+ * are packed in tiles of 16 or 32 and must fit that array (m <= 64 up to
  * K = 14336), else -1 with the reason in charsiu_gpu_error. All calls on a GPU
  * share the array, so two calls running on it at the same time race. The
  * first call on each GPU looks up the array's device address; make it before

@@ -27,7 +27,7 @@ def same(a, b):
 
 @pytest.fixture(scope="module")
 def layer():
-    with Layer(max_k=8256, max_n=128256, max_tensors=96) as L:
+    with Layer(max_k=8256, max_n=128256, max_tensors=200) as L:
         yield L
 
 
@@ -97,14 +97,75 @@ def test_output_head_shape(layer):
 @pytest.mark.parametrize("qt", [G.GGML_Q8_0, G.GGML_Q4_0])
 @pytest.mark.parametrize("k,n", [(2048, 520), (8192, 136)])
 def test_batch_rows_match_single_matvec(layer, m, qt, k, n):
-    """M > 1: q8_0 runs on the tensor cores (tcgen05 kind::i8, tiles of 16,
-    32 or 64 activations), q4_0 on the CUDA cores; every row bit-exact."""
+    """M > 1: q8_0 runs on the tensor cores (tcgen05 kind::i8, tiles of 16
+    or 32 activations), q4_0 on the CUDA cores; every row bit-exact."""
     blk, xs = W.batch_inputs(qt, k, n, m, seed=3)
     tid = layer.add_blocks(qt, k, n, blk)
     qs, ds = zip(*(O.act_quantise(x) for x in xs))
     y = layer.batch(tid, np.stack(qs), np.stack(ds))
     for i in range(m):
         assert same(y[i], O.matvec(qt, blk, k, n, qs[i], ds[i])), f"row {i}"
+
+
+def _dev_acts(torch, xs, dev):
+    """q8 activations on the device, quantised by the oracle (checked above)."""
+    qs, ds = zip(*(O.act_quantise(x) for x in xs))
+    q_t = torch.from_numpy(np.ascontiguousarray(np.stack(qs))).to(dev)
+    d_t = torch.from_numpy(np.ascontiguousarray(np.stack(ds))).to(dev)
+    return qs, ds, q_t, d_t
+
+
+@pytest.mark.parametrize("m", [2, 17, 64])
+@pytest.mark.parametrize("k", [2048, 2080, 544])
+def test_batch_group_dev_one_launch(layer, m, k):
+    """Several q8_0 tensors of one K in one tensor-core launch (as q/k/v and
+    gate/up are grouped), ragged N (a partial last 128-row tile, a partial
+    last group) and K with a partial last segment and chunk; every row of
+    every tensor bit-exact."""
+    torch = pytest.importorskip("torch")
+    dev = torch.device("cuda:0")
+    ns = [520, 136, 9, 2048]
+    ids, blks = [], []
+    for i, n in enumerate(ns):
+        blk, _ = W.matvec_inputs(G.GGML_Q8_0, k, n, seed=400 + i)
+        ids.append(layer.add_blocks(G.GGML_Q8_0, k, n, blk))
+        blks.append(blk)
+    xs = np.random.default_rng(m * 31 + k).normal(size=(m, k)).astype(np.float32)
+    xs[m // 2, :64] = 0.0                 # zero activation blocks
+    qs, ds, q_t, d_t = _dev_acts(torch, xs, dev)
+    ys = [torch.full((m, n), float("nan"), device=dev) for n in ns]
+    stream = torch.cuda.current_stream().cuda_stream
+    assert layer.batch_group_dev(ids, m, q_t.data_ptr(), d_t.data_ptr(),
+                                 [y.data_ptr() for y in ys], stream) == 0
+    torch.cuda.synchronize()
+    for blk, n, y in zip(blks, ns, ys):
+        yc = y.cpu().numpy()
+        for i in range(m):
+            assert same(yc[i], O.matvec(G.GGML_Q8_0, blk, k, n, qs[i], ds[i])), f"n={n} row {i}"
+
+
+@pytest.mark.parametrize("na,pre", [("16", "0"), ("16", "1"), ("32", "0"), ("32", "1")])
+def test_batch_tile_variants_agree(monkeypatch, na, pre):
+    """Every tensor-core tile variant (16 or 32 activations a tile; the int32
+    dots converted in the epilogue or accumulated onto the float-bias
+    constant in tensor memory) gives the reference's bits, on a tensor with
+    more (tile, activation) units than SMs, so CTAs loop."""
+    torch = pytest.importorskip("torch")
+    monkeypatch.setenv("CHARSIU_GPU_QMM_NA", na)
+    monkeypatch.setenv("CHARSIU_GPU_QMM_PRE", pre)
+    dev = torch.device("cuda:0")
+    k, n, m = 2048, 20000, 37
+    with Layer(max_k=k, max_n=n, max_tensors=2) as L:
+        blk, xs = W.batch_inputs(G.GGML_Q8_0, k, n, m, seed=9)
+        tid = L.add_blocks(G.GGML_Q8_0, k, n, blk)
+        qs, ds, q_t, d_t = _dev_acts(torch, xs, dev)
+        y = torch.full((m, n), float("nan"), device=dev)
+        assert L.batch_dev(tid, m, q_t.data_ptr(), d_t.data_ptr(), y.data_ptr(),
+                           torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        yc = y.cpu().numpy()
+        for i in (0, 1, 15, 16, 31, 32, 36):
+            assert same(yc[i], O.matvec(G.GGML_Q8_0, blk, k, n, qs[i], ds[i])), f"row {i}"
 
 
 def test_device_forms_and_quantiser(layer):

@@ -36,7 +36,7 @@ def test_noalloc_matches_batch_dev_on_two_calls_in_a_row():
         tid = L.add_blocks(G.GGML_Q8_0, k, n, blk, "noalloc")
         stream = torch.cuda.current_stream().cuda_stream
         cases = []
-        for m, seed in ((48, 1), (9, 2)):       # tiles of 64, then of 16 activations
+        for m, seed in ((48, 1), (9, 2)):       # tiles of 32, then of 16 activations
             q, d = _device_activations(torch, L, m, k, seed, dev, stream)
             ref = torch.full((m, n), float("nan"), device=dev)
             assert L.batch_dev(tid, m, q.data_ptr(), d.data_ptr(), ref.data_ptr(), stream) == 0
