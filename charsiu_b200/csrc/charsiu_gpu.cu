@@ -8,6 +8,7 @@
 // calls, and says so.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -71,6 +72,8 @@ bool grow_dev(T *&p, size_t &cap, size_t want)
 	return true;
 }
 
+// Pinned host memory, mapped into the device's address space (the direct
+// host call's kernels read and write it in place).
 template <typename T>
 bool grow_host(T *&p, size_t &cap, size_t want)
 {
@@ -80,10 +83,20 @@ bool grow_host(T *&p, size_t &cap, size_t want)
 		cudaFreeHost(p);
 	p = nullptr;
 	cap = 0;
-	if (cudaHostAlloc(&p, want * sizeof(T), cudaHostAllocDefault) != cudaSuccess)
+	if (cudaHostAlloc(&p, want * sizeof(T), cudaHostAllocMapped) != cudaSuccess)
 		return false;
 	cap = want;
 	return true;
+}
+
+// The device address of mapped host memory.
+template <typename T>
+T *dev_view(T *host)
+{
+	void *d = nullptr;
+	if (cudaHostGetDevicePointer(&d, (void *)host, 0) != cudaSuccess)
+		return nullptr;
+	return static_cast<T *>(d);
 }
 
 // One host call captured as a CUDA graph: tensors ids[0..n) at K = k.
@@ -120,6 +133,13 @@ struct charsiu_gpu {
 	// the call's event without another copy
 	volatile int *h_err = nullptr;
 	int *d_err = nullptr;
+	// direct host calls: [0] CTAs done (device), [2..3] start stamp; the flag
+	// words the last CTA raises (mapped host memory), and their sequence
+	uint32_t *d_sync = nullptr;
+	volatile uint32_t *h_flag = nullptr;
+	uint32_t *d_flag = nullptr;
+	uint32_t seq = 0;
+	bool direct = true;  // CHARSIU_GPU_DIRECT=0: every host call through a graph with copies
 	bool smem_set[24] = {};
 	// CTAs per SM for (m, nb): asked of the driver once, never during capture
 	std::vector<std::pair<uint64_t, int>> occ;
@@ -490,6 +510,112 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 	return 0;
 }
 
+// The direct host call, for one activation against tensors of one quant type
+// (every call charsiu's decode makes): the activation, already in mapped
+// host memory, is copied in by act_stage_kernel; the matvec (one launch,
+// programmatic dependent) writes every y straight into mapped host memory,
+// and its last CTA raises a sequence flag there, which the host spins on.
+// No copy-engine transfer, graph or event sits in the call.
+int run_direct(charsiu_gpu *g, const int *ids, unsigned n, unsigned k, size_t abytes, double mb,
+	       float **ys, double t0)
+{
+	uint8_t *act_dev = dev_view(g->h_act);
+	float *y_dev = dev_view(g->h_y);
+	if (!act_dev || !y_dev) {
+		whine(g, "a staging buffer has no device address");
+		return -1;
+	}
+	const uint32_t nb = k / 32;
+	float *yd[QMV_MAX_TENSORS];
+	size_t off = 0;
+	for (unsigned i = 0; i < n; i++) {
+		yd[i] = y_dev + off;
+		off += g->ent[ids[i]].rows;
+	}
+	const uint32_t seq = ++g->seq ? g->seq : ++g->seq;     // never 0, the flag's reset value
+	unsigned long long *t_start = reinterpret_cast<unsigned long long *>(g->d_sync + 2);
+	act_stage_kernel<<<1, 256, 0, g->stream>>>(reinterpret_cast<const uint4 *>(act_dev),
+						   reinterpret_cast<uint4 *>(g->d_act),
+						   (uint32_t)((abytes + 15) / 16), t_start);
+	bool ok = cudaGetLastError() == cudaSuccess;
+	if (ok)
+		g->launches++;
+	QmvParams p;
+	fill_params(g, p, ids, n, yd, k, reinterpret_cast<const int8_t *>(g->d_act),
+		    reinterpret_cast<const float *>(g->d_act + (size_t)nb * 32));
+	p.done_count = g->d_sync;
+	p.done_flag = g->d_flag;
+	p.t_start = t_start;
+	p.seq = seq;
+	ok = ok && !launch_qmv(g, 1, p, g->stream);
+	if (!ok) {
+		whine(g, "the launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+		retire(g, "a launch failed");
+		return -1;
+	}
+	const double t1 = now_us();
+
+	// the reference's budget (src/npudev.c:560-573), as finish() applies it
+	const double budget = g->slow_us + mb * 1000.0;
+	for (uint64_t spins = 1; g->h_flag[0] != seq; spins++) {
+		if (spins & 1023)
+			continue;
+		const double el = now_us() - t0;
+		if (el <= budget)
+			continue;
+		const cudaError_t e = cudaStreamQuery(g->stream);
+		if (e != cudaSuccess && e != cudaErrorNotReady) {
+			whine(g, "CUDA error %s (K=%u)", cudaGetErrorString(e), k);
+			retire(g, "a CUDA error");
+			return -1;
+		}
+		if (e == cudaSuccess && g->h_flag[0] != seq) {
+			whine(g, "a call finished without signalling (K=%u)", k);
+			retire(g, "a call finished without signalling");
+			return -1;
+		}
+		if (el > budget + 10e6) {
+			whine(g, "a call did not finish (K=%u)", k);
+			retire(g, "it stopped answering");
+			return -1;
+		}
+	}
+	std::atomic_thread_fence(std::memory_order_acquire);
+	const double t2 = now_us();
+	if (*g->h_err) {
+		*g->h_err = 0;
+		whine(g, "a kernel wait gave up (K=%u)", k);
+		retire(g, "a kernel wait gave up");
+		return -1;
+	}
+	double took = t2 - t0;
+	if (injected(g, 2))
+		took = budget + 1.0;
+	if (took > budget) {
+		if (++g->strikes >= 3) {
+			whine(g, "three slow calls in a row (K=%u)", k);
+			retire(g, "it stopped answering in time");
+			return -1;
+		}
+	} else {
+		g->strikes = 0;
+	}
+	off = 0;
+	for (unsigned i = 0; i < n; i++) {
+		const size_t cnt = g->ent[ids[i]].rows;
+		memcpy(ys[i], g->h_y + off, cnt * sizeof(float));
+		off += cnt;
+	}
+	const double t3 = now_us();
+	g->calls++;
+	g->weight_mb += mb;
+	g->h2d_us += t1 - t0;
+	g->kern_ms += g->h_flag[1] * 1e-6;
+	g->d2h_us += t3 - t2;
+	g->busy_us += t3 - t0;
+	return 0;
+}
+
 // The host-pointer matvec (charsiu_gpu_matvec / _group / _batch): the
 // activation copied in as one [q | d] block, the kernels, every y copied
 // back, one fence. From its second call on, a given single-activation call
@@ -512,6 +638,7 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	}
 	const uint32_t nb = k / 32;
 	const size_t qbytes = (size_t)m * nb * 32, abytes = qbytes + (size_t)m * nb * sizeof(float);
+	const size_t abytes16 = (abytes + 15) & ~(size_t)15;    // the copy-in moves 16-byte words
 	size_t ytot = 0;
 	double mb = 0;
 	for (unsigned i = 0; i < n; i++) {
@@ -519,7 +646,7 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 		mb += g->ent[ids[i]].weight_mb;
 	}
 	const size_t caps[4] = {g->cap_dact, g->cap_hact, g->cap_dy, g->cap_hy};
-	if (!grow_dev(g->d_act, g->cap_dact, abytes) || !grow_host(g->h_act, g->cap_hact, abytes) ||
+	if (!grow_dev(g->d_act, g->cap_dact, abytes16) || !grow_host(g->h_act, g->cap_hact, abytes16) ||
 	    !grow_dev(g->d_y, g->cap_dy, ytot) || !grow_host(g->h_y, g->cap_hy, ytot)) {
 		whine(g, "a staging buffer would not allocate");
 		return -1;
@@ -535,6 +662,13 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	const double t0 = now_us();
 	memcpy(g->h_act, q, qbytes);
 	memcpy(g->h_act + qbytes, d, (size_t)m * nb * sizeof(float));
+	if (g->direct && m == 1) {
+		bool one_type = true;
+		for (unsigned i = 1; i < n; i++)
+			one_type = one_type && g->ent[ids[i]].type == g->ent[ids[0]].type;
+		if (one_type)
+			return run_direct(g, ids, n, k, abytes, mb, ys, t0);
+	}
 
 	CallGraph *cg = nullptr;
 	if (m == 1) {
@@ -671,6 +805,8 @@ struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	g->sm_count = prop.multiProcessorCount;
 	g->slow_us = (double)env_u("CHARSIU_GPU_SLOW_US", 100000);
 	g->no_pdl = getenv("CHARSIU_GPU_NO_PDL") != nullptr;
+	if (const char *dir = getenv("CHARSIU_GPU_DIRECT"))
+		g->direct = strcmp(dir, "0") != 0;
 	if (const char *na = getenv("CHARSIU_GPU_QMM_NA"))
 		g->qmm_na = !strcmp(na, "16") ? 16 : !strcmp(na, "32") ? 32 : 0;
 	if (const char *pre = getenv("CHARSIU_GPU_QMM_PRE"))
@@ -680,13 +816,21 @@ struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	    cudaEventCreate(&g->ev_k0) != cudaSuccess || cudaEventCreate(&g->ev_k1) != cudaSuccess ||
 	    cudaEventCreateWithFlags(&g->ev_done, cudaEventDisableTiming) != cudaSuccess ||
 	    cudaHostAlloc((void **)&g->h_err, sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
-	    cudaHostGetDevicePointer((void **)&g->d_err, (void *)g->h_err, 0) != cudaSuccess) {
+	    cudaHostGetDevicePointer((void **)&g->d_err, (void *)g->h_err, 0) != cudaSuccess ||
+	    cudaHostAlloc((void **)&g->h_flag, 4 * sizeof(uint32_t), cudaHostAllocMapped) !=
+		    cudaSuccess ||
+	    cudaHostGetDevicePointer((void **)&g->d_flag, (void *)g->h_flag, 0) != cudaSuccess ||
+	    cudaMalloc((void **)&g->d_sync, 4 * sizeof(uint32_t)) != cudaSuccess ||
+	    cudaMemset(g->d_sync, 0, 4 * sizeof(uint32_t)) != cudaSuccess) {
 		charsiu_gpu_close(g);
 		return nullptr;
 	}
 	const size_t nb = max_k / 32;
 	*g->h_err = 0;
-	if (!grow_dev(g->d_act, g->cap_dact, nb * 36) || !grow_host(g->h_act, g->cap_hact, nb * 36) ||
+	for (int i = 0; i < 4; i++)
+		g->h_flag[i] = 0;
+	if (!grow_dev(g->d_act, g->cap_dact, nb * 36 + 16) ||
+	    !grow_host(g->h_act, g->cap_hact, nb * 36 + 16) ||
 	    !grow_dev(g->d_y, g->cap_dy, (size_t)max_n + 64) ||
 	    !grow_host(g->h_y, g->cap_hy, (size_t)max_n + 64)) {
 		charsiu_gpu_close(g);
@@ -719,6 +863,9 @@ void charsiu_gpu_close(struct charsiu_gpu *g)
 	cudaFree(g->d_dots);
 	if (g->h_err)
 		cudaFreeHost((void *)g->h_err);
+	if (g->h_flag)
+		cudaFreeHost((void *)g->h_flag);
+	cudaFree(g->d_sync);
 	cudaFreeHost(g->h_act);
 	cudaFreeHost(g->h_y);
 	cudaFreeHost(g->h_i8);

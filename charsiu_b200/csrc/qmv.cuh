@@ -43,6 +43,13 @@ struct QmvParams {
 	const int8_t *q;         // activation quants [M][nb * 32]
 	const float *d;          // activation deltas [M][nb]
 	int *err;                // set nonzero if a wait gave up (mapped host memory)
+	// direct host calls (M = 1): when done_flag is set, the last CTA to
+	// finish writes `seq` there (mapped host memory) once every y is visible
+	// to the host, and the kernel time since *t_start there + 1
+	uint32_t *done_count;    // device, zero between launches
+	uint32_t *done_flag;     // [0] seq, [1] kernel ns
+	const unsigned long long *t_start;
+	uint32_t seq;
 };
 
 inline size_t qmv_smem_bytes(int m, uint32_t nb)

@@ -222,6 +222,21 @@ qmv1_kernel(const __grid_constant__ QmvParams p)
 				p.t[ti].y[row] = s;
 		}
 	}
+	if (p.done_flag) {
+		// y is host memory: make this CTA's stores visible to the host, then
+		// the last CTA to get here raises the call's flag
+		__threadfence_system();
+		__syncthreads();
+		if (threadIdx.x == 0 && atomicAdd(p.done_count, 1u) == gridDim.x - 1) {
+			*p.done_count = 0;
+			const unsigned long long t1 = globaltimer_ns();
+			const unsigned long long dt = t1 - *(volatile const unsigned long long *)p.t_start;
+			__threadfence_system();
+			p.done_flag[1] = dt > 0xffffffffull ? 0xffffffffu : (uint32_t)dt;
+			__threadfence_system();
+			*(volatile uint32_t *)p.done_flag = p.seq;
+		}
+	}
 }
 
 } // namespace cgpu

@@ -83,6 +83,34 @@ def test_group_equals_singles(layer):
         assert same(y, O.matvec(qt, blk, k, n, q, d))
 
 
+def test_direct_and_graph_calls_agree(monkeypatch):
+    """A host call of one activation runs the direct path (copy-in kernel,
+    y written into mapped host memory, a flag raised by the last CTA); with
+    CHARSIU_GPU_DIRECT=0 the same call goes through a graph of copies and
+    kernels. Both must give the reference's bits, call after call."""
+    k = 2048
+    shapes = [(G.GGML_Q8_0, 2048), (G.GGML_Q8_0, 520), (G.GGML_Q8_0, 9)]
+    blks = [W.matvec_inputs(qt, k, n, seed=500 + i)[0] for i, (qt, n) in enumerate(shapes)]
+    xs = np.random.default_rng(8).normal(size=(5, k)).astype(np.float32)
+    outs = {}
+    for direct in ("1", "0"):
+        monkeypatch.setenv("CHARSIU_GPU_DIRECT", direct)
+        with Layer(max_k=k, max_n=4096, max_tensors=4) as L:
+            ids = [L.add_blocks(qt, k, n, b) for (qt, n), b in zip(shapes, blks)]
+            outs[direct] = []
+            for x in xs:
+                q, d = O.act_quantise(x)
+                outs[direct].append(L.matvec(ids, q, d, k))
+                outs[direct].append(L.matvec(ids[1:2], q, d, k))
+            assert L.calls == 2 * len(xs)
+    for j, x in enumerate(xs):
+        q, d = O.act_quantise(x)
+        for (qt, n), b, y1, y0 in zip(shapes, blks, outs["1"][2 * j], outs["0"][2 * j]):
+            ref = O.matvec(qt, b, k, n, q, d)
+            assert same(y1, ref) and same(y0, ref), f"activation {j} n={n}"
+        assert same(outs["1"][2 * j + 1][0], outs["1"][2 * j][1])
+
+
 def test_output_head_shape(layer):
     """The 2048 -> 128256 tied head, q8_0: 16032 row groups in one launch."""
     k, n = 2048, 128256
