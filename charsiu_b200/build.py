@@ -50,7 +50,8 @@ def _stale(target, deps):
 def build(verbose_ptxas: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)] + \
-        [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE)] + C_SOURCES + [__file__]
+        [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE)] + \
+        [os.path.join(HOST, f) for f in os.listdir(HOST)] + [__file__]
     if not _stale(LIB, deps) and not verbose_ptxas:
         return LIB
     objs = []

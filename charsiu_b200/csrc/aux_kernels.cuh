@@ -61,20 +61,6 @@ __global__ void block_dots_kernel(const uint8_t *__restrict__ data, uint32_t typ
 	dots[idx] = t;
 }
 
-// The direct host call's copy-in: n16 16-byte words of the activation from
-// mapped host memory to device memory, one CTA. It lets the matvec launch at
-// once (the matvec loads weights, then waits for this grid), and stamps the
-// call's start time for the kernel-time account.
-__global__ void act_stage_kernel(const uint4 *__restrict__ src, uint4 *__restrict__ dst,
-				 uint32_t n16, unsigned long long *t_start)
-{
-	pdl_launch_dependents();
-	if (threadIdx.x == 0)
-		*t_start = globaltimer_ns();
-	for (uint32_t i = threadIdx.x; i < n16; i += blockDim.x)
-		dst[i] = src[i];
-}
-
 // charsiu_act_set (reference src/gguf.c:852-881) for m rows of k: one warp
 // per 32-element block. amax is a max, so any reduction order gives the same
 // float; d = amax / 127 and 1 / d are IEEE divisions; the quant is

@@ -14,6 +14,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <ctime>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -139,8 +140,9 @@ struct charsiu_gpu {
 	volatile uint32_t *h_flag = nullptr;
 	uint32_t *d_flag = nullptr;
 	uint32_t seq = 0;
+	QmvInline<QMV_INLINE_MAX_WORDS> *inl = nullptr;    // the direct call's kernel arguments
 	bool direct = true;  // CHARSIU_GPU_DIRECT=0: every host call through a graph with copies
-	bool smem_set[24] = {};
+	bool smem_set[32] = {};
 	// CTAs per SM for (m, nb): asked of the driver once, never during capture
 	std::vector<std::pair<uint64_t, int>> occ;
 
@@ -271,13 +273,29 @@ void fill_params(charsiu_gpu *g, QmvParams &p, const int *ids, unsigned n, float
 // two segments a warp; every tensor of the launch has the same quant type);
 // M = 2, 4, 8 run qmv_kernel<M> (a warp a group). Both sum blocks in the
 // reference's order.
-int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st)
+//
+// `inl` (M = 1 only): a QmvInline<QMV_INLINE_MAX_WORDS> whose .p is p and
+// whose words hold the activation; the launch then runs qmv1_inline_kernel,
+// which reads the activation from its parameters (the first
+// QmvInline<AW> bytes of the buffer, AW by the shape).
+int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
+	       const void *inl = nullptr)
 {
 	static const void *const qmv1_fns[4][2] = {
 		{(const void *)qmv1_kernel<4, false, false>, (const void *)qmv1_kernel<4, true, false>},
 		{(const void *)qmv1_kernel<8, false, false>, (const void *)qmv1_kernel<8, true, false>},
 		{(const void *)qmv1_kernel<8, false, true>, (const void *)qmv1_kernel<8, true, true>},
 		{(const void *)qmv1_kernel<16, false, true>, (const void *)qmv1_kernel<16, true, true>},
+	};
+	static const void *const qmv1_inline_fns[4][2] = {
+		{(const void *)qmv1_inline_kernel<4, false, false, 144>,
+		 (const void *)qmv1_inline_kernel<4, true, false, 144>},
+		{(const void *)qmv1_inline_kernel<8, false, false, 576>,
+		 (const void *)qmv1_inline_kernel<8, true, false, 576>},
+		{(const void *)qmv1_inline_kernel<8, false, true, 576>,
+		 (const void *)qmv1_inline_kernel<8, true, true, 576>},
+		{(const void *)qmv1_inline_kernel<16, false, true, 1008>,
+		 (const void *)qmv1_inline_kernel<16, true, true, 1008>},
 	};
 	static const int qmv1_warps[4] = {4, 8, 8, 16};
 	const void *fn = nullptr;
@@ -290,8 +308,11 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st)
 	if (m == 1) {
 		threads = qmv1_warps[shape] * 32;
 		smem = qmv1_smem_bytes(p.nb);
-		slot = 10 + 2 * shape + (q8 ? 1 : 0);   // 10..17; M > 1 uses slots 2, 4, 8
-		fn = qmv1_fns[shape][q8 ? 1 : 0];
+		// 10..17, inline 24..31; M > 1 uses slots 2, 4, 8, the tensor cores 20..23
+		slot = (inl ? 24 : 10) + 2 * shape + (q8 ? 1 : 0);
+		fn = (inl ? qmv1_inline_fns : qmv1_fns)[shape][q8 ? 1 : 0];
+	} else if (inl) {
+		return -1;
 	} else {
 		smem = qmv_smem_bytes(m, p.nb);
 		slot = m;
@@ -334,7 +355,7 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st)
 	cfg.attrs = attr;
 	cfg.numAttrs = g->no_pdl ? 0 : 1;
 	QmvParams arg = p;
-	void *args[1] = {&arg};
+	void *args[1] = {inl ? const_cast<void *>(inl) : (void *)&arg};
 	const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
 	if (e != cudaSuccess)
 		return -1;
@@ -511,17 +532,16 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 }
 
 // The direct host call, for one activation against tensors of one quant type
-// (every call charsiu's decode makes): the activation, already in mapped
-// host memory, is copied in by act_stage_kernel; the matvec (one launch,
-// programmatic dependent) writes every y straight into mapped host memory,
-// and its last CTA raises a sequence flag there, which the host spins on.
-// No copy-engine transfer, graph or event sits in the call.
-int run_direct(charsiu_gpu *g, const int *ids, unsigned n, unsigned k, size_t abytes, double mb,
-	       float **ys, double t0)
+// (every call charsiu's decode makes): the activation travels inside the
+// launch's own parameters (qmv1_inline_kernel), the matvec writes every y
+// straight into mapped host memory, and its last CTA raises a sequence flag
+// there, which the host spins on. One launch; no copy-engine transfer, graph
+// or event sits in the call.
+int run_direct(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, const float *d,
+	       unsigned k, double mb, float **ys, double t0)
 {
-	uint8_t *act_dev = dev_view(g->h_act);
 	float *y_dev = dev_view(g->h_y);
-	if (!act_dev || !y_dev) {
+	if (!y_dev) {
 		whine(g, "a staging buffer has no device address");
 		return -1;
 	}
@@ -533,21 +553,16 @@ int run_direct(charsiu_gpu *g, const int *ids, unsigned n, unsigned k, size_t ab
 		off += g->ent[ids[i]].rows;
 	}
 	const uint32_t seq = ++g->seq ? g->seq : ++g->seq;     // never 0, the flag's reset value
-	unsigned long long *t_start = reinterpret_cast<unsigned long long *>(g->d_sync + 2);
-	act_stage_kernel<<<1, 256, 0, g->stream>>>(reinterpret_cast<const uint4 *>(act_dev),
-						   reinterpret_cast<uint4 *>(g->d_act),
-						   (uint32_t)((abytes + 15) / 16), t_start);
-	bool ok = cudaGetLastError() == cudaSuccess;
-	if (ok)
-		g->launches++;
-	QmvParams p;
-	fill_params(g, p, ids, n, yd, k, reinterpret_cast<const int8_t *>(g->d_act),
-		    reinterpret_cast<const float *>(g->d_act + (size_t)nb * 32));
-	p.done_count = g->d_sync;
-	p.done_flag = g->d_flag;
-	p.t_start = t_start;
-	p.seq = seq;
-	ok = ok && !launch_qmv(g, 1, p, g->stream);
+	QmvInline<QMV_INLINE_MAX_WORDS> &a = *g->inl;
+	fill_params(g, a.p, ids, n, yd, k, nullptr, nullptr);
+	a.p.done_count = g->d_sync;
+	a.p.done_flag = g->d_flag;
+	a.p.t_start = reinterpret_cast<unsigned long long *>(g->d_sync + 2);
+	a.p.seq = seq;
+	uint8_t *words = reinterpret_cast<uint8_t *>(a.act);
+	memcpy(words, q, (size_t)nb * 32);
+	memcpy(words + (size_t)nb * 32, d, (size_t)nb * sizeof(float));
+	bool ok = !launch_qmv(g, 1, a.p, g->stream, &a);
 	if (!ok) {
 		whine(g, "the launch failed: %s", cudaGetErrorString(cudaGetLastError()));
 		retire(g, "a launch failed");
@@ -660,15 +675,15 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	}
 
 	const double t0 = now_us();
-	memcpy(g->h_act, q, qbytes);
-	memcpy(g->h_act + qbytes, d, (size_t)m * nb * sizeof(float));
-	if (g->direct && m == 1) {
+	if (g->direct && m == 1 && (size_t)nb * 36 <= sizeof(g->inl->act)) {
 		bool one_type = true;
 		for (unsigned i = 1; i < n; i++)
 			one_type = one_type && g->ent[ids[i]].type == g->ent[ids[0]].type;
 		if (one_type)
-			return run_direct(g, ids, n, k, abytes, mb, ys, t0);
+			return run_direct(g, ids, n, q, d, k, mb, ys, t0);
 	}
+	memcpy(g->h_act, q, qbytes);
+	memcpy(g->h_act + qbytes, d, (size_t)m * nb * sizeof(float));
 
 	CallGraph *cg = nullptr;
 	if (m == 1) {
@@ -829,6 +844,11 @@ struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	*g->h_err = 0;
 	for (int i = 0; i < 4; i++)
 		g->h_flag[i] = 0;
+	g->inl = new (std::nothrow) QmvInline<QMV_INLINE_MAX_WORDS>();
+	if (!g->inl) {
+		charsiu_gpu_close(g);
+		return nullptr;
+	}
 	if (!grow_dev(g->d_act, g->cap_dact, nb * 36 + 16) ||
 	    !grow_host(g->h_act, g->cap_hact, nb * 36 + 16) ||
 	    !grow_dev(g->d_y, g->cap_dy, (size_t)max_n + 64) ||
@@ -865,6 +885,7 @@ void charsiu_gpu_close(struct charsiu_gpu *g)
 		cudaFreeHost((void *)g->h_err);
 	if (g->h_flag)
 		cudaFreeHost((void *)g->h_flag);
+	delete g->inl;
 	cudaFree(g->d_sync);
 	cudaFreeHost(g->h_act);
 	cudaFreeHost(g->h_y);

@@ -102,6 +102,15 @@ __device__ __forceinline__ void pdl_launch_dependents()
 	asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// atomic add at device scope with acquire-release ordering; returns the old value
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *addr, uint32_t v)
+{
+	uint32_t old;
+	asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;"
+		     : "=r"(old) : "l"(addr), "r"(v) : "memory");
+	return old;
+}
+
 // sum of four (unsigned byte of a) * (signed byte of b), plus c
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)
 {

@@ -48,7 +48,7 @@ struct QmvParams {
 	// to the host, and the kernel time since *t_start there + 1
 	uint32_t *done_count;    // device, zero between launches
 	uint32_t *done_flag;     // [0] seq, [1] kernel ns
-	const unsigned long long *t_start;
+	unsigned long long *t_start;
 	uint32_t seq;
 };
 

@@ -30,11 +30,25 @@
 
 namespace cgpu {
 
+// (+16: the inline form copies the activation in whole 16-byte words)
 inline size_t qmv1_smem_bytes(uint32_t nb)
 {
 	return (size_t)2 * nb * RG * sizeof(float) +
-	       (size_t)nb * (32 + sizeof(float) + sizeof(int32_t));
+	       (size_t)nb * (32 + sizeof(float) + sizeof(int32_t)) + 16;
 }
+
+// The activation carried in the launch's own parameters (the direct host
+// call): the [q | d] block of nb * 36 bytes, in 16-byte words. The launch
+// brings it to the GPU with the kernel's arguments, so the call needs no copy
+// and no copy-in kernel. AW words: 144 (K <= 2048), 576 (K <= 8192), 1008
+// (K <= 14336); parameter space holds up to 32764 bytes.
+template <int AW>
+struct QmvInline {
+	QmvParams p;
+	uint4 act[AW];
+};
+constexpr int QMV_INLINE_MAX_WORDS = 1008;
+static_assert(sizeof(QmvInline<QMV_INLINE_MAX_WORDS>) <= 32764, "kernel parameter space");
 
 __device__ __forceinline__ uint4 ldg_stream(const uint8_t *p)
 {
@@ -131,9 +145,8 @@ __device__ __forceinline__ void named_barrier(int id, int threads)
 // handles segment warp of each group and, when TWO, also warp + W (so
 // nseg <= W, or nseg <= 2W with TWO); both are loaded before either is
 // computed.
-template <int W, bool Q8, bool TWO>
-__global__ void __launch_bounds__(W * 32)
-qmv1_kernel(const __grid_constant__ QmvParams p)
+template <int W, bool Q8, bool TWO, int AW>
+__device__ __forceinline__ void qmv1_body(const QmvParams &p, const uint4 *inl)
 {
 	extern __shared__ __align__(128) uint8_t smem[];
 	const uint32_t nb = p.nb;
@@ -172,8 +185,17 @@ qmv1_kernel(const __grid_constant__ QmvParams p)
 	if (G < p.total_groups)
 		load(G);
 
+	if (AW) {
+		// [q | d] from parameter space to the same contiguous [aq | ad]
+		if (p.done_flag && blockIdx.x == 0 && threadIdx.x == 0)
+			*p.t_start = globaltimer_ns();
+		uint4 *sa = reinterpret_cast<uint4 *>(aq);
+		const uint32_t n16 = (nb * 36 + 15) / 16;
+		for (uint32_t i = threadIdx.x; i < n16; i += blockDim.x)
+			sa[i] = inl[i];
+	}
 	pdl_wait();
-	{
+	if (!AW) {
 		const uint4 *gq = reinterpret_cast<const uint4 *>(p.q);
 		uint4 *sq = reinterpret_cast<uint4 *>(aq);
 		for (uint32_t i = threadIdx.x; i < nb * 2; i += blockDim.x)
@@ -223,11 +245,13 @@ qmv1_kernel(const __grid_constant__ QmvParams p)
 		}
 	}
 	if (p.done_flag) {
-		// y is host memory: make this CTA's stores visible to the host, then
-		// the last CTA to get here raises the call's flag
-		__threadfence_system();
+		// y is host memory. The barrier brings this CTA's stores to thread 0,
+		// whose acq_rel count releases them at device scope; the last CTA's
+		// count acquires every CTA's, and its system fence orders all of them
+		// before the flag the host spins on. (A system fence in every thread
+		// costs several microseconds a call; this costs one.)
 		__syncthreads();
-		if (threadIdx.x == 0 && atomicAdd(p.done_count, 1u) == gridDim.x - 1) {
+		if (threadIdx.x == 0 && atom_add_acq_rel_gpu(p.done_count, 1u) == gridDim.x - 1) {
 			*p.done_count = 0;
 			const unsigned long long t1 = globaltimer_ns();
 			const unsigned long long dt = t1 - *(volatile const unsigned long long *)p.t_start;
@@ -237,6 +261,20 @@ qmv1_kernel(const __grid_constant__ QmvParams p)
 			*(volatile uint32_t *)p.done_flag = p.seq;
 		}
 	}
+}
+
+template <int W, bool Q8, bool TWO>
+__global__ void __launch_bounds__(W * 32)
+qmv1_kernel(const __grid_constant__ QmvParams p)
+{
+	qmv1_body<W, Q8, TWO, 0>(p, nullptr);
+}
+
+template <int W, bool Q8, bool TWO, int AW>
+__global__ void __launch_bounds__(W * 32)
+qmv1_inline_kernel(const __grid_constant__ QmvInline<AW> a)
+{
+	qmv1_body<W, Q8, TWO, AW>(a.p, a.act);
 }
 
 } // namespace cgpu

@@ -22,6 +22,7 @@
 #include <unistd.h>
 
 #include "charsiu_gpu_llama.h"
+#include "pool.h"
 
 #define API
 
@@ -346,6 +347,7 @@ struct charsiu_gpu_llama {
 	float *rope_cs;           /* cos, sin of each pair at the current pos */
 	int8_t *aq;
 	float *ad;
+	struct pool *pool;        /* attention heads and SiLU chunks; NULL = this thread */
 };
 
 static float half_to_float(uint16_t h)
@@ -563,6 +565,7 @@ API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m)
 			fprintf(stderr, "  %-16s %8.3f ms a token   %5.1f%%\n", stage_name[i],
 				m->stage_ms[i] / m->stage_tok, 100.0 * m->stage_ms[i] / tot);
 	}
+	pool_free(m->pool);
 	if (m->dev && getenv("CHARSIU_GPU_REPORT"))
 		charsiu_gpu_report(m->dev);
 	charsiu_gpu_close(m->dev);
@@ -688,6 +691,14 @@ API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *path, int n_ctx
 	if (!m->rope_cs || !m->kcache || !m->vcache || !m->x || !m->xb || !m->xb2 || !m->hb || !m->hb2 ||
 	    !m->q || !m->k || !m->v || !m->att || !m->logits || !m->aq || !m->ad)
 		goto fail;
+	{
+		/* CHARSIU_GPU_THREADS helpers for the CPU steps (0: none) */
+		const char *e = getenv("CHARSIU_GPU_THREADS");
+		long cpus = sysconf(_SC_NPROCESSORS_ONLN);
+		int threads = e ? atoi(e) : (int)(cpus > 2 ? (cpus - 1 < 8 ? cpus - 1 : 8) : 0);
+
+		m->pool = pool_new(threads);
+	}
 	return m;
 fail:
 	charsiu_gpu_llama_close(m);
@@ -702,9 +713,88 @@ static double now_ms(void)
 	return (double)t.tv_sec * 1e3 + (double)t.tv_nsec / 1e6;
 }
 
+/* One attention head of layer l at pos (src/llama.c:792-817): the scores,
+ * softmax and weighted sum of this head only, so the heads can run on any
+ * threads in any order with the same results. */
+struct attn_job {
+	struct charsiu_gpu_llama *m;
+	uint32_t l;
+	int pos;
+	float scale;
+};
+
+static void attn_head(void *arg, int item)
+{
+	const struct attn_job *j = arg;
+	struct charsiu_gpu_llama *m = j->m;
+	uint32_t h = (uint32_t)item, l = j->l, hd = m->hd;
+	uint32_t kvdim = m->n_head_kv * hd, gqa = m->n_head / m->n_head_kv;
+	int pos = j->pos;
+	float scale = j->scale;
+	const float *qh = m->q + h * hd;
+	float *att = m->att + (size_t)h * m->n_ctx;
+	uint32_t kvh = h / gqa;
+	float *out = m->xb + h * hd;
+
+	/* four positions at a time: four independent chains, each summed over
+	 * i in order, as src/llama.c:798-806 sums one */
+	int t = 0;
+
+	for (; t + 3 <= pos; t += 4) {
+		const float *k0 = m->kcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
+		const float *k1 = k0 + kvdim, *k2 = k1 + kvdim, *k3 = k2 + kvdim;
+		float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+
+		for (uint32_t i = 0; i < hd; i++) {
+			a0 += qh[i] * k0[i];
+			a1 += qh[i] * k1[i];
+			a2 += qh[i] * k2[i];
+			a3 += qh[i] * k3[i];
+		}
+		att[t] = a0 * scale;
+		att[t + 1] = a1 * scale;
+		att[t + 2] = a2 * scale;
+		att[t + 3] = a3 * scale;
+	}
+	for (; t <= pos; t++) {
+		const float *kt = m->kcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
+		float a = 0.0f;
+
+		for (uint32_t i = 0; i < hd; i++)
+			a += qh[i] * kt[i];
+		att[t] = a * scale;
+	}
+	softmax(att, pos + 1);
+	memset(out, 0, hd * sizeof(float));
+	for (t = 0; t <= pos; t++) {
+		const float *vt = m->vcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
+		float a = att[t];
+
+		for (uint32_t i = 0; i < hd; i++)
+			out[i] += a * vt[i];
+	}
+}
+
+/* SiLU(gate) * up over one chunk of the FFN (src/llama.c:831-836) */
+#define SILU_CHUNK 512
+
+static void silu_chunk(void *arg, int item)
+{
+	struct charsiu_gpu_llama *m = arg;
+	uint32_t i0 = (uint32_t)item * SILU_CHUNK;
+	uint32_t i1 = i0 + SILU_CHUNK < m->n_ff ? i0 + SILU_CHUNK : m->n_ff;
+
+	for (uint32_t i = i0; i < i1; i++) {
+		float g = m->hb[i];
+
+		g *= 1.0f / (1.0f + expf(-g));
+		m->hb[i] = g * m->hb2[i];
+	}
+}
+
 API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t token, int pos)
 {
-	uint32_t hd = m->hd, kvdim = m->n_head_kv * hd, gqa = m->n_head / m->n_head_kv;
+	uint32_t hd = m->hd, kvdim = m->n_head_kv * hd;
 	float scale = 1.0f / sqrtf((float)hd);
 	double t0 = now_ms(), t1;
 
@@ -738,49 +828,10 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 		memcpy(vc, m->v, kvdim * sizeof(float));
 		STAGE(ST_ROPE);
 
-		for (uint32_t h = 0; h < m->n_head; h++) {
-			const float *qh = m->q + h * hd;
-			float *att = m->att + (size_t)h * m->n_ctx;
-			uint32_t kvh = h / gqa;
-			float *out = m->xb + h * hd;
+		{
+			struct attn_job job = { m, l, pos, scale };
 
-			/* four positions at a time: four independent chains, each
-			 * summed over i in order, as src/llama.c:798-806 sums one */
-			int t = 0;
-
-			for (; t + 3 <= pos; t += 4) {
-				const float *k0 = m->kcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
-				const float *k1 = k0 + kvdim, *k2 = k1 + kvdim, *k3 = k2 + kvdim;
-				float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-
-				for (uint32_t i = 0; i < hd; i++) {
-					a0 += qh[i] * k0[i];
-					a1 += qh[i] * k1[i];
-					a2 += qh[i] * k2[i];
-					a3 += qh[i] * k3[i];
-				}
-				att[t] = a0 * scale;
-				att[t + 1] = a1 * scale;
-				att[t + 2] = a2 * scale;
-				att[t + 3] = a3 * scale;
-			}
-			for (; t <= pos; t++) {
-				const float *kt = m->kcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
-				float a = 0.0f;
-
-				for (uint32_t i = 0; i < hd; i++)
-					a += qh[i] * kt[i];
-				att[t] = a * scale;
-			}
-			softmax(att, pos + 1);
-			memset(out, 0, hd * sizeof(float));
-			for (int t = 0; t <= pos; t++) {
-				const float *vt = m->vcache + ((size_t)l * m->n_ctx + t) * kvdim + kvh * hd;
-				float a = att[t];
-
-				for (uint32_t i = 0; i < hd; i++)
-					out[i] += a * vt[i];
-			}
+			pool_run(m->pool, attn_head, &job, (int)m->n_head);
 		}
 		STAGE(ST_ATTN);
 		{
@@ -805,12 +856,7 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 				return NULL;
 		}
 		STAGE(ST_GATEUP);
-		for (uint32_t i = 0; i < m->n_ff; i++) {
-			float g = m->hb[i];
-
-			g *= 1.0f / (1.0f + expf(-g));
-			m->hb[i] = g * m->hb2[i];
-		}
+		pool_run(m->pool, silu_chunk, m, (int)((m->n_ff + SILU_CHUNK - 1) / SILU_CHUNK));
 		STAGE(ST_SILU);
 		{
 			int id = L->id[P_DOWN];

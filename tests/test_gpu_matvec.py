@@ -91,7 +91,7 @@ def test_direct_and_graph_calls_agree(monkeypatch):
     k = 2048
     shapes = [(G.GGML_Q8_0, 2048), (G.GGML_Q8_0, 520), (G.GGML_Q8_0, 9)]
     blks = [W.matvec_inputs(qt, k, n, seed=500 + i)[0] for i, (qt, n) in enumerate(shapes)]
-    xs = np.random.default_rng(8).normal(size=(5, k)).astype(np.float32)
+    xs = np.random.default_rng(8).normal(size=(24, k)).astype(np.float32)
     outs = {}
     for direct in ("1", "0"):
         monkeypatch.setenv("CHARSIU_GPU_DIRECT", direct)
