@@ -382,14 +382,17 @@ def cpu_baseline(path):
 # ---- one matvec on its own -------------------------------------------------------
 
 def run_matvec_case(args):
-    """--matvec q8_0:2048:8192: one block-quant matvec shape (M = 1), enough
-    copies of the weights rotated that every launch streams from HBM (their
-    total is at least twice the 126 MB L2), launches replayed as a CUDA graph."""
+    """--matvec q8_0:2048:8192[:M]: one block-quant matvec shape (M = 1 unless
+    given; M > 1 is the batched matvec of M activations), enough copies of the
+    weights rotated that every launch streams from HBM (their total is at
+    least twice the 126 MB L2), launches replayed as a CUDA graph."""
     import torch
     from charsiu_b200.lib import Layer
 
-    qname, k, n = args.matvec.split(":")
+    parts = args.matvec.split(":")
+    qname, k, n = parts[:3]
     k, n = int(k), int(n)
+    m = int(parts[3]) if len(parts) > 3 else 1
     qtype = {"q8_0": G.GGML_Q8_0, "q4_0": G.GGML_Q4_0}[qname]
     blk, _ = W.matvec_inputs(qtype, k, n, seed=1)
     wbytes = blk.nbytes
@@ -398,17 +401,22 @@ def run_matvec_case(args):
     torch.cuda.set_device(dev)
     with Layer(max_k=k, max_n=n, max_tensors=copies) as L:
         ids = [L.add_blocks(qtype, k, n, blk, f"copy{i}") for i in range(copies)]
-        x = torch.randn(k, generator=torch.Generator().manual_seed(7)).to(dev)
-        q = torch.empty(k, dtype=torch.int8, device=dev)
-        d = torch.empty(k // 32, dtype=torch.float32, device=dev)
-        y = torch.empty(n, dtype=torch.float32, device=dev)
+        x = torch.randn(m, k, generator=torch.Generator().manual_seed(7)).to(dev)
+        q = torch.empty((m, k), dtype=torch.int8, device=dev)
+        d = torch.empty((m, k // 32), dtype=torch.float32, device=dev)
+        y = torch.empty((m, n), dtype=torch.float32, device=dev)
         stream = torch.cuda.Stream(device=dev)
-        assert L.act_quantise_dev(x.data_ptr(), 1, k, q.data_ptr(), d.data_ptr(),
+        assert L.act_quantise_dev(x.data_ptr(), m, k, q.data_ptr(), d.data_ptr(),
                                   stream.cuda_stream) == 0
 
         def launch(i):
-            assert L.matvec_dev([ids[i % copies]], q.data_ptr(), d.data_ptr(), [y.data_ptr()],
-                                stream.cuda_stream) == 0
+            if m == 1:
+                rc = L.matvec_dev([ids[i % copies]], q.data_ptr(), d.data_ptr(), [y.data_ptr()],
+                                  stream.cuda_stream)
+            else:
+                rc = L.batch_dev(ids[i % copies], m, q.data_ptr(), d.data_ptr(), y.data_ptr(),
+                                 stream.cuda_stream)
+            assert rc == 0, L.error()
         for i in range(args.warmup):
             launch(i)
         torch.cuda.synchronize()
@@ -428,20 +436,20 @@ def run_matvec_case(args):
         clk = clocks.stop()
         us = e0.elapsed_time(e1) * 1e3 / args.steps
         del graph
-    algo = wbytes + k + 4 * (k // 32) + 4 * n
+    algo = wbytes + m * (k + 4 * (k // 32)) + 4 * m * n
     peak, peak_kind = peaks()
     gbs = algo / (us * 1e-6) / 1e9
     return {"metric": "quant matvec HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(us / 1e3, 6), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": f"{qname} matvec M=1 K={k} N={n}", "weight_copies": copies,
+            "config": {"workload": f"{qname} matvec M={m} K={k} N={n}", "weight_copies": copies,
                        "l2": f"{copies} weight copies rotated ({copies * wbytes / 1e6:.0f} MB "
                              "> 2x L2)"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
                          "bytes_per_launch": algo, "avg_launch_us": round(us, 3)},
-            "gpu_launches": args.steps, "clocks": clk}
+            "gpu_launches": args.steps * (1 if m == 1 else 2), "clocks": clk}
 
 
 # ---- the batched decode step ------------------------------------------------------
@@ -570,8 +578,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=0, metavar="M",
                     help="time one batched decode step of M sequences instead")
-    ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N",
-                    help="time one matvec shape instead of the decode (e.g. q8_0:2048:8192)")
+    ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N[:M]",
+                    help="time one matvec shape instead of the decode (e.g. q8_0:2048:8192; "
+                         "q8_0:2048:8192:64 for 64 activations)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

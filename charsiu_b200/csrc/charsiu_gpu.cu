@@ -419,6 +419,7 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	p.atiles = mt;
 	p.nb = nb;
 	p.m = m;
+	p.one = 1.0f;
 	p.err = g->d_err;
 	if (!tiles)
 		return 0;

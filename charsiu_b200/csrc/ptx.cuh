@@ -153,6 +153,23 @@ __device__ __forceinline__ float2 add2_rn(float2 a, float2 b)
 	return r;
 }
 
+// a * b + c per lane, rounded once (fma.rn.f32x2). With b = 1.0 held in a
+// register the assembler cannot see into (a kernel parameter), this is the
+// packed add of a product computed before it, without the contraction above.
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c)
+{
+	float2 r;
+	asm("{\n\t.reg .b64 x, y, z, w;\n\t"
+	    "mov.b64 x, {%2, %3};\n\t"
+	    "mov.b64 y, {%4, %5};\n\t"
+	    "mov.b64 z, {%6, %7};\n\t"
+	    "fma.rn.f32x2 w, x, y, z;\n\t"
+	    "mov.b64 {%0, %1}, w;\n\t}"
+	    : "=f"(r.x), "=f"(r.y)
+	    : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+	return r;
+}
+
 // fp16 bits -> fp32, exact for every finite value (subnormals included)
 __device__ __forceinline__ float half_bits_to_float(uint16_t h)
 {

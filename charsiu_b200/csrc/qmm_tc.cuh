@@ -21,12 +21,12 @@
 // segment (16 blocks) a stage -- the tile's 16 groups' weight segments as
 // they lie in the device layout (layout.h), already MMA core matrices, and
 // the packed activation tile (qmm_pack_kernel) -- into a double-buffered
-// stage; warp 1 owns tensor memory and lane 0 issues the MMAs; EW = 4 * NA/16
-// epilogue warps (a tensor-memory lane quarter and 16 activations each) read
-// the int32 tiles with tcgen05.ld and accumulate. The conversion, the scale
-// d_w * d_a and the product use the packed fp32x2 operations (two columns an
-// instruction, each lane rounded as the scalar operation rounds); the sum is
-// scalar.
+// stage; warp 1 owns tensor memory and lane 0 issues the MMAs; EW = 4 * NA/8
+// epilogue warps (a tensor-memory lane quarter and 8 activations each) read
+// the int32 tiles with tcgen05.ld and accumulate: per chunk, the four blocks'
+// products first (independent, so they overlap), then the four in-order sums.
+// Every step uses the packed fp32x2 operations (two columns an instruction,
+// each lane rounded as the scalar operation rounds).
 //
 // PRE: the tensor memory of every block slot holds 0x4b400000 before its MMA,
 // which then accumulates onto it, so the int32 comes out as the bits of the
@@ -59,9 +59,11 @@ __host__ inline size_t qmm_smem_bytes(uint32_t na)
 	return 2 * ((size_t)QMM_WSTAGE + qmm_act_seg_bytes(na)) + 16 * sizeof(uint64_t) + 16;
 }
 
+constexpr int QMM_EPI_COLS = 8;            // activations (columns) an epilogue warp owns
+
 __host__ __device__ constexpr int qmm_threads(int na)
 {
-	return (2 + 4 * (na / 16)) * 32;
+	return (2 + 4 * (na / QMM_EPI_COLS)) * 32;
 }
 
 // tensor-memory columns: two chunk buffers of QMM_CHUNK blocks of NA columns
@@ -113,6 +115,7 @@ struct QmmParams {
 	QmmTensor t[QMM_MAX_TENSORS];
 	const uint8_t *act;        // qmm_pack_kernel output
 	uint32_t ntensor, tiles, atiles, nb, m;
+	float one;                 // 1.0 (see the epilogue's sum)
 	int *err;
 };
 
@@ -120,7 +123,8 @@ template <int NA, bool PRE>
 __global__ void __launch_bounds__(qmm_threads(NA), 1)
 qmm_tc_kernel(const __grid_constant__ QmmParams p)
 {
-	constexpr int EW = 4 * (NA / 16);                  // epilogue warps
+	constexpr int CW = QMM_EPI_COLS;                   // activations an epilogue warp
+	constexpr int EW = 4 * (NA / CW);                  // epilogue warps
 	constexpr uint32_t ASEG = qmm_act_seg_bytes(NA);
 	constexpr uint32_t NCOLS = qmm_tmem_cols(NA);
 	extern __shared__ __align__(128) uint8_t smem[];
@@ -253,7 +257,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 				*(volatile int *)p.err = 11;
 		}
 	} else {
-		// ---- epilogue: TMEM lane quarter q, activations e*16 .. e*16+15 -------
+		// ---- epilogue: TMEM lane quarter q, activations e*CW .. e*CW+CW-1 ----
 		const int ew = warp - 2, q = warp % 4, e = ew / 4;
 		const uint32_t r = q * 32 + lane;                  // row of the tile
 		const uint32_t grp = r / RG, rr = r % RG;
@@ -261,7 +265,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 		bool ok = true;
 		if (PRE) {
 			for (uint32_t c = 0; c < NCOLS; c += NA)
-				tmem_fill16(taddr + lane_base + c + e * 16, INT_FLOAT_MAGIC);
+				tmem_fill8(taddr + lane_base + c + e * CW, INT_FLOAT_MAGIC);
 			tmem_wait_st();
 			tc_fence_before();
 			__syncwarp();
@@ -273,13 +277,14 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 		pdl_wait();                  // y may still be read by the kernel before
 		pdl_launch_dependents();
 		const float2 neg_bias = make_float2(-INT_FLOAT_BIAS, -INT_FLOAT_BIAS);
+		const float2 one2 = make_float2(p.one, p.one);
 		uint32_t s_cnt = 0, c_cnt = 0;
 		for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
 			uint32_t ti, tile;
 			locate(u, ti, tile);
-			float2 acc[8];
+			float2 acc[CW / 2];
 #pragma unroll
-			for (int c = 0; c < 8; c++)
+			for (int c = 0; c < CW / 2; c++)
 				acc[c] = make_float2(0.0f, 0.0f);
 			for (uint32_t s = 0; s < nseg && ok; s++, s_cnt++) {
 				const uint32_t st = s_cnt & 1, sb = seg_blocks(nb, s);
@@ -292,7 +297,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 				const uint16_t *dl = reinterpret_cast<const uint16_t *>(
 					stage_w(st) + grp * MAX_SEG_BYTES + sb * RG * 32);
 				const float *da = reinterpret_cast<const float *>(stage_a(st) + SB * 2 * NA * 16) +
-						  e * 16;
+						  e * CW;
 				for (uint32_t b0 = 0; b0 < sb; b0 += QMM_CHUNK, c_cnt++) {
 					const uint32_t buf = c_cnt & 1, nblk = min((uint32_t)QMM_CHUNK, sb - b0);
 					if (!mbar_wait_bounded(&mma_done[buf], (c_cnt >> 1) & 1, WAIT_LIMIT_NS)) {
@@ -302,37 +307,34 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 						break;
 					}
 					tc_fence_after();
-					uint32_t t[QMM_CHUNK][16];
-					const uint32_t col0 = taddr + lane_base + buf * QMM_CHUNK * NA + e * 16;
+					uint32_t t[QMM_CHUNK][CW];
+					const uint32_t col0 = taddr + lane_base + buf * QMM_CHUNK * NA + e * CW;
 #pragma unroll
 					for (int j = 0; j < QMM_CHUNK; j++)
 						if (j < (int)nblk)
-							tmem_ld16(col0 + j * NA, t[j]);
+							tmem_ld8(col0 + j * NA, t[j]);
 					tmem_wait_ld();
 					if (PRE) {
 #pragma unroll
 						for (int j = 0; j < QMM_CHUNK; j++)
 							if (j < (int)nblk)
-								tmem_fill16(col0 + j * NA, INT_FLOAT_MAGIC);
+								tmem_fill8(col0 + j * NA, INT_FLOAT_MAGIC);
 						tmem_wait_st();
 					}
 					tc_fence_before();
 					__syncwarp();
 					if (lane == 0)
 						mbar_arrive(&tfree[buf]);
-#pragma unroll
-					for (int j = 0; j < QMM_CHUNK; j++) {
-						if (j >= (int)nblk)
-							break;
+
+					// block j's products (d_w * d_a) * t, CW columns in pairs
+					auto products = [&](int j, float2 (&pr)[CW / 2]) {
 						const uint32_t bi = b0 + j;
 						const float dw = half_bits_to_float(dl[bi * RG + rr]);
 						const float2 dw2 = make_float2(dw, dw);
 						const float4 *da4 = reinterpret_cast<const float4 *>(da + bi * NA);
 #pragma unroll
-						for (int c4 = 0; c4 < 4; c4++) {
+						for (int c4 = 0; c4 < CW / 4; c4++) {
 							const float4 a4 = da4[c4];
-							const float2 sc0 = mul2_rn(dw2, make_float2(a4.x, a4.y));
-							const float2 sc1 = mul2_rn(dw2, make_float2(a4.z, a4.w));
 							const uint32_t *tt = &t[j][4 * c4];
 							float2 f0, f1;
 							if (PRE) {
@@ -346,15 +348,31 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 							}
 							f0 = add2_rn(f0, neg_bias);
 							f1 = add2_rn(f1, neg_bias);
-							// the sum stays scalar: a packed product feeding a
-							// packed add is contracted into a fused multiply-add
-							// by the assembler (explicit .rn notwithstanding),
-							// which rounds once where the reference rounds twice
-							const float2 p0 = mul2_rn(sc0, f0), p1 = mul2_rn(sc1, f1);
-							acc[2 * c4].x = __fadd_rn(acc[2 * c4].x, p0.x);
-							acc[2 * c4].y = __fadd_rn(acc[2 * c4].y, p0.y);
-							acc[2 * c4 + 1].x = __fadd_rn(acc[2 * c4 + 1].x, p1.x);
-							acc[2 * c4 + 1].y = __fadd_rn(acc[2 * c4 + 1].y, p1.y);
+							pr[2 * c4] = mul2_rn(mul2_rn(dw2, make_float2(a4.x, a4.y)), f0);
+							pr[2 * c4 + 1] = mul2_rn(mul2_rn(dw2, make_float2(a4.z, a4.w)), f1);
+						}
+					};
+					// s = s + product, block by block: fma(product, 1, s) with the
+					// 1 from the kernel's parameters is the rounded add (a packed
+					// add fed by the packed product would be contracted into one
+					// rounding, unlike the reference's two)
+					if (nblk == QMM_CHUNK) {
+						float2 pr[QMM_CHUNK][CW / 2];
+#pragma unroll
+						for (int j = 0; j < QMM_CHUNK; j++)
+							products(j, pr[j]);
+#pragma unroll
+						for (int j = 0; j < QMM_CHUNK; j++)
+#pragma unroll
+							for (int c = 0; c < CW / 2; c++)
+								acc[c] = fma2_rn(pr[j][c], one2, acc[c]);
+					} else {
+						for (int j = 0; j < (int)nblk; j++) {
+							float2 pr[CW / 2];
+							products(j, pr);
+#pragma unroll
+							for (int c = 0; c < CW / 2; c++)
+								acc[c] = fma2_rn(pr[c], one2, acc[c]);
 						}
 					}
 				}
@@ -366,10 +384,10 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 				break;
 			const QmmTensor &T = p.t[ti];
 			const uint32_t row = tile * QMM_TILE_GROUPS * RG + r;
-			const uint32_t a0 = (u % p.atiles) * NA + e * 16;
+			const uint32_t a0 = (u % p.atiles) * NA + e * CW;
 			if (row < T.rows) {
 #pragma unroll
-				for (int c = 0; c < 16; c++) {
+				for (int c = 0; c < CW; c++) {
 					const uint32_t a = a0 + c;
 					if (a < p.m)
 						T.y[(uint64_t)a * T.rows + row] = c & 1 ? acc[c / 2].y : acc[c / 2].x;
