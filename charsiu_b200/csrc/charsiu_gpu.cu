@@ -24,6 +24,7 @@
 #include "i8mm_tc.cuh"
 #include "qmv.cuh"
 #include "qmv1.cuh"
+#include "qmvm.cuh"
 #include "qmm_tc.cuh"
 #include "ref_abi.h"
 
@@ -142,7 +143,7 @@ struct charsiu_gpu {
 	uint32_t seq = 0;
 	QmvInline<QMV_INLINE_MAX_WORDS> *inl = nullptr;    // the direct call's kernel arguments
 	bool direct = true;  // CHARSIU_GPU_DIRECT=0: every host call through a graph with copies
-	bool smem_set[32] = {};
+	bool smem_set[56] = {};
 	// CTAs per SM for (m, nb): asked of the driver once, never during capture
 	std::vector<std::pair<uint64_t, int>> occ;
 
@@ -153,6 +154,11 @@ struct charsiu_gpu {
 	int no_pdl = 0;     // CHARSIU_GPU_NO_PDL: launch without programmatic dependence (control)
 	uint32_t qmm_na = 0;   // CHARSIU_GPU_QMM_NA: activations a tensor-core tile (16, 32; 0 = by m)
 	bool qmm_pre = false;  // CHARSIU_GPU_QMM_PRE=1: the MMA adds the float-bias constant (slower)
+	// CHARSIU_GPU_QMM_MIN_M: q8_0 batches of fewer activations run on the CUDA
+	// cores (qmvm_kernel). Measured crossover on the 1B decode step: the CUDA
+	// cores win at 2, 4 and 8 activations (0.46 / 0.62 / 1.01 ms against
+	// 1.27 / 1.28 / 1.28), the tensor cores from 16 (1.29 against 1.96 ms).
+	uint32_t qmm_min_m = 9;
 	unsigned long inj_at = 0, inj_count = 0;
 	int inj_kind = 0;
 	std::string err;
@@ -271,7 +277,7 @@ void fill_params(charsiu_gpu *g, QmvParams &p, const int *ids, unsigned n, float
 
 // M = 1 runs qmv1_kernel<W, Q8, TWO> (W warps share one 8-row group, one or
 // two segments a warp; every tensor of the launch has the same quant type);
-// M = 2, 4, 8 run qmv_kernel<M> (a warp a group). Both sum blocks in the
+// M = 2, 4, 8 run qmvm_kernel<W, Q8, TWO, M> (the same shapes). Both sum blocks in the
 // reference's order.
 //
 // `inl` (M = 1 only): a QmvInline<QMV_INLINE_MAX_WORDS> whose .p is p and
@@ -300,7 +306,7 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
 	static const int qmv1_warps[4] = {4, 8, 8, 16};
 	const void *fn = nullptr;
 	size_t smem = 0;
-	int threads = QMV_WARPS * 32, slot = 0;
+	int threads = 0, slot = 0;
 	const bool q8 = p.t[0].type == TYPE_Q8_0;
 	const uint32_t nseg = nsegments(p.nb);
 	const int shape = nseg <= 4 ? 0 : nseg <= 8 ? 1 : nseg <= 16 ? 2 : 3;
@@ -314,18 +320,29 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
 	} else if (inl) {
 		return -1;
 	} else {
-		smem = qmv_smem_bytes(m, p.nb);
-		slot = m;
-		switch (m) {
-		case 2: fn = (const void *)qmv_kernel<2>; break;
-		case 4: fn = (const void *)qmv_kernel<4>; break;
-		case 8: fn = (const void *)qmv_kernel<8>; break;
-		default: return -1;
-		}
+		// M = 2, 4, 8: qmvm_kernel, the same shapes as M = 1
+#define QMVM_ROW(W, TWO, M) \
+	{(const void *)qmvm_kernel<W, false, TWO, M>, (const void *)qmvm_kernel<W, true, TWO, M>}
+		static const void *const qmvm_fns[4][3][2] = {
+			{QMVM_ROW(4, false, 2), QMVM_ROW(4, false, 4), QMVM_ROW(4, false, 8)},
+			{QMVM_ROW(8, false, 2), QMVM_ROW(8, false, 4), QMVM_ROW(8, false, 8)},
+			{QMVM_ROW(8, true, 2), QMVM_ROW(8, true, 4), QMVM_ROW(8, true, 8)},
+			{QMVM_ROW(16, true, 2), QMVM_ROW(16, true, 4), QMVM_ROW(16, true, 8)},
+		};
+#undef QMVM_ROW
+		const int mi = m == 2 ? 0 : m == 4 ? 1 : m == 8 ? 2 : -1;
+		if (mi < 0)
+			return -1;
+		threads = qmv1_warps[shape] * 32;
+		smem = qmvm_smem_bytes(m, p.nb);
+		if (smem > QMV_SMEM_MAX)
+			return -1;
+		slot = 32 + (2 * shape + (q8 ? 1 : 0)) * 3 + mi;    // 32..55
+		fn = qmvm_fns[shape][mi][q8 ? 1 : 0];
 	}
 	if (!g->smem_set[slot]) {
 		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-					 227 * 1024) != cudaSuccess)
+					 (int)QMV_SMEM_MAX) != cudaSuccess)
 			return -1;
 		g->smem_set[slot] = true;
 	}
@@ -451,6 +468,16 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	return 0;
 }
 
+// Activations a CUDA-core launch takes: 8, 4 or 2 while that many are left
+// and their term buffers fit shared memory, else 1.
+unsigned qmvm_chunk(unsigned left, uint32_t nb)
+{
+	for (unsigned c : {8u, 4u, 2u})
+		if (left >= c && qmvm_smem_bytes((int)c, nb) <= QMV_SMEM_MAX)
+			return c;
+	return 1;
+}
+
 // One launch per quant type present among ids (the M = 1 kernel takes one
 // type a launch; a decode's groups are always a single type).
 int launch_matvec1(charsiu_gpu *g, const int *ids, unsigned n, float *const *ys, uint32_t k,
@@ -492,13 +519,14 @@ int check_ids(charsiu_gpu *g, const int *ids, unsigned n, unsigned k)
 }
 
 // Queue the kernels of one host call: one launch per chunk of at most
-// QMV_MAX_M activation rows (the M = 1 path one launch per quant type).
+// QMV_MAX_M activation rows (qmvm_chunk; the M = 1 path one launch per quant
+// type), unless the batch goes to the tensor cores.
 int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k, unsigned m)
 {
 	const uint32_t nb = k / 32;
 	const int8_t *dq = reinterpret_cast<const int8_t *>(g->d_act);
 	const float *dd = reinterpret_cast<const float *>(g->d_act + (size_t)m * nb * 32);
-	if (m > 1) {
+	if (m >= g->qmm_min_m) {
 		// q8_0 on the tensor cores; q4_0 on the CUDA cores below
 		bool all_q8 = true;
 		for (unsigned i = 0; i < n; i++)
@@ -514,8 +542,7 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 		}
 	}
 	for (unsigned m0 = 0, mc = 0; m0 < m; m0 += mc) {
-		const unsigned left = m - m0;
-		mc = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+		mc = qmvm_chunk(m - m0, nb);
 		float *yd[QMV_MAX_TENSORS];
 		size_t off = 0;
 		for (unsigned i = 0; i < n; i++) {
@@ -825,6 +852,8 @@ struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned
 		g->direct = strcmp(dir, "0") != 0;
 	if (const char *na = getenv("CHARSIU_GPU_QMM_NA"))
 		g->qmm_na = !strcmp(na, "16") ? 16 : !strcmp(na, "32") ? 32 : 0;
+	if (const char *mm = getenv("CHARSIU_GPU_QMM_MIN_M"))
+		g->qmm_min_m = atoi(mm) > 2 ? (uint32_t)atoi(mm) : 2;
 	if (const char *pre = getenv("CHARSIU_GPU_QMM_PRE"))
 		g->qmm_pre = !strcmp(pre, "1");
 	g->ent.reserve(max_tensors);
@@ -1082,14 +1111,13 @@ int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m, cons
 	const Ent &e = g->ent[id];
 	const uint32_t nb = e.nb;
 	cudaStream_t st = stream ? (cudaStream_t)stream : g->stream;
-	if (m > 1 && e.type == TYPE_Q8_0) {
+	if (m >= g->qmm_min_m && e.type == TYPE_Q8_0) {
 		if (!grow_dev(g->d_pack, g->cap_pack, qmm_pack_bytes(qmm_na(g, m), m, nb)))
 			return -1;
 		return launch_qmm(g, &id, 1, q, d, m, &y, g->d_pack, st);
 	}
 	for (unsigned m0 = 0; m0 < m;) {
-		const unsigned left = m - m0;
-		const unsigned mc = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+		const unsigned mc = qmvm_chunk(m - m0, nb);
 		float *yd[1] = {y + (size_t)m0 * e.rows};
 		QmvParams p;
 		fill_params(g, p, &id, 1, yd, (uint32_t)e.k, q + (size_t)m0 * nb * 32,
@@ -1114,7 +1142,7 @@ int charsiu_gpu_matvec_batch_group_dev(struct charsiu_gpu *g, const int *ids, un
 		    g->ent[ids[i]].k != g->ent[ids[0]].k)
 			return -1;
 	cudaSetDevice(g->device);
-	bool all_q8 = m > 1;
+	bool all_q8 = m >= g->qmm_min_m;
 	for (unsigned i = 0; i < n; i++)
 		all_q8 = all_q8 && g->ent[ids[i]].type == TYPE_Q8_0;
 	if (all_q8) {

@@ -124,50 +124,55 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c)
 	return __dp4a(static_cast<int>(a), static_cast<int>(b), c);
 }
 
-// Packed fp32 pairs (sm_100): each lane rounds to nearest as mul.rn.f32 /
-// add.rn.f32 do. Unlike the scalar forms, a mul.rn.f32x2 whose result feeds
-// an add.rn.f32x2 is contracted by the assembler into one fused
-// multiply-add (seen on sm_100a with CUDA 12.9), so code that needs the
-// product rounded before the sum must not pair these two.
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b)
+// Packed fp32 pairs (sm_100), held as one 64-bit register (low word = first
+// lane), so no packing moves sit between consecutive operations. Each lane
+// rounds to nearest as mul.rn.f32 / add.rn.f32 / fma.rn.f32 do.
+//
+// Unlike the scalar forms, a mul.rn.f32x2 whose result feeds an
+// add.rn.f32x2 is contracted by the assembler into one fused multiply-add
+// (seen on sm_100a with CUDA 12.9: 1-ulp differences), so code that needs
+// the product rounded before the sum uses fma2_rn(product, 1.0, s) with the
+// 1.0 in a register the assembler cannot see into (a kernel parameter):
+// that rounds once, after the exact product-times-one, which is the add.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi)
 {
-	float2 r;
-	asm("{\n\t.reg .b64 x, y, z;\n\t"
-	    "mov.b64 x, {%2, %3};\n\t"
-	    "mov.b64 y, {%4, %5};\n\t"
-	    "mul.rn.f32x2 z, x, y;\n\t"
-	    "mov.b64 {%0, %1}, z;\n\t}"
-	    : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-	return r;
+	return (uint64_t)__float_as_uint(hi) << 32 | __float_as_uint(lo);
 }
 
-__device__ __forceinline__ float2 add2_rn(float2 a, float2 b)
+__device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi)
 {
-	float2 r;
-	asm("{\n\t.reg .b64 x, y, z;\n\t"
-	    "mov.b64 x, {%2, %3};\n\t"
-	    "mov.b64 y, {%4, %5};\n\t"
-	    "add.rn.f32x2 z, x, y;\n\t"
-	    "mov.b64 {%0, %1}, z;\n\t}"
-	    : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-	return r;
+	return (uint64_t)hi << 32 | lo;
 }
 
-// a * b + c per lane, rounded once (fma.rn.f32x2). With b = 1.0 held in a
-// register the assembler cannot see into (a kernel parameter), this is the
-// packed add of a product computed before it, without the contraction above.
-__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c)
+__device__ __forceinline__ float lo2(uint64_t v)
 {
-	float2 r;
-	asm("{\n\t.reg .b64 x, y, z, w;\n\t"
-	    "mov.b64 x, {%2, %3};\n\t"
-	    "mov.b64 y, {%4, %5};\n\t"
-	    "mov.b64 z, {%6, %7};\n\t"
-	    "fma.rn.f32x2 w, x, y, z;\n\t"
-	    "mov.b64 {%0, %1}, w;\n\t}"
-	    : "=f"(r.x), "=f"(r.y)
-	    : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-	return r;
+	return __uint_as_float((uint32_t)v);
+}
+
+__device__ __forceinline__ float hi2(uint64_t v)
+{
+	return __uint_as_float((uint32_t)(v >> 32));
+}
+
+__device__ __forceinline__ uint64_t mul2_rn(uint64_t a, uint64_t b)
+{
+	uint64_t d;
+	asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+	return d;
+}
+
+__device__ __forceinline__ uint64_t add2_rn(uint64_t a, uint64_t b)
+{
+	uint64_t d;
+	asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+	return d;
+}
+
+__device__ __forceinline__ uint64_t fma2_rn(uint64_t a, uint64_t b, uint64_t c)
+{
+	uint64_t d;
+	asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+	return d;
 }
 
 // fp16 bits -> fp32, exact for every finite value (subnormals included)

@@ -123,25 +123,6 @@ struct QmmParams {
 	int *err;
 };
 
-// The epilogue's arithmetic on column pairs, packed fp32x2 (each lane rounds
-// as the scalar operation does; about 10% faster here than one scalar
-// operation a lane, measured).
-__device__ __forceinline__ float2 epi_mul(float2 a, float2 b)
-{
-	return mul2_rn(a, b);
-}
-
-__device__ __forceinline__ float2 epi_add(float2 a, float2 b)
-{
-	return add2_rn(a, b);
-}
-
-// s + product, the product already rounded (see the epilogue)
-__device__ __forceinline__ float2 epi_acc(float2 s, float2 prod, float2 one)
-{
-	return fma2_rn(prod, one, s);
-}
-
 template <int NA, bool PRE>
 __global__ void __launch_bounds__(qmm_threads(NA), 1)
 qmm_tc_kernel(const __grid_constant__ QmmParams p)
@@ -303,16 +284,16 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 		}
 		pdl_wait();                  // y may still be read by the kernel before
 		pdl_launch_dependents();
-		const float2 neg_bias = make_float2(-INT_FLOAT_BIAS, -INT_FLOAT_BIAS);
-		const float2 one2 = make_float2(p.one, p.one);
+		const uint64_t neg_bias = pack2(-INT_FLOAT_BIAS, -INT_FLOAT_BIAS);
+		const uint64_t one2 = pack2(p.one, p.one);
 		uint32_t s_cnt = 0, c_cnt = 0;
 		for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
 			uint32_t ti, tile;
 			locate(u, ti, tile);
-			float2 acc[CW / 2];
+			uint64_t acc[CW / 2];           // column pairs, packed
 #pragma unroll
 			for (int c = 0; c < CW / 2; c++)
-				acc[c] = make_float2(0.0f, 0.0f);
+				acc[c] = 0;                 // +0.0f, +0.0f
 			for (uint32_t s = 0; s < nseg && ok; s++, s_cnt++) {
 				const uint32_t st = s_cnt & 1, sb = seg_blocks(nb, s);
 				if (!mbar_wait_bounded(&full[st], (s_cnt >> 1) & 1, WAIT_LIMIT_NS)) {
@@ -335,13 +316,15 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 						break;
 					}
 					tc_fence_after();
-					uint32_t t[QMM_CHUNK][CW];
+					// the chunk's tiles as packed float bits 1.5 * 2^23 + t
+					static_assert(CW == 8 && QMM_CHUNK == 4, "tmem_ld_chunk4 shape");
+					uint64_t tp[QMM_CHUNK][CW / 2];
 					const uint32_t col0 = taddr + lane_base + buf * QMM_CHUNK * NA + e * CW;
-#pragma unroll
-					for (int j = 0; j < QMM_CHUNK; j++)
-						if (j < (int)nblk)
-							tmem_ld8(col0 + j * NA, t[j]);
-					tmem_wait_ld();
+					if (nblk == QMM_CHUNK)
+						tmem_ld_chunk4<!PRE>(col0, NA, tp);
+					else
+						for (int j = 0; j < (int)nblk; j++)
+							tmem_ld_block<!PRE>(col0 + j * NA, tp[j]);
 					if (PRE) {
 #pragma unroll
 						for (int j = 0; j < QMM_CHUNK; j++)
@@ -355,29 +338,18 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 						mbar_arrive(&tfree[buf]);
 
 					// block j's products (d_w * d_a) * t, CW columns in pairs
-					auto products = [&](int j, float2 (&pr)[CW / 2]) {
+					auto products = [&](int j, uint64_t (&pr)[CW / 2]) {
 						const uint32_t bi = b0 + j;
 						const float dw = half_bits_to_float(dl[bi * RG + rr]);
-						const float2 dw2 = make_float2(dw, dw);
-						const float4 *da4 = reinterpret_cast<const float4 *>(da + bi * NA);
+						const uint64_t dw2 = pack2(dw, dw);
+						const ulonglong2 *da2 = reinterpret_cast<const ulonglong2 *>(da + bi * NA);
 #pragma unroll
 						for (int c4 = 0; c4 < CW / 4; c4++) {
-							const float4 a4 = da4[c4];
-							const uint32_t *tt = &t[j][4 * c4];
-							float2 f0, f1;
-							if (PRE) {
-								f0 = make_float2(__uint_as_float(tt[0]), __uint_as_float(tt[1]));
-								f1 = make_float2(__uint_as_float(tt[2]), __uint_as_float(tt[3]));
-							} else {
-								f0 = make_float2(__uint_as_float(INT_FLOAT_MAGIC + tt[0]),
-										 __uint_as_float(INT_FLOAT_MAGIC + tt[1]));
-								f1 = make_float2(__uint_as_float(INT_FLOAT_MAGIC + tt[2]),
-										 __uint_as_float(INT_FLOAT_MAGIC + tt[3]));
-							}
-							f0 = epi_add(f0, neg_bias);
-							f1 = epi_add(f1, neg_bias);
-							pr[2 * c4] = epi_mul(epi_mul(dw2, make_float2(a4.x, a4.y)), f0);
-							pr[2 * c4 + 1] = epi_mul(epi_mul(dw2, make_float2(a4.z, a4.w)), f1);
+							const ulonglong2 a = da2[c4];
+							const uint64_t f0 = add2_rn(tp[j][2 * c4], neg_bias);
+							const uint64_t f1 = add2_rn(tp[j][2 * c4 + 1], neg_bias);
+							pr[2 * c4] = mul2_rn(mul2_rn(dw2, a.x), f0);
+							pr[2 * c4 + 1] = mul2_rn(mul2_rn(dw2, a.y), f1);
 						}
 					};
 					// s = s + product, block by block: fma(product, 1, s) with the
@@ -385,7 +357,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 					// add fed by the packed product would be contracted into one
 					// rounding, unlike the reference's two)
 					if (nblk == QMM_CHUNK) {
-						float2 pr[QMM_CHUNK][CW / 2];
+						uint64_t pr[QMM_CHUNK][CW / 2];
 #pragma unroll
 						for (int j = 0; j < QMM_CHUNK; j++)
 							products(j, pr[j]);
@@ -393,14 +365,14 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 						for (int j = 0; j < QMM_CHUNK; j++)
 #pragma unroll
 							for (int c = 0; c < CW / 2; c++)
-								acc[c] = epi_acc(acc[c], pr[j][c], one2);
+								acc[c] = fma2_rn(pr[j][c], one2, acc[c]);
 					} else {
 						for (int j = 0; j < (int)nblk; j++) {
-							float2 pr[CW / 2];
+							uint64_t pr[CW / 2];
 							products(j, pr);
 #pragma unroll
 							for (int c = 0; c < CW / 2; c++)
-								acc[c] = epi_acc(acc[c], pr[c], one2);
+								acc[c] = fma2_rn(pr[c], one2, acc[c]);
 						}
 					}
 				}
@@ -418,7 +390,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 				for (int c = 0; c < CW; c++) {
 					const uint32_t a = a0 + c;
 					if (a < p.m)
-						T.y[(uint64_t)a * T.rows + row] = c & 1 ? acc[c / 2].y : acc[c / 2].x;
+						T.y[(uint64_t)a * T.rows + row] = c & 1 ? hi2(acc[c / 2]) : lo2(acc[c / 2]);
 				}
 			}
 		}

@@ -118,6 +118,141 @@ __device__ __forceinline__ void tmem_wait_ld()
 	asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Four blocks' tiles of one chunk (block j at taddr + j * stride; 32 lanes x
+// 8 columns each) loaded, waited for, and packed in column pairs in one asm
+// statement, so the loaded registers feed packed fp32x2 operations directly.
+// MAGIC: each int32 t becomes the bits of the float 1.5 * 2^23 + t
+// (|t| < 2^22; see small_int_to_float); otherwise the words are kept as they
+// are (tensor memory already holds 1.5 * 2^23 + t).
+template <bool MAGIC>
+__device__ __forceinline__ void tmem_ld_chunk4(uint32_t taddr, uint32_t stride, uint64_t (&p)[4][4])
+{
+	if (MAGIC)
+		asm volatile("{\n\t.reg .b32 r<32>;\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r0, r1, r2, r3, r4, r5, r6, r7}, [%16];\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r8, r9, r10, r11, r12, r13, r14, r15}, [%17];\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r16, r17, r18, r19, r20, r21, r22, r23}, [%18];\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r24, r25, r26, r27, r28, r29, r30, r31}, [%19];\n\t"
+			     "tcgen05.wait::ld.sync.aligned;\n\t"
+			     "add.u32 r0, r0, 0x4b400000;\n\t"
+			     "add.u32 r1, r1, 0x4b400000;\n\t"
+			     "add.u32 r2, r2, 0x4b400000;\n\t"
+			     "add.u32 r3, r3, 0x4b400000;\n\t"
+			     "add.u32 r4, r4, 0x4b400000;\n\t"
+			     "add.u32 r5, r5, 0x4b400000;\n\t"
+			     "add.u32 r6, r6, 0x4b400000;\n\t"
+			     "add.u32 r7, r7, 0x4b400000;\n\t"
+			     "add.u32 r8, r8, 0x4b400000;\n\t"
+			     "add.u32 r9, r9, 0x4b400000;\n\t"
+			     "add.u32 r10, r10, 0x4b400000;\n\t"
+			     "add.u32 r11, r11, 0x4b400000;\n\t"
+			     "add.u32 r12, r12, 0x4b400000;\n\t"
+			     "add.u32 r13, r13, 0x4b400000;\n\t"
+			     "add.u32 r14, r14, 0x4b400000;\n\t"
+			     "add.u32 r15, r15, 0x4b400000;\n\t"
+			     "add.u32 r16, r16, 0x4b400000;\n\t"
+			     "add.u32 r17, r17, 0x4b400000;\n\t"
+			     "add.u32 r18, r18, 0x4b400000;\n\t"
+			     "add.u32 r19, r19, 0x4b400000;\n\t"
+			     "add.u32 r20, r20, 0x4b400000;\n\t"
+			     "add.u32 r21, r21, 0x4b400000;\n\t"
+			     "add.u32 r22, r22, 0x4b400000;\n\t"
+			     "add.u32 r23, r23, 0x4b400000;\n\t"
+			     "add.u32 r24, r24, 0x4b400000;\n\t"
+			     "add.u32 r25, r25, 0x4b400000;\n\t"
+			     "add.u32 r26, r26, 0x4b400000;\n\t"
+			     "add.u32 r27, r27, 0x4b400000;\n\t"
+			     "add.u32 r28, r28, 0x4b400000;\n\t"
+			     "add.u32 r29, r29, 0x4b400000;\n\t"
+			     "add.u32 r30, r30, 0x4b400000;\n\t"
+			     "add.u32 r31, r31, 0x4b400000;\n\t"
+			     "mov.b64 %0, {r0, r1};\n\t"
+			     "mov.b64 %1, {r2, r3};\n\t"
+			     "mov.b64 %2, {r4, r5};\n\t"
+			     "mov.b64 %3, {r6, r7};\n\t"
+			     "mov.b64 %4, {r8, r9};\n\t"
+			     "mov.b64 %5, {r10, r11};\n\t"
+			     "mov.b64 %6, {r12, r13};\n\t"
+			     "mov.b64 %7, {r14, r15};\n\t"
+			     "mov.b64 %8, {r16, r17};\n\t"
+			     "mov.b64 %9, {r18, r19};\n\t"
+			     "mov.b64 %10, {r20, r21};\n\t"
+			     "mov.b64 %11, {r22, r23};\n\t"
+			     "mov.b64 %12, {r24, r25};\n\t"
+			     "mov.b64 %13, {r26, r27};\n\t"
+			     "mov.b64 %14, {r28, r29};\n\t"
+			     "mov.b64 %15, {r30, r31};\n\t"
+			     "}"
+			     : "=l"(p[0][0]), "=l"(p[0][1]), "=l"(p[0][2]), "=l"(p[0][3]), "=l"(p[1][0]), "=l"(p[1][1]), "=l"(p[1][2]), "=l"(p[1][3]), "=l"(p[2][0]), "=l"(p[2][1]), "=l"(p[2][2]), "=l"(p[2][3]), "=l"(p[3][0]), "=l"(p[3][1]), "=l"(p[3][2]), "=l"(p[3][3])
+			     : "r"(taddr), "r"(taddr + stride), "r"(taddr + 2 * stride), "r"(taddr + 3 * stride)
+			     : "memory");
+	else
+		asm volatile("{\n\t.reg .b32 r<32>;\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r0, r1, r2, r3, r4, r5, r6, r7}, [%16];\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r8, r9, r10, r11, r12, r13, r14, r15}, [%17];\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r16, r17, r18, r19, r20, r21, r22, r23}, [%18];\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r24, r25, r26, r27, r28, r29, r30, r31}, [%19];\n\t"
+			     "tcgen05.wait::ld.sync.aligned;\n\t"
+			     "mov.b64 %0, {r0, r1};\n\t"
+			     "mov.b64 %1, {r2, r3};\n\t"
+			     "mov.b64 %2, {r4, r5};\n\t"
+			     "mov.b64 %3, {r6, r7};\n\t"
+			     "mov.b64 %4, {r8, r9};\n\t"
+			     "mov.b64 %5, {r10, r11};\n\t"
+			     "mov.b64 %6, {r12, r13};\n\t"
+			     "mov.b64 %7, {r14, r15};\n\t"
+			     "mov.b64 %8, {r16, r17};\n\t"
+			     "mov.b64 %9, {r18, r19};\n\t"
+			     "mov.b64 %10, {r20, r21};\n\t"
+			     "mov.b64 %11, {r22, r23};\n\t"
+			     "mov.b64 %12, {r24, r25};\n\t"
+			     "mov.b64 %13, {r26, r27};\n\t"
+			     "mov.b64 %14, {r28, r29};\n\t"
+			     "mov.b64 %15, {r30, r31};\n\t"
+			     "}"
+			     : "=l"(p[0][0]), "=l"(p[0][1]), "=l"(p[0][2]), "=l"(p[0][3]), "=l"(p[1][0]), "=l"(p[1][1]), "=l"(p[1][2]), "=l"(p[1][3]), "=l"(p[2][0]), "=l"(p[2][1]), "=l"(p[2][2]), "=l"(p[2][3]), "=l"(p[3][0]), "=l"(p[3][1]), "=l"(p[3][2]), "=l"(p[3][3])
+			     : "r"(taddr), "r"(taddr + stride), "r"(taddr + 2 * stride), "r"(taddr + 3 * stride)
+			     : "memory");
+}
+
+// The same for one block, for a chunk's ragged tail.
+template <bool MAGIC>
+__device__ __forceinline__ void tmem_ld_block(uint32_t taddr, uint64_t (&p)[4])
+{
+	if (MAGIC)
+		asm volatile("{\n\t.reg .b32 r<8>;\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r0, r1, r2, r3, r4, r5, r6, r7}, [%4];\n\t"
+			     "tcgen05.wait::ld.sync.aligned;\n\t"
+			     "add.u32 r0, r0, 0x4b400000;\n\t"
+			     "add.u32 r1, r1, 0x4b400000;\n\t"
+			     "add.u32 r2, r2, 0x4b400000;\n\t"
+			     "add.u32 r3, r3, 0x4b400000;\n\t"
+			     "add.u32 r4, r4, 0x4b400000;\n\t"
+			     "add.u32 r5, r5, 0x4b400000;\n\t"
+			     "add.u32 r6, r6, 0x4b400000;\n\t"
+			     "add.u32 r7, r7, 0x4b400000;\n\t"
+			     "mov.b64 %0, {r0, r1};\n\t"
+			     "mov.b64 %1, {r2, r3};\n\t"
+			     "mov.b64 %2, {r4, r5};\n\t"
+			     "mov.b64 %3, {r6, r7};\n\t"
+			     "}"
+			     : "=l"(p[0]), "=l"(p[1]), "=l"(p[2]), "=l"(p[3])
+			     : "r"(taddr)
+			     : "memory");
+	else
+		asm volatile("{\n\t.reg .b32 r<8>;\n\t"
+			     "tcgen05.ld.sync.aligned.32x32b.x8.b32 {r0, r1, r2, r3, r4, r5, r6, r7}, [%4];\n\t"
+			     "tcgen05.wait::ld.sync.aligned;\n\t"
+			     "mov.b64 %0, {r0, r1};\n\t"
+			     "mov.b64 %1, {r2, r3};\n\t"
+			     "mov.b64 %2, {r4, r5};\n\t"
+			     "mov.b64 %3, {r6, r7};\n\t"
+			     "}"
+			     : "=l"(p[0]), "=l"(p[1]), "=l"(p[2]), "=l"(p[3])
+			     : "r"(taddr)
+			     : "memory");
+}
+
 // The same 32 lanes x 16 columns, every word set to `v`.
 __device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t v)
 {

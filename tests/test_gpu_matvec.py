@@ -121,18 +121,34 @@ def test_output_head_shape(layer):
     assert same(y, O.matvec(G.GGML_Q8_0, blk, k, n, q, d))
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 13, 32, 64, 100])
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 9, 13, 32, 64, 100])
 @pytest.mark.parametrize("qt", [G.GGML_Q8_0, G.GGML_Q4_0])
 @pytest.mark.parametrize("k,n", [(2048, 520), (8192, 136)])
 def test_batch_rows_match_single_matvec(layer, m, qt, k, n):
-    """M > 1: q8_0 runs on the tensor cores (tcgen05 kind::i8, tiles of 16
-    or 32 activations), q4_0 on the CUDA cores; every row bit-exact."""
+    """M > 1: q8_0 batches of 9 or more run on the tensor cores (tcgen05
+    kind::i8, tiles of 16 or 32 activations), smaller ones and every q4_0
+    batch on the CUDA cores (qmvm_kernel); every row bit-exact."""
     blk, xs = W.batch_inputs(qt, k, n, m, seed=3)
     tid = layer.add_blocks(qt, k, n, blk)
     qs, ds = zip(*(O.act_quantise(x) for x in xs))
     y = layer.batch(tid, np.stack(qs), np.stack(ds))
     for i in range(m):
         assert same(y[i], O.matvec(qt, blk, k, n, qs[i], ds[i])), f"row {i}"
+
+
+@pytest.mark.parametrize("m", [2, 3, 5, 8, 13])
+@pytest.mark.parametrize("k,n", [(2048, 520), (8192, 136), (544, 40)])
+def test_batch_on_cuda_cores_q8(monkeypatch, m, k, n):
+    """q8_0 batches below CHARSIU_GPU_QMM_MIN_M run on the CUDA cores
+    (qmvm_kernel, chunks of 8/4/2/1 activations): every row bit-exact."""
+    monkeypatch.setenv("CHARSIU_GPU_QMM_MIN_M", "65")
+    blk, xs = W.batch_inputs(G.GGML_Q8_0, k, n, m, seed=11)
+    with Layer(max_k=k, max_n=n, max_tensors=2) as L:
+        tid = L.add_blocks(G.GGML_Q8_0, k, n, blk)
+        qs, ds = zip(*(O.act_quantise(x) for x in xs))
+        y = L.batch(tid, np.stack(qs), np.stack(ds))
+    for i in range(m):
+        assert same(y[i], O.matvec(G.GGML_Q8_0, blk, k, n, qs[i], ds[i])), f"row {i}"
 
 
 def _dev_acts(torch, xs, dev):
@@ -147,9 +163,9 @@ def _dev_acts(torch, xs, dev):
 @pytest.mark.parametrize("k", [2048, 2080, 544])
 def test_batch_group_dev_one_launch(layer, m, k):
     """Several q8_0 tensors of one K in one tensor-core launch (as q/k/v and
-    gate/up are grouped), ragged N (a partial last 128-row tile, a partial
-    last group) and K with a partial last segment and chunk; every row of
-    every tensor bit-exact."""
+    gate/up are grouped; m = 2 takes the CUDA cores, one launch a tensor),
+    ragged N (a partial last 128-row tile, a partial last group) and K with a
+    partial last segment and chunk; every row of every tensor bit-exact."""
     torch = pytest.importorskip("torch")
     dev = torch.device("cuda:0")
     ns = [520, 136, 9, 2048]
@@ -181,6 +197,7 @@ def test_batch_tile_variants_agree(monkeypatch, na, pre):
     torch = pytest.importorskip("torch")
     monkeypatch.setenv("CHARSIU_GPU_QMM_NA", na)
     monkeypatch.setenv("CHARSIU_GPU_QMM_PRE", pre)
+    monkeypatch.setenv("CHARSIU_GPU_QMM_MIN_M", "2")
     dev = torch.device("cuda:0")
     k, n, m = 2048, 20000, 37
     with Layer(max_k=k, max_n=n, max_tensors=2) as L:
