@@ -452,6 +452,53 @@ def run_matvec_case(args):
             "gpu_launches": args.steps * (1 if m == 1 else 2), "clocks": clk}
 
 
+# ---- the int8 matmul with the NPU output stage --------------------------------------
+
+def run_int8_case(args):
+    """--int8 M:K:N: the signed-int8 matmul with charsiu's output stage
+    (cpu_reference, tools/charsiu_matmul.c:41-81) through the public C ABI
+    (charsiu_gpu_matmul_i8_flat, host buffers in and out), K calls timed on
+    the host clock; the reference's cpu_reference on the same operands on this
+    box's host, one thread, for the baseline. Every call's output is the same
+    bytes as the reference's (checked once here; the tests check it fully)."""
+    from charsiu_b200.lib import Layer
+    from oracle import oracle as O
+
+    m, k, n = (int(v) for v in args.int8.split(":"))
+    a, w, bias = W.i8_inputs(m, k, n, 0)
+    sc = W.i8_scales(m, k, n, 0)
+    with Layer(max_k=max(k, 32), max_n=n, max_tensors=1) as L:
+        out = L.matmul_i8(a, w, bias, *sc)
+        for _ in range(args.warmup):
+            L.matmul_i8(a, w, bias, *sc)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            L.matmul_i8(a, w, bias, *sc)
+        dt = (time.perf_counter() - t0) / args.steps
+        launches = L.launches
+    ref = O.ref_matmul_i8(a, w, bias, *sc) if O.have_ref() else O.matmul_i8(a, w, bias, *sc)
+    if not np.array_equal(out, ref):
+        raise RuntimeError("int8 matmul differs from the reference")
+    reps = max(1, int(0.5 / max(1e-6, m * n * k * 2e-9)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        (O.ref_matmul_i8 if O.have_ref() else O.matmul_i8)(a, w, bias, *sc)
+    cpu = (time.perf_counter() - t0) / reps
+    algo = m * k + n * k + 4 * n + m * n
+    return {"metric": "int8 matmul + output stage, us a call", "value": round(dt * 1e6, 2),
+            "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 5), "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"int8 matmul M={m} K={k} N={n}, zero points 128, "
+                                   "NPU output stage", "bytes_per_call": algo,
+                       "path": "charsiu_gpu_matmul_i8_flat (host buffers, copies inside)"},
+            "byte_exact_vs_reference": True,
+            "gpu_launches": launches,
+            "cpu_baseline": {"value": round(cpu * 1e6, 2), "unit": "us", "cores": 1,
+                             "kind": "reference" if O.have_ref() else "port",
+                             "sample": f"{reps} calls of cpu_reference on the same operands"}}
+
+
 # ---- the batched decode step ------------------------------------------------------
 
 def run_batch_case(args):
@@ -578,6 +625,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=0, metavar="M",
                     help="time one batched decode step of M sequences instead")
+    ap.add_argument("--int8", default=None, metavar="M:K:N",
+                    help="time the int8 matmul with the NPU output stage (e.g. 224:64:64)")
     ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N[:M]",
                     help="time one matvec shape instead of the decode (e.g. q8_0:2048:8192; "
                          "q8_0:2048:8192:64 for 64 activations)")
@@ -603,6 +652,9 @@ def main():
             return
         if args.batch:
             print(json.dumps(run_batch_case(args)), flush=True)
+            return
+        if args.int8:
+            print(json.dumps(run_int8_case(args)), flush=True)
             return
         if args.impl == "reference":
             out = run_reference(args, rank, world, dist)
