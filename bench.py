@@ -138,9 +138,12 @@ class TokenChain:
 
     world == 1: the whole model here. world > 1 (column split): this rank holds
     its slab of every tensor, and each launch group's slabs (one contiguous
-    buffer a group) are all-gathered with one NCCL collective."""
+    buffer a group) are all-gathered with one NCCL collective -- or, fused,
+    every launch stores its rows straight into every rank's full outputs over
+    NVLink and the next launch waits on the arrivals
+    (charsiu_gpu_matvec_gather_dev)."""
 
-    def __init__(self, gg, dev, rank=0, world=1, dist=None):
+    def __init__(self, gg, dev, rank=0, world=1, dist=None, fused=False):
         import torch
         from charsiu_b200.lib import Layer
 
@@ -178,8 +181,41 @@ class TokenChain:
                              if world > 1 else None)
         self.bytes_per_token = sum(algorithmic_bytes(gg, g, k, lambda nm: self.rows[nm])
                                    for g, k in self.groups)
+        self.fused = fused and world > 1
+        if self.fused:
+            L = self.layer
+            # this rank's full outputs (every tensor of every launch) and its sync
+            # words, shared with every rank by IPC handle
+            self.mine = [[L.ipc_alloc(4 * gg.tensors[nm].n) for nm in g] for g, _ in self.groups]
+            self.mine_sync = L.ipc_alloc(4 * (len(self.groups) + 8))
+            own = [[L.ipc_handle(p) for p in row] for row in self.mine] + \
+                [[L.ipc_handle(self.mine_sync)]]
+            allh = [None] * world
+            dist.all_gather_object(allh, own)
+            self.peer = {}
+            for r in range(world):
+                if r != rank:
+                    self.peer[r] = [[L.ipc_open(h) for h in row] for row in allh[r]]
+            view = lambda r: (self.mine + [[self.mine_sync]]) if r == rank else self.peer[r]
+            self.syncs = [view(r)[-1][0] for r in range(world)]
+            self.flat = [[view(r)[j][i] for r in range(world) for i in range(len(g))]
+                         for j, (g, _) in enumerate(self.groups)]
+            self.gsum = [sum((gg.tensors[nm].n + 7) // 8 for nm in g) for g, _ in self.groups]
+            dist.barrier()
 
     def token(self, stream):
+        if self.fused:
+            L, last = self.layer, len(self.groups) - 1
+            assert L.gather_epoch_dev(self.mine_sync, stream.cuda_stream) == 0
+            for j, (g, k) in enumerate(self.groups):
+                q, d = self.acts[k]
+                prev = j - 1 if j else last           # launch 0 waits for the last token's head
+                rc = L.matvec_gather_dev([self.ids[nm] for nm in g], q.data_ptr(), d.data_ptr(),
+                                         self.flat[j], self.syncs, signal_idx=1 + j,
+                                         wait_idx=1 + prev, wait_mult=self.gsum[prev],
+                                         wait_adj=0 if j else -1, stream=stream.cuda_stream)
+                assert rc == 0, L.error()
+            return
         for (g, k), (buf, ptrs), full in zip(self.groups, self.bufs, self.full):
             q, d = self.acts[k]
             rc = self.layer.matvec_dev([self.ids[nm] for nm in g], q.data_ptr(), d.data_ptr(),
@@ -189,6 +225,20 @@ class TokenChain:
                 self.dist.all_gather_into_tensor(full, buf)
 
     def close(self):
+        if self.fused:
+            self.torch.cuda.synchronize()
+            if self.layer.kernel_error():
+                raise RuntimeError("a fused-gather wait gave up: " + self.layer.error())
+            self.dist.barrier()
+            for rows in self.peer.values():
+                for row in rows:
+                    for p in row:
+                        self.layer.ipc_free(p, True)
+            self.dist.barrier()
+            for row in self.mine:
+                for p in row:
+                    self.layer.ipc_free(p, False)
+            self.layer.ipc_free(self.mine_sync, False)
         self.layer.close()
 
 
@@ -270,6 +320,19 @@ def run_ours(args, rank, world, dist):
                  "ms_per_step": round(ms_split, 5),
                  "workload": f"one decode stream, every tensor column-split over {world} GPUs, "
                              "one NCCL all-gather per launch group (65 a token)"}
+        fused = {"workload": "the same split, each launch storing its rows into every "
+                             "rank's outputs over NVLink and waiting on arrival counters "
+                             "(matvec and all-gather in one kernel), as a CUDA graph a token"}
+        try:
+            fz = TokenChain(gg, dev, rank, world, dist, fused=True)
+            ms_fused, _ = time_chain(fz, max(1, min(args.steps, 500)), 5, barrier, dist, world,
+                                     dev, True, False)
+            fz.close()
+            fused.update(value=round(1000.0 / ms_fused, 2), unit=UNIT,
+                         ms_per_step=round(ms_fused, 5))
+        except (RuntimeError, AssertionError) as e:   # reported, not fatal to the headline
+            fused["error"] = str(e)[:200]
+        split["fused"] = fused
 
     e2e = run_e2e(path, args, lib, world, dist, dev)
 

@@ -138,12 +138,13 @@ struct charsiu_gpu {
 	// direct host calls: [0] CTAs done (device), [2..3] start stamp; the flag
 	// words the last CTA raises (mapped host memory), and their sequence
 	uint32_t *d_sync = nullptr;
+	uint32_t *d_gather_count = nullptr;   // the fused gather's CTAs-done count
 	volatile uint32_t *h_flag = nullptr;
 	uint32_t *d_flag = nullptr;
 	uint32_t seq = 0;
 	QmvInline<QMV_INLINE_MAX_WORDS> *inl = nullptr;    // the direct call's kernel arguments
 	bool direct = true;  // CHARSIU_GPU_DIRECT=0: every host call through a graph with copies
-	bool smem_set[56] = {};
+	bool smem_set[64] = {};
 	// CTAs per SM for (m, nb): asked of the driver once, never during capture
 	std::vector<std::pair<uint64_t, int>> occ;
 
@@ -284,9 +285,23 @@ void fill_params(charsiu_gpu *g, QmvParams &p, const int *ids, unsigned n, float
 // whose words hold the activation; the launch then runs qmv1_inline_kernel,
 // which reads the activation from its parameters (the first
 // QmvInline<AW> bytes of the buffer, AW by the shape).
+//
+// `gth` (M = 1 only): the launch is qmv1_gather_kernel, the matvec fused with
+// its all-gather over peer memory; it goes without programmatic dependence,
+// so its wait for the other ranks never overlaps a kernel of its own GPU.
 int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
-	       const void *inl = nullptr)
+	       const void *inl = nullptr, const QmvGather *gth = nullptr)
 {
+	static const void *const qmv1_gather_fns[4][2] = {
+		{(const void *)qmv1_gather_kernel<4, false, false>,
+		 (const void *)qmv1_gather_kernel<4, true, false>},
+		{(const void *)qmv1_gather_kernel<8, false, false>,
+		 (const void *)qmv1_gather_kernel<8, true, false>},
+		{(const void *)qmv1_gather_kernel<8, false, true>,
+		 (const void *)qmv1_gather_kernel<8, true, true>},
+		{(const void *)qmv1_gather_kernel<16, false, true>,
+		 (const void *)qmv1_gather_kernel<16, true, true>},
+	};
 	static const void *const qmv1_fns[4][2] = {
 		{(const void *)qmv1_kernel<4, false, false>, (const void *)qmv1_kernel<4, true, false>},
 		{(const void *)qmv1_kernel<8, false, false>, (const void *)qmv1_kernel<8, true, false>},
@@ -314,10 +329,10 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
 	if (m == 1) {
 		threads = qmv1_warps[shape] * 32;
 		smem = qmv1_smem_bytes(p.nb);
-		// 10..17, inline 24..31; M > 1 uses slots 2, 4, 8, the tensor cores 20..23
-		slot = (inl ? 24 : 10) + 2 * shape + (q8 ? 1 : 0);
-		fn = (inl ? qmv1_inline_fns : qmv1_fns)[shape][q8 ? 1 : 0];
-	} else if (inl) {
+		// 10..17, inline 24..31, gather 56..63; the tensor cores 20..23, M > 1 32..55
+		slot = (gth ? 56 : inl ? 24 : 10) + 2 * shape + (q8 ? 1 : 0);
+		fn = (gth ? qmv1_gather_fns : inl ? qmv1_inline_fns : qmv1_fns)[shape][q8 ? 1 : 0];
+	} else if (inl || gth) {
 		return -1;
 	} else {
 		// M = 2, 4, 8: qmvm_kernel, the same shapes as M = 1
@@ -370,9 +385,10 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
 	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 	cfg.attrs = attr;
-	cfg.numAttrs = g->no_pdl ? 0 : 1;
+	cfg.numAttrs = g->no_pdl || gth ? 0 : 1;
 	QmvParams arg = p;
-	void *args[1] = {inl ? const_cast<void *>(inl) : (void *)&arg};
+	QmvGather garg = gth ? *gth : QmvGather{};
+	void *args[2] = {inl ? const_cast<void *>(inl) : (void *)&arg, &garg};
 	const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
 	if (e != cudaSuccess)
 		return -1;
@@ -917,6 +933,7 @@ void charsiu_gpu_close(struct charsiu_gpu *g)
 		cudaFreeHost((void *)g->h_flag);
 	delete g->inl;
 	cudaFree(g->d_sync);
+	cudaFree(g->d_gather_count);
 	cudaFreeHost(g->h_act);
 	cudaFreeHost(g->h_y);
 	cudaFreeHost(g->h_i8);
@@ -1156,6 +1173,142 @@ int charsiu_gpu_matvec_batch_group_dev(struct charsiu_gpu *g, const int *ids, un
 		if (charsiu_gpu_matvec_batch_dev(g, ids[i], m, q, d, ys[i], stream))
 			return -1;
 	return 0;
+}
+
+// ---- the matvec fused with its all-gather (column split over GPUs) ------------
+
+void *charsiu_gpu_ipc_alloc(struct charsiu_gpu *g, size_t bytes)
+{
+	if (!g || !bytes)
+		return nullptr;
+	cudaSetDevice(g->device);
+	void *p = nullptr;
+	if (cudaMalloc(&p, bytes) != cudaSuccess)
+		return nullptr;
+	if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+		cudaFree(p);
+		return nullptr;
+	}
+	return p;
+}
+
+int charsiu_gpu_ipc_handle(struct charsiu_gpu *g, void *ptr, unsigned char *handle)
+{
+	if (!g || !ptr || !handle)
+		return -1;
+	cudaSetDevice(g->device);
+	cudaIpcMemHandle_t h;
+	static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+	if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess)
+		return -1;
+	memcpy(handle, &h, sizeof(h));
+	return 0;
+}
+
+void *charsiu_gpu_ipc_open(struct charsiu_gpu *g, const unsigned char *handle)
+{
+	if (!g || !handle)
+		return nullptr;
+	cudaSetDevice(g->device);
+	cudaIpcMemHandle_t h;
+	memcpy(&h, handle, sizeof(h));
+	void *p = nullptr;
+	if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+		return nullptr;
+	return p;
+}
+
+void charsiu_gpu_ipc_free(struct charsiu_gpu *g, void *ptr, int opened)
+{
+	if (!g || !ptr)
+		return;
+	cudaSetDevice(g->device);
+	if (opened)
+		cudaIpcCloseMemHandle(ptr);
+	else
+		cudaFree(ptr);
+}
+
+int charsiu_gpu_read_device(struct charsiu_gpu *g, const void *dev_ptr, void *host, size_t bytes)
+{
+	if (!g || !dev_ptr || !host)
+		return -1;
+	cudaSetDevice(g->device);
+	return cudaMemcpy(host, dev_ptr, bytes, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
+}
+
+int charsiu_gpu_kernel_error(struct charsiu_gpu *g)
+{
+	if (!g || !g->h_err)
+		return -1;
+	const int e = *g->h_err;
+	if (e) {
+		*g->h_err = 0;
+		whine(g, "a kernel wait gave up (code %d)", e);
+		retire(g, "a kernel wait gave up");
+	}
+	return e;
+}
+
+int charsiu_gpu_gather_epoch_dev(struct charsiu_gpu *g, uint32_t *sync_local, void *stream)
+{
+	if (!g || g->dead || !sync_local)
+		return -1;
+	cudaSetDevice(g->device);
+	gather_epoch_kernel<<<1, 32, 0, stream ? (cudaStream_t)stream : g->stream>>>(sync_local);
+	if (cudaGetLastError() != cudaSuccess)
+		return -1;
+	g->launches++;
+	return 0;
+}
+
+int charsiu_gpu_matvec_gather_dev(struct charsiu_gpu *g, const int *ids, unsigned n,
+				  const int8_t *q, const float *d, float *const *full_ys,
+				  uint32_t *const *syncs, unsigned signal_idx, unsigned wait_idx,
+				  unsigned wait_mult, int wait_adj, void *stream)
+{
+	if (!g || g->dead || !ids || !q || !d || !full_ys || !syncs || ((uintptr_t)q & 15) ||
+	    g->world > (unsigned)QMV_MAX_RANKS || !n || n > (unsigned)QMV_MAX_TENSORS)
+		return -1;
+	uint32_t k = 0;
+	for (unsigned i = 0; i < n; i++) {
+		if (ids[i] < 0 || (size_t)ids[i] >= g->ent.size())
+			return -1;
+		const Ent &e = g->ent[ids[i]];
+		if (i && (e.k != k || e.type != g->ent[ids[0]].type))
+			return -1;
+		k = (uint32_t)e.k;
+	}
+	cudaSetDevice(g->device);
+	QmvGather gth = {};
+	for (unsigned r = 0; r < g->world; r++) {
+		if (!syncs[r])
+			return -1;
+		gth.sync[r] = syncs[r];
+		for (unsigned i = 0; i < n; i++) {
+			if (!full_ys[r * n + i])
+				return -1;
+			gth.y[r][i] = full_ys[r * n + i];
+		}
+	}
+	for (unsigned i = 0; i < n; i++)
+		gth.row0[i] = (uint32_t)g->ent[ids[i]].row0;
+	if (!g->d_gather_count) {
+		if (cudaMalloc((void **)&g->d_gather_count, sizeof(uint32_t)) != cudaSuccess ||
+		    cudaMemset(g->d_gather_count, 0, sizeof(uint32_t)) != cudaSuccess)
+			return -1;
+	}
+	gth.cta_count = g->d_gather_count;
+	gth.world = g->world;
+	gth.rank = g->rank;
+	gth.signal_idx = signal_idx;
+	gth.wait_idx = wait_idx;
+	gth.wait_mult = wait_mult;
+	gth.wait_adj = wait_adj;
+	float *unused[QMV_MAX_TENSORS] = {};
+	QmvParams p;
+	fill_params(g, p, ids, n, unused, k, q, d);
+	return launch_qmv(g, 1, p, stream ? (cudaStream_t)stream : g->stream, nullptr, &gth);
 }
 
 // The batched q8_0 matvec with nothing allocated: the same pack and

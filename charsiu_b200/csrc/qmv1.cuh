@@ -48,6 +48,46 @@ struct QmvInline {
 	uint4 act[AW];
 };
 constexpr int QMV_INLINE_MAX_WORDS = 1008;
+
+// The matvec fused with its all-gather (a tensor column-split over `world`
+// GPUs, one process a GPU): this rank computes its slab of rows and stores
+// each y straight into every rank's full output over NVLink (peer stores),
+// then, once all its CTAs are done, adds its number of 8-row groups to every
+// rank's arrival counter for this launch (red.release.sys). A later launch that reads the
+// gathered output first waits, on its own GPU, until its arrival counter
+// shows every rank's groups for this token. sync words: [0] the token epoch
+// (gather_epoch_kernel adds 1 at each token's start), [1 + k] the arrivals
+// of launch k, monotonic: after token t it holds (t + 1) * groups of launch k.
+constexpr int QMV_MAX_RANKS = 8;
+
+struct QmvGather {
+	float *y[QMV_MAX_RANKS][QMV_MAX_TENSORS];  // each rank's full output of each tensor
+	uint32_t *sync[QMV_MAX_RANKS];              // each rank's sync words
+	uint32_t *cta_count;                        // this GPU's: CTAs done, zero between launches
+	uint32_t row0[QMV_MAX_TENSORS];             // this rank's first row of each tensor
+	uint32_t world, rank;
+	uint32_t signal_idx;                        // arrival word this launch adds to
+	uint32_t wait_idx, wait_mult;               // wait for sync[wait_idx] >= (epoch + adj) * mult
+	int32_t wait_adj;                           // (wait_mult 0: no wait)
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
+{
+	uint32_t v;
+	asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+	return v;
+}
+
+__device__ __forceinline__ void red_release_sys_add(uint32_t *p, uint32_t v)
+{
+	asm volatile("red.release.sys.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+__global__ void gather_epoch_kernel(uint32_t *sync_local)
+{
+	if (threadIdx.x == 0 && blockIdx.x == 0)
+		sync_local[0] += 1;
+}
 static_assert(sizeof(QmvInline<QMV_INLINE_MAX_WORDS>) <= 32764, "kernel parameter space");
 
 __device__ __forceinline__ uint4 ldg_stream(const uint8_t *p)
@@ -146,7 +186,8 @@ __device__ __forceinline__ void named_barrier(int id, int threads)
 // nseg <= W, or nseg <= 2W with TWO); both are loaded before either is
 // computed.
 template <int W, bool Q8, bool TWO, int AW>
-__device__ __forceinline__ void qmv1_body(const QmvParams &p, const uint4 *inl)
+__device__ __forceinline__ void qmv1_body(const QmvParams &p, const uint4 *inl,
+					  const QmvGather *gth = nullptr)
 {
 	extern __shared__ __align__(128) uint8_t smem[];
 	const uint32_t nb = p.nb;
@@ -195,6 +236,23 @@ __device__ __forceinline__ void qmv1_body(const QmvParams &p, const uint4 *inl)
 			sa[i] = inl[i];
 	}
 	pdl_wait();
+	if (gth && gth->wait_mult) {
+		// the gathered input of this launch: every rank's part must be in
+		if (threadIdx.x == 0) {
+			const uint32_t *syn = gth->sync[gth->rank];
+			const uint32_t target =
+				(uint32_t)((int32_t)ld_acquire_sys(&syn[0]) + gth->wait_adj) * gth->wait_mult;
+			const unsigned long long t0 = globaltimer_ns();
+			while ((int32_t)(ld_acquire_sys(&syn[gth->wait_idx]) - target) < 0) {
+				if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+					*(volatile int *)p.err = 12;
+					break;
+				}
+				__nanosleep(64);
+			}
+		}
+		__syncthreads();
+	}
 	if (!AW) {
 		const uint4 *gq = reinterpret_cast<const uint4 *>(p.q);
 		uint4 *sq = reinterpret_cast<uint4 *>(aq);
@@ -240,8 +298,28 @@ __device__ __forceinline__ void qmv1_body(const QmvParams &p, const uint4 *inl)
 			for (uint32_t b = 0; b < nb; b++)
 				s = __fadd_rn(s, t[b * RG]);
 			const uint32_t row = lg * RG + lane;
-			if (row < p.t[ti].rows)
-				p.t[ti].y[row] = s;
+			if (row < p.t[ti].rows) {
+				if (gth) {
+					for (uint32_t r = 0; r < gth->world; r++)
+						gth->y[r][ti][gth->row0[ti] + row] = s;
+				} else {
+					p.t[ti].y[row] = s;
+				}
+			}
+		}
+	}
+	if (gth) {
+		// this CTA's stores (peer ones included) reach thread 0 through the
+		// barrier and are released at device scope by its count; the last CTA
+		// acquires every CTA's, and one system fence then orders all of them
+		// before it adds this rank's groups to every rank's arrival word (a
+		// system-scope release in every CTA costs several microseconds)
+		__syncthreads();
+		if (threadIdx.x == 0 && atom_add_acq_rel_gpu(gth->cta_count, 1u) == gridDim.x - 1) {
+			*gth->cta_count = 0;
+			__threadfence_system();
+			for (uint32_t r = 0; r < gth->world; r++)
+				red_release_sys_add(gth->sync[r] + gth->signal_idx, p.total_groups);
 		}
 	}
 	if (p.done_flag) {
@@ -268,6 +346,13 @@ __global__ void __launch_bounds__(W * 32)
 qmv1_kernel(const __grid_constant__ QmvParams p)
 {
 	qmv1_body<W, Q8, TWO, 0>(p, nullptr);
+}
+
+template <int W, bool Q8, bool TWO>
+__global__ void __launch_bounds__(W * 32)
+qmv1_gather_kernel(const __grid_constant__ QmvParams p, const __grid_constant__ QmvGather gth)
+{
+	qmv1_body<W, Q8, TWO, 0>(p, nullptr, &gth);
 }
 
 template <int W, bool Q8, bool TWO, int AW>

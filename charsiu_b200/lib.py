@@ -43,6 +43,15 @@ SIGNATURES = [
     ("charsiu_gpu_matvec_batch_dev", C.c_int, [_vp, C.c_int, C.c_uint, _vp, _vp, _vp, _vp]),
     ("charsiu_gpu_matvec_batch_group_dev", C.c_int,
      [_vp, _vp, C.c_uint, C.c_uint, _vp, _vp, _vp, _vp]),
+    ("charsiu_gpu_ipc_alloc", C.c_void_p, [_vp, C.c_size_t]),
+    ("charsiu_gpu_ipc_handle", C.c_int, [_vp, _vp, _vp]),
+    ("charsiu_gpu_ipc_open", C.c_void_p, [_vp, _vp]),
+    ("charsiu_gpu_ipc_free", None, [_vp, _vp, C.c_int]),
+    ("charsiu_gpu_gather_epoch_dev", C.c_int, [_vp, _vp, _vp]),
+    ("charsiu_gpu_kernel_error", C.c_int, [_vp]),
+    ("charsiu_gpu_read_device", C.c_int, [_vp, _vp, _vp, C.c_size_t]),
+    ("charsiu_gpu_matvec_gather_dev", C.c_int,
+     [_vp, _vp, C.c_uint, _vp, _vp, _vp, _vp, C.c_uint, C.c_uint, C.c_uint, C.c_int, _vp]),
     ("charsiu_gpu_matvec_batch_noalloc", C.c_int, [_vp, C.c_int, C.c_uint, _vp, _vp, _vp, _vp]),
     ("charsiu_gpu_act_quantise_dev", C.c_int, [_vp, _vp, C.c_uint, C.c_uint, _vp, _vp, _vp]),
     ("charsiu_gpu_calls", C.c_ulong, [_vp]),
@@ -221,6 +230,53 @@ class Layer:
         return self.L.charsiu_gpu_matvec_batch_group_dev(self.h, C.addressof(idarr), len(ids),
                                                          m, q_ptr, d_ptr, C.addressof(yarr),
                                                          stream or None)
+
+    # the matvec fused with its all-gather (one process a GPU, rank/world at open)
+    def ipc_alloc(self, nbytes: int) -> int:
+        p = self.L.charsiu_gpu_ipc_alloc(self.h, nbytes)
+        if not p:
+            raise GpuError("ipc_alloc failed")
+        return p
+
+    def ipc_handle(self, ptr: int) -> bytes:
+        buf = (C.c_ubyte * 64)()
+        self._check(self.L.charsiu_gpu_ipc_handle(self.h, ptr, buf), "ipc_handle")
+        return bytes(buf)
+
+    def ipc_open(self, handle: bytes) -> int:
+        buf = (C.c_ubyte * 64).from_buffer_copy(handle)
+        p = self.L.charsiu_gpu_ipc_open(self.h, buf)
+        if not p:
+            raise GpuError("ipc_open failed")
+        return p
+
+    def ipc_free(self, ptr: int, opened: bool):
+        self.L.charsiu_gpu_ipc_free(self.h, ptr, int(opened))
+
+    def read_device(self, ptr: int, out: np.ndarray) -> np.ndarray:
+        self._check(self.L.charsiu_gpu_read_device(self.h, ptr, _p(out), out.nbytes),
+                    "read_device")
+        return out
+
+    def gather_epoch_dev(self, sync_ptr: int, stream: int = 0) -> int:
+        return self.L.charsiu_gpu_gather_epoch_dev(self.h, sync_ptr, stream or None)
+
+    def kernel_error(self) -> int:
+        return self.L.charsiu_gpu_kernel_error(self.h)
+
+    def matvec_gather_dev(self, ids, q_ptr: int, d_ptr: int, full_ptrs, sync_ptrs,
+                          signal_idx: int, wait_idx: int = 0, wait_mult: int = 0,
+                          wait_adj: int = 0, stream: int = 0) -> int:
+        """full_ptrs: rank-major [world][len(ids)] device pointers (peer ones
+        from ipc_open); sync_ptrs: [world]."""
+        ids = list(ids)
+        idarr = (C.c_int * len(ids))(*ids)
+        farr = (C.c_void_p * len(full_ptrs))(*full_ptrs)
+        sarr = (C.c_void_p * len(sync_ptrs))(*sync_ptrs)
+        return self.L.charsiu_gpu_matvec_gather_dev(self.h, C.addressof(idarr), len(ids), q_ptr,
+                                                    d_ptr, C.addressof(farr), C.addressof(sarr),
+                                                    signal_idx, wait_idx, wait_mult, wait_adj,
+                                                    stream or None)
 
     def batch_noalloc(self, tid: int, m: int, q_ptr: int, d_ptr: int, y_ptr: int,
                       stream: int = 0) -> int:

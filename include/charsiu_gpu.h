@@ -151,6 +151,50 @@ CHARSIU_GPU_API int charsiu_gpu_matvec_batch_group_dev(struct charsiu_gpu *g, co
 						       unsigned n, unsigned m, const int8_t *q,
 						       const float *d, float *const *ys,
 						       void *stream);
+/* ---- the matvec fused with its all-gather ------------------------------------ */
+/*
+ * For a layer opened with charsiu_gpu_open_ex(..., rank, world) in each of
+ * `world` processes, one a GPU, that need every rank to hold the whole y (the
+ * column-split decode). No counterpart in the reference (charsiu has one
+ * device).
+ *
+ * Buffers the peers write are allocated here (charsiu_gpu_ipc_alloc: plain
+ * device memory, zeroed) and shared with a 64-byte handle
+ * (charsiu_gpu_ipc_handle; exchange the bytes between processes, then
+ * charsiu_gpu_ipc_open gives this process's pointer to a peer's buffer;
+ * charsiu_gpu_ipc_free releases either kind).
+ *
+ * charsiu_gpu_matvec_gather_dev runs the matvec of this rank's slab and
+ * stores each y into every rank's full output full_ys[r * n + i] (tensor
+ * ids[i], rank r: the whole N floats), then adds the groups it finished to
+ * word signal_idx of every rank's sync array syncs[r] (uint32). With
+ * wait_mult > 0 it first waits, on this GPU, until its own word wait_idx
+ * reaches (epoch + wait_adj) * wait_mult, epoch being word 0, which
+ * charsiu_gpu_gather_epoch_dev adds 1 to (call it at each token's start). The
+ * wait gives up after one second (the layer then retires). The launches run
+ * without programmatic dependence. 0 when queued on `stream`.
+ */
+CHARSIU_GPU_API void *charsiu_gpu_ipc_alloc(struct charsiu_gpu *g, size_t bytes);
+CHARSIU_GPU_API int charsiu_gpu_ipc_handle(struct charsiu_gpu *g, void *ptr,
+					   unsigned char *handle);
+CHARSIU_GPU_API void *charsiu_gpu_ipc_open(struct charsiu_gpu *g, const unsigned char *handle);
+CHARSIU_GPU_API void charsiu_gpu_ipc_free(struct charsiu_gpu *g, void *ptr, int opened);
+/* Copy `bytes` of device memory (this GPU's, or a peer's opened above) to the
+ * host; waits for it. 0 on success. */
+CHARSIU_GPU_API int charsiu_gpu_read_device(struct charsiu_gpu *g, const void *dev_ptr,
+					    void *host, size_t bytes);
+CHARSIU_GPU_API int charsiu_gpu_gather_epoch_dev(struct charsiu_gpu *g, uint32_t *sync_local,
+						 void *stream);
+/* The first nonzero code a kernel of the _dev forms wrote since the last
+ * call (a bounded wait that gave up), then clears it; a nonzero code retires
+ * the layer, as a host call's would. 0: none. */
+CHARSIU_GPU_API int charsiu_gpu_kernel_error(struct charsiu_gpu *g);
+CHARSIU_GPU_API int charsiu_gpu_matvec_gather_dev(struct charsiu_gpu *g, const int *ids,
+						  unsigned n, const int8_t *q, const float *d,
+						  float *const *full_ys, uint32_t *const *syncs,
+						  unsigned signal_idx, unsigned wait_idx,
+						  unsigned wait_mult, int wait_adj, void *stream);
+
 /* The batched matvec of charsiu_gpu_matvec_batch_dev, for callers that
  * cannot allocate GPU memory while they run -- a server whose own memory
  * pool already owns the GPU's free memory, or a latency-bound loop that must

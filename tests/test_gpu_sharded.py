@@ -92,3 +92,90 @@ def test_nccl_ranks_one_per_gpu():
             p.join(300)
             assert p.exitcode == 0
         assert all(result[r] for r in range(world))
+
+
+def _gather_rank(rank, world, port, result):
+    """One rank of the fused matvec + all-gather: the slab's y stored into every
+    rank's full output over peer memory, arrivals counted in every rank's sync
+    words; the second launch waits for the first's arrivals from every rank."""
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        k = 2048
+        shapes = [(2056, 11), (512, 12), (128256, 13)]       # ragged, small, the head
+        blks = [W.matvec_inputs(G.GGML_Q8_0, k, n, seed=s)[0] for n, s in shapes]
+        x = np.random.default_rng(3).normal(size=k).astype(np.float32)
+        q, d = O.act_quantise(x)
+        dev = torch.device("cuda", rank)
+        ok = True
+        with Layer(max_k=k, max_n=128256, max_tensors=4, device=rank, rank=rank,
+                   world=world) as L:
+            ids = [L.add_blocks(G.GGML_Q8_0, k, n, b) for (n, _), b in zip(shapes, blks)]
+            mine = [L.ipc_alloc(4 * n) for n, _ in shapes] + [L.ipc_alloc(64)]
+            allh = [None] * world
+            dist.all_gather_object(allh, [L.ipc_handle(p) for p in mine])
+            bufs = [mine if r == rank else [L.ipc_open(h) for h in allh[r]]
+                    for r in range(world)]                 # bufs[r]: rank r's, as seen here
+            syncs = [bufs[r][3] for r in range(world)]
+            groups = [(n + 7) // 8 for n, _ in shapes]
+            qt_ = torch.from_numpy(q).to(dev)
+            dt_ = torch.from_numpy(d).to(dev)
+            s = torch.cuda.current_stream().cuda_stream
+            dist.barrier()                       # every rank's buffers exist and are zero
+            ok &= L.gather_epoch_dev(mine[3], s) == 0
+            # launch 1: tensors 0 and 1 together; launch 2: the head, after every
+            # rank's part of launch 1 has arrived in this rank's sync words
+            ok &= L.matvec_gather_dev(ids[:2], qt_.data_ptr(), dt_.data_ptr(),
+                                      [bufs[r][i] for r in range(world) for i in (0, 1)],
+                                      syncs, signal_idx=1, stream=s) == 0
+            ok &= L.matvec_gather_dev(ids[2:], qt_.data_ptr(), dt_.data_ptr(),
+                                      [bufs[r][2] for r in range(world)], syncs,
+                                      signal_idx=2, wait_idx=1, wait_mult=groups[0] + groups[1],
+                                      wait_adj=0, stream=s) == 0
+            torch.cuda.synchronize()
+            ok &= L.kernel_error() == 0
+            dist.barrier()                       # every rank's stores into this rank are done
+            for (n, _), b, p in zip(shapes, blks, mine):
+                got = L.read_device(p, np.empty(n, dtype=np.float32))
+                want = O.matvec(G.GGML_Q8_0, b, k, n, q, d)
+                ok &= bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+            counts = L.read_device(mine[3], np.empty(16, dtype=np.uint32))
+            ok &= bool(counts[0] == 1 and counts[1] == groups[0] + groups[1]
+                       and counts[2] == groups[2])
+            dist.barrier()
+            for r in range(world):
+                if r != rank:
+                    for p in bufs[r]:
+                        L.ipc_free(p, True)
+            dist.barrier()
+            for p in mine:
+                L.ipc_free(p, False)
+        result[rank] = bool(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_gather_ranks_one_per_gpu():
+    torch = pytest.importorskip("torch")
+    ngpu = torch.cuda.device_count()
+    if ngpu < 2:
+        pytest.skip("the fused gather waits on other GPUs: needs two or more")
+    import torch.multiprocessing as mp
+    world = min(ngpu, 8)
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_gather_rank, args=(r, world, port, result))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+            assert p.exitcode == 0
+        assert all(result[r] for r in range(world))
