@@ -22,9 +22,11 @@ import struct
 
 import numpy as np
 
-GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0 = 0, 1, 2, 8
-BLOCK_BYTES = {GGML_Q8_0: 34, GGML_Q4_0: 18}
-TYPE_NAMES = {GGML_F32: "f32", GGML_F16: "f16", GGML_Q4_0: "q4_0", GGML_Q8_0: "q8_0"}
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q6_K = 0, 1, 2, 8, 14
+BLOCK_BYTES = {GGML_Q8_0: 34, GGML_Q4_0: 18, GGML_Q6_K: 210}
+BLOCK_ELEMS = {GGML_Q8_0: 32, GGML_Q4_0: 32, GGML_Q6_K: 256}
+TYPE_NAMES = {GGML_F32: "f32", GGML_F16: "f16", GGML_Q4_0: "q4_0", GGML_Q8_0: "q8_0",
+              GGML_Q6_K: "q6_K"}
 
 # GGUF value types (reference include/charsiu_llm.h:28-32)
 V_U32, V_I32, V_F32, V_STRING, V_ARRAY, V_U64 = 4, 5, 6, 8, 9, 10
@@ -64,7 +66,19 @@ def proj_shapes(s: LlamaShape):
 
 
 def quant_blocks(rng: np.random.Generator, qtype: int, n: int, k: int) -> np.ndarray:
-    """n rows of k columns as raw GGML blocks: uint8 [n, k/32*block_bytes]."""
+    """n rows of k columns as raw GGML blocks: uint8 [n, k/elems*block_bytes].
+
+    q6_K super-blocks (256 weights, 210 bytes: ql[128], qh[64], int8
+    scales[16], fp16 d) get uniform 6-bit weights, scales in [-64, 63] and
+    d = |N(0, 0.02)| / 2048, so d * scale * q stays near the other types'."""
+    if qtype == GGML_Q6_K:
+        nsb = k // 256
+        blk = np.empty((n, nsb, 210), dtype=np.uint8)
+        blk[:, :, 0:192] = rng.integers(0, 256, size=(n, nsb, 192), dtype=np.uint8)
+        blk[:, :, 192:208] = rng.integers(-64, 64, size=(n, nsb, 16), dtype=np.int8).view(np.uint8)
+        d = (np.abs(rng.normal(0.0, 0.02, size=(n, nsb))) / 2048.0).astype(np.float16)
+        blk[:, :, 208:210] = d.view(np.uint8).reshape(n, nsb, 2)
+        return blk.reshape(n, nsb * 210)
     nb = k // 32
     if qtype == GGML_Q8_0:
         blk = np.empty((n, nb, 34), dtype=np.uint8)
@@ -106,9 +120,9 @@ def _kv_str_array(key: str, items) -> bytes:
     return b"".join(parts)
 
 
-def _tensor_list(s: LlamaShape, qtype: int):
+def _tensor_list(s: LlamaShape, qtype: int, embd_qtype: int):
     """(name, ne0, ne1, type) in file order."""
-    out = [("token_embd.weight", s.n_embd, s.n_vocab, qtype),
+    out = [("token_embd.weight", s.n_embd, s.n_vocab, embd_qtype),
            ("output_norm.weight", s.n_embd, 1, GGML_F32)]
     for l in range(s.n_layer):
         out.append((f"blk.{l}.attn_norm.weight", s.n_embd, 1, GGML_F32))
@@ -121,13 +135,16 @@ def _tensor_list(s: LlamaShape, qtype: int):
 def _nbytes(ne0: int, ne1: int, t: int) -> int:
     if t == GGML_F32:
         return ne0 * ne1 * 4
-    return ne0 // 32 * BLOCK_BYTES[t] * ne1
+    return ne0 // BLOCK_ELEMS[t] * BLOCK_BYTES[t] * ne1
 
 
 def write_llama(path: str, shape: LlamaShape = LLAMA_3_2_1B, qtype: int = GGML_Q8_0,
-                seed: int = 0) -> str:
-    """Write a seeded random-init Llama GGUF (tied head, no output.weight)."""
-    tensors = _tensor_list(shape, qtype)
+                seed: int = 0, embd_qtype: int | None = None) -> str:
+    """Write a seeded random-init Llama GGUF (tied head, no output.weight).
+
+    embd_qtype: the type of token_embd (and so of the tied head); llama.cpp
+    writes q6_K there in q4_0 files. Default: qtype."""
+    tensors = _tensor_list(shape, qtype, qtype if embd_qtype is None else embd_qtype)
     kv = [
         _kv_str("general.architecture", "llama"),
         _kv_str("general.name", f"synthetic-llama-seed{seed}"),
@@ -169,7 +186,7 @@ def write_llama(path: str, shape: LlamaShape = LLAMA_3_2_1B, qtype: int = GGML_Q
             v = (1.0 + rng.normal(0.0, 0.01, size=ne0 * ne1)).astype(np.float32)
             mm[o:o + v.nbytes] = v.view(np.uint8)
         else:
-            rb = ne0 // 32 * BLOCK_BYTES[t]
+            rb = ne0 // BLOCK_ELEMS[t] * BLOCK_BYTES[t]
             step = max(1, (64 << 20) // rb)
             for r0 in range(0, ne1, step):
                 r1 = min(ne1, r0 + step)

@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from .gguf import GGML_Q4_0, GGML_Q8_0, LLAMA_3_2_1B, TINY, quant_blocks
+from .gguf import GGML_Q4_0, GGML_Q6_K, GGML_Q8_0, LLAMA_3_2_1B, TINY, quant_blocks
 
 # small shapes whose inputs are stored as fixtures (ragged N and odd nb included)
 MATVEC_GOLDEN = {
@@ -23,6 +23,8 @@ MATVEC_GOLDEN = {
     "q4_k256_n64": (GGML_Q4_0, 256, 64, 12),
     "q8_k96_n40": (GGML_Q8_0, 96, 40, 13),
     "q4_k160_n19": (GGML_Q4_0, 160, 19, 14),
+    "q6k_k256_n64": (GGML_Q6_K, 256, 64, 15),
+    "q6k_k2048_n41": (GGML_Q6_K, 2048, 41, 16),
 }
 # the two matvec workload shapes: outputs stored, inputs regenerated from seeds
 MATVEC_SEEDED = {
@@ -44,6 +46,9 @@ DECODE = {
     "tiny_q4": {"shape": TINY, "qtype": GGML_Q4_0, "seed": 2, "n_gen": 24, "n_ctx": 64},
     "llama1b_q8": {"shape": LLAMA_3_2_1B, "qtype": GGML_Q8_0, "seed": 0, "n_gen": 24,
                    "n_ctx": 64},
+    # a q4_0 file as llama.cpp writes one: token_embd (the tied head) in q6_K
+    "tiny_q4_q6k": {"shape": TINY, "qtype": GGML_Q4_0, "embd_qtype": GGML_Q6_K, "seed": 3,
+                    "n_gen": 24, "n_ctx": 64},
 }
 
 

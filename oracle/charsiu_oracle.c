@@ -57,6 +57,7 @@ uint64_t orc_row_bytes(uint32_t type, uint64_t k)
 	switch (type) {
 	case ORC_Q8_0: return k / 32 * 34;
 	case ORC_Q4_0: return k / 32 * 18;
+	case ORC_Q6_K: return k / 256 * 210;
 	case ORC_F32:  return k * 4;
 	case ORC_F16:  return k * 2;
 	default:       return 0;
@@ -139,12 +140,68 @@ static float dot_row(uint32_t type, const uint8_t *row, const int8_t *q,
 	return s;
 }
 
+/*
+ * q6_K (src/gguf.c:449-454 for the 210-byte super-block, :1109-1145 for the
+ * integer dot). A super-block holds 256 weights as two halves of 128; in half
+ * h, byte l (0..63) of ql and byte l (0..31) of qh give four 6-bit weights
+ * (low nibble of ql[l] / ql[l + 32], high nibble of the same, each with two
+ * bits of qh[l] above it), minus 32. Every 16 weights have one int8 scale; an
+ * activation block (32) covers two such runs, so each run's integer dot is
+ * scaled by ((d * scale) * d_a) and added to the row's sum in the order
+ * (super-block, half, run pair g, run k).
+ */
+static int q6_weight(const uint8_t *ql, const uint8_t *qh, unsigned k, unsigned l)
+{
+	unsigned lo = (k & 1) ? ql[l + 32] : ql[l];
+	unsigned nib = (k & 2) ? lo >> 4 : lo & 0x0f;
+	unsigned hi = (qh[l] >> (2 * k)) & 3;
+
+	return (int)(nib | (hi << 4)) - 32;
+}
+
+static float dot_row_q6k(const uint8_t *row, const int8_t *q, const float *d, uint64_t nsb)
+{
+	float s = 0.0f;
+
+	for (uint64_t i = 0; i < nsb; i++) {
+		const uint8_t *sb = row + i * 210;
+		float dd = orc_half_to_float(rd16(sb + 208));
+
+		for (unsigned h = 0; h < 2; h++) {
+			const uint8_t *ql = sb + h * 64, *qh = sb + 128 + h * 32;
+			const int8_t *sc = (const int8_t *)(sb + 192) + h * 8;
+			const int8_t *xq = q + i * 256 + h * 128;
+			const float *xd = d + i * 8 + h * 4;
+
+			for (unsigned g = 0; g < 2; g++)
+				for (unsigned k = 0; k < 4; k++) {
+					int32_t t = 0;
+
+					for (unsigned j = 0; j < 16; j++) {
+						unsigned l = g * 16 + j;
+
+						t += q6_weight(ql, qh, k, l) * xq[k * 32 + l];
+					}
+					s += dd * (float)sc[g + 2 * k] * xd[k] * (float)t;
+				}
+		}
+	}
+	return s;
+}
+
 int orc_matvec(uint32_t type, const void *blocks, uint64_t k, const int8_t *q,
 	       const float *d, float *y, uint64_t row0, uint64_t nrows)
 {
 	const uint8_t *base = blocks;
 	uint64_t rb = orc_row_bytes(type, k);
 
+	if (type == ORC_Q6_K) {
+		if (k % 256)
+			return -1;
+		for (uint64_t r = row0; r < row0 + nrows; r++)
+			y[r] = dot_row_q6k(base + r * rb, q, d, k / 256);
+		return 0;
+	}
 	if ((type != ORC_Q8_0 && type != ORC_Q4_0) || k % 32)
 		return -1;
 	for (uint64_t r = row0; r < row0 + nrows; r++)
@@ -204,6 +261,24 @@ int orc_row_f32(uint32_t type, const void *data, uint64_t k, uint64_t row,
 			for (int j = 0; j < 16; j++) {
 				dst[b * 32 + j] = dd * (float)((blk[2 + j] & 0x0f) - 8);
 				dst[b * 32 + j + 16] = dd * (float)((blk[2 + j] >> 4) - 8);
+			}
+		}
+		return 0;
+	case ORC_Q6_K:
+		/* (d * scale) * q, the order of src/gguf.c:457-479 */
+		for (uint64_t i = 0; i < k / 256; i++) {
+			const uint8_t *sb = p + i * 210;
+			float dd = orc_half_to_float(rd16(sb + 208));
+
+			for (unsigned h = 0; h < 2; h++) {
+				const uint8_t *ql = sb + h * 64, *qh = sb + 128 + h * 32;
+				const int8_t *sc = (const int8_t *)(sb + 192) + h * 8;
+				float *out = dst + i * 256 + h * 128;
+
+				for (unsigned l = 0; l < 32; l++)
+					for (unsigned kk = 0; kk < 4; kk++)
+						out[kk * 32 + l] = dd * (float)sc[l / 16 + 2 * kk] *
+								   (float)q6_weight(ql, qh, kk, l);
 			}
 		}
 		return 0;

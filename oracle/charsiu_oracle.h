@@ -23,12 +23,13 @@ extern "C" {
 #endif
 
 /* ggml type numbers, as include/charsiu_llm.h:35-38 fixes them */
-enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8 };
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_Q6_K = 14 };
 
 /* src/gguf.c:26-55 */
 float orc_half_to_float(uint16_t h);
 
-/* Bytes of one row of a q8_0 / q4_0 tensor with k columns (src/gguf.c:1166,1170). */
+/* Bytes of one row of a q8_0 / q4_0 / q6_K tensor with k columns
+ * (src/gguf.c:1166, 1170, 1178). */
 uint64_t orc_row_bytes(uint32_t type, uint64_t k);
 
 /*
@@ -38,14 +39,15 @@ uint64_t orc_row_bytes(uint32_t type, uint64_t k);
 void orc_act_quantise(const float *x, int n, int8_t *q, float *d, float *bs);
 
 /*
- * src/gguf.c:1149-1171 with dotq_q8_0 (:1098-1107) and dotq_q4_0
- * (:1061-1077): rows [row0, row0 + nrows) of y from the integer block dots.
- * Returns -1 for a type the integer path does not take.
+ * src/gguf.c:1149-1171 with dotq_q8_0 (:1098-1107), dotq_q4_0 (:1061-1077)
+ * and dotq_q6_K (:1109-1145): rows [row0, row0 + nrows) of y from the integer
+ * dots. Returns -1 for a type this restates not (q4_1) or a ragged K.
  */
 int orc_matvec(uint32_t type, const void *blocks, uint64_t k, const int8_t *q,
 	       const float *d, float *y, uint64_t row0, uint64_t nrows);
 
-/* The integer block dots alone: dots[r * nb + b] for rows [0, n). */
+/* The integer block dots alone: dots[r * nb + b] for rows [0, n); q8_0 and
+ * q4_0 (32-element blocks) only. */
 int orc_block_dots(uint32_t type, const void *blocks, uint64_t k, uint64_t n,
 		   const int8_t *q, int32_t *dots);
 

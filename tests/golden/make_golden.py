@@ -4,12 +4,13 @@ Run here, where the reference tree is mounted:  python tests/golden/make_golden.
 It builds oracle/_ref/libcharsiu_ref.so (the reference compiled from its own
 sources by oracle/Makefile) and records what the reference computes:
 
-  golden.npz         act_set + gguf_matvec (q8_0, q4_0), cpu_reference int8
+  golden.npz         act_set + gguf_matvec (q8_0, q4_0, q6_K), cpu_reference int8
                      outputs at the four int8 workload shapes, and the chosen
                      requant scales;
   golden_decode.json greedy token ids and logit digests of charsiu's own
-                     llama_forward on two seeded synthetic models: the tiny
-                     test model and the Llama-3.2-1B-shaped one.
+                     llama_forward on seeded synthetic models: the tiny test
+                     models (q8_0; q4_0; q4_0 with a q6_K embedding and head)
+                     and the Llama-3.2-1B-shaped one.
 
 Inputs are regenerated from the recorded seeds (numpy PCG64); a sha256 of each
 input is stored beside it so generator drift is caught rather than trusted.
@@ -50,13 +51,13 @@ def main() -> None:
     for name, (qt, k, n, seed) in W.MATVEC_GOLDEN.items():
         blk, x = W.matvec_inputs(qt, k, n, seed)
         y, q, d = O.ref_matvec(qt, blk, k, n, x)
-        dots = O.block_dots(qt, blk, k, n, q)
         out[f"{name}_blocks"] = blk
         out[f"{name}_x"] = x
         out[f"{name}_y"] = y
         out[f"{name}_q"] = q
         out[f"{name}_d"] = d
-        out[f"{name}_dots"] = dots
+        if qt in (G.GGML_Q8_0, G.GGML_Q4_0):        # dots of 32-element blocks
+            out[f"{name}_dots"] = O.block_dots(qt, blk, k, n, q)
 
     # larger matvec shapes: outputs only, inputs from seeds
     for name, (qt, k, n, seed) in W.MATVEC_SEEDED.items():
@@ -82,7 +83,8 @@ def main() -> None:
     with tempfile.TemporaryDirectory() as td:
         for name, spec in W.DECODE.items():
             path = os.path.join(td, f"{name}.gguf")
-            G.write_llama(path, spec["shape"], spec["qtype"], spec["seed"])
+            G.write_llama(path, spec["shape"], spec["qtype"], spec["seed"],
+                          embd_qtype=spec.get("embd_qtype"))
             prompt = W.prompt_ids(spec["shape"].n_vocab, spec["seed"])
             toks, pm, gm, lg = O.ref_greedy(path, prompt, spec["n_gen"], n_ctx=spec["n_ctx"],
                                             threads=os.cpu_count(),

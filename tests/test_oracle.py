@@ -38,7 +38,8 @@ def test_act_and_matvec_match_golden(name):
     assert np.array_equal(bits(d), bits(GOLD[f"{name}_d"]))
     y = O.matvec(qt, blk, k, n, q, d)
     assert np.array_equal(bits(y), bits(GOLD[f"{name}_y"]))
-    assert np.array_equal(O.block_dots(qt, blk, k, n, q), GOLD[f"{name}_dots"])
+    if f"{name}_dots" in GOLD:
+        assert np.array_equal(O.block_dots(qt, blk, k, n, q), GOLD[f"{name}_dots"])
 
 
 @pytest.mark.parametrize("name", list(W.MATVEC_SEEDED))
@@ -107,12 +108,13 @@ def test_half_to_float_all_values():
     assert np.isnan(got[~finite]).all()
 
 
-@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4"])
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4", "tiny_q4_q6k"])
 def test_decode_matches_golden(name, tmp_path):
     spec = W.DECODE[name]
     gold = GOLD_DECODE[name]
     path = str(tmp_path / f"{name}.gguf")
-    G.write_llama(path, spec["shape"], spec["qtype"], spec["seed"])
+    G.write_llama(path, spec["shape"], spec["qtype"], spec["seed"],
+                  embd_qtype=spec.get("embd_qtype"))
     with open(path, "rb") as f:
         assert hashlib.sha256(f.read()).hexdigest() == gold["gguf_sha256"]
     prompt = W.prompt_ids(spec["shape"].n_vocab, spec["seed"])
@@ -130,7 +132,9 @@ needs_ref = pytest.mark.skipif(not O.have_ref(), reason="reference build absent"
 
 @needs_ref
 @pytest.mark.parametrize("qt,k,n,seed", [(G.GGML_Q8_0, 64, 33, 5), (G.GGML_Q4_0, 1024, 40, 6),
-                                         (G.GGML_Q8_0, 8192, 16, 7), (G.GGML_Q4_0, 32, 9, 8)])
+                                         (G.GGML_Q8_0, 8192, 16, 7), (G.GGML_Q4_0, 32, 9, 8),
+                                         (G.GGML_Q6_K, 256, 9, 21), (G.GGML_Q6_K, 2048, 40, 22),
+                                         (G.GGML_Q6_K, 8192, 7, 23)])
 def test_restatement_matches_reference_matvec(qt, k, n, seed):
     blk, x = W.matvec_inputs(qt, k, n, seed)
     x[::7] = 0.0                         # blocks with zeros and a few all-zero ones
@@ -155,10 +159,11 @@ def test_restatement_matches_reference_int8(m, k, n, zp):
 
 
 @needs_ref
-def test_restatement_matches_reference_decode(tmp_path):
-    shape = G.LlamaShape(128, 2, 4, 2, 256, 300, ctx_train=64)
+@pytest.mark.parametrize("embd", [None, G.GGML_Q6_K])
+def test_restatement_matches_reference_decode(tmp_path, embd):
+    shape = G.LlamaShape(256, 2, 4, 2, 256, 300, ctx_train=64)
     path = str(tmp_path / "m.gguf")
-    G.write_llama(path, shape, G.GGML_Q4_0, seed=9)
+    G.write_llama(path, shape, G.GGML_Q4_0, seed=9, embd_qtype=embd)
     prompt = np.array([3, 1, 4, 1, 5, 9], np.int32)
     tr, _, _, lr = O.ref_greedy(path, prompt, 8, n_ctx=32, want_logits=shape.n_vocab)
     om = O.OracleModel(G.GGUFFile(path), n_ctx=32)
