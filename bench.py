@@ -456,7 +456,7 @@ def run_matvec_case(args):
     qname, k, n = parts[:3]
     k, n = int(k), int(n)
     m = int(parts[3]) if len(parts) > 3 else 1
-    qtype = {"q8_0": G.GGML_Q8_0, "q4_0": G.GGML_Q4_0}[qname]
+    qtype = {"q8_0": G.GGML_Q8_0, "q4_0": G.GGML_Q4_0, "q6_K": G.GGML_Q6_K}[qname]
     blk, _ = W.matvec_inputs(qtype, k, n, seed=1)
     wbytes = blk.nbytes
     copies = max(2, -(-2 * 126 * 2 ** 20 // wbytes))

@@ -25,6 +25,7 @@
 #include "qmv.cuh"
 #include "qmv1.cuh"
 #include "qmvm.cuh"
+#include "q6k.cuh"
 #include "qmm_tc.cuh"
 #include "ref_abi.h"
 
@@ -496,10 +497,66 @@ unsigned qmvm_chunk(unsigned left, uint32_t nb)
 
 // One launch per quant type present among ids (the M = 1 kernel takes one
 // type a launch; a decode's groups are always a single type).
+// q6_K: q6k_kernel, one launch a tensor, a warp for 16 rows at a time.
+int launch_q6k(charsiu_gpu *g, const Ent &e, float *y, const int8_t *q, const float *d,
+	       cudaStream_t st)
+{
+	Q6kParams p;
+	p.w = e.data;
+	p.y = y;
+	p.rows = (uint32_t)e.rows;
+	p.nsb = (uint32_t)(e.k / 256);
+	p.q = q;
+	p.d = d;
+	if (!p.rows)
+		return 0;
+	const size_t smem = q6k_smem_bytes(p.nsb);
+	const int slot = 18;
+	if (!g->smem_set[slot]) {
+		if (cudaFuncSetAttribute((const void *)q6k_kernel,
+					 cudaFuncAttributeMaxDynamicSharedMemorySize,
+					 (int)QMV_SMEM_MAX) != cudaSuccess)
+			return -1;
+		g->smem_set[slot] = true;
+	}
+	int occ = 0;
+	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, q6k_kernel, Q6K_WARPS * 32, smem) !=
+		    cudaSuccess || occ < 1)
+		return -1;
+	// rows a warp: enough that the resident warps cover the tensor in one
+	// pass, at most Q6K_ROWS
+	const unsigned warps = (unsigned)occ * g->sm_count * Q6K_WARPS;
+	unsigned rpw = (p.rows + warps - 1) / warps;
+	rpw = rpw < 1 ? 1 : rpw > (unsigned)Q6K_ROWS ? (unsigned)Q6K_ROWS : rpw;
+	p.rows_per_warp = rpw;
+	unsigned grid = (unsigned)occ * g->sm_count;
+	const unsigned need = (p.rows + Q6K_WARPS * rpw - 1) / (Q6K_WARPS * rpw);
+	if (need < grid)
+		grid = need;
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = dim3(grid);
+	cfg.blockDim = dim3(Q6K_WARPS * 32);
+	cfg.dynamicSmemBytes = smem;
+	cfg.stream = st;
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = attr;
+	cfg.numAttrs = g->no_pdl ? 0 : 1;
+	void *args[1] = {&p};
+	if (cudaLaunchKernelExC(&cfg, (const void *)q6k_kernel, args) != cudaSuccess)
+		return -1;
+	g->launches++;
+	return 0;
+}
+
 int launch_matvec1(charsiu_gpu *g, const int *ids, unsigned n, float *const *ys, uint32_t k,
 		   const int8_t *q, const float *d, cudaStream_t st)
 {
-	for (uint32_t type : {TYPE_Q8_0, TYPE_Q4_0}) {
+	for (unsigned i = 0; i < n; i++)
+		if (g->ent[ids[i]].type == TYPE_Q6_K && launch_q6k(g, g->ent[ids[i]], ys[i], q, d, st))
+			return -1;
+	for (uint32_t type : {TYPE_Q8_0, TYPE_Q4_0}) {    // q6_K: above
 		int sub[QMV_MAX_TENSORS];
 		float *sy[QMV_MAX_TENSORS];
 		unsigned ns = 0;
@@ -557,20 +614,38 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 			return launch_qmm(g, ids, n, dq, dd, m, yd, g->d_pack, g->stream);
 		}
 	}
-	for (unsigned m0 = 0, mc = 0; m0 < m; m0 += mc) {
-		mc = qmvm_chunk(m - m0, nb);
-		float *yd[QMV_MAX_TENSORS];
-		size_t off = 0;
-		for (unsigned i = 0; i < n; i++) {
-			yd[i] = g->d_y + off + (size_t)m0 * g->ent[ids[i]].rows;
-			off += (size_t)m * g->ent[ids[i]].rows;
+	// the CUDA cores: each quant type its own launches (a kernel takes one);
+	// q6_K one activation at a time
+	size_t base[QMV_MAX_TENSORS];
+	size_t off = 0;
+	for (unsigned i = 0; i < n; i++) {
+		base[i] = off;
+		off += (size_t)m * g->ent[ids[i]].rows;
+	}
+	for (uint32_t type : {TYPE_Q8_0, TYPE_Q4_0, TYPE_Q6_K}) {
+		int sub[QMV_MAX_TENSORS];
+		size_t sbase[QMV_MAX_TENSORS];
+		unsigned ns = 0;
+		for (unsigned i = 0; i < n; i++)
+			if (g->ent[ids[i]].type == type) {
+				sub[ns] = ids[i];
+				sbase[ns++] = base[i];
+			}
+		if (!ns)
+			continue;
+		for (unsigned m0 = 0, mc = 0; m0 < m; m0 += mc) {
+			mc = type == TYPE_Q6_K ? 1 : qmvm_chunk(m - m0, nb);
+			float *yd[QMV_MAX_TENSORS];
+			for (unsigned i = 0; i < ns; i++)
+				yd[i] = g->d_y + sbase[i] + (size_t)m0 * g->ent[sub[i]].rows;
+			QmvParams p;
+			fill_params(g, p, sub, ns, yd, k, dq + (size_t)m0 * nb * 32,
+				    dd + (size_t)m0 * nb);
+			const int rc = mc == 1 ? launch_matvec1(g, sub, ns, yd, k, p.q, p.d, g->stream)
+					       : launch_qmv(g, (int)mc, p, g->stream);
+			if (rc)
+				return -1;
 		}
-		QmvParams p;
-		fill_params(g, p, ids, n, yd, k, dq + (size_t)m0 * nb * 32, dd + (size_t)m0 * nb);
-		const int rc = mc == 1 ? launch_matvec1(g, ids, n, yd, k, p.q, p.d, g->stream)
-				       : launch_qmv(g, (int)mc, p, g->stream);
-		if (rc)
-			return -1;
 	}
 	return 0;
 }
@@ -719,7 +794,8 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	}
 
 	const double t0 = now_us();
-	if (g->direct && m == 1 && (size_t)nb * 36 <= sizeof(g->inl->act)) {
+	if (g->direct && m == 1 && (size_t)nb * 36 <= sizeof(g->inl->act) &&
+	    g->ent[ids[0]].type != TYPE_Q6_K) {
 		bool one_type = true;
 		for (unsigned i = 1; i < n; i++)
 			one_type = one_type && g->ent[ids[i]].type == g->ent[ids[0]].type;
@@ -958,13 +1034,14 @@ int charsiu_gpu_add_blocks(struct charsiu_gpu *g, uint32_t type, uint64_t k, uin
 		whine(g, "the GPU path is already retired");
 		return -1;
 	}
-	if (type != TYPE_Q8_0 && type != TYPE_Q4_0) {
-		whine(g, "type %u is not q8_0 or q4_0 (%s)", type, name ? name : "?");
+	if (type != TYPE_Q8_0 && type != TYPE_Q4_0 && type != TYPE_Q6_K) {
+		whine(g, "type %u is not q8_0, q4_0 or q6_K (%s)", type, name ? name : "?");
 		return -1;
 	}
-	if (!blocks || !k || k % 32 || !n || k > g->max_k) {
-		whine(g, "K=%llu is not a multiple of 32 within the opened maximum (%s)",
-		      (unsigned long long)k, name ? name : "?");
+	const uint32_t kunit = type == TYPE_Q6_K ? 256 : 32;
+	if (!blocks || !k || k % kunit || !n || k > g->max_k) {
+		whine(g, "K=%llu is not a multiple of %u within the opened maximum (%s)",
+		      (unsigned long long)k, kunit, name ? name : "?");
 		return -1;
 	}
 	if (n > g->max_n) {
@@ -993,8 +1070,10 @@ int charsiu_gpu_add_blocks(struct charsiu_gpu *g, uint32_t type, uint64_t k, uin
 	const uint64_t rend = g1 * RG < n ? g1 * RG : n;
 	e.rows = rend > e.row0 ? rend - e.row0 : 0;
 	e.groups = (uint32_t)((e.rows + RG - 1) / RG);
-	e.bytes = (size_t)e.groups * group_bytes(type, e.nb);
-	const uint64_t rb = (uint64_t)e.nb * (quant_bytes(type) + 2);
+	const bool q6 = type == TYPE_Q6_K;
+	const uint32_t nsb = (uint32_t)(k / 256);
+	e.bytes = q6 ? (size_t)e.rows * q6k_row_bytes(nsb) : (size_t)e.groups * group_bytes(type, e.nb);
+	const uint64_t rb = q6 ? (uint64_t)nsb * 210 : (uint64_t)e.nb * (quant_bytes(type) + 2);
 	e.weight_mb = (double)e.rows * rb / 1e6;
 
 	if (injected(g, 3) || (e.bytes && cudaMalloc(&e.data, e.bytes) != cudaSuccess)) {
@@ -1014,9 +1093,15 @@ int charsiu_gpu_add_blocks(struct charsiu_gpu *g, uint32_t type, uint64_t k, uin
 			const uint64_t nr = e.rows - r0 < cr ? e.rows - r0 : cr;
 			ok = cudaMemcpyAsync(stage, src + r0 * rb, nr * rb, cudaMemcpyHostToDevice,
 					     g->stream) == cudaSuccess;
-			const uint64_t thr = nr * e.nb;
-			repack_kernel<<<(unsigned)((thr + 255) / 256), 256, 0, g->stream>>>(
-				stage, type, e.nb, (uint32_t)r0, (uint32_t)nr, e.data);
+			if (q6) {
+				const uint64_t thr = nr * nsb;
+				q6k_repack_kernel<<<(unsigned)((thr + 255) / 256), 256, 0, g->stream>>>(
+					stage, nsb, (uint32_t)nr, e.data + r0 * q6k_row_bytes(nsb));
+			} else {
+				const uint64_t thr = nr * e.nb;
+				repack_kernel<<<(unsigned)((thr + 255) / 256), 256, 0, g->stream>>>(
+					stage, type, e.nb, (uint32_t)r0, (uint32_t)nr, e.data);
+			}
 			ok = ok && cudaGetLastError() == cudaSuccess &&
 			     cudaStreamSynchronize(g->stream) == cudaSuccess;
 		}
@@ -1134,7 +1219,7 @@ int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, unsigned m, cons
 		return launch_qmm(g, &id, 1, q, d, m, &y, g->d_pack, st);
 	}
 	for (unsigned m0 = 0; m0 < m;) {
-		const unsigned mc = qmvm_chunk(m - m0, nb);
+		const unsigned mc = e.type == TYPE_Q6_K ? 1 : qmvm_chunk(m - m0, nb);
 		float *yd[1] = {y + (size_t)m0 * e.rows};
 		QmvParams p;
 		fill_params(g, p, &id, 1, yd, (uint32_t)e.k, q + (size_t)m0 * nb * 32,
@@ -1275,7 +1360,7 @@ int charsiu_gpu_matvec_gather_dev(struct charsiu_gpu *g, const int *ids, unsigne
 		if (ids[i] < 0 || (size_t)ids[i] >= g->ent.size())
 			return -1;
 		const Ent &e = g->ent[ids[i]];
-		if (i && (e.k != k || e.type != g->ent[ids[0]].type))
+		if ((i && (e.k != k || e.type != g->ent[ids[0]].type)) || e.type == TYPE_Q6_K)
 			return -1;
 		k = (uint32_t)e.k;
 	}
@@ -1520,6 +1605,10 @@ int charsiu_gpu_block_dots(struct charsiu_gpu *g, int id, const int8_t *q, int32
 		return -1;
 	cudaSetDevice(g->device);
 	const Ent &e = g->ent[id];
+	if (e.type == TYPE_Q6_K) {
+		whine(g, "block dots are of 32-element blocks: q8_0 and q4_0 only (%s)", e.name);
+		return -1;
+	}
 	const size_t cnt = (size_t)e.rows * e.nb;
 	if (!grow_dev(g->d_q, g->cap_dq, (size_t)e.nb * 32) ||
 	    !grow_dev(g->d_dots, g->cap_dots, cnt ? cnt : 1))

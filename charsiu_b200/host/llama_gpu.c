@@ -26,7 +26,7 @@
 
 #define API
 
-enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8 };
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q6_K = 14 };
 
 /* ---- a GGUF v2/v3 reader (the format src/gguf.c:207-358 reads) ----------- */
 
@@ -125,6 +125,7 @@ static uint64_t tensor_bytes(uint32_t type, const uint64_t ne[4])
 	case T_F16: return n * 2;
 	case T_Q8_0: return n / 32 * 34;
 	case T_Q4_0: return n / 32 * 18;
+	case T_Q6_K: return n / 256 * 210;
 	default: return 0;
 	}
 }
@@ -401,6 +402,29 @@ static int row_f32(const struct gt *t, uint64_t row, float *dst)
 			for (int j = 0; j < 16; j++) {
 				dst[b * 32 + j] = d * (float)((p[2 + j] & 0x0f) - 8);
 				dst[b * 32 + j + 16] = d * (float)((p[2 + j] >> 4) - 8);
+			}
+		}
+		return 0;
+	case T_Q6_K:
+		/* deq_q6_K (src/gguf.c:457-479): (d * scale) * q, q the 6-bit
+		 * weight minus 32 from a nibble of ql and two bits of qh */
+		p = t->data + row * (k / 256 * 210);
+		for (uint64_t i = 0; i < k / 256; i++, p += 210) {
+			float d = half_to_float((uint16_t)(p[208] | p[209] << 8));
+
+			for (unsigned h = 0; h < 2; h++) {
+				const uint8_t *ql = p + h * 64, *qh = p + 128 + h * 32;
+				const int8_t *sc = (const int8_t *)(p + 192) + h * 8;
+				float *y = dst + i * 256 + h * 128;
+
+				for (unsigned l = 0; l < 32; l++)
+					for (unsigned r = 0; r < 4; r++) {
+						unsigned lo = (r & 1) ? ql[l + 32] : ql[l];
+						int q = (int)(((r & 2) ? lo >> 4 : lo & 0x0f) |
+							      (((qh[l] >> (2 * r)) & 3u) << 4)) - 32;
+
+						y[r * 32 + l] = d * (float)sc[l / 16 + 2 * r] * (float)q;
+					}
 			}
 		}
 		return 0;

@@ -71,13 +71,15 @@ CHARSIU_GPU_API void charsiu_gpu_close(struct charsiu_gpu *g);
 /* ---- weights ------------------------------------------------------------- */
 
 /* charsiu_npu_add (include/charsiu_llm.h:191, src/npudev.c:389-461), for the
- * GGUF tensor: q8_0 or q4_0, ne[0] = K a multiple of 32, ne[1] = N. The host
+ * GGUF tensor: q8_0 or q4_0 with ne[0] = K a multiple of 32, or q6_K (the
+ * head of a llama.cpp q4_0 file) with K a multiple of 256; ne[1] = N. The host
  * tensor stays the caller's. Returns an id >= 0, or -1 (tensor stays on the
  * CPU). Adding the same tensor again returns its existing id. */
 CHARSIU_GPU_API int charsiu_gpu_add(struct charsiu_gpu *g, const struct gguf_tensor *w);
 
-/* Flat form of charsiu_gpu_add: `blocks` is N rows of K/32 GGML blocks
- * (34 bytes q8_0, 18 bytes q4_0), row major, as in a GGUF file. */
+/* Flat form of charsiu_gpu_add: `blocks` is N rows of GGML blocks (34 bytes
+ * a 32-weight q8_0 block, 18 q4_0, 210 a 256-weight q6_K super-block), row
+ * major, as in a GGUF file. */
 CHARSIU_GPU_API int charsiu_gpu_add_blocks(struct charsiu_gpu *g, uint32_t type, uint64_t k,
 			   uint64_t n, const void *blocks, const char *name);
 

@@ -51,7 +51,8 @@ int orc_matvec(uint32_t type, const void *blocks, uint64_t k, const int8_t *q,
 int orc_block_dots(uint32_t type, const void *blocks, uint64_t k, uint64_t n,
 		   const int8_t *q, int32_t *dots);
 
-/* src/gguf.c:1217-1256: one row dequantised to fp32 (f32, q8_0, q4_0). */
+/* src/gguf.c:1217-1278: one row dequantised to fp32 (f32, f16, q8_0, q4_0,
+ * q6_K). */
 int orc_row_f32(uint32_t type, const void *data, uint64_t k, uint64_t row,
 		float *dst);
 

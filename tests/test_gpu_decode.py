@@ -39,11 +39,14 @@ def oracle_step_logits(om, prompt, tokens):
     return np.stack(out)
 
 
-@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4"])
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4", "tiny_q4_q6k"])
 def test_tiny_models(name, tmp_path):
+    """tiny_q4_q6k is a q4_0 file as llama.cpp writes one: its token_embd, and
+    so the tied head, is q6_K (the embedding row and the head both exact)."""
     spec, gold = W.DECODE[name], GOLD[name]
     path = str(tmp_path / f"{name}.gguf")
-    G.write_llama(path, spec["shape"], spec["qtype"], spec["seed"])
+    G.write_llama(path, spec["shape"], spec["qtype"], spec["seed"],
+                  embd_qtype=spec.get("embd_qtype"))
     prompt = np.array(gold["prompt"], np.int32)
     with Llama(path, n_ctx=spec["n_ctx"]) as m:
         toks, logits, _ = m.greedy(prompt, spec["n_gen"], want_logits=True)
