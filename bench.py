@@ -334,7 +334,8 @@ def run_ours(args, rank, world, dist):
             fused["error"] = str(e)[:200]
         split["fused"] = fused
 
-    e2e = run_e2e(path, args, lib, world, dist, dev)
+    e2e = run_e2e_resident(path, args, world, dist, dev)
+    e2e["host_routed"] = run_e2e(path, args, lib, world, dist, dev)
 
     out = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
@@ -420,6 +421,51 @@ def run_e2e(path, args, lib, world=1, dist=None, dev=None):
             "stages_ms_per_step": stages,
             "api": "charsiu_gpu_llama_forward (C ABI, host buffers), positions "
                    f"{len(prompt) + n_warm}..{len(prompt) + n_warm + n_gen_timed - 1}"}
+
+
+def golden_match(toks) -> bool:
+    """The timed run's greedy tokens against the reference's (the committed
+    fixture: charsiu_run on this model), over the tokens both have."""
+    with open(os.path.join(ROOT, "tests", "golden", "golden_decode.json")) as f:
+        gold = json.load(f)["llama1b_q8"]["tokens"]
+    n = min(len(gold), len(toks))
+    return bool(n) and [int(t) for t in toks[:n]] == gold[:n]
+
+
+def run_e2e_resident(path, args, world=1, dist=None, dev=None):
+    """The greedy decode through the public C ABI with the whole step on the
+    device (charsiu_gpu_llama_set_resident + charsiu_gpu_llama_greedy): each
+    timed step copies its token and position in from pinned host memory and
+    its argmax token back, and replays one CUDA graph. At N GPUs every rank
+    decodes its own stream; the rate is the sum over ranks, from the slowest
+    rank's time."""
+    from charsiu_b200.lib import Llama
+
+    n_gen_timed = max(1, min(args.steps, 500))
+    n_warm = max(3, min(args.warmup, 8))
+    prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
+    n_ctx = len(prompt) + max(n_gen_timed, n_warm) + 1
+    if world > 1:
+        dist.barrier()
+    with Llama(path, n_ctx=n_ctx, device=dev.index if dev is not None else 0,
+               resident=True) as m:
+        m.greedy(prompt, n_warm)            # builds and captures the step's graphs
+        toks, _, gen_ms = m.greedy(prompt, n_gen_timed)
+        launches = m.step_launches
+    dt = gen_ms / 1e3
+    if world > 1:
+        import torch
+        t = torch.tensor([dt], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    return {"value": round(world * n_gen_timed / dt, 2), "unit": UNIT,
+            "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4, "steps": n_gen_timed,
+            "warmup": n_warm, "ms_per_step": round(dt * 1e3 / n_gen_timed, 4),
+            "kernels_per_step": launches,
+            "tokens_match_reference": golden_match(toks),
+            "api": "charsiu_gpu_llama_greedy after charsiu_gpu_llama_set_resident(1) (C ABI): "
+                   "token + position in (pinned host -> device), argmax token out, one CUDA "
+                   f"graph a token; positions {len(prompt)}..{len(prompt) + n_gen_timed - 1}"}
 
 
 def cpu_baseline(path):

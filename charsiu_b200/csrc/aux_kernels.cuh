@@ -31,6 +31,55 @@ __global__ void repack_kernel(const uint8_t *__restrict__ raw, uint32_t type, ui
 	dd[1] = src[1];
 }
 
+// gguf_row_f32 of one row (reference src/gguf.c:1217-1256) read back out of
+// the device layout: q8_0 d * q, q4_0 d * (nibble - 8), q6_K (d * scale) * q
+// (deq_q6_K, src/gguf.c:457-479). The row index is read from device memory
+// (*row); an index outside [0, rows) writes 1 to *err and leaves out alone.
+// One thread an element.
+__global__ void row_f32_kernel(const uint8_t *__restrict__ data, uint32_t type, uint64_t k,
+			       uint32_t rows, const int32_t *__restrict__ row,
+			       float *__restrict__ out, int *__restrict__ err)
+{
+	pdl_wait();
+	const int32_t r = *row;
+	const uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+	if (r < 0 || (uint32_t)r >= rows) {
+		if (e == 0)
+			*err = 1;
+		return;
+	}
+	if (e >= k)
+		return;
+	if (type == TYPE_Q6_K) {
+		const uint32_t nsb = (uint32_t)(k / 256), i = (uint32_t)(e / 256), w = (uint32_t)(e % 256);
+		const uint8_t *wr = data + (uint64_t)r * q6k_row_bytes(nsb);
+		const uint8_t *sb = wr + (size_t)i * 208;
+		const uint32_t h = w / 128, kk = (w % 128) / 32, l = w % 32;
+		const uint8_t lo = sb[h * 64 + (kk & 1) * 32 + l];
+		const uint32_t nib = (kk & 2) ? lo >> 4 : lo & 0x0fu;
+		const int q = (int)(nib | ((sb[128 + h * 32 + l] >> (2 * kk)) & 3u) << 4) - 32;
+		const int8_t sc = (int8_t)sb[192 + h * 8 + l / 16 + 2 * kk];
+		const uint16_t db = (uint16_t)(wr[(size_t)nsb * 208 + 2 * i] |
+					       wr[(size_t)nsb * 208 + 2 * i + 1] << 8);
+		out[e] = __fmul_rn(__fmul_rn(half_bits_to_float(db), (float)sc), (float)q);
+		return;
+	}
+	const uint32_t nb = (uint32_t)(k / 32), b = (uint32_t)(e / 32), j = (uint32_t)(e % 32);
+	const uint32_t g = (uint32_t)r / RG, rr = (uint32_t)r % RG;
+	const uint32_t seg = b / SB, bi = b % SB, sbn = seg_blocks(nb, seg), qb = quant_bytes(type);
+	const uint8_t *segp = data + (uint64_t)g * group_bytes(type, nb) + seg_offset(type, seg);
+	const uint8_t *dp = segp + (uint64_t)sbn * RG * qb + ((uint64_t)bi * RG + rr) * 2;
+	const float dd = half_bits_to_float((uint16_t)(dp[0] | dp[1] << 8));
+	int q;
+	if (type == TYPE_Q8_0) {
+		q = (int8_t)segp[quant_offset(type, bi, j / 16, rr) + j % 16];
+	} else {
+		const uint8_t byte = segp[quant_offset(type, bi, 0, rr) + j % 16];
+		q = (int)(j < 16 ? byte & 0x0f : byte >> 4) - 8;
+	}
+	out[e] = __fmul_rn(dd, (float)q);
+}
+
 // The integer block dots of rows [0, rows), read back out of the layout: the
 // test hook that pins both the repack and the dot against dotq_*'s t.
 __global__ void block_dots_kernel(const uint8_t *__restrict__ data, uint32_t type,

@@ -879,6 +879,43 @@ int run_matvec(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 
 } // namespace
 
+// ---- what the decode step (decoder.cu) asks of the layer ------------------------
+
+namespace cgpu {
+
+int layer_device(const charsiu_gpu *g)
+{
+	return g->device;
+}
+
+bool layer_no_pdl(const charsiu_gpu *g)
+{
+	return g->no_pdl != 0;
+}
+
+bool layer_whole(const charsiu_gpu *g)
+{
+	return g->world == 1;
+}
+
+// K, rows and quant type of tensor id; false for an unknown id
+bool layer_tensor(const charsiu_gpu *g, int id, uint64_t *k, uint64_t *rows, uint32_t *type)
+{
+	if (id < 0 || (size_t)id >= g->ent.size())
+		return false;
+	*k = g->ent[id].k;
+	*rows = g->ent[id].rows;
+	*type = g->ent[id].type;
+	return true;
+}
+
+void layer_whine(charsiu_gpu *g, const char *why)
+{
+	whine(g, "%s", why);
+}
+
+} // namespace cgpu
+
 // ---- scratch for charsiu_gpu_matvec_batch_noalloc -----------------------------
 //
 // For callers that cannot allocate device memory while they run, the batched
@@ -1441,6 +1478,33 @@ int charsiu_gpu_act_quantise_dev(struct charsiu_gpu *g, const float *x, unsigned
 	act_quantise_kernel<<<(unsigned)((threads + 255) / 256), 256, 0,
 			      stream ? (cudaStream_t)stream : g->stream>>>(x, m, k, nb, q, d);
 	if (cudaGetLastError() != cudaSuccess)
+		return -1;
+	g->launches++;
+	return 0;
+}
+
+int charsiu_gpu_row_dev(struct charsiu_gpu *g, int id, const int32_t *row, float *out,
+			void *stream)
+{
+	if (!g || g->dead || !row || !out || id < 0 || (size_t)id >= g->ent.size())
+		return -1;
+	const Ent &e = g->ent[id];
+	if (e.row0 != 0 || e.rows != e.n) {
+		whine(g, "%s is split over GPUs; a row lookup needs all of it", e.name);
+		return -1;
+	}
+	cudaSetDevice(g->device);
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = dim3((unsigned)((e.k + 255) / 256));
+	cfg.blockDim = dim3(256);
+	cfg.stream = stream ? (cudaStream_t)stream : g->stream;
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = attr;
+	cfg.numAttrs = g->no_pdl ? 0 : 1;
+	if (cudaLaunchKernelEx(&cfg, row_f32_kernel, (const uint8_t *)e.data, e.type, (uint64_t)e.k,
+			       (uint32_t)e.rows, row, out, g->d_err) != cudaSuccess)
 		return -1;
 	g->launches++;
 	return 0;

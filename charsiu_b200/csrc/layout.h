@@ -73,4 +73,14 @@ __host__ __device__ constexpr uint32_t quant_offset(uint32_t type, uint32_t bi, 
 	return bi * RG * quant_bytes(type) + c * RG * 16 + r * 16;
 }
 
+// q6_K (256-weight super-blocks of 210 bytes) has a layout of its own: a row
+// is its super-blocks' first 208 bytes (ql[128], qh[64], int8 scales[16]) back
+// to back, then their fp16 d's, padded to 16 bytes; rows back to back.
+constexpr uint32_t TYPE_Q6_K = 14;
+
+__host__ __device__ inline uint64_t q6k_row_bytes(uint32_t nsb)
+{
+	return (uint64_t)nsb * 208 + ((nsb * 2u + 15u) & ~15u);
+}
+
 } // namespace cgpu

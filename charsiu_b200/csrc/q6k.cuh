@@ -35,18 +35,12 @@
 
 namespace cgpu {
 
-constexpr uint32_t TYPE_Q6_K = 14;
 constexpr int Q6K_WARPS = 8;
 // rows a warp sums side by side (lane r: row r). Measured on the 2048 x 128256
 // head: 1 (a lane-0 sum) 74 us, 4 70 us, 8 66 us, 16 92 us (its term buffers
 // cost occupancy).
 constexpr int Q6K_ROWS = 8;
 constexpr int Q6K_TSTRIDE = 129;      // floats a row of the term buffer: 128 + 1 (banks)
-
-__host__ __device__ inline uint64_t q6k_row_bytes(uint32_t nsb)
-{
-	return (uint64_t)nsb * 208 + ((nsb * 2u + 15u) & ~15u);
-}
 
 // GGUF rows (210-byte super-blocks) -> the device layout; one thread a
 // super-block. Load time only.

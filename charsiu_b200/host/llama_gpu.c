@@ -349,6 +349,8 @@ struct charsiu_gpu_llama {
 	int8_t *aq;
 	float *ad;
 	struct pool *pool;        /* attention heads and SiLU chunks; NULL = this thread */
+	struct charsiu_gpu_decoder *dec;   /* the whole step on the device, when resident */
+	int resident;
 };
 
 static float half_to_float(uint16_t h)
@@ -560,6 +562,71 @@ static void rope(float *v, uint32_t nheads, uint32_t hd, const float *cs)
 	}
 }
 
+/* Build the device-resident step (charsiu_gpu_decoder_*) of this model: the
+ * projections already on the layer, the embedding (the head's copy when it is
+ * tied, else its own), the norm weights, and RoPE's (cos, sin) for every
+ * position, computed here with the same calls as rope_angles. */
+static struct charsiu_gpu_decoder *make_decoder(struct charsiu_gpu_llama *m)
+{
+	struct charsiu_gpu_decoder_desc d;
+	struct charsiu_gpu_decoder *dec = NULL;
+	int *ids = malloc((size_t)m->n_layer * P_N * sizeof(int));
+	const float **an = malloc(m->n_layer * sizeof(*an)), **fn = malloc(m->n_layer * sizeof(*fn));
+	float *cs = malloc((size_t)m->n_ctx * m->hd * sizeof(float));
+	int embd_id = m->out_id;
+
+	if (!ids || !an || !fn || !cs)
+		goto out;
+	if (m->tok != m->out) {
+		embd_id = charsiu_gpu_add_blocks(m->dev, m->tok->type, m->tok->ne[0], m->tok->ne[1],
+						 m->tok->data, m->tok->name);
+		if (embd_id < 0)
+			goto out;
+	}
+	for (uint32_t l = 0; l < m->n_layer; l++) {
+		for (int p = 0; p < P_N; p++)
+			ids[l * P_N + p] = m->L[l].id[p];
+		an[l] = m->L[l].attn_norm;
+		fn[l] = m->L[l].ffn_norm;
+	}
+	for (int pos = 0; pos < m->n_ctx; pos++)
+		rope_angles(cs + (size_t)pos * m->hd, m->hd, pos, m->base);
+	memset(&d, 0, sizeof(d));
+	d.n_embd = m->n_embd;
+	d.n_layer = m->n_layer;
+	d.n_head = m->n_head;
+	d.n_head_kv = m->n_head_kv;
+	d.n_ff = m->n_ff;
+	d.head_dim = m->hd;
+	d.n_vocab = m->n_vocab;
+	d.n_ctx = (uint32_t)m->n_ctx;
+	d.rms_eps = m->eps;
+	d.embd_id = embd_id;
+	d.head_id = m->out_id;
+	d.proj_ids = ids;
+	d.attn_norm = an;
+	d.ffn_norm = fn;
+	d.out_norm = m->out_norm;
+	d.rope_cs = cs;
+	dec = charsiu_gpu_decoder_new(m->dev, &d);
+out:
+	free(ids);
+	free(an);
+	free(fn);
+	free(cs);
+	return dec;
+}
+
+API int charsiu_gpu_llama_set_resident(struct charsiu_gpu_llama *m, int on)
+{
+	if (!m)
+		return -1;
+	if (on && !m->dec && !(m->dec = make_decoder(m)))
+		return -1;
+	m->resident = on != 0;
+	return 0;
+}
+
 /* quantise x once, then every projection of it as one group call (or one at
  * a time under CHARSIU_GPU_NOGROUP, the control) */
 static int project(struct charsiu_gpu_llama *m, const float *x, uint32_t k, const int *ids,
@@ -590,6 +657,7 @@ API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m)
 				m->stage_ms[i] / m->stage_tok, 100.0 * m->stage_ms[i] / tot);
 	}
 	pool_free(m->pool);
+	charsiu_gpu_decoder_free(m->dec);
 	if (m->dev && getenv("CHARSIU_GPU_REPORT"))
 		charsiu_gpu_report(m->dev);
 	charsiu_gpu_close(m->dev);
@@ -723,6 +791,12 @@ API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *path, int n_ctx
 
 		m->pool = pool_new(threads);
 	}
+	{
+		const char *e = getenv("CHARSIU_GPU_RESIDENT");
+
+		if (e && atoi(e) && charsiu_gpu_llama_set_resident(m, 1))
+			goto fail;
+	}
 	return m;
 fail:
 	charsiu_gpu_llama_close(m);
@@ -826,6 +900,11 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 
 	if (pos < 0 || pos >= m->n_ctx || token < 0 || (uint32_t)token >= m->tok->ne[1])
 		return NULL;
+	if (m->resident) {
+		if (charsiu_gpu_decoder_step(m->dec, token, pos, 1, NULL))
+			return NULL;
+		return charsiu_gpu_decoder_logits(m->dec);
+	}
 	if (row_f32(m->tok, (uint64_t)token, m->x))
 		return NULL;
 	rope_angles(m->rope_cs, hd, pos, m->base);
@@ -938,6 +1017,34 @@ API int32_t charsiu_gpu_llama_argmax(const float *logits, uint32_t n)
 	return best;
 }
 
+/* charsiu_gpu_llama_greedy on the resident step: the argmax comes back with
+ * each step, the logits only when the caller keeps them */
+static int greedy_resident(struct charsiu_gpu_llama *m, const int32_t *prompt, int n_prompt,
+			   int n_gen, int32_t *out, float *logits, double *gen_ms)
+{
+	int pos = 0;
+	int32_t next = 0;
+	double t0;
+
+	for (int i = 0; i < n_prompt; i++)
+		if (charsiu_gpu_decoder_step(m->dec, prompt[i], pos++,
+					     logits && i == n_prompt - 1, &next))
+			return -1;
+	t0 = now_ms();
+	for (int i = 0; i < n_gen; i++) {
+		out[i] = next;
+		if (logits)
+			memcpy(logits + (size_t)i * m->n_vocab, charsiu_gpu_decoder_logits(m->dec),
+			       (size_t)m->n_vocab * sizeof(float));
+		/* as charsiu_run: every generated token is fed back */
+		if (charsiu_gpu_decoder_step(m->dec, out[i], pos++, logits && i + 1 < n_gen, &next))
+			return -1;
+	}
+	if (gen_ms)
+		*gen_ms = now_ms() - t0;
+	return n_gen;
+}
+
 API int charsiu_gpu_llama_greedy(struct charsiu_gpu_llama *m, const int32_t *prompt,
 				 int n_prompt, int n_gen, int32_t *out, float *logits,
 				 double *gen_ms)
@@ -948,6 +1055,8 @@ API int charsiu_gpu_llama_greedy(struct charsiu_gpu_llama *m, const int32_t *pro
 
 	if (!m || n_prompt < 1 || n_gen < 0 || n_prompt + n_gen > m->n_ctx)
 		return -1;
+	if (m->resident)
+		return greedy_resident(m, prompt, n_prompt, n_gen, out, logits, gen_ms);
 	for (int i = 0; i < n_prompt; i++)
 		if (!(lg = charsiu_gpu_llama_forward(m, prompt[i], pos++)))
 			return -1;
@@ -973,4 +1082,9 @@ API uint32_t charsiu_gpu_llama_vocab(const struct charsiu_gpu_llama *m)
 API struct charsiu_gpu *charsiu_gpu_llama_layer(struct charsiu_gpu_llama *m)
 {
 	return m ? m->dev : NULL;
+}
+
+API struct charsiu_gpu_decoder *charsiu_gpu_llama_decoder(struct charsiu_gpu_llama *m)
+{
+	return m ? m->dec : NULL;
 }

@@ -71,6 +71,14 @@ SIGNATURES = [
     ("charsiu_gpu_llama_stage_name", C.c_char_p, [C.c_int]),
     ("charsiu_gpu_llama_vocab", C.c_uint32, [_vp]),
     ("charsiu_gpu_llama_layer", _vp, [_vp]),
+    ("charsiu_gpu_llama_set_resident", C.c_int, [_vp, C.c_int]),
+    ("charsiu_gpu_llama_decoder", _vp, [_vp]),
+    ("charsiu_gpu_row_dev", C.c_int, [_vp, C.c_int, _vp, _vp, _vp]),
+    ("charsiu_gpu_decoder_new", _vp, [_vp, _vp]),
+    ("charsiu_gpu_decoder_free", None, [_vp]),
+    ("charsiu_gpu_decoder_step", C.c_int, [_vp, C.c_int32, C.c_int, C.c_int, _vp]),
+    ("charsiu_gpu_decoder_logits", C.POINTER(C.c_float), [_vp]),
+    ("charsiu_gpu_decoder_launches", C.c_uint, [_vp]),
 ]
 
 
@@ -284,6 +292,10 @@ class Layer:
         return self.L.charsiu_gpu_matvec_batch_noalloc(self.h, tid, m, q_ptr, d_ptr, y_ptr,
                                                        stream or None)
 
+    def row_dev(self, tid: int, row_ptr: int, out_ptr: int, stream: int = 0) -> int:
+        """gguf_row_f32 of row *row_ptr (device int32) into out_ptr (device)."""
+        return self.L.charsiu_gpu_row_dev(self.h, tid, row_ptr, out_ptr, stream or None)
+
     def act_quantise_dev(self, x_ptr: int, m: int, k: int, q_ptr: int, d_ptr: int,
                          stream: int = 0) -> int:
         return self.L.charsiu_gpu_act_quantise_dev(self.h, x_ptr, m, k, q_ptr, d_ptr,
@@ -293,12 +305,24 @@ class Layer:
 class Llama:
     """charsiu_gpu_llama: the decode loop with every projection on the GPU."""
 
-    def __init__(self, path: str, n_ctx: int = 0, device: int = 0):
+    def __init__(self, path: str, n_ctx: int = 0, device: int = 0, resident: bool = False):
         self.L = lib()
         self.h = self.L.charsiu_gpu_llama_open(path.encode(), n_ctx, device)
         if not self.h:
             raise GpuError(f"charsiu_gpu_llama_open failed for {path}")
         self.n_vocab = self.L.charsiu_gpu_llama_vocab(self.h)
+        if resident:
+            try:
+                self.set_resident(True)
+            except GpuError:
+                self.close()
+                raise
+
+    def set_resident(self, on: bool = True):
+        """Every later forward on the device (charsiu_gpu_llama_set_resident)."""
+        if self.L.charsiu_gpu_llama_set_resident(self.h, int(on)):
+            msg = self.L.charsiu_gpu_error(self.layer_handle).decode()
+            raise GpuError(f"the device decode step would not build: {msg}")
 
     def close(self):
         if self.h:
@@ -314,6 +338,12 @@ class Llama:
     @property
     def layer_handle(self):
         return self.L.charsiu_gpu_llama_layer(self.h)
+
+    @property
+    def step_launches(self) -> int:
+        """Kernels one device-resident step launches (0 before it is built)."""
+        dec = self.L.charsiu_gpu_llama_decoder(self.h)
+        return self.L.charsiu_gpu_decoder_launches(dec) if dec else 0
 
     def report(self):
         self.L.charsiu_gpu_report(self.layer_handle)

@@ -219,6 +219,61 @@ CHARSIU_GPU_API int charsiu_gpu_act_quantise_dev(struct charsiu_gpu *g, const fl
 				 unsigned m, unsigned k, int8_t *q, float *d,
 				 void *stream);
 
+/* gguf_row_f32 (src/gguf.c:1217-1256) of one row of tensor id -- the
+ * embedding lookup -- from the layer's copy, bit-exact: out fp32 [K]. The row
+ * index is read from device memory (*row), so a captured graph can take a new
+ * token each replay; an index outside the tensor writes a nonzero code that
+ * charsiu_gpu_kernel_error returns. The whole tensor must be on this GPU
+ * (world 1). */
+CHARSIU_GPU_API int charsiu_gpu_row_dev(struct charsiu_gpu *g, int id, const int32_t *row,
+					float *out, void *stream);
+
+/* ---- the decode step on the device ------------------------------------------ */
+/*
+ * llama_forward (src/llama.c:743-856) with every step on the GPU: the
+ * embedding row, rmsnorm, the activation quantiser, the projections (this
+ * layer's matvecs), RoPE and the KV cache, attention, SiLU, the residual adds,
+ * the head and llama_argmax, replayed as one CUDA graph a token. The logits
+ * are the reference's bit for bit: every sum keeps the reference's order and
+ * rounding, and expf is a table of the host C library's own expf over every
+ * float where it is neither 1, 0 nor inf (2.2 GB of device memory, built once
+ * a process and GPU, checked against expf for every float it leaves out).
+ * No counterpart in the reference, which runs these steps on the CPU.
+ *
+ * The model: projection ids (tensors added to g) per layer in the order q, k,
+ * v, o, gate, up, down; the embedding and head ids (the same tensor when the
+ * head is tied); host fp32 norm weights, copied at creation; rope_cs the
+ * (cos, sin) pair i of every position, [n_ctx][head_dim], as
+ * src/llama.c:364-383 computes them. Requires n_head * head_dim = n_embd,
+ * head_dim a multiple of 32, n_embd and n_ff multiples of 32, n_embd at most
+ * 8192, and a layer opened with world 1.
+ */
+struct charsiu_gpu_decoder;
+
+struct charsiu_gpu_decoder_desc {
+	uint32_t n_embd, n_layer, n_head, n_head_kv, n_ff, head_dim, n_vocab, n_ctx;
+	float rms_eps;
+	int embd_id, head_id;
+	const int *proj_ids;               /* [n_layer][7] */
+	const float *const *attn_norm;     /* [n_layer] -> n_embd floats */
+	const float *const *ffn_norm;      /* [n_layer] -> n_embd floats */
+	const float *out_norm;             /* n_embd floats */
+	const float *rope_cs;              /* [n_ctx][head_dim] */
+};
+
+CHARSIU_GPU_API struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(
+	struct charsiu_gpu *g, const struct charsiu_gpu_decoder_desc *desc);
+CHARSIU_GPU_API void charsiu_gpu_decoder_free(struct charsiu_gpu_decoder *dec);
+/* One token at pos (positions run 0, 1, 2, ... as llama_forward's callers
+ * step them): *next gets llama_argmax of its logits; with want_logits the
+ * logits are also copied back, readable at charsiu_gpu_decoder_logits until
+ * the next step. 0 on success, -1 on failure (charsiu_gpu_error says why). */
+CHARSIU_GPU_API int charsiu_gpu_decoder_step(struct charsiu_gpu_decoder *dec, int32_t token,
+					     int pos, int want_logits, int32_t *next);
+CHARSIU_GPU_API const float *charsiu_gpu_decoder_logits(const struct charsiu_gpu_decoder *dec);
+/* kernels one step launches */
+CHARSIU_GPU_API unsigned charsiu_gpu_decoder_launches(const struct charsiu_gpu_decoder *dec);
+
 /* ---- accounting ----------------------------------------------------------- */
 
 /* charsiu_npu_submits (include/charsiu_llm.h:197): calls that ran. */

@@ -33,6 +33,16 @@ CHARSIU_GPU_API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *ggu
 						 int device);
 CHARSIU_GPU_API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m);
 
+/* Run every later forward on the device (on != 0: charsiu_gpu_decoder_*,
+ * include/charsiu_gpu.h -- the rmsnorm, RoPE, attention, SiLU, residuals and
+ * argmax as well as the projections, one CUDA graph a token, the same logits
+ * bit for bit) or with the CPU steps here (0, the default: the reference's
+ * loop with only its matvecs routed). The first switch on builds the device
+ * step, which keeps its own KV cache: switch before the first token. The
+ * environment variable CHARSIU_GPU_RESIDENT=1 switches on at open. 0 on
+ * success; -1 if the device step cannot be built (the mode is unchanged). */
+CHARSIU_GPU_API int charsiu_gpu_llama_set_resident(struct charsiu_gpu_llama *m, int on);
+
 /* llama_forward (include/charsiu_llm.h:307): one token at `pos`, the logits
  * out (n_vocab floats, valid until the next call). NULL on failure. */
 CHARSIU_GPU_API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t token, int pos);
@@ -58,6 +68,8 @@ CHARSIU_GPU_API const char *charsiu_gpu_llama_stage_name(int i);
 CHARSIU_GPU_API uint32_t charsiu_gpu_llama_vocab(const struct charsiu_gpu_llama *m);
 /* the device layer the model runs on (for its report and counters) */
 CHARSIU_GPU_API struct charsiu_gpu *charsiu_gpu_llama_layer(struct charsiu_gpu_llama *m);
+/* the device step, once charsiu_gpu_llama_set_resident has built it; else NULL */
+CHARSIU_GPU_API struct charsiu_gpu_decoder *charsiu_gpu_llama_decoder(struct charsiu_gpu_llama *m);
 
 #ifdef __cplusplus
 }

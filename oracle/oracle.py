@@ -59,6 +59,8 @@ def lib():
         L.orc_greedy.restype = C.c_int
         L.orc_argmax.argtypes = [C.POINTER(C.c_float), C.c_uint32]
         L.orc_argmax.restype = C.c_int32
+        L.orc_row_f32.argtypes = [C.c_uint32, C.c_void_p, C.c_uint64, C.c_uint64, _f32p]
+        L.orc_row_f32.restype = C.c_int
         _lib = L
     return _lib
 
@@ -111,6 +113,14 @@ def matvec(qtype: int, blocks: np.ndarray, k: int, n: int, q: np.ndarray, d: np.
                           y, 0, n)
     assert rc == 0
     return y
+
+
+def row_f32(qtype: int, blocks: np.ndarray, k: int, row: int) -> np.ndarray:
+    """gguf_row_f32 of one row (the embedding lookup)."""
+    out = np.empty(k, dtype=np.float32)
+    rc = lib().orc_row_f32(qtype, _ptr(blocks), k, row, out)
+    assert rc == 0, rc
+    return out
 
 
 def block_dots(qtype: int, blocks: np.ndarray, k: int, n: int, q: np.ndarray):
