@@ -736,6 +736,8 @@ def main():
                     help="time one batched decode step of M sequences instead")
     ap.add_argument("--int8", default=None, metavar="M:K:N",
                     help="time the int8 matmul with the NPU output stage (e.g. 224:64:64)")
+    ap.add_argument("--resident", action="store_true",
+                    help="time only the device-resident greedy decode (the e2e leg)")
     ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N[:M]",
                     help="time one matvec shape instead of the decode (e.g. q8_0:2048:8192; "
                          "q8_0:2048:8192:64 for 64 activations)")
@@ -764,6 +766,15 @@ def main():
             return
         if args.int8:
             print(json.dumps(run_int8_case(args)), flush=True)
+            return
+        if args.resident:
+            import torch
+            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+            torch.cuda.set_device(dev)
+            barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
+            out = run_e2e_resident(model_path(rank, barrier), args, world, dist, dev)
+            if rank == 0:
+                print(json.dumps(out), flush=True)
             return
         if args.impl == "reference":
             out = run_reference(args, rank, world, dist)

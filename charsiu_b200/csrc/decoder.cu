@@ -198,12 +198,13 @@ struct charsiu_gpu_decoder {
 	int8_t *aq = nullptr;
 	float *ad = nullptr;
 	int *io = nullptr;            // FWD_IO_WORDS (device)
+	float *part_v = nullptr;      // the argmax's per-CTA results
+	uint32_t *part_i = nullptr;
 	int *h_io = nullptr;          // pinned
 	float *h_logits = nullptr;    // pinned
 	cudaGraphExec_t exec[2] = {nullptr, nullptr};   // [want_logits]
 	bool warm[2] = {false, false};
 	unsigned launches = 0;        // kernels a step
-	bool attn_smem_set = false;
 };
 
 namespace {
@@ -236,8 +237,8 @@ bool launch(charsiu_gpu_decoder *dec, K kernel, unsigned grid, unsigned block, s
 
 bool norm_quant(charsiu_gpu_decoder *dec, const float *add, const float *w)
 {
-	return launch(dec, fwd_norm_quant_kernel, 1, FWD_NORM_THREADS, 0, dec->x, add, w,
-		      dec->n_embd, dec->eps, dec->aq, dec->ad);
+	return launch(dec, fwd_norm_quant_kernel, 1, FWD_NORM_THREADS, fwd_norm_smem(dec->n_embd),
+		      dec->x, add, w, dec->n_embd, dec->eps, dec->aq, dec->ad);
 }
 
 bool matvec(charsiu_gpu_decoder *dec, const int *ids, unsigned n, float *const *ys)
@@ -265,7 +266,6 @@ bool queue_step(charsiu_gpu_decoder *dec, bool want_logits)
 		dec->launches += (unsigned)(charsiu_gpu_launches(dec->g) - before);
 	}
 	const size_t attn_smem = fwd_attention_smem(dec->n_ctx, dec->hd);
-	const unsigned rope_threads = std::max((dec->n_head + dec->n_head_kv) * dec->hd / 2, kvdim);
 	for (uint32_t l = 0; l < dec->n_layer; l++) {
 		const int *id = dec->ids.data() + (size_t)l * P_N;
 		float *kc = dec->kc + l * layer_kv, *vc = dec->vc + l * layer_kv;
@@ -276,14 +276,12 @@ bool queue_step(charsiu_gpu_decoder *dec, bool want_logits)
 			if (!matvec(dec, id + P_Q, 3, ys))
 				return fail(dec, "the q, k, v matvec failed");
 		}
-		if (!launch(dec, fwd_rope_kv_kernel, (rope_threads + 255) / 256, 256, 0, dec->qv, dec->kv,
-			    (const float *)dec->vv, (const float *)dec->rope, (const int *)dec->io, kc, vc,
-			    dec->n_head, dec->n_head_kv, dec->hd))
-			return fail(dec, "a launch failed (rope)");
 		if (!launch(dec, fwd_attention_kernel, dec->n_head, FWD_ATTN_THREADS, attn_smem,
-			    (const float *)dec->qv, (const float *)kc, (const float *)vc,
-			    (const int *)dec->io, dec->n_head, dec->n_head_kv, dec->hd, dec->n_ctx,
-			    dec->scale, (const float *)dec->exptab, dec->aq, dec->ad))
+			    (const float *)dec->qv, (const float *)dec->kv, (const float *)dec->vv,
+			    (const float *)dec->rope, kc, vc, (const int *)dec->io, dec->n_head,
+			    dec->n_head_kv, dec->hd, dec->n_ctx, fwd_attention_tile(dec->hd), dec->scale,
+			    (const float *)dec->exptab,
+			    dec->aq, dec->ad))
 			return fail(dec, "a launch failed (attention)");
 		{
 			float *ys[1] = {dec->xb2};
@@ -314,8 +312,9 @@ bool queue_step(charsiu_gpu_decoder *dec, bool want_logits)
 		if (!matvec(dec, &dec->head_id, 1, ys))
 			return fail(dec, "the output head failed");
 	}
-	if (!launch(dec, fwd_argmax_kernel, 1, FWD_ARGMAX_THREADS, 0, (const float *)dec->logits,
-		    dec->n_vocab, dec->io))
+	if (!launch(dec, fwd_argmax_kernel, FWD_ARGMAX_CTAS, FWD_ARGMAX_THREADS, 0,
+		    (const float *)dec->logits, dec->n_vocab, dec->io,
+		    reinterpret_cast<uint32_t *>(dec->io + FWD_IO_TICKET), dec->part_v, dec->part_i))
 		return fail(dec, "a launch failed (argmax)");
 	if (cudaMemcpyAsync(dec->h_io + FWD_IO_NEXT, dec->io + FWD_IO_NEXT, sizeof(int),
 			    cudaMemcpyDeviceToHost, dec->st) != cudaSuccess)
@@ -336,7 +335,8 @@ void release(charsiu_gpu_decoder *dec)
 	for (void *p : {(void *)dec->norm, (void *)dec->rope, (void *)dec->kc, (void *)dec->vc,
 			(void *)dec->x, (void *)dec->qv, (void *)dec->kv, (void *)dec->vv,
 			(void *)dec->xb2, (void *)dec->hb, (void *)dec->hb2, (void *)dec->logits,
-			(void *)dec->aq, (void *)dec->ad, (void *)dec->io})
+			(void *)dec->aq, (void *)dec->ad, (void *)dec->io, (void *)dec->part_v,
+			(void *)dec->part_i})
 		if (p)
 			cudaFree(p);
 	if (dec->h_io)
@@ -365,7 +365,8 @@ struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
 	}
 	const uint32_t n = d->n_embd, hd = d->head_dim;
 	if (!d->n_layer || !d->n_head || !d->n_head_kv || d->n_head % d->n_head_kv || !hd ||
-	    hd % 32 || d->n_head * hd != n || n % 32 || n > FWD_NORM_MAX || !d->n_ff ||
+	    hd % 32 || hd > (uint32_t)FWD_ATTN_THREADS || d->n_head * hd != n || n % 32 ||
+	    n > FWD_NORM_MAX || !d->n_ff ||
 	    d->n_ff % 32 || !d->n_vocab || !d->n_ctx ||
 	    fwd_attention_smem(d->n_ctx, hd) > 227 * 1024) {
 		layer_whine(g, "the decode step does not take this model's shape");
@@ -444,6 +445,8 @@ struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
 	ok = ok && cudaMalloc(&dec->aq, widest) == cudaSuccess;
 	ok = ok && cudaMalloc(&dec->ad, (size_t)widest / 32 * 4) == cudaSuccess;
 	ok = ok && cudaMalloc(&dec->io, FWD_IO_WORDS * sizeof(int)) == cudaSuccess;
+	ok = ok && cudaMalloc(&dec->part_v, FWD_ARGMAX_CTAS * sizeof(float)) == cudaSuccess;
+	ok = ok && cudaMalloc(&dec->part_i, FWD_ARGMAX_CTAS * sizeof(uint32_t)) == cudaSuccess;
 	ok = ok && cudaHostAlloc(&dec->h_io, FWD_IO_WORDS * sizeof(int), cudaHostAllocDefault) ==
 			   cudaSuccess;
 	ok = ok && cudaHostAlloc(&dec->h_logits, (size_t)d->n_vocab * 4, cudaHostAllocDefault) ==
@@ -463,6 +466,10 @@ struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
 		ok = ok && cudaMemset(dec->vc, 0, kvn * 4) == cudaSuccess;
 		ok = ok && cudaMemset(dec->io, 0, FWD_IO_WORDS * sizeof(int)) == cudaSuccess;
 	}
+	if (ok && fwd_norm_smem(n) > 48 * 1024)
+		ok = cudaFuncSetAttribute((const void *)fwd_norm_quant_kernel,
+					  cudaFuncAttributeMaxDynamicSharedMemorySize,
+					  (int)fwd_norm_smem(n)) == cudaSuccess;
 	const size_t attn_smem = fwd_attention_smem(d->n_ctx, hd);
 	if (ok && attn_smem > 48 * 1024)
 		ok = cudaFuncSetAttribute((const void *)fwd_attention_kernel,

@@ -27,9 +27,10 @@ namespace cgpu {
 constexpr uint32_t EXPTAB_E0 = 101, EXPTAB_NE = 33;
 constexpr uint64_t EXPTAB_ENTRIES = 2ull * EXPTAB_NE << 23;
 
-// The step's small device inputs and outputs: the token, its position, and
-// the argmax of its logits.
-constexpr int FWD_IO_TOKEN = 0, FWD_IO_POS = 1, FWD_IO_NEXT = 2, FWD_IO_WORDS = 4;
+// The step's small device inputs and outputs: the token, its position, the
+// argmax of its logits, and the argmax's arrival ticket (zero between steps).
+constexpr int FWD_IO_TOKEN = 0, FWD_IO_POS = 1, FWD_IO_NEXT = 2, FWD_IO_TICKET = 3,
+	      FWD_IO_WORDS = 4;
 
 __device__ __forceinline__ float exp_exact(float x, const float *__restrict__ tab)
 {
@@ -60,23 +61,87 @@ __device__ __forceinline__ void quantise_block_warp(float v, int lane, int8_t *q
 		*d = dd;
 }
 
+// 16-byte asynchronous copy global -> shared (LDGSTS), and the wait for all
+// of this thread's
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem)
+{
+	const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+	asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all()
+{
+	asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// The sum of n squares sq[0..n) in order from 0 (one fp32 chain): the
+// reference's `ss += x[i] * x[i]` once the squares are rounded. Run by one
+// whole warp; every lane returns the sum. A chunk of 2048 is held 64 a lane
+// in registers and the lanes add their 64 in turn, the running sum passed on
+// by a shuffle, so the chain is dependent adds and nothing else (4 cycles a
+// term); the tail below a chunk comes from shared memory.
+__device__ __forceinline__ float ordered_sum_warp(const float *sq, uint32_t n, int lane)
+{
+	float ss = 0.0f;
+	uint32_t i0 = 0;
+	for (; i0 + 2048 <= n; i0 += 2048) {
+		float v[64];
+		const float4 *s4 = reinterpret_cast<const float4 *>(sq + i0 + lane * 64);
+#pragma unroll
+		for (int j = 0; j < 16; j++) {
+			const float4 t = s4[j];
+			v[4 * j] = t.x;
+			v[4 * j + 1] = t.y;
+			v[4 * j + 2] = t.z;
+			v[4 * j + 3] = t.w;
+		}
+#pragma unroll 1
+		for (int l = 0; l < 32; l++) {
+			if (lane == l) {
+#pragma unroll
+				for (int j = 0; j < 64; j++)
+					ss = __fadd_rn(ss, v[j]);
+			}
+			ss = __shfl_sync(0xffffffffu, ss, l);
+		}
+	}
+	if (lane == 0) {
+#pragma unroll 8
+		for (uint32_t i = i0; i < n; i++)
+			ss = __fadd_rn(ss, sq[i]);
+	}
+	return __shfl_sync(0xffffffffu, ss, 0);
+}
+
 // x (+ add, written back to x when add is given), then rmsnorm with weights
 // w (src/llama.c:316-326: ss += x*x in order, scale = 1 / sqrtf(ss / n + eps),
 // out = x * scale * w), then the quantiser of the result. One CTA; n a
-// multiple of 32, at most FWD_NORM_MAX. The sum of squares is one chain of n
-// dependent adds in thread 0 (the squares and shared-memory loads sit off the
-// chain); everything else is spread over the CTA.
+// multiple of 32, at most FWD_NORM_MAX. The weights are fetched before the
+// previous kernel is done (they do not depend on it), the squares by every
+// thread, the chain by warp 0 (ordered_sum_warp).
 constexpr uint32_t FWD_NORM_MAX = 8192;
-constexpr int FWD_NORM_THREADS = 1024;
+constexpr int FWD_NORM_THREADS = 512;
+
+inline size_t fwd_norm_smem(uint32_t n)
+{
+	return (size_t)3 * n * sizeof(float);
+}
 
 __global__ void __launch_bounds__(FWD_NORM_THREADS)
 fwd_norm_quant_kernel(float *__restrict__ x, const float *__restrict__ add,
 		      const float *__restrict__ w, uint32_t n, float eps, int8_t *__restrict__ q,
 		      float *__restrict__ d)
 {
-	__shared__ float xs[FWD_NORM_MAX];
+	extern __shared__ __align__(16) float nsm[];
+	float *xs = nsm, *sq = nsm + n, *ws = nsm + 2 * n;      // fwd_norm_smem(n)
 	__shared__ float scale_s;
+	for (uint32_t i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+		cp_async16(ws + i, w + i);
 	pdl_wait();
+	// the next kernel (a matvec) may launch now and start its weight loads
+	// while the chain below runs; it reads nothing of this one's before its
+	// own wait, which returns once this grid is done
+	pdl_launch_dependents();
 	for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
 		float v = x[i];
 		if (add) {
@@ -84,108 +149,154 @@ fwd_norm_quant_kernel(float *__restrict__ x, const float *__restrict__ add,
 			x[i] = v;
 		}
 		xs[i] = v;
+		sq[i] = __fmul_rn(v, v);
+	}
+	cp_async_wait_all();
+	__syncthreads();
+	if (threadIdx.x < 32) {
+		const float ss = ordered_sum_warp(sq, n, threadIdx.x);
+		if (threadIdx.x == 0)
+			scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
 	}
 	__syncthreads();
-	if (threadIdx.x == 0) {
-		float ss = 0.0f;
-#pragma unroll 16
-		for (uint32_t i = 0; i < n; i++)
-			ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
-		scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-	}
-	__syncthreads();
-	pdl_launch_dependents();
 	const float scale = scale_s;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	for (uint32_t b = warp; b < n / 32; b += blockDim.x / 32) {
 		const uint32_t i = b * 32 + lane;
-		const float v = __fmul_rn(__fmul_rn(xs[i], scale), w[i]);
+		const float v = __fmul_rn(__fmul_rn(xs[i], scale), ws[i]);
 		quantise_block_warp(v, lane, q + b * 32, d + b);
 	}
 }
 
-// RoPE of q (n_head heads) and k (n_head_kv) at this token's position, with
-// the (cos, sin) pairs of that position from a table the host filled with the
-// reference's own libm calls (src/llama.c:364-383), then k and v into the
-// layer's cache row of that position (src/llama.c:781-789).
-__global__ void fwd_rope_kv_kernel(float *__restrict__ qv, float *__restrict__ kv,
-				   const float *__restrict__ vv, const float *__restrict__ rope_cs,
-				   const int *__restrict__ io, float *__restrict__ kcache,
-				   float *__restrict__ vcache, uint32_t n_head, uint32_t n_head_kv,
-				   uint32_t hd)
+// One head of attention at this token's position, RoPE and the KV cache
+// included (src/llama.c:364-383, 781-817):
+//   q and this head's k rotated by the position's (cos, sin) pairs, from a
+//   table the host filled with the reference's own libm calls; the CTA of the
+//   first query head of each KV head writes the rotated k and v into the
+//   layer's cache row of the position (the other heads of the group rotate k
+//   for themselves, the same bits, and read only rows before the position);
+//   scores a_t = (sum_i q_i k_ti, in order) * scale; softmax (the max, expf,
+//   the sum over t in order, the division); out_i = sum_t att_t v_ti in order
+//   from 0; then the quantiser of the head's outputs (head_dim a multiple of
+//   32, so every 32-block of the attention output lies inside one head).
+// One CTA a head. K and V pass through shared memory a tile of positions at a
+// time (rows of hd + 4 floats: 16-byte copies, and a float4 read a row per
+// lane meets no bank conflict); the first tile's cache rows -- written by
+// earlier tokens, so independent of the kernels before this one -- are
+// copied in before this kernel waits on them. Each score's dot runs in one
+// thread, the softmax sum in thread 0, each out_i in one thread.
+constexpr int FWD_ATTN_THREADS = 256;
+constexpr size_t FWD_ATTN_TILE_BYTES = 140 * 1024;      // both tiles
+
+inline uint32_t fwd_attention_tile(uint32_t hd)
 {
-	pdl_wait();
-	const uint32_t half = hd / 2, kvdim = n_head_kv * hd;
-	const uint32_t pairs = (n_head + n_head_kv) * half;
-	const int pos = io[FWD_IO_POS];
-	const float *cs = rope_cs + (size_t)pos * hd;
-	const size_t row = (size_t)pos * kvdim;
-	for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < pairs; j += gridDim.x * blockDim.x) {
-		const uint32_t hh = j / half, i = j % half;
-		float *p = hh < n_head ? qv + hh * hd : kv + (hh - n_head) * hd;
-		const float c = cs[2 * i], s = cs[2 * i + 1];
-		const float x0 = p[2 * i], x1 = p[2 * i + 1];
-		const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-		const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-		p[2 * i] = y0;
-		p[2 * i + 1] = y1;
-		if (hh >= n_head) {
-			const uint32_t off = (hh - n_head) * hd + 2 * i;
-			kcache[row + off] = y0;
-			kcache[row + off + 1] = y1;
-		}
-	}
-	for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < kvdim; j += gridDim.x * blockDim.x)
-		vcache[row + j] = vv[j];
-	pdl_launch_dependents();
+	uint32_t t = (uint32_t)(FWD_ATTN_TILE_BYTES / (2 * (hd + 4) * sizeof(float)));
+	t = t > (uint32_t)FWD_ATTN_THREADS ? (uint32_t)FWD_ATTN_THREADS : t;
+	return t / 32 * 32;
 }
 
-// One head of attention at this position (src/llama.c:792-817), then the
-// quantiser of the head's outputs (head_dim a multiple of 32, so every
-// 32-block of the attention output lies inside one head): scores
-// a_t = (sum_i q_i k_ti, in order) * scale; softmax (the max, expf, the sum
-// over t in order, the division); out_i = sum_t att_t v_ti in order from 0.
-// One CTA a head. Each score's dot runs in one thread, the softmax sum in
-// thread 0, each out_i in one thread.
-constexpr int FWD_ATTN_THREADS = 256;
+// the scores' region, rounded up to whole 16-byte words so the tiles after it
+// start on a 16-byte boundary (their float4 reads and 16-byte copies need one)
+__host__ __device__ inline uint32_t fwd_attention_att_floats(uint32_t n_ctx)
+{
+	return (n_ctx + 3u) & ~3u;
+}
 
 inline size_t fwd_attention_smem(uint32_t n_ctx, uint32_t hd)
 {
-	return ((size_t)n_ctx + 2 * hd) * sizeof(float);
+	return ((size_t)fwd_attention_att_floats(n_ctx) + 4 * hd +
+		2 * (size_t)fwd_attention_tile(hd) * (hd + 4)) * sizeof(float);
 }
 
 __global__ void __launch_bounds__(FWD_ATTN_THREADS)
-fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kcache,
-		     const float *__restrict__ vcache, const int *__restrict__ io,
-		     uint32_t n_head, uint32_t n_head_kv, uint32_t hd, uint32_t n_ctx, float scale,
-		     const float *__restrict__ exptab, int8_t *__restrict__ q,
-		     float *__restrict__ d)
+fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
+		     const float *__restrict__ vv, const float *__restrict__ rope_cs,
+		     float *__restrict__ kcache, float *__restrict__ vcache,
+		     const int *__restrict__ io, uint32_t n_head, uint32_t n_head_kv, uint32_t hd,
+		     uint32_t n_ctx, uint32_t tile, float scale, const float *__restrict__ exptab,
+		     int8_t *__restrict__ q, float *__restrict__ d)
 {
 	extern __shared__ __align__(16) float fsm[];
+	const uint32_t rs = hd + 4;
 	float *att = fsm;                  // n_ctx scores
-	float *qs = fsm + n_ctx;           // this head's q
-	float *os = qs + hd;               // this head's outputs
+	float *qs = att + fwd_attention_att_floats(n_ctx);     // this head's q, rotated
+	float *kp = qs + hd;               // its KV head's k at this position, rotated
+	float *vp = kp + hd;               // and v
+	float *os = vp + hd;               // this head's outputs
+	float *kt = os + hd;               // tile rows of K
+	float *vt = kt + (size_t)tile * rs;
 	__shared__ float red[FWD_ATTN_THREADS / 32];
 	__shared__ float sum_s;
-	pdl_wait();
-	const uint32_t h = blockIdx.x, kvdim = n_head_kv * hd;
-	const uint32_t kvh = h / (n_head / n_head_kv);
-	const int np = io[FWD_IO_POS] + 1;
-	for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x)
-		qs[i] = qv[h * hd + i];
-	__syncthreads();
-	const float *kh = kcache + kvh * hd, *vh = vcache + kvh * hd;
-	for (int t = threadIdx.x; t < np; t += blockDim.x) {
-		const float4 *kt = reinterpret_cast<const float4 *>(kh + (size_t)t * kvdim);
-		float a = 0.0f;
-		for (uint32_t i = 0; i < hd / 4; i++) {
-			const float4 k4 = kt[i];
-			a = __fadd_rn(a, __fmul_rn(qs[4 * i], k4.x));
-			a = __fadd_rn(a, __fmul_rn(qs[4 * i + 1], k4.y));
-			a = __fadd_rn(a, __fmul_rn(qs[4 * i + 2], k4.z));
-			a = __fadd_rn(a, __fmul_rn(qs[4 * i + 3], k4.w));
+	const uint32_t h = blockIdx.x, kvdim = n_head_kv * hd, gqa = n_head / n_head_kv;
+	const uint32_t kvh = h / gqa;
+	// the position came in with the step's first copy, before any kernel of it
+	const int pos = io[FWD_IO_POS], np = pos + 1;
+	float *kc = kcache + kvh * hd, *vc = vcache + kvh * hd;
+	// cache rows t0 .. t0 + nt - 1 below pos into a tile
+	auto issue = [&](float *dst, const float *cache, int t0, int nt) {
+		const uint32_t q4 = hd / 4;
+		for (uint32_t j = threadIdx.x; j < (uint32_t)nt * q4; j += blockDim.x) {
+			const int t = t0 + (int)(j / q4);
+			const uint32_t i = (j % q4) * 4;
+			if (t < pos)
+				cp_async16(dst + (size_t)(t - t0) * rs + i, cache + (size_t)t * kvdim + i);
 		}
-		att[t] = __fmul_rn(a, scale);
+	};
+	// and row pos, when the tile holds it, from this CTA's own copy
+	auto own_row = [&](float *dst, const float *own, int t0, int nt) {
+		if (pos >= t0 && pos < t0 + nt)
+			for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x)
+				dst[(size_t)(pos - t0) * rs + i] = own[i];
+	};
+	const int nt0 = np < (int)tile ? np : (int)tile;
+	issue(kt, kc, 0, nt0);
+	issue(vt, vc, 0, nt0);
+	pdl_wait();
+	pdl_launch_dependents();
+	const float *cs = rope_cs + (size_t)pos * hd;
+	for (uint32_t i = threadIdx.x; i < hd / 2; i += blockDim.x) {
+		const float c = cs[2 * i], s = cs[2 * i + 1];
+		float x0 = qv[h * hd + 2 * i], x1 = qv[h * hd + 2 * i + 1];
+		qs[2 * i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+		qs[2 * i + 1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+		x0 = kv[kvh * hd + 2 * i];
+		x1 = kv[kvh * hd + 2 * i + 1];
+		kp[2 * i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+		kp[2 * i + 1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+	}
+	for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x)
+		vp[i] = vv[kvh * hd + i];
+	__syncthreads();
+	if (h % gqa == 0)
+		for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
+			kc[(size_t)pos * kvdim + i] = kp[i];
+			vc[(size_t)pos * kvdim + i] = vp[i];
+		}
+	own_row(kt, kp, 0, nt0);
+	own_row(vt, vp, 0, nt0);
+	cp_async_wait_all();
+	__syncthreads();
+	for (int t0 = 0; t0 < np; t0 += (int)tile) {
+		const int nt = np - t0 < (int)tile ? np - t0 : (int)tile;
+		if (t0) {
+			__syncthreads();
+			issue(kt, kc, t0, nt);
+			own_row(kt, kp, t0, nt);
+			cp_async_wait_all();
+			__syncthreads();
+		}
+		if ((int)threadIdx.x < nt) {
+			const float4 *k4 = reinterpret_cast<const float4 *>(kt + (size_t)threadIdx.x * rs);
+			float a = 0.0f;
+			for (uint32_t i = 0; i < hd / 4; i++) {
+				const float4 k = k4[i];
+				a = __fadd_rn(a, __fmul_rn(qs[4 * i], k.x));
+				a = __fadd_rn(a, __fmul_rn(qs[4 * i + 1], k.y));
+				a = __fadd_rn(a, __fmul_rn(qs[4 * i + 2], k.z));
+				a = __fadd_rn(a, __fmul_rn(qs[4 * i + 3], k.w));
+			}
+			att[t0 + threadIdx.x] = __fmul_rn(a, scale);
+		}
 	}
 	__syncthreads();
 	// the max: any order gives the reference's value for NaN-free scores (a NaN
@@ -204,27 +315,34 @@ fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kca
 	for (int t = threadIdx.x; t < np; t += blockDim.x)
 		att[t] = exp_exact(__fsub_rn(att[t], mx), exptab);
 	__syncthreads();
-	if (threadIdx.x == 0) {
-		float s = 0.0f;
-#pragma unroll 8
-		for (int t = 0; t < np; t++)
-			s = __fadd_rn(s, att[t]);
-		sum_s = s;
+	if (threadIdx.x < 32) {
+		const float s = ordered_sum_warp(att, (uint32_t)np, threadIdx.x);
+		if (threadIdx.x == 0)
+			sum_s = s;
 	}
 	__syncthreads();
 	const float sum = sum_s;
 	for (int t = threadIdx.x; t < np; t += blockDim.x)
 		att[t] = __fdiv_rn(att[t], sum);
 	__syncthreads();
-	for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
-		float o = 0.0f;
+	float o = 0.0f;
+	for (int t0 = 0; t0 < np; t0 += (int)tile) {
+		const int nt = np - t0 < (int)tile ? np - t0 : (int)tile;
+		if (t0) {
+			__syncthreads();
+			issue(vt, vc, t0, nt);
+			own_row(vt, vp, t0, nt);
+			cp_async_wait_all();
+			__syncthreads();
+		}
+		if (threadIdx.x < hd)
 #pragma unroll 4
-		for (int t = 0; t < np; t++)
-			o = __fadd_rn(o, __fmul_rn(att[t], vh[(size_t)t * kvdim + i]));
-		os[i] = o;
+			for (int t = 0; t < nt; t++)
+				o = __fadd_rn(o, __fmul_rn(att[t0 + t], vt[(size_t)t * rs + threadIdx.x]));
 	}
+	if (threadIdx.x < hd)
+		os[threadIdx.x] = o;
 	__syncthreads();
-	pdl_launch_dependents();
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	for (uint32_t b = warp; b < hd / 32; b += blockDim.x / 32) {
 		const uint32_t e = h * hd + b * 32;
@@ -239,6 +357,7 @@ __global__ void fwd_silu_quant_kernel(const float *__restrict__ gate, const floa
 				      int8_t *__restrict__ q, float *__restrict__ d)
 {
 	pdl_wait();
+	pdl_launch_dependents();
 	const uint32_t b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
 	const int lane = threadIdx.x & 31;
 	if (b < n / 32) {
@@ -248,54 +367,86 @@ __global__ void fwd_silu_quant_kernel(const float *__restrict__ gate, const floa
 		g = __fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
 		quantise_block_warp(__fmul_rn(g, up[i]), lane, q + b * 32, d + b);
 	}
-	pdl_launch_dependents();
 }
 
 // llama_argmax (src/llama.c:860-868): the first index of the maximum, a NaN
 // never taken past index 0 (and index 0 kept when it is NaN), into
-// io[FWD_IO_NEXT]. One CTA: each thread the first maximum of its stride,
-// then the CTA's (value, smallest index) reduction.
-constexpr int FWD_ARGMAX_THREADS = 1024;
+// io[FWD_IO_NEXT]. Each thread keeps the first maximum of the elements it
+// visits (in increasing index order); (value, index) pairs then merge by the
+// larger value, the smaller index on a tie, over the warp, the CTA, and --
+// in the CTA that arrives last on `ticket` -- the grid's per-CTA results
+// (`part`, FWD_ARGMAX_CTAS pairs). The last CTA resets the ticket.
+constexpr int FWD_ARGMAX_THREADS = 256, FWD_ARGMAX_CTAS = 64;
+constexpr uint32_t ARGMAX_NONE = 0xffffffffu;
 
-__global__ void __launch_bounds__(FWD_ARGMAX_THREADS)
-fwd_argmax_kernel(const float *__restrict__ x, uint32_t n, int *__restrict__ io)
+__device__ __forceinline__ void argmax_merge(float &bv, uint32_t &bi, float ov, uint32_t oi)
 {
-	__shared__ float rv[FWD_ARGMAX_THREADS / 32];
-	__shared__ uint32_t ri[FWD_ARGMAX_THREADS / 32];
-	pdl_wait();
-	float bv = -__int_as_float(0x7f800000);
-	uint32_t bi = 0xffffffffu;
-	for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-		const float v = x[i];
-		if (v > bv || (v == bv && bi == 0xffffffffu)) {
-			bv = v;
-			bi = i;
-		}
+	if (oi != ARGMAX_NONE && (bi == ARGMAX_NONE || ov > bv || (ov == bv && oi < bi))) {
+		bv = ov;
+		bi = oi;
 	}
+}
+
+__device__ __forceinline__ void argmax_block(float &bv, uint32_t &bi, float *rv, uint32_t *ri)
+{
 	for (int o = 16; o; o >>= 1) {
 		const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
 		const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-		if (oi != 0xffffffffu && (bi == 0xffffffffu || ov > bv || (ov == bv && oi < bi))) {
-			bv = ov;
-			bi = oi;
-		}
+		argmax_merge(bv, bi, ov, oi);
 	}
 	if ((threadIdx.x & 31) == 0) {
 		rv[threadIdx.x >> 5] = bv;
 		ri[threadIdx.x >> 5] = bi;
 	}
 	__syncthreads();
-	if (threadIdx.x == 0) {
-		for (int w = 1; w < FWD_ARGMAX_THREADS / 32; w++)
-			if (ri[w] != 0xffffffffu &&
-			    (bi == 0xffffffffu || rv[w] > bv || (rv[w] == bv && ri[w] < bi))) {
-				bv = rv[w];
-				bi = ri[w];
-			}
-		const float x0 = x[0];
-		io[FWD_IO_NEXT] = (x0 != x0 || bi == 0xffffffffu) ? 0 : (int)bi;
-	}
+	if (threadIdx.x == 0)
+		for (int w = 1; w < (int)(blockDim.x / 32); w++)
+			argmax_merge(bv, bi, rv[w], ri[w]);
+}
+
+__global__ void __launch_bounds__(FWD_ARGMAX_THREADS)
+fwd_argmax_kernel(const float *__restrict__ x, uint32_t n, int *__restrict__ io,
+		  uint32_t *__restrict__ ticket, float *__restrict__ part_v,
+		  uint32_t *__restrict__ part_i)
+{
+	__shared__ float rv[FWD_ARGMAX_THREADS / 32];
+	__shared__ uint32_t ri[FWD_ARGMAX_THREADS / 32];
+	pdl_wait();
 	pdl_launch_dependents();
+	float bv = -__int_as_float(0x7f800000);
+	uint32_t bi = ARGMAX_NONE;
+	auto take = [&](float v, uint32_t i) {
+		if (v > bv || (v == bv && bi == ARGMAX_NONE)) {
+			bv = v;
+			bi = i;
+		}
+	};
+	const float4 *x4 = reinterpret_cast<const float4 *>(x);
+	const uint32_t n4 = n / 4, stride = gridDim.x * blockDim.x;
+	for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < n4; j += stride) {
+		const float4 v = x4[j];
+		take(v.x, 4 * j);
+		take(v.y, 4 * j + 1);
+		take(v.z, 4 * j + 2);
+		take(v.w, 4 * j + 3);
+	}
+	if (blockIdx.x == 0 && threadIdx.x < n - n4 * 4)
+		take(x[n4 * 4 + threadIdx.x], n4 * 4 + threadIdx.x);
+	argmax_block(bv, bi, rv, ri);
+	if (threadIdx.x == 0) {
+		part_v[blockIdx.x] = bv;
+		part_i[blockIdx.x] = bi;
+		if (atom_add_acq_rel_gpu(ticket, 1u) == gridDim.x - 1) {
+			*ticket = 0;
+			float fv = part_v[0];
+			uint32_t fi = part_i[0];
+			for (uint32_t c = 1; c < gridDim.x; c++)
+				argmax_merge(fv, fi, ((volatile float *)part_v)[c],
+					     ((volatile uint32_t *)part_i)[c]);
+			const float x0 = x[0];
+			io[FWD_IO_NEXT] = (x0 != x0 || fi == ARGMAX_NONE) ? 0 : (int)fi;
+		}
+	}
 }
 
 } // namespace cgpu

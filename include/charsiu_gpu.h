@@ -245,7 +245,7 @@ CHARSIU_GPU_API int charsiu_gpu_row_dev(struct charsiu_gpu *g, int id, const int
  * head is tied); host fp32 norm weights, copied at creation; rope_cs the
  * (cos, sin) pair i of every position, [n_ctx][head_dim], as
  * src/llama.c:364-383 computes them. Requires n_head * head_dim = n_embd,
- * head_dim a multiple of 32, n_embd and n_ff multiples of 32, n_embd at most
+ * head_dim a multiple of 32 and at most 256, n_embd and n_ff multiples of 32, n_embd at most
  * 8192, and a layer opened with world 1.
  */
 struct charsiu_gpu_decoder;
