@@ -545,6 +545,16 @@ int charsiu_gpu_decoder_step(struct charsiu_gpu_decoder *dec, int32_t token, int
 	return 0;
 }
 
+int charsiu_gpu_ordered_sum_dev(struct charsiu_gpu *g, const float *a, unsigned n, float *out,
+				void *stream)
+{
+	if (!g || !a || !out || !n || n > ORDERED_SUM_MAX_N)
+		return -1;
+	cudaSetDevice(layer_device(g));
+	ordered_sum_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(a, n, out);
+	return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 const float *charsiu_gpu_decoder_logits(const struct charsiu_gpu_decoder *dec)
 {
 	return dec ? dec->h_logits : nullptr;

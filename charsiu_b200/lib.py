@@ -79,6 +79,7 @@ SIGNATURES = [
     ("charsiu_gpu_decoder_step", C.c_int, [_vp, C.c_int32, C.c_int, C.c_int, _vp]),
     ("charsiu_gpu_decoder_logits", C.POINTER(C.c_float), [_vp]),
     ("charsiu_gpu_decoder_launches", C.c_uint, [_vp]),
+    ("charsiu_gpu_ordered_sum_dev", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp]),
 ]
 
 
@@ -291,6 +292,10 @@ class Layer:
         """The batched matvec with no device allocation (fixed 1 MiB scratch)."""
         return self.L.charsiu_gpu_matvec_batch_noalloc(self.h, tid, m, q_ptr, d_ptr, y_ptr,
                                                        stream or None)
+
+    def ordered_sum_dev(self, a_ptr: int, n: int, out_ptr: int, stream: int = 0) -> int:
+        """The sequential fp32 sum of n non-negative device floats into out_ptr."""
+        return self.L.charsiu_gpu_ordered_sum_dev(self.h, a_ptr, n, out_ptr, stream or None)
 
     def row_dev(self, tid: int, row_ptr: int, out_ptr: int, stream: int = 0) -> int:
         """gguf_row_f32 of row *row_ptr (device int32) into out_ptr (device)."""

@@ -294,6 +294,13 @@ CHARSIU_GPU_API int charsiu_gpu_dead(const struct charsiu_gpu *g);
 CHARSIU_GPU_API int charsiu_gpu_block_dots(struct charsiu_gpu *g, int id, const int8_t *q,
 			   int32_t *dots);
 
+/* The decode step's ordered sum on the device: *out =
+ * fl(...fl(fl(0 + a[0]) + a[1]) ... + a[n-1]), the sequential fp32 sum
+ * (rmsnorm's sum of squares, src/llama.c:321-322, and the softmax sum).
+ * a and out are device pointers, n <= 8192. Queued on `stream`. */
+CHARSIU_GPU_API int charsiu_gpu_ordered_sum_dev(struct charsiu_gpu *g, const float *a,
+						unsigned n, float *out, void *stream);
+
 /* Host-side fault injection (no GPU fault is ever made): from call number
  * `at` on (1-based, counting matvec/group/batch/matmul calls), `count` calls
  * fail as `kind` says: 1 = the launch reports an error, 2 = the call is slow
