@@ -13,19 +13,25 @@ device.
           HBM, replayed as one CUDA graph per token, timed with CUDA events.
           1.31 GB a token is far larger than the 126 MB L2, so every token
           streams its weights from HBM.
-  e2e     tokens/s of the real greedy decode through the public C ABI
-          (charsiu_gpu_llama_*): CPU rmsnorm/rope/attention/SwiGLU as
-          charsiu does them, every projection a host-buffer call with its
-          host->device and device->host copies inside the timed region.
+  e2e     tokens/s of the workload's greedy decode (6 prompt ids, 24 tokens)
+          through the public C ABI (charsiu_gpu_llama_greedy) with the whole
+          step on the device (charsiu_gpu_llama_set_resident): each token's
+          id and position copied in from pinned host memory and its argmax
+          copied back inside the timed region, one CUDA graph a token, logits
+          the reference's bit for bit. e2e.host_routed is the drop-in form:
+          charsiu's CPU rmsnorm/rope/attention/SwiGLU on the host and every
+          projection a host-buffer call (charsiu_gpu_llama_forward).
   roofline the matvec kernel's algorithmic bytes per launch over its average
           launch time in the timed region, against the measured HBM copy peak.
   cpu_baseline charsiu's own CPU decode (the reference compiled from its
           sources, oracle/_ref) on this box's host cores.
 
-At N GPUs every tensor is column-split across the ranks and each launch
-group's output slabs are all-gathered (NCCL) into the full vector, so one
-decode stream runs on N GPUs: strong scaling.
+At N GPUs every GPU decodes its own stream with the whole model (no
+collective, weak scaling); the column_split key times one stream with every
+tensor split over the N GPUs (NCCL all-gathers, and the fused matvec +
+all-gather over NVLink).
 
+  python bench.py --resident    the e2e leg alone
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
 from __future__ import annotations
@@ -433,39 +439,46 @@ def golden_match(toks) -> bool:
 
 
 def run_e2e_resident(path, args, world=1, dist=None, dev=None):
-    """The greedy decode through the public C ABI with the whole step on the
-    device (charsiu_gpu_llama_set_resident + charsiu_gpu_llama_greedy): each
-    timed step copies its token and position in from pinned host memory and
-    its argmax token back, and replays one CUDA graph. At N GPUs every rank
-    decodes its own stream; the rate is the sum over ranks, from the slowest
-    rank's time."""
+    """The workload's greedy decode (6 prompt ids, 24 generated tokens) through
+    the public C ABI with the whole step on the device
+    (charsiu_gpu_llama_set_resident + charsiu_gpu_llama_greedy), repeated from
+    the prompt until about K tokens are timed: each timed step copies its
+    token and position in from pinned host memory and its argmax token back,
+    and replays one CUDA graph. At N GPUs every rank decodes its own stream;
+    the rate is the sum over ranks, from the slowest rank's time."""
     from charsiu_b200.lib import Llama
 
-    n_gen_timed = max(1, min(args.steps, 500))
-    n_warm = max(3, min(args.warmup, 8))
+    n_gen = SPEC["n_gen"]
+    reps = max(1, min(args.steps, 480) // n_gen)
     prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
-    n_ctx = len(prompt) + max(n_gen_timed, n_warm) + 1
+    n_ctx = len(prompt) + n_gen + 1
     if world > 1:
         dist.barrier()
+    total_ms, match = 0.0, True
     with Llama(path, n_ctx=n_ctx, device=dev.index if dev is not None else 0,
                resident=True) as m:
-        m.greedy(prompt, n_warm)            # builds and captures the step's graphs
-        toks, _, gen_ms = m.greedy(prompt, n_gen_timed)
+        for _ in range(2):                      # builds and captures the step's graphs
+            m.greedy(prompt, n_gen)
+        for _ in range(reps):
+            toks, _, gen_ms = m.greedy(prompt, n_gen)
+            total_ms += gen_ms
+            match = match and golden_match(toks)
         launches = m.step_launches
-    dt = gen_ms / 1e3
+    dt = total_ms / 1e3
     if world > 1:
         import torch
         t = torch.tensor([dt], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
-    return {"value": round(world * n_gen_timed / dt, 2), "unit": UNIT,
-            "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4, "steps": n_gen_timed,
-            "warmup": n_warm, "ms_per_step": round(dt * 1e3 / n_gen_timed, 4),
-            "kernels_per_step": launches,
-            "tokens_match_reference": golden_match(toks),
+    steps = reps * n_gen
+    return {"value": round(world * steps / dt, 2), "unit": UNIT,
+            "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4, "steps": steps,
+            "warmup": 2 * (len(prompt) + n_gen), "ms_per_step": round(dt * 1e3 / steps, 4),
+            "kernels_per_step": launches, "tokens_match_reference": match,
             "api": "charsiu_gpu_llama_greedy after charsiu_gpu_llama_set_resident(1) (C ABI): "
                    "token + position in (pinned host -> device), argmax token out, one CUDA "
-                   f"graph a token; positions {len(prompt)}..{len(prompt) + n_gen_timed - 1}"}
+                   f"graph a token; {reps} greedy runs of the workload, positions "
+                   f"{len(prompt)}..{len(prompt) + n_gen - 1} timed"}
 
 
 def cpu_baseline(path):
