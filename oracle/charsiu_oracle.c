@@ -287,6 +287,95 @@ int orc_row_f32(uint32_t type, const void *data, uint64_t k, uint64_t row,
 	}
 }
 
+/* ---- the NPU number format (src/npuquant.c, src/npudev.c, src/gguf.c) ---- */
+
+int orc_npu_tensor_build(uint32_t type, const void *data, uint64_t k, uint64_t n,
+			 int8_t *q, float *scale, int32_t *wsum)
+{
+	float *row = malloc(k * sizeof(float));
+
+	if (!row)
+		return -1;
+	for (uint64_t r = 0; r < n; r++) {
+		float amax = 0.0f, d, id;
+		int32_t sum = 0;
+
+		if (orc_row_f32(type, data, k, r, row) < 0) {
+			free(row);
+			return -1;
+		}
+		for (uint64_t i = 0; i < k; i++) {
+			float a = fabsf(row[i]);
+
+			if (a > amax)
+				amax = a;
+		}
+		/* symmetric over [-127, 127] (src/npuquant.c:196-201) */
+		d = amax / 127.0f;
+		id = d != 0.0f ? 1.0f / d : 0.0f;
+		scale[r] = d;
+		for (uint64_t i = 0; i < k; i++) {
+			int v = (int)lrintf(row[i] * id);
+
+			if (v > 127)
+				v = 127;
+			if (v < -127)
+				v = -127;
+			q[r * k + i] = (int8_t)v;
+			sum += v;
+		}
+		if (wsum)
+			wsum[r] = sum;
+	}
+	free(row);
+	return 0;
+}
+
+void orc_act_quantise_one(const float *x, int n, int8_t *q1, float *d1)
+{
+	int nb = (n + 31) / 32;
+	float amax = 0.0f, d, id;
+
+	for (int i = 0; i < n; i++) {
+		float av = x[i] < 0.0f ? -x[i] : x[i];
+
+		if (av > amax)
+			amax = av;
+	}
+	d = amax / 127.0f;
+	id = d != 0.0f ? 1.0f / d : 0.0f;
+	*d1 = d;
+	for (int i = 0; i < nb * 32; i++) {
+		int v = i < n ? (int)lrintf(x[i] * id) : 0;
+
+		if (v > 127)
+			v = 127;
+		if (v < -127)
+			v = -127;
+		q1[i] = (int8_t)v;
+	}
+}
+
+void orc_npu_matvec(const int8_t *q, const float *scale, uint64_t k, uint64_t n,
+		    const int8_t *q1, float d1, int model, float *y)
+{
+	for (uint64_t r = 0; r < n; r++) {
+		const int8_t *w = q + r * k;
+		int32_t acc = 0;
+
+		for (uint64_t i = 0; i < k; i++)
+			acc += (int32_t)w[i] * (int32_t)q1[i];
+		if (model == 0) {
+			y[r] = (float)acc * d1 * scale[r];
+		} else {
+			double a = 0.0;
+
+			a += (double)acc * scale[r];
+			y[r] = (float)(a * d1);
+		}
+	}
+}
+
 /* ---- int8 matmul + output stage (tools/charsiu_matmul.c:41-81) ---------- */
 
 void orc_matmul_i8(unsigned m, unsigned k, unsigned n, const uint8_t *a,
@@ -322,8 +411,8 @@ struct orc_state {
 	int n_ctx;
 	float *kcache, *vcache;
 	float *x, *xb, *xb2, *hb, *hb2, *q, *k, *v, *att, *logits;
-	int8_t *aq;
-	float *ad;
+	int8_t *aq, *aq1;
+	float *ad, ad1;
 };
 
 struct orc_state *orc_state_new(const struct orc_model *m, int n_ctx)
@@ -350,7 +439,8 @@ struct orc_state *orc_state_new(const struct orc_model *m, int n_ctx)
 	s->logits = calloc(m->n_vocab, sizeof(float));
 	s->aq = calloc((size_t)(widest + 31) / 32 * 32, 1);
 	s->ad = calloc((size_t)(widest + 31) / 32, sizeof(float));
-	if (!s->kcache || !s->vcache || !s->x || !s->xb || !s->xb2 || !s->hb ||
+	s->aq1 = calloc((size_t)(widest + 31) / 32 * 32, 1);
+	if (!s->aq1 || !s->kcache || !s->vcache || !s->x || !s->xb || !s->xb2 || !s->hb ||
 	    !s->hb2 || !s->q || !s->k || !s->v || !s->att || !s->logits ||
 	    !s->aq || !s->ad) {
 		orc_state_free(s);
@@ -366,7 +456,7 @@ void orc_state_free(struct orc_state *s)
 	free(s->kcache); free(s->vcache);
 	free(s->x); free(s->xb); free(s->xb2); free(s->hb); free(s->hb2);
 	free(s->q); free(s->k); free(s->v); free(s->att); free(s->logits);
-	free(s->aq); free(s->ad);
+	free(s->aq); free(s->ad); free(s->aq1);
 	free(s);
 }
 
@@ -416,17 +506,36 @@ static void rope(float *v, uint32_t nheads, uint32_t hd, int pos, float base)
 	}
 }
 
-/* quantise once, then each projection of it (llama.c:178-183, 215-248) */
+/* quantise once, then each projection of it (llama.c:178-183, 215-248); in
+ * the NPU format the single-scale activation and the tensor's npu copy
+ * (llama.c:255-290) */
+static void project_nq(struct orc_state *s, uint32_t kdim, const int8_t *nq,
+		       const float *nscale, uint32_t ndim, float *y)
+{
+	orc_npu_matvec(nq, nscale, kdim, ndim, s->aq1, s->ad1, s->m->npu - 1, y);
+}
+
 static void project(struct orc_state *s, const float *x, uint32_t kdim,
-		    const void *w, uint32_t type, uint32_t ndim, float *y)
+		    const void *w, uint32_t type, uint32_t ndim, float *y,
+		    const int8_t *nq, const float *nscale)
 {
 	orc_act_quantise(x, (int)kdim, s->aq, s->ad, NULL);
+	if (s->m->npu) {
+		orc_act_quantise_one(x, (int)kdim, s->aq1, &s->ad1);
+		project_nq(s, kdim, nq, nscale, ndim, y);
+		return;
+	}
 	orc_matvec(type, w, kdim, s->aq, s->ad, y, 0, ndim);
 }
 
 static void project_again(struct orc_state *s, uint32_t kdim, const void *w,
-			  uint32_t type, uint32_t ndim, float *y)
+			  uint32_t type, uint32_t ndim, float *y,
+			  const int8_t *nq, const float *nscale)
 {
+	if (s->m->npu) {
+		project_nq(s, kdim, nq, nscale, ndim, y);
+		return;
+	}
 	orc_matvec(type, w, kdim, s->aq, s->ad, y, 0, ndim);
 }
 
@@ -447,9 +556,12 @@ const float *orc_forward(struct orc_state *s, int32_t token, int pos)
 		float *vc = s->vcache + ((size_t)l * s->n_ctx + pos) * kvdim;
 
 		rmsnorm(s->xb, s->x, L->attn_norm, m->n_embd, m->rms_eps);
-		project(s, s->xb, m->n_embd, L->w[0], L->type[0], m->n_head * hd, s->q);
-		project_again(s, m->n_embd, L->w[1], L->type[1], kvdim, s->k);
-		project_again(s, m->n_embd, L->w[2], L->type[2], kvdim, s->v);
+		project(s, s->xb, m->n_embd, L->w[0], L->type[0], m->n_head * hd, s->q,
+			L->nq[0], L->nscale[0]);
+		project_again(s, m->n_embd, L->w[1], L->type[1], kvdim, s->k, L->nq[1],
+			      L->nscale[1]);
+		project_again(s, m->n_embd, L->w[2], L->type[2], kvdim, s->v, L->nq[2],
+			      L->nscale[2]);
 
 		rope(s->q, m->n_head, hd, pos, m->rope_base);
 		rope(s->k, m->n_head_kv, hd, pos, m->rope_base);
@@ -484,26 +596,31 @@ const float *orc_forward(struct orc_state *s, int32_t token, int pos)
 			}
 		}
 
-		project(s, s->xb, m->n_embd, L->w[3], L->type[3], m->n_embd, s->xb2);
+		project(s, s->xb, m->n_embd, L->w[3], L->type[3], m->n_embd, s->xb2,
+			L->nq[3], L->nscale[3]);
 		for (uint32_t i = 0; i < m->n_embd; i++)
 			s->x[i] += s->xb2[i];
 
 		rmsnorm(s->xb, s->x, L->ffn_norm, m->n_embd, m->rms_eps);
-		project(s, s->xb, m->n_embd, L->w[4], L->type[4], m->n_ff, s->hb);
-		project_again(s, m->n_embd, L->w[5], L->type[5], m->n_ff, s->hb2);
+		project(s, s->xb, m->n_embd, L->w[4], L->type[4], m->n_ff, s->hb,
+			L->nq[4], L->nscale[4]);
+		project_again(s, m->n_embd, L->w[5], L->type[5], m->n_ff, s->hb2, L->nq[5],
+			      L->nscale[5]);
 		for (uint32_t i = 0; i < m->n_ff; i++) {
 			float g = s->hb[i];
 
 			g *= 1.0f / (1.0f + expf(-g));
 			s->hb[i] = g * s->hb2[i];
 		}
-		project(s, s->hb, m->n_ff, L->w[6], L->type[6], m->n_embd, s->xb2);
+		project(s, s->hb, m->n_ff, L->w[6], L->type[6], m->n_embd, s->xb2,
+			L->nq[6], L->nscale[6]);
 		for (uint32_t i = 0; i < m->n_embd; i++)
 			s->x[i] += s->xb2[i];
 	}
 
 	rmsnorm(s->xb, s->x, m->out_norm, m->n_embd, m->rms_eps);
-	project(s, s->xb, m->n_embd, m->output, m->out_type, m->n_vocab, s->logits);
+	project(s, s->xb, m->n_embd, m->output, m->out_type, m->n_vocab, s->logits,
+		m->out_nq, m->out_nscale);
 	return s->logits;
 }
 

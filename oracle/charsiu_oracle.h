@@ -66,12 +66,42 @@ void orc_matmul_i8(unsigned m, unsigned k, unsigned n, const uint8_t *a,
 		   float wt_scale, float out_scale, int in_zp, int wt_zp,
 		   int out_zp, int8_t *out);
 
+/* ---- the NPU number format (CHARSIU_NPU_QUANT) --------------------------- */
+
+/*
+ * npu_tensor_build in its default form (src/npuquant.c:34-296 with none of
+ * its CHARSIU_NPU_* experiment switches set: eight bits, one scale a row, no
+ * k factor): each row dequantised (gguf_row_f32), amax over it, d = amax /
+ * 127, q = lrintf(x * (1 / d)) clamped to [-127, 127]; wsum = the row's sum
+ * of q. q [n][k] row major, scale [n], wsum [n] (may be NULL). -1 for a type
+ * orc_row_f32 reads not.
+ */
+int orc_npu_tensor_build(uint32_t type, const void *data, uint64_t k, uint64_t n,
+			 int8_t *q, float *scale, int32_t *wsum);
+
+/* charsiu_act_set's single-scale form (src/gguf.c:883-910): d1 = amax / 127,
+ * q1[i] = lrintf(x[i] * (1 / d1)) clamped to [-127, 127], zero past n; q1
+ * holds nb * 32 bytes. */
+void orc_act_quantise_one(const float *x, int n, int8_t *q1, float *d1);
+
+/*
+ * y = W x in the NPU format, acc[r] = sum_k q[r][k] * q1[k] (exact int32):
+ *   model 0: the device path, src/npudev.c:604-605 (and :707-708):
+ *            y[r] = (float)acc * d1 * scale[r], in float, left to right;
+ *   model 1: the CPU model, src/npuquant.c:447-544 (one scale a row, no k
+ *            factor): y[r] = (float)(((double)acc * scale[r]) * d1).
+ */
+void orc_npu_matvec(const int8_t *q, const float *scale, uint64_t k, uint64_t n,
+		    const int8_t *q1, float d1, int model, float *y);
+
 /* ---- the decode loop (src/llama.c:316-386, 743-868) --------------------- */
 
 struct orc_layer {
 	const float *attn_norm, *ffn_norm;            /* f32 [n_embd] */
 	const void *w[7];                             /* q k v o gate up down */
 	uint32_t type[7];
+	const int8_t *nq[7];                          /* NPU format (npu != 0) */
+	const float *nscale[7];
 };
 
 struct orc_model {
@@ -81,6 +111,16 @@ struct orc_model {
 	const void *output;    uint32_t out_type;     /* may be tok_embd */
 	const float *out_norm;
 	const struct orc_layer *layers;
+	/*
+	 * 0: every projection and the head through gguf_matvec. 1 or 2: through
+	 * the NPU format (CHARSIU_NPU_QUANT, src/llama.c:110-312), the tensors'
+	 * npu_tensor_build copies in nq / nscale and out_nq / out_nscale, the
+	 * arithmetic of orc_npu_matvec model npu - 1 (1: the device's, 2: the
+	 * CPU model's).
+	 */
+	int npu;
+	const int8_t *out_nq;
+	const float *out_nscale;
 };
 
 struct orc_state;

@@ -61,6 +61,12 @@ def lib():
         L.orc_argmax.restype = C.c_int32
         L.orc_row_f32.argtypes = [C.c_uint32, C.c_void_p, C.c_uint64, C.c_uint64, _f32p]
         L.orc_row_f32.restype = C.c_int
+        L.orc_npu_tensor_build.argtypes = [C.c_uint32, C.c_void_p, C.c_uint64, C.c_uint64, _i8p,
+                                           _f32p, _i32p]
+        L.orc_npu_tensor_build.restype = C.c_int
+        L.orc_act_quantise_one.argtypes = [_f32p, C.c_int, _i8p, C.POINTER(C.c_float)]
+        L.orc_npu_matvec.argtypes = [_i8p, _f32p, C.c_uint64, C.c_uint64, _i8p, C.c_float,
+                                     C.c_int, _f32p]
         _lib = L
     return _lib
 
@@ -88,6 +94,12 @@ def ref():
                                        C.POINTER(C.c_double), C.POINTER(C.c_double), C.c_void_p,
                                        C.c_void_p]
         R.ref_greedy_timed.restype = C.c_int
+        R.ref_npu_tensor_build.argtypes = [C.c_uint32, C.c_void_p, C.c_uint64, C.c_uint64, _i8p,
+                                           _f32p, _i32p]
+        R.ref_npu_tensor_build.restype = C.c_int
+        R.ref_act_q1.argtypes = [_f32p, C.c_int, _i8p, C.POINTER(C.c_float)]
+        R.ref_act_q1.restype = C.c_int
+        R.ref_npu_matvec.argtypes = [_i8p, _f32p, C.c_uint64, C.c_uint64, _i8p, C.c_float, _f32p]
         _ref = R
     return _ref
 
@@ -123,6 +135,33 @@ def row_f32(qtype: int, blocks: np.ndarray, k: int, row: int) -> np.ndarray:
     return out
 
 
+def npu_tensor_build(qtype: int, blocks: np.ndarray, k: int, n: int):
+    """npu_tensor_build's default form: (q int8 [n, k], scale [n], wsum [n])."""
+    q = np.zeros((n, k), dtype=np.int8)
+    scale = np.zeros(n, dtype=np.float32)
+    wsum = np.zeros(n, dtype=np.int32)
+    assert lib().orc_npu_tensor_build(qtype, _ptr(blocks), k, n, q, scale, wsum) == 0
+    return q, scale, wsum
+
+
+def act_quantise_one(x: np.ndarray):
+    """charsiu_act_set's single-scale form: (q1 [nb * 32], d1)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q1 = np.zeros((x.size + 31) // 32 * 32, dtype=np.int8)
+    d1 = C.c_float()
+    lib().orc_act_quantise_one(x, x.size, q1, C.byref(d1))
+    return q1, np.float32(d1.value)
+
+
+def npu_matvec(q: np.ndarray, scale: np.ndarray, q1: np.ndarray, d1, model: int = 0):
+    """y in the NPU format: model 0 the device path's arithmetic, 1 the CPU model's."""
+    n, k = q.shape
+    y = np.zeros(n, dtype=np.float32)
+    lib().orc_npu_matvec(np.ascontiguousarray(q), np.ascontiguousarray(scale, dtype=np.float32),
+                         k, n, np.ascontiguousarray(q1), float(d1), model, y)
+    return y
+
+
 def block_dots(qtype: int, blocks: np.ndarray, k: int, n: int, q: np.ndarray):
     out = np.zeros((n, k // 32), dtype=np.int32)
     rc = lib().orc_block_dots(qtype, _ptr(blocks), k, n, np.ascontiguousarray(q), out)
@@ -142,7 +181,7 @@ def matmul_i8(a, w, bias, in_scale, wt_scale, out_scale, in_zp=128, wt_zp=128, o
 
 class _Layer(C.Structure):
     _fields_ = [("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p), ("w", C.c_void_p * 7),
-                ("type", C.c_uint32 * 7)]
+                ("type", C.c_uint32 * 7), ("nq", C.c_void_p * 7), ("nscale", C.c_void_p * 7)]
 
 
 class _Model(C.Structure):
@@ -150,17 +189,32 @@ class _Model(C.Structure):
                 ("n_head_kv", C.c_uint32), ("n_ff", C.c_uint32), ("n_vocab", C.c_uint32),
                 ("head_dim", C.c_uint32), ("rms_eps", C.c_float), ("rope_base", C.c_float),
                 ("tok_embd", C.c_void_p), ("tok_type", C.c_uint32), ("output", C.c_void_p),
-                ("out_type", C.c_uint32), ("out_norm", C.c_void_p), ("layers", C.c_void_p)]
+                ("out_type", C.c_uint32), ("out_norm", C.c_void_p), ("layers", C.c_void_p),
+                ("npu", C.c_int), ("out_nq", C.c_void_p), ("out_nscale", C.c_void_p)]
 
 
 class OracleModel:
-    """The restated decode loop over a GGUF file's tensors (mapped, not copied)."""
+    """The restated decode loop over a GGUF file's tensors (mapped, not copied).
 
-    def __init__(self, gguf, n_ctx: int = 64):
+    npu = 0: charsiu's default path (gguf_matvec). npu = 1 or 2: the NPU
+    format of CHARSIU_NPU_QUANT -- every projection and the head through its
+    npu_tensor_build copy (built here), with the device path's arithmetic (1)
+    or the CPU model's (2)."""
+
+    def __init__(self, gguf, n_ctx: int = 64, npu: int = 0):
         from charsiu_b200.gguf import PROJ_NAMES
         s = gguf.shape()
         self.gguf, self.shape = gguf, s
         T = gguf.tensors
+        self._keep = []
+
+        def npu_copy(name):
+            t = T[name]
+            k, n = int(t.ne[0]), int(t.ne[1])
+            q, scale, _ = npu_tensor_build(t.type, gguf.data(name), k, n)
+            self._keep += [q, scale]
+            return _ptr(q), _ptr(scale)
+
         layers = (_Layer * s.n_layer)()
         for l in range(s.n_layer):
             L = layers[l]
@@ -169,12 +223,16 @@ class OracleModel:
             for i, nm in enumerate(PROJ_NAMES):
                 L.w[i] = _ptr(gguf.data(f"blk.{l}.{nm}.weight"))
                 L.type[i] = T[f"blk.{l}.{nm}.weight"].type
+                if npu:
+                    L.nq[i], L.nscale[i] = npu_copy(f"blk.{l}.{nm}.weight")
         out = "output.weight" if "output.weight" in T else "token_embd.weight"
+        out_nq, out_nscale = npu_copy(out) if npu else (None, None)
         self._layers = layers
         self.m = _Model(s.n_embd, s.n_layer, s.n_head, s.n_head_kv, s.n_ff, s.n_vocab, s.head_dim,
                         s.rms_eps, s.rope_base, _ptr(gguf.data("token_embd.weight")),
                         T["token_embd.weight"].type, _ptr(gguf.data(out)), T[out].type,
-                        _ptr(gguf.data("output_norm.weight")), C.addressof(layers))
+                        _ptr(gguf.data("output_norm.weight")), C.addressof(layers), npu,
+                        out_nq, out_nscale)
         self.n_ctx = n_ctx
 
     def greedy(self, prompt, n_gen: int) -> np.ndarray:

@@ -154,3 +154,69 @@ int ref_greedy_timed(const char *path, const int32_t *prompt, int n_prompt,
 	llama_free(&m);
 	return i;
 }
+
+/* ---- the NPU number format (CHARSIU_NPU_QUANT), for the restatement's pins */
+
+/* npu_tensor_build (src/npuquant.c:34-296) on a caller's raw GGUF rows */
+int ref_npu_tensor_build(uint32_t type, const void *data, uint64_t k, uint64_t n,
+			 int8_t *q, float *scale, int32_t *wsum)
+{
+	struct gguf_tensor w;
+	struct npu_tensor t;
+
+	memset(&w, 0, sizeof(w));
+	snprintf(w.name, sizeof(w.name), "probe");
+	w.n_dims = 2;
+	w.ne[0] = k;
+	w.ne[1] = n;
+	w.ne[2] = w.ne[3] = 1;
+	w.type = type;
+	w.data = data;
+	if (npu_tensor_build(&t, &w) < 0)
+		return -1;
+	memcpy(q, t.q, (size_t)n * k);
+	memcpy(scale, t.scale, (size_t)n * sizeof(float));
+	memcpy(wsum, t.wsum, (size_t)n * sizeof(int32_t));
+	npu_tensor_free(&t);
+	return 0;
+}
+
+/* charsiu_act_set's single-scale activation (src/gguf.c:883-910); valid only
+ * in a process whose CHARSIU_NPU_QUANT was set before its first call */
+int ref_act_q1(const float *x, int n, int8_t *q1, float *d1)
+{
+	struct charsiu_act a;
+	int rc = -1;
+
+	if (charsiu_act_alloc(&a, n) < 0)
+		return -1;
+	charsiu_act_set(&a, x, n);
+	if (a.q1_valid) {
+		memcpy(q1, a.q1, (size_t)a.nb * 32);
+		*d1 = a.d1;
+		rc = 0;
+	}
+	charsiu_act_free(&a);
+	return rc;
+}
+
+/* npu_matvec (src/npuquant.c:447-544), the CPU model, one scale a row */
+void ref_npu_matvec(const int8_t *q, const float *scale, uint64_t k, uint64_t n,
+		    const int8_t *q1, float d1, float *y)
+{
+	struct npu_tensor t;
+	struct charsiu_act a;
+
+	memset(&t, 0, sizeof(t));
+	memset(&a, 0, sizeof(a));
+	t.q = (int8_t *)q;
+	t.scale = (float *)scale;
+	t.kgroup = k;
+	t.n = n;
+	t.k = k;
+	a.n = (int)k;
+	a.q1 = (int8_t *)q1;
+	a.d1 = d1;
+	a.q1_valid = 1;
+	npu_matvec(&t, &a, y, 0, n);
+}

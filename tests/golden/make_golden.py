@@ -10,7 +10,9 @@ sources by oracle/Makefile) and records what the reference computes:
   golden_decode.json greedy token ids and logit digests of charsiu's own
                      llama_forward on seeded synthetic models: the tiny test
                      models (q8_0; q4_0; q4_0 with a q6_K embedding and head)
-                     and the Llama-3.2-1B-shaped one.
+                     and the Llama-3.2-1B-shaped one; under "npu", the same
+                     in charsiu's NPU number format (CHARSIU_NPU_QUANT=1, its
+                     CPU model), added by  python tests/golden/make_golden.py --npu
 
 Inputs are regenerated from the recorded seeds (numpy PCG64); a sha256 of each
 input is stored beside it so generator drift is caught rather than trusted.
@@ -20,6 +22,7 @@ from __future__ import annotations
 import hashlib
 import json
 import os
+import subprocess
 import sys
 import tempfile
 
@@ -99,5 +102,52 @@ def main() -> None:
         json.dump(dec, f, indent=1)
 
 
+def npu_child(out_path: str) -> None:
+    """In a process started with CHARSIU_NPU_QUANT=1: the reference's greedy
+    decode in the NPU number format (its CPU model, src/npuquant.c) on every
+    decode workload, into out_path as JSON."""
+    assert os.environ.get("CHARSIU_NPU_QUANT") == "1"
+    res = {}
+    with tempfile.TemporaryDirectory() as td:
+        for name, spec in W.DECODE.items():
+            path = os.path.join(td, f"{name}.gguf")
+            G.write_llama(path, spec["shape"], spec["qtype"], spec["seed"],
+                          embd_qtype=spec.get("embd_qtype"))
+            prompt = W.prompt_ids(spec["shape"].n_vocab, spec["seed"])
+            toks, pm, gm, lg = O.ref_greedy(path, prompt, spec["n_gen"], n_ctx=spec["n_ctx"],
+                                            threads=os.cpu_count(),
+                                            want_logits=spec["shape"].n_vocab)
+            res[name] = {"tokens": toks.tolist(), "logits_sha256": sha(lg),
+                         "logits_head": lg[:8].tolist()}
+            print("npu", name, toks.tolist(), f"gen {gm:.0f} ms")
+    with open(out_path, "w") as f:
+        json.dump(res, f)
+
+
+def npu() -> None:
+    """Add the NPU-format decode goldens ("npu" key) to golden_decode.json,
+    leaving every other entry as it is."""
+    O.build()
+    assert O.have_ref(), "the reference tree is needed to make golden vectors"
+    with tempfile.TemporaryDirectory() as td:
+        out = os.path.join(td, "npu.json")
+        env = dict(os.environ, CHARSIU_NPU_QUANT="1")
+        subprocess.run([sys.executable, os.path.abspath(__file__), "--npu-child", out], env=env,
+                       check=True)
+        with open(out) as f:
+            res = json.load(f)
+    path = os.path.join(HERE, "golden_decode.json")
+    with open(path) as f:
+        dec = json.load(f)
+    dec["npu"] = res
+    with open(path, "w") as f:
+        json.dump(dec, f, indent=1)
+
+
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 2 and sys.argv[1] == "--npu-child":
+        npu_child(sys.argv[2])
+    elif len(sys.argv) > 1 and sys.argv[1] == "--npu":
+        npu()
+    else:
+        main()
