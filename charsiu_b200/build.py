@@ -22,7 +22,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libcharsiu_gpu.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-CU_SOURCES = ["charsiu_gpu.cu", "decoder.cu"]
+CU_SOURCES = ["charsiu_gpu.cu", "decoder.cu", "npu_layer.cu"]
 C_SOURCES = [os.path.join(HOST, f) for f in sorted(os.listdir(HOST)) if f.endswith(".c")] \
     if os.path.isdir(HOST) else []
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",

@@ -1,0 +1,173 @@
+// SPDX-License-Identifier: GPL-2.0-or-later
+// The matvec of charsiu's NPU number format (CHARSIU_NPU_QUANT): int8 weights
+// with one fp32 scale a row (npu_tensor_build, reference src/npuquant.c:34-296)
+// against an int8 activation with ONE scale d1 (charsiu_act_set's q1,
+// src/gguf.c:883-910):
+//     acc[r] = sum_k q[r][k] * q1[k]                 (exact int32)
+//     y[r]   = (float)acc[r] * d1 * scale[r]         (src/npudev.c:605, 710)
+// in float, left to right, as the NPU layer computes it from the accumulator
+// the hardware returns. The integer sum is exact in any order, so a warp may
+// split a row any way; only the two multiplies are ordered.
+//
+// Device layout: each tensor's rows back to back, a row padded with zeros to
+// kp bytes (kp = K rounded up to 16), so a lane's 16-byte loads are aligned.
+// A warp takes R rows at a time; lane L reads 16-byte chunks L, L + 32, ... of
+// each, U chunks of each row per step (R * U = 16 loads in flight a lane), and
+// dots them with dp4a against the activation staged in shared memory; one
+// warp reduction a row, and lane j writes row j.
+#pragma once
+
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace cgpu {
+
+constexpr int NPU_MAX_TENSORS = 8;
+constexpr int NPU_WARPS = 8;
+constexpr int NPU_INLINE_WORDS = 896;        // the activation in kernel parameters, up to K = 14336
+
+struct NpuTensor {
+	const int8_t *w;         // [rows][kp]
+	const float *scale;      // [rows]
+	float *y;
+	uint32_t rows, row_end;  // row_end: rows of this and every tensor before it
+};
+
+struct NpuParams {
+	NpuTensor t[NPU_MAX_TENSORS];
+	uint32_t ntensor, total_rows, kp;
+	float d1;
+	const int8_t *q1;        // kp bytes (device); unused when the activation is inline
+	// direct host calls: when done_flag is set, the last CTA to finish
+	// writes `seq` there (mapped host memory) once every y is visible to the
+	// host, and the kernel time since *t_start + 1
+	uint32_t *done_count;
+	uint32_t *done_flag;
+	unsigned long long *t_start;
+	uint32_t seq;
+};
+
+// The activation carried in the launch's parameters (a direct host call):
+// kp bytes in 16-byte words.
+template <int AW>
+struct NpuInline {
+	NpuParams p;
+	uint4 act[AW];
+};
+static_assert(sizeof(NpuInline<NPU_INLINE_WORDS>) <= 32764, "kernel parameter space");
+
+__device__ __forceinline__ int dp4a_s(uint32_t a, uint32_t b, int c)
+{
+	return __dp4a((int)a, (int)b, c);
+}
+
+template <int R, int U, int AW>
+__device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
+{
+	extern __shared__ __align__(16) uint8_t npu_smem[];
+	const uint32_t nch = p.kp / 16;
+	uint4 *act = reinterpret_cast<uint4 *>(npu_smem);
+	if (AW && p.done_flag && blockIdx.x == 0 && threadIdx.x == 0)
+		*p.t_start = globaltimer_ns();
+	if (AW) {
+		for (uint32_t i = threadIdx.x; i < nch; i += blockDim.x)
+			act[i] = inl[i];
+	}
+	pdl_wait();
+	if (!AW) {
+		const uint4 *g4 = reinterpret_cast<const uint4 *>(p.q1);
+		for (uint32_t i = threadIdx.x; i < nch; i += blockDim.x)
+			act[i] = g4[i];
+	}
+	__syncthreads();
+	pdl_launch_dependents();
+
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const uint32_t nw = gridDim.x * NPU_WARPS;
+	for (uint32_t r0 = (blockIdx.x * NPU_WARPS + warp) * R; r0 < p.total_rows; r0 += nw * R) {
+		const int8_t *wr[R];
+		uint32_t ti[R];
+#pragma unroll
+		for (int j = 0; j < R; j++) {
+			const uint32_t r = r0 + j;
+			uint32_t t = 0;
+			while (t + 1 < p.ntensor && r >= p.t[t].row_end)
+				t++;
+			ti[j] = t;
+			wr[j] = r < p.total_rows
+				? p.t[t].w + (uint64_t)(r - (p.t[t].row_end - p.t[t].rows)) * p.kp
+				: nullptr;
+		}
+		int acc[R];
+#pragma unroll
+		for (int j = 0; j < R; j++)
+			acc[j] = 0;
+		for (uint32_t c0 = lane; c0 < nch; c0 += 32 * U) {
+			uint4 wv[R][U];
+#pragma unroll
+			for (int j = 0; j < R; j++)
+#pragma unroll
+				for (int u = 0; u < U; u++) {
+					const uint32_t c = c0 + 32 * u;
+					wv[j][u] = (wr[j] && c < nch) ? ldg_stream((const uint8_t *)wr[j] + c * 16)
+								     : make_uint4(0, 0, 0, 0);
+				}
+#pragma unroll
+			for (int u = 0; u < U; u++) {
+				const uint32_t c = c0 + 32 * u;
+				if (c < nch) {
+					const uint4 a = act[c];
+#pragma unroll
+					for (int j = 0; j < R; j++) {
+						acc[j] = dp4a_s(wv[j][u].x, a.x, acc[j]);
+						acc[j] = dp4a_s(wv[j][u].y, a.y, acc[j]);
+						acc[j] = dp4a_s(wv[j][u].z, a.z, acc[j]);
+						acc[j] = dp4a_s(wv[j][u].w, a.w, acc[j]);
+					}
+				}
+			}
+		}
+#pragma unroll
+		for (int j = 0; j < R; j++) {
+			const int s = __reduce_add_sync(0xffffffffu, acc[j]);
+			if (lane == j && wr[j]) {
+				const NpuTensor &t = p.t[ti[j]];
+				const uint32_t row = r0 + j - (t.row_end - t.rows);
+				t.y[row] = __fmul_rn(__fmul_rn(__int2float_rn(s), p.d1), t.scale[row]);
+			}
+		}
+	}
+	if (AW && p.done_flag) {
+		// y is mapped host memory: this CTA's stores reach thread 0 through
+		// the barrier and are released at device scope by its count; the
+		// last CTA acquires them all and orders them before the flag with one
+		// system fence
+		__syncthreads();
+		if (threadIdx.x == 0 && atom_add_acq_rel_gpu(p.done_count, 1u) == gridDim.x - 1) {
+			*p.done_count = 0;
+			const unsigned long long dt =
+				globaltimer_ns() - *(volatile const unsigned long long *)p.t_start;
+			__threadfence_system();
+			p.done_flag[1] = dt > 0xffffffffull ? 0xffffffffu : (uint32_t)dt;
+			__threadfence_system();
+			*(volatile uint32_t *)p.done_flag = p.seq;
+		}
+	}
+}
+
+template <int R, int U>
+__global__ void __launch_bounds__(NPU_WARPS * 32)
+npumv_kernel(const __grid_constant__ NpuParams p)
+{
+	npumv_body<R, U, 0>(p, nullptr);
+}
+
+template <int R, int U, int AW>
+__global__ void __launch_bounds__(NPU_WARPS * 32)
+npumv_inline_kernel(const __grid_constant__ NpuInline<AW> a)
+{
+	npumv_body<R, U, AW>(a.p, a.act);
+}
+
+} // namespace cgpu

@@ -175,6 +175,22 @@ __device__ __forceinline__ uint64_t fma2_rn(uint64_t a, uint64_t b, uint64_t c)
 	return d;
 }
 
+// 16 bytes (2 bytes) of streamed read-only data: no L1 allocation
+__device__ __forceinline__ uint4 ldg_stream(const uint8_t *p)
+{
+	uint4 v;
+	asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+		     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+	return v;
+}
+
+__device__ __forceinline__ uint16_t ldg_stream_u16(const uint8_t *p)
+{
+	uint16_t v;
+	asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+	return v;
+}
+
 // fp16 bits -> fp32, exact for every finite value (subnormals included)
 __device__ __forceinline__ float half_bits_to_float(uint16_t h)
 {

@@ -90,21 +90,6 @@ __global__ void gather_epoch_kernel(uint32_t *sync_local)
 }
 static_assert(sizeof(QmvInline<QMV_INLINE_MAX_WORDS>) <= 32764, "kernel parameter space");
 
-__device__ __forceinline__ uint4 ldg_stream(const uint8_t *p)
-{
-	uint4 v;
-	asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-		     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-	return v;
-}
-
-__device__ __forceinline__ uint16_t ldg_stream_u16(const uint8_t *p)
-{
-	uint16_t v;
-	asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
-	return v;
-}
-
 // One segment's raw bytes for this lane: step j covers blocks 4j..4j+3; lane
 // l reads block p = l>>3, row r = l&7 (q8_0: its two 16-byte chunks; q4_0:
 // its one) and that block-row's fp16 delta.

@@ -1,11 +1,12 @@
 // SPDX-License-Identifier: GPL-2.0-or-later
-// The byte layouts of the three charsiu structs this layer reads, so it can
+// The byte layouts of the charsiu structs this layer reads, so it can
 // take them by pointer without including charsiu's headers. They must match
 // the reference's definitions field for field on LP64 (x86-64, aarch64):
 //   struct gguf_tensor    include/charsiu_llm.h:51-59
 //   struct charsiu_act    include/charsiu_llm.h:100-119
 //   struct charsiu_matmul include/charsiu.h:113-119
 //   struct charsiu_job    include/charsiu.h:194-225
+//   struct npu_tensor     include/charsiu_llm.h:143-161
 // tests/test_abi.py compiles these against the reference headers and
 // compares every offset.
 #pragma once
@@ -51,7 +52,34 @@ struct RefJob {
 	int acc_out;
 };
 
+struct RefNpuTensor {
+	int8_t *q;               // [n][k]
+	float *scale;            // n * ngroup
+	uint64_t kgroup;         // 0 or k: one scale a row
+	float *kscale;           // NULL when off
+	double *astat;
+	uint64_t acalls;
+	double *acov;
+	float *xcal;
+	unsigned nxcal;
+	int32_t *wsum;
+	uint64_t n, k;
+	double rms_rel;
+	float out_scale;
+	double out_clip;
+	uint64_t out_calls;
+	float amax_lo, amax_hi;
+	char name[80];
+};
+
 static_assert(sizeof(RefGgufTensor) == 152, "gguf_tensor layout");
+static_assert(sizeof(RefNpuTensor) == 216, "npu_tensor layout");
+static_assert(offsetof(RefNpuTensor, kgroup) == 16 && offsetof(RefNpuTensor, kscale) == 24,
+	      "npu_tensor.kgroup/kscale");
+static_assert(offsetof(RefNpuTensor, n) == 80 && offsetof(RefNpuTensor, k) == 88,
+	      "npu_tensor.n/k");
+static_assert(offsetof(RefNpuTensor, name) == 136, "npu_tensor.name");
+static_assert(offsetof(RefAct, q1) == 48 && offsetof(RefAct, d1) == 56, "charsiu_act.q1/d1");
 static_assert(offsetof(RefGgufTensor, ne) == 88, "gguf_tensor.ne");
 static_assert(offsetof(RefGgufTensor, type) == 120, "gguf_tensor.type");
 static_assert(offsetof(RefGgufTensor, data) == 136, "gguf_tensor.data");

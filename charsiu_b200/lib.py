@@ -80,6 +80,18 @@ SIGNATURES = [
     ("charsiu_gpu_decoder_logits", C.POINTER(C.c_float), [_vp]),
     ("charsiu_gpu_decoder_launches", C.c_uint, [_vp]),
     ("charsiu_gpu_ordered_sum_dev", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp]),
+    ("charsiu_npu_open", _vp, [C.c_uint, C.c_uint, C.c_uint]),
+    ("charsiu_npu_close", None, [_vp]),
+    ("charsiu_npu_add", C.c_int, [_vp, _vp]),
+    ("charsiu_npu_matvec", C.c_int, [_vp, C.c_int, _vp, _vp]),
+    ("charsiu_npu_matvec_group", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp]),
+    ("charsiu_npu_submits", C.c_ulong, [_vp]),
+    ("charsiu_npu_report", None, [_vp]),
+    ("charsiu_npu_add_flat", C.c_int, [_vp, _vp, _vp, C.c_uint64, C.c_uint64, C.c_char_p]),
+    ("charsiu_npu_matvec_flat", C.c_int, [_vp, _vp, C.c_uint, _vp, C.c_float, C.c_uint, _vp]),
+    ("charsiu_npu_matvec_dev", C.c_int, [_vp, _vp, C.c_uint, _vp, C.c_float, _vp, _vp]),
+    ("charsiu_npu_error", C.c_char_p, [_vp]),
+    ("charsiu_npu_dead", C.c_int, [_vp]),
 ]
 
 
@@ -383,3 +395,92 @@ class Llama:
         if rc != n_gen:
             raise GpuError(f"greedy failed: {self.L.charsiu_gpu_error(self.layer_handle)}")
         return out, lg, ms.value
+
+
+class NpuActStruct(C.Structure):
+    """struct charsiu_act (include/charsiu_llm.h:100-119), for the struct forms."""
+    _fields_ = [("f", C.c_void_p), ("n", C.c_int), ("nb", C.c_int), ("q", C.c_void_p),
+                ("d", C.c_void_p), ("bs", C.c_void_p), ("quantised", C.c_int),
+                ("q1", C.c_void_p), ("d1", C.c_float), ("q1_valid", C.c_int)]
+
+
+class NpuTensorStruct(C.Structure):
+    """struct npu_tensor (include/charsiu_llm.h:143-161), for the struct forms."""
+    _fields_ = [("q", C.c_void_p), ("scale", C.c_void_p), ("kgroup", C.c_uint64),
+                ("kscale", C.c_void_p), ("astat", C.c_void_p), ("acalls", C.c_uint64),
+                ("acov", C.c_void_p), ("xcal", C.c_void_p), ("nxcal", C.c_uint),
+                ("wsum", C.c_void_p), ("n", C.c_uint64), ("k", C.c_uint64),
+                ("rms_rel", C.c_double), ("out_scale", C.c_float), ("out_clip", C.c_double),
+                ("out_calls", C.c_uint64), ("amax_lo", C.c_float), ("amax_hi", C.c_float),
+                ("name", C.c_char * 80)]
+
+
+class NpuLayer:
+    """charsiu_npu_*: charsiu's NPU device layer (the NPU number format) on the GPU."""
+
+    def __init__(self, max_k: int, max_n: int, max_tensors: int = 16):
+        self.L = lib()
+        self.h = self.L.charsiu_npu_open(max_k, max_n, max_tensors)
+        if not self.h:
+            raise GpuError("charsiu_npu_open failed")
+        self.rows = {}
+
+    def close(self):
+        if self.h:
+            self.L.charsiu_npu_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def error(self) -> str:
+        return self.L.charsiu_npu_error(self.h).decode()
+
+    @property
+    def calls(self) -> int:
+        return self.L.charsiu_npu_submits(self.h)
+
+    @property
+    def dead(self) -> bool:
+        return bool(self.L.charsiu_npu_dead(self.h))
+
+    def report(self):
+        self.L.charsiu_npu_report(self.h)
+
+    def add(self, q: np.ndarray, scale: np.ndarray, name: str = "") -> int:
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        scale = np.ascontiguousarray(scale, dtype=np.float32)
+        n, k = q.shape
+        tid = self.L.charsiu_npu_add_flat(self.h, _p(q), _p(scale), n, k, name.encode())
+        if tid < 0:
+            raise GpuError(f"add {name}: {self.error()}")
+        self.rows[tid] = n
+        return tid
+
+    def add_struct(self, t: NpuTensorStruct) -> int:
+        tid = self.L.charsiu_npu_add(self.h, C.byref(t))
+        if tid >= 0:
+            self.rows[tid] = t.n
+        return tid
+
+    def matvec(self, ids, q1: np.ndarray, d1, k: int):
+        ids = list(ids)
+        q1 = np.ascontiguousarray(q1, dtype=np.int8)
+        ys = [np.empty(self.rows[i], dtype=np.float32) for i in ids]
+        idarr = (C.c_int * len(ids))(*ids)
+        yarr = (C.c_void_p * len(ids))(*[_p(y) for y in ys])
+        rc = self.L.charsiu_npu_matvec_flat(self.h, C.addressof(idarr), len(ids), _p(q1),
+                                            float(d1), k, C.addressof(yarr))
+        if rc:
+            raise GpuError(f"npu matvec: {self.error()}")
+        return ys
+
+    def matvec_dev(self, ids, q1_ptr: int, d1, ys_ptrs, stream: int = 0) -> int:
+        ids = list(ids)
+        idarr = (C.c_int * len(ids))(*ids)
+        yarr = (C.c_void_p * len(ids))(*ys_ptrs)
+        return self.L.charsiu_npu_matvec_dev(self.h, C.addressof(idarr), len(ids), q1_ptr,
+                                             float(d1), C.addressof(yarr), stream or None)

@@ -20,7 +20,8 @@ def declared():
         if h.endswith(".h"):
             with open(os.path.join(INCLUDE, h)) as f:
                 txt = f.read()
-            names |= set(re.findall(r"CHARSIU_GPU_API[^;{]*?\b(charsiu_gpu\w*)\s*\(", txt))
+            names |= set(re.findall(r"CHARSIU_GPU_API[^;{]*?\b(charsiu_(?:gpu|npu)\w*)\s*\(",
+                                    txt))
     return names
 
 
@@ -60,11 +61,14 @@ LAYOUT_PROBE = r"""
 #include "charsiu_llm.h"
 #define P(T, f) printf(#T "." #f " %zu\n", offsetof(struct T, f))
 int main(void) {
-  printf("gguf_tensor %zu\nact %zu\njob %zu\n", sizeof(struct gguf_tensor),
-         sizeof(struct charsiu_act), sizeof(struct charsiu_job));
+  printf("gguf_tensor %zu\nact %zu\njob %zu\nnpu_tensor %zu\n", sizeof(struct gguf_tensor),
+         sizeof(struct charsiu_act), sizeof(struct charsiu_job), sizeof(struct npu_tensor));
   P(gguf_tensor, ne); P(gguf_tensor, type); P(gguf_tensor, data);
   P(charsiu_act, q); P(charsiu_act, d); P(charsiu_act, quantised); P(charsiu_act, n);
   P(charsiu_job, input_scale); P(charsiu_job, input_zero_point); P(charsiu_job, acc_out);
+  P(charsiu_act, q1); P(charsiu_act, d1);
+  P(npu_tensor, kgroup); P(npu_tensor, kscale); P(npu_tensor, n); P(npu_tensor, k);
+  P(npu_tensor, name);
   return 0; }
 """
 
@@ -73,6 +77,9 @@ MIRROR = {
     "gguf_tensor.ne": 88, "gguf_tensor.type": 120, "gguf_tensor.data": 136,
     "charsiu_act.q": 16, "charsiu_act.d": 24, "charsiu_act.quantised": 40, "charsiu_act.n": 8,
     "charsiu_job.input_scale": 36, "charsiu_job.input_zero_point": 48, "charsiu_job.acc_out": 60,
+    "npu_tensor": 216, "charsiu_act.q1": 48, "charsiu_act.d1": 56,
+    "npu_tensor.kgroup": 16, "npu_tensor.kscale": 24, "npu_tensor.n": 80, "npu_tensor.k": 88,
+    "npu_tensor.name": 136,
 }
 
 
