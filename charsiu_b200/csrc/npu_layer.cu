@@ -311,9 +311,14 @@ extern "C" {
 
 struct charsiu_npu *charsiu_npu_open(unsigned max_k, unsigned max_n, unsigned max_tensors)
 {
-	int device = 0, ndev = 0;
-	if (const char *e = getenv("CHARSIU_GPU_DEVICE"))
-		device = atoi(e);
+	const char *e = getenv("CHARSIU_GPU_DEVICE");
+	return charsiu_npu_open_ex(max_k, max_n, max_tensors, e ? atoi(e) : 0);
+}
+
+struct charsiu_npu *charsiu_npu_open_ex(unsigned max_k, unsigned max_n, unsigned max_tensors,
+					int device)
+{
+	int ndev = 0;
 	if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
 		fprintf(stderr, "charsiu: no CUDA device %d\n", device);
 		return nullptr;

@@ -22,6 +22,7 @@
 #include <unistd.h>
 
 #include "charsiu_gpu_llama.h"
+#include "charsiu_npu.h"
 #include "pool.h"
 
 #define API
@@ -351,6 +352,12 @@ struct charsiu_gpu_llama {
 	struct pool *pool;        /* attention heads and SiLU chunks; NULL = this thread */
 	struct charsiu_gpu_decoder *dec;   /* the whole step on the device, when resident */
 	int resident;
+	/* CHARSIU_NPU_QUANT: every projection and the head in the NPU number
+	 * format, through charsiu_npu_* (src/llama.c:110-312) */
+	int npu_mode;
+	struct charsiu_npu *npu;
+	int8_t *aq1;              /* the activation under one scale */
+	float ad1;
 };
 
 static float half_to_float(uint16_t h)
@@ -507,6 +514,103 @@ static void act_set(struct charsiu_gpu_llama *m, const float *x, int n)
 	}
 }
 
+/* charsiu_act_set's single-scale form (src/gguf.c:883-910), for the NPU
+ * number format: d1 = amax / 127, q1 = lrintf(x * (1 / d1)) clamped to
+ * [-127, 127], zero past n */
+static void act_q1(struct charsiu_gpu_llama *m, const float *x, int n)
+{
+	int nb = (n + 31) / 32;
+	float amax = 0.0f, d, id;
+
+	for (int i = 0; i < n; i++) {
+		float av = x[i] < 0.0f ? -x[i] : x[i];
+
+		if (av > amax)
+			amax = av;
+	}
+	d = amax / 127.0f;
+	id = d != 0.0f ? 1.0f / d : 0.0f;
+	m->ad1 = d;
+	for (int i = 0; i < nb * 32; i++) {
+		int v = i < n ? (int)lrintf(x[i] * id) : 0;
+
+		if (v > 127)
+			v = 127;
+		if (v < -127)
+			v = -127;
+		m->aq1[i] = (int8_t)v;
+	}
+}
+
+/* npu_tensor_build's default form (src/npuquant.c:34-296: eight bits, one
+ * scale a row, no k factor), rows [r0, r1) of t: each row dequantised, amax,
+ * d = amax / 127, q = lrintf(x * (1 / d)) clamped to [-127, 127] */
+struct npu_build_job {
+	const struct gt *t;
+	int8_t *q;
+	float *scale;
+	uint64_t rows_per_item;
+	int failed;
+};
+
+static void npu_build_rows(void *arg, int item)
+{
+	struct npu_build_job *j = arg;
+	uint64_t k = j->t->ne[0], n = j->t->ne[1];
+	uint64_t r0 = (uint64_t)item * j->rows_per_item;
+	uint64_t r1 = r0 + j->rows_per_item < n ? r0 + j->rows_per_item : n;
+	float *row = malloc(k * sizeof(float));
+
+	if (!row) {
+		j->failed = 1;
+		return;
+	}
+	for (uint64_t r = r0; r < r1; r++) {
+		float amax = 0.0f, d, id;
+
+		if (row_f32(j->t, r, row)) {
+			j->failed = 1;
+			break;
+		}
+		for (uint64_t i = 0; i < k; i++) {
+			float a = fabsf(row[i]);
+
+			if (a > amax)
+				amax = a;
+		}
+		d = amax / 127.0f;
+		id = d != 0.0f ? 1.0f / d : 0.0f;
+		j->scale[r] = d;
+		for (uint64_t i = 0; i < k; i++) {
+			int v = (int)lrintf(row[i] * id);
+
+			if (v > 127)
+				v = 127;
+			if (v < -127)
+				v = -127;
+			j->q[r * k + i] = (int8_t)v;
+		}
+	}
+	free(row);
+}
+
+/* the NPU-format copy of t on the GPU layer: its id, or -1 */
+static int add_npu(struct charsiu_gpu_llama *m, const struct gt *t)
+{
+	uint64_t k = t->ne[0], n = t->ne[1];
+	struct npu_build_job j = { t, malloc(n * k), malloc(n * sizeof(float)), 64, 0 };
+	int id = -1;
+
+	if (j.q && j.scale) {
+		pool_run(m->pool, npu_build_rows, &j, (int)((n + j.rows_per_item - 1) / j.rows_per_item));
+		if (!j.failed)
+			id = charsiu_npu_add_flat(m->npu, j.q, j.scale, n, k, t->name);
+	}
+	free(j.q);
+	free(j.scale);
+	return id;
+}
+
 static void rmsnorm(float *out, const float *x, const float *gw, uint32_t n, float eps)
 {
 	float ss = 0.0f, scale;
@@ -621,6 +725,11 @@ API int charsiu_gpu_llama_set_resident(struct charsiu_gpu_llama *m, int on)
 {
 	if (!m)
 		return -1;
+	if (on && m->npu_mode) {
+		fprintf(stderr, "charsiu: the device step runs the GGML formats, not the NPU "
+				"number format\n");
+		return -1;
+	}
 	if (on && !m->dec && !(m->dec = make_decoder(m)))
 		return -1;
 	m->resident = on != 0;
@@ -632,6 +741,15 @@ API int charsiu_gpu_llama_set_resident(struct charsiu_gpu_llama *m, int on)
 static int project(struct charsiu_gpu_llama *m, const float *x, uint32_t k, const int *ids,
 		   float **ys, unsigned n)
 {
+	if (m->npu_mode) {
+		act_q1(m, x, (int)k);
+		if (n > 1 && !m->nogroup)
+			return charsiu_npu_matvec_flat(m->npu, ids, n, m->aq1, m->ad1, k, ys);
+		for (unsigned i = 0; i < n; i++)
+			if (charsiu_npu_matvec_flat(m->npu, &ids[i], 1, m->aq1, m->ad1, k, &ys[i]))
+				return -1;
+		return 0;
+	}
 	act_set(m, x, (int)k);
 	if (n > 1 && !m->nogroup)
 		return charsiu_gpu_matvec_q(m->dev, ids, n, m->aq, m->ad, k, ys);
@@ -658,6 +776,9 @@ API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m)
 	}
 	pool_free(m->pool);
 	charsiu_gpu_decoder_free(m->dec);
+	if (m->npu && getenv("CHARSIU_GPU_REPORT"))
+		charsiu_npu_report(m->npu);
+	charsiu_npu_close(m->npu);
 	if (m->dev && getenv("CHARSIU_GPU_REPORT"))
 		charsiu_gpu_report(m->dev);
 	charsiu_gpu_close(m->dev);
@@ -665,7 +786,7 @@ API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m)
 	free(m->kcache); free(m->vcache);
 	free(m->x); free(m->xb); free(m->xb2); free(m->hb); free(m->hb2);
 	free(m->q); free(m->k); free(m->v); free(m->att); free(m->logits);
-	free(m->aq); free(m->ad); free(m->rope_cs);
+	free(m->aq); free(m->ad); free(m->rope_cs); free(m->aq1);
 	gclose(&m->g);
 	free(m);
 }
@@ -735,6 +856,26 @@ API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *path, int n_ctx
 				     m->n_layer * 9 + 2, device, 0, 1);
 	if (!m->dev)
 		goto fail;
+	{
+		/* CHARSIU_GPU_THREADS helpers for the CPU steps (0: none) */
+		const char *e = getenv("CHARSIU_GPU_THREADS");
+		long cpus = sysconf(_SC_NPROCESSORS_ONLN);
+		int threads = e ? atoi(e) : (int)(cpus > 2 ? (cpus - 1 < 8 ? cpus - 1 : 8) : 0);
+
+		m->pool = pool_new(threads);
+	}
+	{
+		const char *e = getenv("CHARSIU_NPU_QUANT");
+
+		m->npu_mode = e && *e != '0';
+	}
+	if (m->npu_mode) {
+		m->npu = charsiu_npu_open_ex(widest, m->n_vocab > widest ? m->n_vocab : widest,
+					     m->n_layer * 9 + 2, device);
+		m->aq1 = calloc((size_t)(widest + 31) / 32 * 32, 1);
+		if (!m->npu || !m->aq1)
+			goto fail;
+	}
 	m->L = calloc(m->n_layer, sizeof(*m->L));
 	if (!m->L)
 		goto fail;
@@ -753,14 +894,17 @@ API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *path, int n_ctx
 			snprintf(key, sizeof(key), "blk.%u.%s.weight", l, pname[p]);
 			if (!(L->w[p] = need(m, key)))
 				goto fail;
-			L->id[p] = charsiu_gpu_add_blocks(m->dev, L->w[p]->type, L->w[p]->ne[0],
-							  L->w[p]->ne[1], L->w[p]->data, key);
+			L->id[p] = m->npu_mode
+				? add_npu(m, L->w[p])
+				: charsiu_gpu_add_blocks(m->dev, L->w[p]->type, L->w[p]->ne[0],
+							 L->w[p]->ne[1], L->w[p]->data, key);
 			if (L->id[p] < 0)
 				goto fail;
 		}
 	}
-	m->out_id = charsiu_gpu_add_blocks(m->dev, m->out->type, m->out->ne[0], m->out->ne[1],
-					   m->out->data, m->out->name);
+	m->out_id = m->npu_mode ? add_npu(m, m->out)
+				: charsiu_gpu_add_blocks(m->dev, m->out->type, m->out->ne[0],
+							 m->out->ne[1], m->out->data, m->out->name);
 	if (m->out_id < 0)
 		goto fail;
 
@@ -783,14 +927,6 @@ API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *path, int n_ctx
 	if (!m->rope_cs || !m->kcache || !m->vcache || !m->x || !m->xb || !m->xb2 || !m->hb || !m->hb2 ||
 	    !m->q || !m->k || !m->v || !m->att || !m->logits || !m->aq || !m->ad)
 		goto fail;
-	{
-		/* CHARSIU_GPU_THREADS helpers for the CPU steps (0: none) */
-		const char *e = getenv("CHARSIU_GPU_THREADS");
-		long cpus = sysconf(_SC_NPROCESSORS_ONLN);
-		int threads = e ? atoi(e) : (int)(cpus > 2 ? (cpus - 1 < 8 ? cpus - 1 : 8) : 0);
-
-		m->pool = pool_new(threads);
-	}
 	{
 		const char *e = getenv("CHARSIU_GPU_RESIDENT");
 
@@ -1087,4 +1223,9 @@ API struct charsiu_gpu *charsiu_gpu_llama_layer(struct charsiu_gpu_llama *m)
 API struct charsiu_gpu_decoder *charsiu_gpu_llama_decoder(struct charsiu_gpu_llama *m)
 {
 	return m ? m->dec : NULL;
+}
+
+API struct charsiu_npu *charsiu_gpu_llama_npu(struct charsiu_gpu_llama *m)
+{
+	return m ? m->npu : NULL;
 }

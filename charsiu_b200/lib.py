@@ -73,6 +73,7 @@ SIGNATURES = [
     ("charsiu_gpu_llama_layer", _vp, [_vp]),
     ("charsiu_gpu_llama_set_resident", C.c_int, [_vp, C.c_int]),
     ("charsiu_gpu_llama_decoder", _vp, [_vp]),
+    ("charsiu_gpu_llama_npu", _vp, [_vp]),
     ("charsiu_gpu_row_dev", C.c_int, [_vp, C.c_int, _vp, _vp, _vp]),
     ("charsiu_gpu_decoder_new", _vp, [_vp, _vp]),
     ("charsiu_gpu_decoder_free", None, [_vp]),
@@ -81,6 +82,7 @@ SIGNATURES = [
     ("charsiu_gpu_decoder_launches", C.c_uint, [_vp]),
     ("charsiu_gpu_ordered_sum_dev", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp]),
     ("charsiu_npu_open", _vp, [C.c_uint, C.c_uint, C.c_uint]),
+    ("charsiu_npu_open_ex", _vp, [C.c_uint, C.c_uint, C.c_uint, C.c_int]),
     ("charsiu_npu_close", None, [_vp]),
     ("charsiu_npu_add", C.c_int, [_vp, _vp]),
     ("charsiu_npu_matvec", C.c_int, [_vp, C.c_int, _vp, _vp]),
@@ -355,6 +357,12 @@ class Llama:
     @property
     def layer_handle(self):
         return self.L.charsiu_gpu_llama_layer(self.h)
+
+    @property
+    def npu_calls(self) -> int:
+        """Calls of the NPU-format layer (CHARSIU_NPU_QUANT=1 at open), else 0."""
+        h = self.L.charsiu_gpu_llama_npu(self.h)
+        return self.L.charsiu_npu_submits(h) if h else 0
 
     @property
     def step_launches(self) -> int:

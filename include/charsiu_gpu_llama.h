@@ -68,6 +68,11 @@ CHARSIU_GPU_API const char *charsiu_gpu_llama_stage_name(int i);
 CHARSIU_GPU_API uint32_t charsiu_gpu_llama_vocab(const struct charsiu_gpu_llama *m);
 /* the device layer the model runs on (for its report and counters) */
 CHARSIU_GPU_API struct charsiu_gpu *charsiu_gpu_llama_layer(struct charsiu_gpu_llama *m);
+/* the NPU-format layer when the model was opened with CHARSIU_NPU_QUANT=1
+ * (every projection and the head in charsiu's NPU number format through
+ * charsiu_npu_*, include/charsiu_npu.h, as src/llama.c:110-312 routes them);
+ * else NULL */
+CHARSIU_GPU_API struct charsiu_npu *charsiu_gpu_llama_npu(struct charsiu_gpu_llama *m);
 /* the device step, once charsiu_gpu_llama_set_resident has built it; else NULL */
 CHARSIU_GPU_API struct charsiu_gpu_decoder *charsiu_gpu_llama_decoder(struct charsiu_gpu_llama *m);
 

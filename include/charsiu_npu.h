@@ -40,6 +40,9 @@ struct charsiu_act;
  * CHARSIU_GPU_DEVICE names. NULL without a B200. */
 CHARSIU_GPU_API struct charsiu_npu *charsiu_npu_open(unsigned max_k, unsigned max_n,
 						     unsigned max_tensors);
+/* the same on CUDA device `device` */
+CHARSIU_GPU_API struct charsiu_npu *charsiu_npu_open_ex(unsigned max_k, unsigned max_n,
+							unsigned max_tensors, int device);
 CHARSIU_GPU_API void charsiu_npu_close(struct charsiu_npu *g);
 
 /* charsiu_npu_add (src/npudev.c:389-461): copy t's int8 rows and scales to the
