@@ -342,6 +342,17 @@ def run_ours(args, rank, world, dist):
 
     e2e = run_e2e_resident(path, args, world, dist, dev)
     e2e["host_routed"] = run_e2e(path, args, lib, world, dist, dev)
+    npu_format = None
+    if world == 1:
+        # charsiu's NPU number format (CHARSIU_NPU_QUANT): its matvec at the
+        # gate/up shape, and the workload's decode with every projection on it
+        us, algo, copies, _ = npu_matvec_case(2048, 8192, 200, 10)
+        peak, _ = peaks()
+        gbs = algo / (us * 1e-6) / 1e9
+        npu_format = {"matvec_k2048_n8192": {"value": round(gbs, 1), "unit": "GB/s",
+                                             "frac": round(gbs / peak, 4),
+                                             "us_per_launch": round(us, 3)},
+                      "decode_e2e": npu_decode_e2e(path, args.steps)}
 
     out = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
@@ -359,6 +370,8 @@ def run_ours(args, rank, world, dist):
            "clocks": clk}
     if split:
         out["column_split"] = split
+    if npu_format:
+        out["npu_format"] = npu_format
     if rank == 0 and world == 1:
         out["cpu_baseline"] = cpu_baseline(path)
     return out
@@ -574,6 +587,110 @@ def run_matvec_case(args):
             "gpu_launches": args.steps * (1 if m == 1 else 2), "clocks": clk}
 
 
+# ---- charsiu's NPU number format (CHARSIU_NPU_QUANT) ----------------------------------
+
+def npu_matvec_case(k: int, n: int, steps: int, warmup: int):
+    """One NPU-format matvec shape (int8 rows, one scale a row, one activation
+    scale) through charsiu_npu_matvec_dev, copies of the weights rotated past
+    2x L2, replayed as a CUDA graph: (us a launch, algorithmic bytes, copies,
+    clocks)."""
+    import torch
+    from charsiu_b200.lib import NpuLayer
+
+    # the format's shapes and ranges: int8 rows in [-127, 127], a scale a row
+    # of the q8_0 workload's size, an activation quantised to [-127, 127]
+    rng = np.random.default_rng(1)
+    q = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    s = (np.abs(rng.normal(0.0, 0.02, n)) / 127).astype(np.float32)
+    q1 = np.zeros((k + 31) // 32 * 32, np.int8)
+    q1[:k] = rng.integers(-127, 128, size=k, dtype=np.int8)
+    d1 = np.float32(0.03)
+    wbytes = q.nbytes
+    copies = max(2, -(-2 * 126 * 2 ** 20 // wbytes))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    with NpuLayer(k, n, copies) as L:
+        ids = [L.add(q, s, f"copy{i}") for i in range(copies)]
+        q1_t = torch.from_numpy(q1[:(k + 15) // 16 * 16].copy()).to(dev)
+        y = torch.empty(n, dtype=torch.float32, device=dev)
+        stream = torch.cuda.Stream(device=dev)
+
+        def launch(i):
+            assert L.matvec_dev([ids[i % copies]], q1_t.data_ptr(), d1, [y.data_ptr()],
+                                stream.cuda_stream) == 0, L.error()
+        for i in range(warmup):
+            launch(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(steps):
+                launch(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        clocks = Clocks(0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        us = e0.elapsed_time(e1) * 1e3 / steps
+        del graph
+    algo = wbytes + 4 * n + (k + 15) // 16 * 16 + 4 * n
+    return us, algo, copies, clk
+
+
+def npu_decode_e2e(path: str, steps: int):
+    """The workload's greedy decode in the NPU number format through the C ABI
+    (charsiu_gpu_llama_forward after opening with CHARSIU_NPU_QUANT=1): every
+    projection and the head a charsiu_npu_* call with host buffers."""
+    from charsiu_b200.lib import Llama
+
+    os.environ["CHARSIU_NPU_QUANT"] = "1"
+    try:
+        prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
+        n_gen = SPEC["n_gen"]
+        reps = max(1, min(steps, 96) // n_gen)
+        total_ms, ok = 0.0, True
+        with open(os.path.join(ROOT, "tests", "golden", "golden_decode.json")) as f:
+            gold = json.load(f)["npu"]["llama1b_q8"]["tokens"]
+        with Llama(path, n_ctx=len(prompt) + n_gen + 1) as m:
+            m.greedy(prompt, n_gen)
+            for _ in range(reps):
+                toks, _, gen_ms = m.greedy(prompt, n_gen)
+                total_ms += gen_ms
+                ok = ok and toks.tolist() == gold
+            calls = m.npu_calls
+    finally:
+        del os.environ["CHARSIU_NPU_QUANT"]
+    return {"value": round(reps * n_gen / (total_ms / 1e3), 2), "unit": UNIT,
+            "steps": reps * n_gen, "ms_per_step": round(total_ms / (reps * n_gen), 4),
+            "tokens_match_reference": ok, "npu_calls": calls,
+            "api": "charsiu_gpu_llama_greedy, opened with CHARSIU_NPU_QUANT=1: each "
+                   "projection and the head a charsiu_npu_* host call"}
+
+
+def run_npu_case(args):
+    """--npu K:N: the NPU-format matvec at one shape; with the decode too when
+    K:N is the default 2048:8192."""
+    k, n = (int(v) for v in args.npu.split(":"))
+    us, algo, copies, clk = npu_matvec_case(k, n, args.steps, args.warmup)
+    peak, peak_kind = peaks()
+    gbs = algo / (us * 1e-6) / 1e9
+    return {"metric": "NPU-format int8 matvec HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(us / 1e3, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"NPU-format matvec M=1 K={k} N={n} (int8 rows, one scale "
+                                   "a row, one activation scale)", "weight_copies": copies,
+                       "l2": f"{copies} weight copies rotated (> 2x L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "bytes_per_launch": algo, "avg_launch_us": round(us, 3)},
+            "gpu_launches": args.steps, "clocks": clk}
+
+
 # ---- the int8 matmul with the NPU output stage --------------------------------------
 
 def run_int8_case(args):
@@ -749,6 +866,8 @@ def main():
                     help="time one batched decode step of M sequences instead")
     ap.add_argument("--int8", default=None, metavar="M:K:N",
                     help="time the int8 matmul with the NPU output stage (e.g. 224:64:64)")
+    ap.add_argument("--npu", default=None, metavar="K:N",
+                    help="time the NPU-format (CHARSIU_NPU_QUANT) matvec at one shape")
     ap.add_argument("--resident", action="store_true",
                     help="time only the device-resident greedy decode (the e2e leg)")
     ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N[:M]",
@@ -779,6 +898,9 @@ def main():
             return
         if args.int8:
             print(json.dumps(run_int8_case(args)), flush=True)
+            return
+        if args.npu:
+            print(json.dumps(run_npu_case(args)), flush=True)
             return
         if args.resident:
             import torch

@@ -49,7 +49,8 @@ struct NpuEnt {
 	double weight_mb;
 };
 
-// The launch shape for kp-byte rows: R rows a warp, U chunks a row a step.
+// The kernel for kp-byte rows: R rows a warp at most, U chunks a row a step
+// (R * U = 16 loads in flight a lane).
 struct Shape {
 	int r, u;
 };
@@ -66,6 +67,16 @@ Shape shape_for(uint32_t kp)
 	if (ch <= 8)
 		return {2, 8};
 	return {1, 16};
+}
+
+// Rows a warp takes: the kernel's R, or CHARSIU_GPU_NPU_ROWS (`fixed`) when
+// set. Fewer rows a warp for the smaller tensors, to spread them over every
+// SM, measured slower (K=2048: N=8192 6.5 against 5.2 us, N=2048 3.7 against
+// 3.3 us): these launches pay a fixed ~3 us (N=512 takes 2.9 us), not a
+// shortage of loads in flight.
+uint32_t rows_per_warp(int r_max, int fixed)
+{
+	return (uint32_t)(fixed > 0 && fixed < r_max ? fixed : r_max);
 }
 
 } // namespace
@@ -89,6 +100,7 @@ struct charsiu_npu {
 	unsigned long calls = 0, launches = 0;
 	double busy_us = 0, kern_ms = 0, weight_mb = 0, slow_us = 100000;
 	int strikes = 0, dead = 0, whined = 0, no_pdl = 0;
+	int rows = 0;                      // CHARSIU_GPU_NPU_ROWS: rows a warp (0: by size)
 	std::string err;
 };
 
@@ -183,8 +195,8 @@ int launch(charsiu_npu *g, const NpuParams &p, const void *inl, cudaStream_t st)
 			return -1;
 		g->occ[slot] = occ;
 	}
-	const uint32_t units = (p.total_rows + (uint32_t)sh.r * NPU_WARPS - 1) /
-			       ((uint32_t)sh.r * NPU_WARPS);
+	const uint32_t rpw = rows_per_warp(sh.r, g->rows);
+	const uint32_t units = (p.total_rows + rpw * NPU_WARPS - 1) / (rpw * NPU_WARPS);
 	unsigned grid = (unsigned)g->occ[slot] * g->sm_count;
 	if (units < grid)
 		grid = units ? units : 1;
@@ -199,6 +211,9 @@ int launch(charsiu_npu *g, const NpuParams &p, const void *inl, cudaStream_t st)
 	cfg.attrs = attr;
 	cfg.numAttrs = g->no_pdl ? 0 : 1;
 	NpuParams arg = p;
+	arg.rows_per_warp = rpw;
+	if (inl)
+		static_cast<NpuInline<NPU_INLINE_WORDS> *>(const_cast<void *>(inl))->p.rows_per_warp = rpw;
 	void *args[1] = {inl ? const_cast<void *>(inl) : (void *)&arg};
 	if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess)
 		return -1;
@@ -345,6 +360,8 @@ struct charsiu_npu *charsiu_npu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	if (const char *e = getenv("CHARSIU_GPU_SLOW_US"))
 		g->slow_us = (double)strtoul(e, nullptr, 0);
 	g->no_pdl = getenv("CHARSIU_GPU_NO_PDL") != nullptr;
+	if (const char *e = getenv("CHARSIU_GPU_NPU_ROWS"))
+		g->rows = atoi(e);
 	g->ent.reserve(max_tensors);
 	g->cap_y = (size_t)max_n * NPU_MAX_TENSORS;
 	g->inl = new (std::nothrow) NpuInline<NPU_INLINE_WORDS>();

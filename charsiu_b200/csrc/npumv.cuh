@@ -11,10 +11,13 @@
 //
 // Device layout: each tensor's rows back to back, a row padded with zeros to
 // kp bytes (kp = K rounded up to 16), so a lane's 16-byte loads are aligned.
-// A warp takes R rows at a time; lane L reads 16-byte chunks L, L + 32, ... of
-// each, U chunks of each row per step (R * U = 16 loads in flight a lane), and
-// dots them with dp4a against the activation staged in shared memory; one
-// warp reduction a row, and lane j writes row j.
+// A warp takes up to R rows at a time (rows_per_warp, chosen by the host so
+// that small tensors still spread over every SM); lane L reads 16-byte chunks
+// L, L + 32, ... of each, U chunks of each row per step (R * U <= 16 loads in
+// flight a lane), and dots them with dp4a against the activation staged in
+// shared memory; one warp reduction a row, and lane j writes row j. The first
+// rows' first chunks are loaded before the wait on the previous kernel, and
+// each next batch's while the current one's sums are reduced.
 #pragma once
 
 #include <cstdint>
@@ -37,6 +40,7 @@ struct NpuTensor {
 struct NpuParams {
 	NpuTensor t[NPU_MAX_TENSORS];
 	uint32_t ntensor, total_rows, kp;
+	uint32_t rows_per_warp;  // 1 .. the kernel's R
 	float d1;
 	const int8_t *q1;        // kp bytes (device); unused when the activation is inline
 	// direct host calls: when done_flag is set, the last CTA to finish
@@ -68,6 +72,45 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 	extern __shared__ __align__(16) uint8_t npu_smem[];
 	const uint32_t nch = p.kp / 16;
 	uint4 *act = reinterpret_cast<uint4 *>(npu_smem);
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const uint32_t nw = gridDim.x * NPU_WARPS;
+
+	// rows r0 .. r0 + R - 1: their tensors and row pointers
+	const uint32_t rpw = p.rows_per_warp;
+	const int8_t *wr[R];
+	uint32_t ti[R];
+	auto setup = [&](uint32_t r0) {
+#pragma unroll
+		for (int j = 0; j < R; j++) {
+			const uint32_t r = r0 + j;
+			uint32_t t = 0;
+			while (t + 1 < p.ntensor && r >= p.t[t].row_end)
+				t++;
+			ti[j] = t;
+			wr[j] = ((uint32_t)j < rpw && r < p.total_rows)
+				? p.t[t].w + (uint64_t)(r - (p.t[t].row_end - p.t[t].rows)) * p.kp
+				: nullptr;
+		}
+	};
+	uint4 wv[R][U];
+	auto load = [&](uint32_t c0) {
+#pragma unroll
+		for (int j = 0; j < R; j++)
+#pragma unroll
+			for (int u = 0; u < U; u++) {
+				const uint32_t c = c0 + 32 * u;
+				wv[j][u] = (wr[j] && c < nch) ? ldg_stream((const uint8_t *)wr[j] + c * 16)
+							     : make_uint4(0, 0, 0, 0);
+			}
+	};
+
+	// the first rows' first chunks go now: weights never depend on the
+	// kernel before this one
+	if (rpw < 1 || rpw > (uint32_t)R)
+		return;
+	uint32_t r0 = (blockIdx.x * NPU_WARPS + warp) * rpw;
+	setup(r0);
+	load(lane);
 	if (AW && p.done_flag && blockIdx.x == 0 && threadIdx.x == 0)
 		*p.t_start = globaltimer_ns();
 	if (AW) {
@@ -83,36 +126,14 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 	__syncthreads();
 	pdl_launch_dependents();
 
-	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const uint32_t nw = gridDim.x * NPU_WARPS;
-	for (uint32_t r0 = (blockIdx.x * NPU_WARPS + warp) * R; r0 < p.total_rows; r0 += nw * R) {
-		const int8_t *wr[R];
-		uint32_t ti[R];
-#pragma unroll
-		for (int j = 0; j < R; j++) {
-			const uint32_t r = r0 + j;
-			uint32_t t = 0;
-			while (t + 1 < p.ntensor && r >= p.t[t].row_end)
-				t++;
-			ti[j] = t;
-			wr[j] = r < p.total_rows
-				? p.t[t].w + (uint64_t)(r - (p.t[t].row_end - p.t[t].rows)) * p.kp
-				: nullptr;
-		}
+	while (r0 < p.total_rows) {
 		int acc[R];
 #pragma unroll
 		for (int j = 0; j < R; j++)
 			acc[j] = 0;
 		for (uint32_t c0 = lane; c0 < nch; c0 += 32 * U) {
-			uint4 wv[R][U];
-#pragma unroll
-			for (int j = 0; j < R; j++)
-#pragma unroll
-				for (int u = 0; u < U; u++) {
-					const uint32_t c = c0 + 32 * u;
-					wv[j][u] = (wr[j] && c < nch) ? ldg_stream((const uint8_t *)wr[j] + c * 16)
-								     : make_uint4(0, 0, 0, 0);
-				}
+			if (c0 != (uint32_t)lane)
+				load(c0);
 #pragma unroll
 			for (int u = 0; u < U; u++) {
 				const uint32_t c = c0 + 32 * u;
@@ -128,14 +149,29 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 				}
 			}
 		}
+		// where this batch's rows go, then the next batch's first chunks in
+		// flight while this one's sums are reduced and stored
+		float *yp[R];
+		float sc[R];
 #pragma unroll
 		for (int j = 0; j < R; j++) {
-			const int s = __reduce_add_sync(0xffffffffu, acc[j]);
+			yp[j] = nullptr;
+			sc[j] = 0.0f;
 			if (lane == j && wr[j]) {
 				const NpuTensor &t = p.t[ti[j]];
 				const uint32_t row = r0 + j - (t.row_end - t.rows);
-				t.y[row] = __fmul_rn(__fmul_rn(__int2float_rn(s), p.d1), t.scale[row]);
+				yp[j] = t.y + row;
+				sc[j] = t.scale[row];
 			}
+		}
+		r0 += nw * rpw;
+		setup(r0);
+		load(lane);
+#pragma unroll
+		for (int j = 0; j < R; j++) {
+			const int s = __reduce_add_sync(0xffffffffu, acc[j]);
+			if (yp[j])
+				*yp[j] = __fmul_rn(__fmul_rn(__int2float_rn(s), p.d1), sc[j]);
 		}
 	}
 	if (AW && p.done_flag) {
