@@ -248,6 +248,83 @@ class TokenChain:
         self.layer.close()
 
 
+class BatchChain:
+    """One decode step of M sequences: every projection and the head, grouped
+    as the decode groups them, each group one packing of the M activations and
+    one tensor-core launch (charsiu_gpu_matvec_batch_group_dev). world > 1:
+    every tensor column-split over the ranks (this rank computes its slab of
+    rows for all M sequences) and each group's slabs all-gathered with one
+    NCCL collective, so every rank holds the whole batch's outputs."""
+
+    def __init__(self, gg, m, dev, rank=0, world=1, dist=None):
+        import torch
+        from charsiu_b200.lib import Layer
+
+        self.torch, self.dist, self.m = torch, dist, m
+        self.groups = launch_groups(SHAPE)
+        names = [nm for g, _ in self.groups for nm in g]
+        self.layer = Layer(max_k=max(SHAPE.n_embd, SHAPE.n_ff), max_n=SHAPE.n_vocab,
+                           max_tensors=len(names) + 1, device=dev.index, rank=rank, world=world)
+        self.ids = {}
+        for nm in names:
+            t = gg.tensors[nm]
+            self.ids[nm] = self.layer.add_blocks(t.type, t.k, t.n, np.asarray(gg.data(nm)), nm)
+        self.acts = {}
+        for k in (SHAPE.n_embd, SHAPE.n_ff):
+            x = torch.randn(m, k, generator=torch.Generator().manual_seed(k)).to(dev)
+            q = torch.empty((m, k), dtype=torch.int8, device=dev)
+            d = torch.empty((m, k // 32), dtype=torch.float32, device=dev)
+            assert self.layer.act_quantise_dev(x.data_ptr(), m, k, q.data_ptr(), d.data_ptr(),
+                                               torch.cuda.current_stream().cuda_stream) == 0
+            self.acts[k] = (q, d)
+        # a group's outputs back to back, each tensor's [M][slab] padded to the
+        # widest rank's slab so that a gather moves equal pieces
+        self.bufs, self.full = [], []
+        for g, _ in self.groups:
+            sizes = [m * shard.slab_rows(gg.tensors[nm].n, world) for nm in g]
+            buf = torch.zeros(sum(sizes), dtype=torch.float32, device=dev)
+            ptrs, off = [], 0
+            for sz in sizes:
+                ptrs.append(buf[off:].data_ptr())
+                off += sz
+            self.bufs.append((buf, ptrs))
+            self.full.append(torch.zeros(world * sum(sizes), dtype=torch.float32, device=dev)
+                             if world > 1 else None)
+        self.weight_bytes = sum(gg.tensors[nm].nbytes for nm in names)
+
+    def token(self, stream):
+        for (g, k), (buf, ptrs), full in zip(self.groups, self.bufs, self.full):
+            q, d = self.acts[k]
+            rc = self.layer.batch_group_dev([self.ids[nm] for nm in g], self.m, q.data_ptr(),
+                                            d.data_ptr(), ptrs, stream.cuda_stream)
+            assert rc == 0, self.layer.error()
+            if full is not None:
+                self.dist.all_gather_into_tensor(full, buf)
+
+    def close(self):
+        self.layer.close()
+
+
+def batched_steps(gg, dev, rank, world, dist, barrier, ms=(8, 32, 64), steps=50, warmup=3):
+    """tok/s of one batched decode step at each M (config: every tensor split
+    over the world's GPUs when world > 1): M sequences a step, the max over
+    ranks of the step time."""
+    out = {}
+    for m in ms:
+        chain = BatchChain(gg, m, dev, rank, world, dist)
+        ms_step, _ = time_chain(chain, steps, warmup, barrier, dist, world, dev, world == 1,
+                                False)
+        chain.close()
+        out[f"m{m}"] = {"value": round(m * 1000.0 / ms_step, 1), "unit": UNIT,
+                        "ms_per_step": round(ms_step, 5)}
+    out["workload"] = ("one decode step of M sequences: the 112 projections and the head as "
+                       "grouped batched matvecs (tcgen05 kind::i8 from M = 9, the CUDA cores "
+                       "below)" +
+                       (f", every tensor column-split over {world} GPUs and each group's "
+                        "slabs NCCL-all-gathered" if world > 1 else ""))
+    return out
+
+
 def time_chain(chain, steps, warmup, barrier, dist, world, dev, graph_ok, sample_clocks):
     """ms a token, the max over ranks; the chain as one CUDA graph when graph_ok."""
     torch = chain.torch
@@ -340,6 +417,8 @@ def run_ours(args, rank, world, dist):
             fused["error"] = str(e)[:200]
         split["fused"] = fused
 
+    batched = batched_steps(gg, dev, rank, world, dist, barrier)
+
     e2e = run_e2e_resident(path, args, world, dist, dev)
     e2e["host_routed"] = run_e2e(path, args, lib, world, dist, dev)
     npu_format = None
@@ -372,6 +451,7 @@ def run_ours(args, rank, world, dist):
         out["column_split"] = split
     if npu_format:
         out["npu_format"] = npu_format
+    out["batched"] = batched
     if rank == 0 and world == 1:
         out["cpu_baseline"] = cpu_baseline(path)
     return out
