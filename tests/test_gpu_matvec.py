@@ -239,6 +239,35 @@ def test_batch_tile_variants_agree(monkeypatch, na, pre):
             assert same(yc[i], O.matvec(G.GGML_Q8_0, blk, k, n, qs[i], ds[i])), f"row {i}"
 
 
+@pytest.mark.parametrize("pre", ["0", "1"])
+def test_batch_extreme_blocks(monkeypatch, pre):
+    """Blocks at the int8 extremes, where a block's dot is largest
+    (32 * 128 * 127), on both epilogues, with ragged K (a partial last
+    16-block segment)."""
+    torch = pytest.importorskip("torch")
+    monkeypatch.setenv("CHARSIU_GPU_QMM_MIN_M", "2")
+    monkeypatch.setenv("CHARSIU_GPU_QMM_PRE", pre)
+    dev = torch.device("cuda:0")
+    k, n, m = 2080, 300, 20
+    rng = np.random.default_rng(77)
+    blk = G.quant_blocks(rng, G.GGML_Q8_0, n, k)
+    b3 = blk.reshape(n, k // 32, 34)
+    pattern = rng.choice(np.array([-128, -127, 127], dtype=np.int8), size=(n, k // 32, 32))
+    b3[:, :, 2:] = pattern.view(np.uint8)
+    xs = rng.normal(size=(m, k)).astype(np.float32)
+    xs[:, ::3] *= 40.0                    # many activations quantise to +-127
+    with Layer(max_k=k, max_n=n, max_tensors=2) as L:
+        tid = L.add_blocks(G.GGML_Q8_0, k, n, blk)
+        qs, ds, q_t, d_t = _dev_acts(torch, xs, dev)
+        y = torch.full((m, n), float("nan"), device=dev)
+        assert L.batch_dev(tid, m, q_t.data_ptr(), d_t.data_ptr(), y.data_ptr(),
+                           torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        yc = y.cpu().numpy()
+    for i in range(m):
+        assert same(yc[i], O.matvec(G.GGML_Q8_0, blk, k, n, qs[i], ds[i])), f"row {i}"
+
+
 def test_device_forms_and_quantiser(layer):
     torch = pytest.importorskip("torch")
     k, n, m = 8192, 2048, 4
