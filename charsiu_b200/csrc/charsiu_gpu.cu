@@ -401,12 +401,25 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
 // tiles of NA (16 or 32) rows once, then one persistent launch over every
 // (128-row tile, NA activations) unit of the tensors `ids` (same K, at most
 // QMM_MAX_TENSORS). NA = 16 for m <= 16, else 32 (CHARSIU_GPU_QMM_NA picks
-// one for every m). `pack` (device) holds at least qmm_pack_bytes(na, m, nb).
+// one for every m). `pack` (device) holds at least qmm_pack_bytes(qmm_na(g, m),
+// m, nb), which covers every NA a launch may pick (qmm_launch_na).
 uint32_t qmm_na(const charsiu_gpu *g, uint32_t m)
 {
 	if (g->qmm_na)
 		return g->qmm_na;
 	return m <= 16 ? 16 : 32;
+}
+
+// The NA of one launch of `tiles` row tiles: 32 where its units fill the SMs,
+// else 16, which doubles the units (an epilogue warp's share of a unit is the
+// same either way, so a unit of 16 takes about as long as one of 32). At
+// m = 64 that moves the 2048-row launches (o, down) from 32 SMs to 64.
+uint32_t qmm_launch_na(const charsiu_gpu *g, uint32_t m, uint32_t tiles)
+{
+	const uint32_t na = qmm_na(g, m);
+	if (g->qmm_na || na == 16)
+		return na;
+	return (uint64_t)tiles * ((m + 31) / 32) < (uint64_t)g->sm_count ? 16 : 32;
 }
 
 size_t qmm_pack_bytes(uint32_t na, uint32_t m, uint32_t nb)
@@ -419,7 +432,10 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 {
 	if (!n || n > (unsigned)QMM_MAX_TENSORS)
 		return -1;
-	const uint32_t na = qmm_na(g, m), nb = g->ent[ids[0]].nb;
+	uint32_t tiles = 0;
+	for (unsigned i = 0; i < n; i++)
+		tiles += (g->ent[ids[i]].groups + QMM_TILE_GROUPS - 1) / QMM_TILE_GROUPS;
+	const uint32_t na = qmm_launch_na(g, m, tiles), nb = g->ent[ids[0]].nb;
 	const uint32_t mt = (m + na - 1) / na, nseg = nsegments(nb);
 	cudaLaunchAttribute attr[1];
 	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -437,15 +453,15 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	g->launches++;
 
 	QmmParams p = {};
-	uint32_t tiles = 0;
+	uint32_t tile_end = 0;
 	for (unsigned i = 0; i < n; i++) {
 		const Ent &e = g->ent[ids[i]];
 		p.t[i].w = e.data;
 		p.t[i].y = ys[i];
 		p.t[i].rows = (uint32_t)e.rows;
 		p.t[i].groups = e.groups;
-		tiles += (e.groups + QMM_TILE_GROUPS - 1) / QMM_TILE_GROUPS;
-		p.t[i].tile_end = tiles;
+		tile_end += (e.groups + QMM_TILE_GROUPS - 1) / QMM_TILE_GROUPS;
+		p.t[i].tile_end = tile_end;
 	}
 	p.act = pack;
 	p.ntensor = n;
