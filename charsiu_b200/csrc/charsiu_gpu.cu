@@ -410,16 +410,25 @@ uint32_t qmm_na(const charsiu_gpu *g, uint32_t m)
 	return m <= 16 ? 16 : 32;
 }
 
-// The NA of one launch of `tiles` row tiles: 32 where its units fill the SMs,
-// else 16, which doubles the units (an epilogue warp's share of a unit is the
-// same either way, so a unit of 16 takes about as long as one of 32). At
-// m = 64 that moves the 2048-row launches (o, down) from 32 SMs to 64.
-uint32_t qmm_launch_na(const charsiu_gpu *g, uint32_t m, uint32_t tiles)
+// The (NA, EC) of one launch of `tiles` row tiles: the smallest units that
+// still run in one round on the SMs. An epilogue warp's share of a unit is
+// the same in every shape (32 rows, 8 activations), so a smaller unit takes
+// no longer than a larger one and more of them run side by side; once they
+// no longer fit one round, the larger units' fewer rounds win. At m = 64 the
+// 2048-row launches (o, down) run 128 units of (tile, 8 activations) instead
+// of 32 of (tile, 32). A forced NA (CHARSIU_GPU_QMM_NA) or PRE keeps EC = NA.
+void qmm_launch_shape(const charsiu_gpu *g, uint32_t m, uint32_t tiles, uint32_t &na,
+		      uint32_t &ec)
 {
-	const uint32_t na = qmm_na(g, m);
-	if (g->qmm_na || na == 16)
-		return na;
-	return (uint64_t)tiles * ((m + 31) / 32) < (uint64_t)g->sm_count ? 16 : 32;
+	na = ec = qmm_na(g, m);
+	if (g->qmm_na || g->qmm_pre)
+		return;
+	const uint64_t sms = (uint64_t)g->sm_count;
+	const uint64_t u16 = (uint64_t)tiles * ((m + 15) / 16);
+	if (na == 32 && u16 > sms)
+		return;
+	na = 16;
+	ec = 2 * u16 <= sms ? 8 : 16;
 }
 
 size_t qmm_pack_bytes(uint32_t na, uint32_t m, uint32_t nb)
@@ -435,7 +444,9 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	uint32_t tiles = 0;
 	for (unsigned i = 0; i < n; i++)
 		tiles += (g->ent[ids[i]].groups + QMM_TILE_GROUPS - 1) / QMM_TILE_GROUPS;
-	const uint32_t na = qmm_launch_na(g, m, tiles), nb = g->ent[ids[0]].nb;
+	uint32_t na, ec;
+	qmm_launch_shape(g, m, tiles, na, ec);
+	const uint32_t nb = g->ent[ids[0]].nb;
 	const uint32_t mt = (m + na - 1) / na, nseg = nsegments(nb);
 	cudaLaunchAttribute attr[1];
 	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -473,23 +484,25 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	p.err = g->d_err;
 	if (!tiles)
 		return 0;
-	const bool pre = g->qmm_pre;
-	const void *fn = na == 16 ? (pre ? (const void *)qmm_tc_kernel<16, true>
-					 : (const void *)qmm_tc_kernel<16, false>)
-				  : (pre ? (const void *)qmm_tc_kernel<32, true>
-					 : (const void *)qmm_tc_kernel<32, false>);
-	const int slot = 20 + (na == 32 ? 2 : 0) + (pre ? 1 : 0);
-	const size_t smem = qmm_smem_bytes(na);
+	const bool pre = g->qmm_pre && ec == na;
+	const void *fn = na == 32 ? (pre ? (const void *)qmm_tc_kernel<32, 32, true>
+					 : (const void *)qmm_tc_kernel<32, 32, false>)
+			 : ec == 8 ? (const void *)qmm_tc_kernel<16, 8, false>
+				   : (pre ? (const void *)qmm_tc_kernel<16, 16, true>
+					  : (const void *)qmm_tc_kernel<16, 16, false>);
+	// smem_set slots: 20..23 (NA, PRE), 19 the 8-activation slices
+	const int slot = ec == 8 ? 19 : 20 + (na == 32 ? 2 : 0) + (pre ? 1 : 0);
+	const size_t smem = qmm_smem_bytes(na, ec);
 	if (!g->smem_set[slot]) {
 		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
 					 (int)smem) != cudaSuccess)
 			return -1;
 		g->smem_set[slot] = true;
 	}
-	const uint32_t units = tiles * mt;
+	const uint32_t units = tiles * mt * (na / ec);
 	cudaLaunchConfig_t cfg = {};
 	cfg.gridDim = dim3(units < (uint32_t)g->sm_count ? units : (uint32_t)g->sm_count);
-	cfg.blockDim = dim3(qmm_threads((int)na));
+	cfg.blockDim = dim3(qmm_threads((int)ec));
 	cfg.dynamicSmemBytes = smem;
 	cfg.stream = st;
 	cfg.attrs = attr;

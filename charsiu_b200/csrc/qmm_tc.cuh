@@ -14,14 +14,18 @@
 // one commit a chunk, into four chunk buffers of tensor memory, so the
 // epilogue drains one chunk while the MMAs fill the others.
 //
-// Work units are (128-row tile of one tensor, NA activations); a persistent
-// grid deals them round robin, activation tile fastest so the CTAs sharing a
-// weight tile run together (the second and later reads of it hit L2). Warp
+// Work units are (128-row tile of one tensor, NA activations, a slice of EC
+// of those activations); a persistent grid deals them round robin, slice and
+// activation tile fastest so the CTAs sharing a weight tile run together (the
+// second and later reads of it hit L2). With EC < NA each CTA still issues
+// the whole NA-wide MMA (the tensor pipe is nearly idle here) and its
+// epilogue takes only its slice: twice the units, for launches too small to
+// fill the SMs otherwise. Warp
 // roles: warp 0 lane 0 issues the single-destination bulk copies of one K
 // segment (16 blocks) a stage -- the tile's 16 groups' weight segments as
 // they lie in the device layout (layout.h), already MMA core matrices, and
 // the packed activation tile (qmm_pack_kernel) -- into a double-buffered
-// stage; warp 1 owns tensor memory and lane 0 issues the MMAs; EW = 4 * NA/8
+// stage; warp 1 owns tensor memory and lane 0 issues the MMAs; EW = 4 * EC/8
 // epilogue warps (a tensor-memory lane quarter and 8 activations each) read
 // the int32 tiles with tcgen05.ld and accumulate: per chunk, the four blocks'
 // products first (independent, so they overlap), then the four in-order sums.
@@ -58,16 +62,29 @@ __host__ __device__ constexpr uint32_t qmm_act_seg_bytes(uint32_t na)
 	return SB * 2 * na * 16 + SB * na * 4;
 }
 
-__host__ inline size_t qmm_smem_bytes(uint32_t na)
-{
-	return 2 * ((size_t)QMM_WSTAGE + qmm_act_seg_bytes(na)) + 24 * sizeof(uint64_t) + 16;
-}
-
 constexpr int QMM_EPI_COLS = 8;            // activations (columns) an epilogue warp owns
 
-__host__ __device__ constexpr int qmm_threads(int na)
+// An epilogue warp's private copy of one segment's scales: the d_w of its 32
+// rows (4 groups x 16 blocks x 8 rows fp16) and the d_a of its 8 activations
+// (16 blocks x 8 fp32). Taken when the segment lands, so the stage can be
+// refilled as soon as the MMAs are done with it.
+constexpr uint32_t QMM_PRIV_DW = 4 * SB * RG * 2;                       // 1024
+constexpr uint32_t QMM_PRIV_BYTES = QMM_PRIV_DW + SB * QMM_EPI_COLS * 4;  // 1536
+
+__host__ __device__ constexpr uint32_t qmm_bar_bytes()
 {
-	return (2 + 4 * (na / QMM_EPI_COLS)) * 32;
+	return 24 * sizeof(uint64_t) + 16;
+}
+
+__host__ inline size_t qmm_smem_bytes(uint32_t na, uint32_t ec)
+{
+	return 2 * ((size_t)QMM_WSTAGE + qmm_act_seg_bytes(na)) + qmm_bar_bytes() +
+	       (size_t)4 * (ec / QMM_EPI_COLS) * QMM_PRIV_BYTES;
+}
+
+__host__ __device__ constexpr int qmm_threads(int ec)
+{
+	return (2 + 4 * (ec / QMM_EPI_COLS)) * 32;
 }
 
 // tensor-memory columns: QMM_TBUFS chunk buffers of QMM_CHUNK blocks of NA columns
@@ -123,12 +140,15 @@ struct QmmParams {
 	int *err;
 };
 
-template <int NA, bool PRE>
-__global__ void __launch_bounds__(qmm_threads(NA), 1)
+template <int NA, int EC, bool PRE>
+__global__ void __launch_bounds__(qmm_threads(EC), 1)
 qmm_tc_kernel(const __grid_constant__ QmmParams p)
 {
 	constexpr int CW = QMM_EPI_COLS;                   // activations an epilogue warp
-	constexpr int EW = 4 * (NA / CW);                  // epilogue warps
+	constexpr int EW = 4 * (EC / CW);                  // epilogue warps
+	constexpr uint32_t SL = NA / EC;                   // slices a tile
+	static_assert(NA % EC == 0 && EC % CW == 0 && (!PRE || EC == NA),
+		      "slices of whole epilogue warps; PRE fills every column it reads");
 	constexpr uint32_t ASEG = qmm_act_seg_bytes(NA);
 	constexpr uint32_t NCOLS = qmm_tmem_cols(NA);
 	static_assert(NCOLS >= 32 && NCOLS <= 512 && (NCOLS & (NCOLS - 1)) == 0,
@@ -140,10 +160,11 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 	uint64_t *full = bars, *freeb = bars + 2, *mma_done = bars + 4;
 	uint64_t *tfree = mma_done + QMM_TBUFS;
 	uint32_t *taddr_s = reinterpret_cast<uint32_t *>(tfree + QMM_TBUFS);
+	uint8_t *priv_all = smem + 2 * (QMM_WSTAGE + ASEG) + qmm_bar_bytes();
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const uint32_t nb = p.nb, nseg = nsegments(nb);
-	const uint32_t units = p.tiles * p.atiles;
+	const uint32_t units = p.tiles * p.atiles * SL;
 
 	if (warp == 1) {
 		tmem_alloc(taddr_s, NCOLS);
@@ -167,7 +188,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 
 	// the tensor and row tile of unit u
 	auto locate = [&](uint32_t u, uint32_t &ti, uint32_t &tile) {
-		const uint32_t rt = u / p.atiles;
+		const uint32_t rt = u / (p.atiles * SL);
 		ti = 0;
 		while (ti + 1 < p.ntensor && rt >= p.t[ti].tile_end)
 			ti++;
@@ -185,7 +206,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 				const QmmTensor &T = p.t[ti];
 				const uint32_t g0 = tile * QMM_TILE_GROUPS;
 				const uint32_t tgroups = min((uint32_t)QMM_TILE_GROUPS, T.groups - g0);
-				const uint8_t *act = p.act + (uint64_t)(u % p.atiles) * nseg * ASEG;
+				const uint8_t *act = p.act + (uint64_t)((u / SL) % p.atiles) * nseg * ASEG;
 				for (uint32_t s = 0; s < nseg; s++, s_cnt++) {
 					const uint32_t st = s_cnt & 1, sb = seg_blocks(nb, s);
 					if (s_cnt >= 2 &&
@@ -269,7 +290,8 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 		// ---- epilogue: TMEM lane quarter q, activations e*CW .. e*CW+CW-1 ----
 		const int ew = warp - 2, q = warp % 4, e = ew / 4;
 		const uint32_t r = q * 32 + lane;                  // row of the tile
-		const uint32_t grp = r / RG, rr = r % RG;
+		const uint32_t rr = r % RG;
+		uint8_t *priv = priv_all + ew * QMM_PRIV_BYTES;
 		const uint32_t lane_base = (uint32_t)(q * 32) << 16;
 		bool ok = true;
 		if (PRE) {
@@ -290,6 +312,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 		for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
 			uint32_t ti, tile;
 			locate(u, ti, tile);
+			const uint32_t cb = (u % SL) * EC + e * CW;   // this warp's first column of the tile
 			uint64_t acc[CW / 2];           // column pairs, packed
 #pragma unroll
 			for (int c = 0; c < CW / 2; c++)
@@ -302,10 +325,31 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 					ok = false;
 					break;
 				}
-				const uint16_t *dl = reinterpret_cast<const uint16_t *>(
-					stage_w(st) + grp * MAX_SEG_BYTES + sb * RG * 32);
-				const float *da = reinterpret_cast<const float *>(stage_a(st) + SB * 2 * NA * 16) +
-						  e * CW;
+				// this warp's scales of the segment into its private copy, then
+				// the stage is free as far as the epilogue goes: word w of a
+				// group's d_w (16 bytes) is block w's 8 rows; lane L's d_a
+				// word is block L/2, activations cb + 4*(L&1) ..
+				{
+					const uint32_t g0 = (uint32_t)q * 4;
+#pragma unroll
+					for (int h = 0; h < 2; h++) {
+						const uint32_t idx = lane + 32 * h, gl = idx / SB, w = idx % SB;
+						reinterpret_cast<uint4 *>(priv)[idx] =
+							*reinterpret_cast<const uint4 *>(
+								stage_w(st) + (g0 + gl) * MAX_SEG_BYTES +
+								sb * RG * 32 + w * 16);
+					}
+					const uint32_t bi = lane >> 1, hf = lane & 1;
+					reinterpret_cast<uint4 *>(priv + QMM_PRIV_DW)[lane] =
+						*reinterpret_cast<const uint4 *>(
+							stage_a(st) + SB * 2 * NA * 16 +
+							(bi * NA + cb + 4 * hf) * 4);
+				}
+				__syncwarp();
+				if (lane == 0)
+					mbar_arrive(&freeb[st]);
+				const uint16_t *dl = reinterpret_cast<const uint16_t *>(priv) + (lane / RG) * SB * RG;
+				const float *da = reinterpret_cast<const float *>(priv + QMM_PRIV_DW);
 				for (uint32_t b0 = 0; b0 < sb; b0 += QMM_CHUNK, c_cnt++) {
 					const uint32_t buf = c_cnt % QMM_TBUFS, nblk = min((uint32_t)QMM_CHUNK, sb - b0);
 					if (!mbar_wait_bounded(&mma_done[buf], (c_cnt / QMM_TBUFS) & 1,
@@ -319,7 +363,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 					// the chunk's tiles as packed float bits 1.5 * 2^23 + t
 					static_assert(CW == 8 && QMM_CHUNK == 4, "tmem_ld_chunk4 shape");
 					uint64_t tp[QMM_CHUNK][CW / 2];
-					const uint32_t col0 = taddr + lane_base + buf * QMM_CHUNK * NA + e * CW;
+					const uint32_t col0 = taddr + lane_base + buf * QMM_CHUNK * NA + cb;
 					if (nblk == QMM_CHUNK)
 						tmem_ld_chunk4<!PRE>(col0, NA, tp);
 					else
@@ -342,7 +386,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 						const uint32_t bi = b0 + j;
 						const float dw = half_bits_to_float(dl[bi * RG + rr]);
 						const uint64_t dw2 = pack2(dw, dw);
-						const ulonglong2 *da2 = reinterpret_cast<const ulonglong2 *>(da + bi * NA);
+						const ulonglong2 *da2 = reinterpret_cast<const ulonglong2 *>(da + bi * CW);
 #pragma unroll
 						for (int c4 = 0; c4 < CW / 4; c4++) {
 							const ulonglong2 a = da2[c4];
@@ -376,15 +420,13 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 						}
 					}
 				}
-				__syncwarp();
-				if (lane == 0)
-					mbar_arrive(&freeb[st]);
+				__syncwarp();      // the private copy is read until here
 			}
 			if (!ok)
 				break;
 			const QmmTensor &T = p.t[ti];
 			const uint32_t row = tile * QMM_TILE_GROUPS * RG + r;
-			const uint32_t a0 = (u % p.atiles) * NA + e * CW;
+			const uint32_t a0 = ((u / SL) % p.atiles) * NA + cb;
 			if (row < T.rows) {
 #pragma unroll
 				for (int c = 0; c < CW; c++) {
