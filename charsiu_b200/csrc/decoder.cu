@@ -551,7 +551,7 @@ int charsiu_gpu_ordered_sum_dev(struct charsiu_gpu *g, const float *a, unsigned 
 	if (!g || !a || !out || !n || n > ORDERED_SUM_MAX_N)
 		return -1;
 	cudaSetDevice(layer_device(g));
-	ordered_sum_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(a, n, out);
+	ordered_sum_kernel<<<1, ORDERED_SUM_THREADS, 0, (cudaStream_t)stream>>>(a, n, out);
 	return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

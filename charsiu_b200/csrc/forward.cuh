@@ -47,17 +47,26 @@ __device__ __forceinline__ float exp_exact(float x, const float *__restrict__ ta
 	return tab[idx];
 }
 
-// The test hook's kernel: *out = ordered_sum_seq(a[0..n)) from shared memory.
+// The test hook's kernel, one CTA of ORDERED_SUM_THREADS: out[0] =
+// ordered_sum_seq(a[0..n)) and out[1] = ordered_sum_nonneg_cta of the same,
+// from shared memory.
 constexpr uint32_t ORDERED_SUM_MAX_N = 8192;
+constexpr int ORDERED_SUM_THREADS = 512;
 
-__global__ void ordered_sum_kernel(const float *__restrict__ a, uint32_t n, float *__restrict__ out)
+__global__ void __launch_bounds__(ORDERED_SUM_THREADS)
+ordered_sum_kernel(const float *__restrict__ a, uint32_t n, float *__restrict__ out)
 {
 	__shared__ __align__(16) float sm[ORDERED_SUM_MAX_N];
+	__shared__ OsumShared osum;
 	for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
 		sm[i] = a[i];
 	__syncthreads();
 	if (threadIdx.x == 0)
-		*out = ordered_sum_seq(sm, n);
+		out[0] = ordered_sum_seq(sm, n);
+	const float s = n <= 4 * blockDim.x ? ordered_sum_nonneg_cta<4>(sm, n, osum)
+					    : ordered_sum_nonneg_cta<16>(sm, n, osum);
+	if (threadIdx.x == 0)
+		out[1] = s;
 }
 
 // x (+ add, written back to x when add is given), then rmsnorm with weights
@@ -65,7 +74,7 @@ __global__ void ordered_sum_kernel(const float *__restrict__ a, uint32_t n, floa
 // out = x * scale * w), then the quantiser of the result. One CTA; n a
 // multiple of 32, at most FWD_NORM_MAX. The weights are fetched before the
 // previous kernel is done (they do not depend on it), the squares by every
-// thread, their ordered sum by thread 0 (ordered_sum_seq).
+// thread, their ordered sum by the CTA (ordered_sum_nonneg_cta).
 constexpr uint32_t FWD_NORM_MAX = 8192;
 constexpr int FWD_NORM_THREADS = 512;
 

@@ -73,10 +73,275 @@ __device__ __forceinline__ float ordered_sum_seq(const float *a, uint32_t n)
 	return s;
 }
 
+// The same sum, bit for bit, by a whole CTA, for terms that are all >= +0
+// and finite (the rmsnorm's squares); any other term sends the CTA down
+// ordered_sum_seq. Exact, not approximate: while the running sum s stays in
+// one binade [2^e, 2^(e+1)) it is m * u on that binade's grid
+// (u = 2^(e-23), m an integer in [2^23, 2^24)), and adding a term t that
+// keeps it there rounds (m + t/u) to the nearest integer, ties to even. So
+// away from binade changes and ties the sum is an integer prefix sum of
+// q = rne(t/u), which one CTA scan computes for all terms at once:
+//  1. an fp32 prefix sum of the terms (any order) predicts the binade of the
+//     running sum before each term; a term after which the prediction
+//     changes binade (and the last term) is a CROSSING;
+//  2. per term q = rne(t/u) on its predicted grid (ties: rounded down and
+//     flagged), and one 64-bit exclusive scan of q | ties << 40 | crossings
+//     << 52 gives every term its grid offset and its rank among the ties
+//     and crossings, which list themselves in shared memory;
+//  3. warp 0 walks the crossings in order. Each lane first prepares one or
+//     two crossings in parallel: the run of grid terms before it, its offset,
+//     and how many of its ties round up (a tie rounds up when m + floor(t/u)
+//     is odd at that point) for either parity of m at the run's start. Then,
+//     crossing by crossing, in registers: check that s is in the predicted
+//     binade, add the run's offset and round-ups to m, check that m stayed
+//     below 2^24, and add the crossing term with a real fp32 add.
+// A failed check (the fp32 prediction off near a power of two, too many
+// ties or crossings to list) makes lane 0 finish with plain adds from the
+// last exact point, so the result is always the sequential sum. Terms are
+// read EPT a thread at most (n <= EPT * blockDim, else the sequential form);
+// every thread gets the sum.
+constexpr int OSUM_CMAX = 64;       // crossings listed
+constexpr int OSUM_TMAX = 256;      // ties listed
+
+struct OsumShared {
+	float wf[32];                    // per-warp fp32 totals
+	float woff[33];                  // their prefix: warp w starts at woff[w]
+	unsigned long long wq[32];       // per-warp packed totals
+	unsigned long long wqoff[32];    // their exclusive prefix
+	uint32_t wbad[32];               // per-warp: a term that is not >= +0 and finite
+	uint32_t anybad;
+	uint32_t c_idx[OSUM_CMAX], c_qx[OSUM_CMAX], c_b[OSUM_CMAX], c_t[OSUM_CMAX];
+	uint32_t t_qx[OSUM_TMAX], t_k[OSUM_TMAX];
+	uint32_t ncross, nties;
+	float result;
+};
+
+__device__ __forceinline__ uint32_t binade_field(float v)
+{
+	return (__float_as_uint(v) >> 23) & 0xffu;
+}
+
+template <int EPT>
+__device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &sh)
+{
+	const uint32_t tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
+	const uint32_t ept = (n + nt - 1) / nt;
+	const uint32_t i0 = tid * ept;
+	float v[EPT];
+	bool bad = ept > (uint32_t)EPT;
+#pragma unroll
+	for (int k = 0; k < EPT; k++) {
+		const uint32_t i = i0 + k;
+		v[k] = ((uint32_t)k < ept && i < n) ? t[i] : 0.0f;
+		bad |= !(v[k] >= 0.0f && v[k] <= 3.402823466e38f);       // NaN, < 0, inf
+	}
+
+	// 1. fp32 prefix sums (this thread's terms in order, then warps, then the
+	//    CTA), only to predict binades
+	float tsum = 0.0f;
+#pragma unroll
+	for (int k = 0; k < EPT; k++)
+		tsum = __fadd_rn(tsum, v[k]);
+	float inc = tsum;
+#pragma unroll
+	for (int o = 1; o < 32; o <<= 1) {
+		const float y = __shfl_up_sync(0xffffffffu, inc, o);
+		if (lane >= (uint32_t)o)
+			inc = __fadd_rn(inc, y);
+	}
+	float ex = __shfl_up_sync(0xffffffffu, inc, 1);
+	if (lane == 0)
+		ex = 0.0f;
+	bad = __any_sync(0xffffffffu, bad);
+	if (lane == 31) {
+		sh.wf[wid] = inc;
+		sh.wbad[wid] = bad;
+	}
+	__syncthreads();
+	// warp 0 turns the warp totals into each warp's starting value (the one
+	// value both the warp and the last lane of the warp before it use)
+	if (wid == 0) {
+		const uint32_t nw = nt / 32;
+		const float y = lane < nw ? sh.wf[lane] : 0.0f;
+		const bool wb = __any_sync(0xffffffffu, lane < nw && sh.wbad[lane]);
+		float wi = y;
+#pragma unroll
+		for (int o = 1; o < 32; o <<= 1) {
+			const float z = __shfl_up_sync(0xffffffffu, wi, o);
+			if (lane >= (uint32_t)o)
+				wi = __fadd_rn(wi, z);
+		}
+		sh.woff[lane + 1] = wi;
+		if (lane == 0) {
+			sh.woff[0] = 0.0f;
+			sh.anybad = wb;
+		}
+	}
+	__syncthreads();
+	if (sh.anybad) {
+		if (tid == 0)
+			sh.result = ordered_sum_seq(t, n);
+		__syncthreads();
+		return sh.result;
+	}
+	float X = __fadd_rn(sh.woff[wid], ex);
+	// the prediction after this thread's last term must be the very value the
+	// next thread starts from (its X), so that the runs of step 3 never mix
+	// two predicted grids: the next lane's X, or the next warp's first
+	float x_next = __shfl_down_sync(0xffffffffu, X, 1);
+	if (lane == 31)
+		x_next = sh.woff[wid + 1];
+
+	// 2. grid offsets, ties, crossings
+	unsigned long long pk[EPT];
+	uint32_t bk[EPT];
+	unsigned long long lsum = 0;
+#pragma unroll
+	for (int k = 0; k < EPT; k++) {
+		const uint32_t i = i0 + k;
+		const float P = (uint32_t)k + 1 == ept ? x_next : __fadd_rn(X, v[k]);
+		const uint32_t b = binade_field(X), bn = binade_field(P);
+		bk[k] = b;
+		unsigned long long q = 1ull << 52;                      // a crossing
+		if (b == bn && b >= 23 && b <= 254 && i != n - 1) {
+			const float f = __fmul_rn(v[k], __uint_as_float((277u - b) << 23));  // t / u
+			if (f < 16777216.0f) {
+				const bool tie = __fsub_rn(f, truncf(f)) == 0.5f;
+				q = tie ? ((unsigned long long)__float2uint_rz(f) | 1ull << 40)
+					: (unsigned long long)__float2uint_rn(f);
+			}
+		}
+		pk[k] = ((uint32_t)k < ept && i < n) ? q : 0ull;
+		lsum += pk[k];
+		X = P;
+	}
+	unsigned long long qinc = lsum;
+#pragma unroll
+	for (int o = 1; o < 32; o <<= 1) {
+		const unsigned long long y = __shfl_up_sync(0xffffffffu, qinc, o);
+		if (lane >= (uint32_t)o)
+			qinc += y;
+	}
+	unsigned long long qex = qinc - lsum;
+	if (lane == 31)
+		sh.wq[wid] = qinc;
+	__syncthreads();
+	if (wid == 0) {
+		const uint32_t nw = nt / 32;
+		const unsigned long long y = lane < nw ? sh.wq[lane] : 0ull;
+		unsigned long long wi = y;
+#pragma unroll
+		for (int o = 1; o < 32; o <<= 1) {
+			const unsigned long long z = __shfl_up_sync(0xffffffffu, wi, o);
+			if (lane >= (uint32_t)o)
+				wi += z;
+		}
+		sh.wqoff[lane] = wi - y;
+		if (lane == 31) {
+			sh.ncross = (uint32_t)(wi >> 52);
+			sh.nties = (uint32_t)(wi >> 40) & 0xfffu;
+		}
+	}
+	__syncthreads();
+	qex += sh.wqoff[wid];
+#pragma unroll
+	for (int k = 0; k < EPT; k++) {
+		const uint32_t i = i0 + k;
+		if (pk[k] >> 52) {
+			const uint32_t r = (uint32_t)(qex >> 52);
+			if (r < OSUM_CMAX) {
+				sh.c_idx[r] = i;
+				sh.c_qx[r] = (uint32_t)qex;
+				sh.c_b[r] = bk[k];
+				sh.c_t[r] = (uint32_t)(qex >> 40) & 0xfffu;     // ties before it
+			}
+		} else if ((pk[k] >> 40) & 0xfffu) {
+			const uint32_t r = (uint32_t)(qex >> 40) & 0xfffu;
+			if (r < OSUM_TMAX) {
+				sh.t_qx[r] = (uint32_t)qex;
+				sh.t_k[r] = (uint32_t)pk[k];
+			}
+		}
+		qex += pk[k];
+	}
+	__syncthreads();
+
+	// 3. warp 0: each lane prepares crossings lane and lane + 32 -- the run of
+	//    grid terms before it (its offset, and what its ties add for either
+	//    parity of m at the run's start), then the chain over the crossings
+	//    in order, in registers
+	if (wid == 0) {
+		const uint32_t nc = sh.ncross, ntie = sh.nties;
+		bool ok = nc <= (uint32_t)OSUM_CMAX && ntie <= (uint32_t)OSUM_TMAX;
+		float tc[2];
+		uint32_t rb[2], rq[2], rup[2];     // rup: ties' round-ups (bit 0..15: m even, 16..: odd)
+		bool rrun[2];
+#pragma unroll
+		for (int h = 0; h < 2; h++) {
+			const uint32_t r = lane + 32 * h;
+			tc[h] = 0.0f;
+			rb[h] = rq[h] = rup[h] = 0;
+			rrun[h] = false;
+			if (ok && r < nc) {
+				const uint32_t c = sh.c_idx[r], st = r ? sh.c_idx[r - 1] + 1 : 0;
+				const uint32_t q0 = r ? sh.c_qx[r - 1] : 0, t0 = r ? sh.c_t[r - 1] : 0;
+				tc[h] = t[c];
+				rb[h] = sh.c_b[r];
+				rq[h] = sh.c_qx[r] - q0;
+				rrun[h] = c > st;
+				uint32_t up0 = 0, up1 = 0;
+				for (uint32_t j = t0; j < sh.c_t[r]; j++) {
+					const uint32_t o = sh.t_qx[j] - q0 + sh.t_k[j];
+					up0 += (o + up0) & 1u;
+					up1 += (1u + o + up1) & 1u;
+				}
+				rup[h] = (up0 & 0xffffu) | up1 << 16;
+			}
+		}
+		// (batches of 8 crossings: a batch's shuffles do not wait on s)
+		float s = 0.0f;
+		uint32_t done = 0;
+		for (uint32_t r0 = 0; ok && r0 < nc; r0 += 8) {
+#pragma unroll
+			for (int j = 0; j < 8; j++) {
+				const uint32_t r = r0 + j;
+				const int h = (r >> 5) & 1, src = r & 31;
+				const float c_t = __shfl_sync(0xffffffffu, h ? tc[1] : tc[0], src);
+				const uint32_t b = __shfl_sync(0xffffffffu, h ? rb[1] : rb[0], src);
+				const uint32_t q = __shfl_sync(0xffffffffu, h ? rq[1] : rq[0], src);
+				const uint32_t up = __shfl_sync(0xffffffffu, h ? rup[1] : rup[0], src);
+				const bool run = __shfl_sync(0xffffffffu, h ? rrun[1] : rrun[0], src);
+				if (ok && r < nc) {
+					if (run) {
+						const uint32_t m = (__float_as_uint(s) & 0x7fffffu) | 0x800000u;
+						const uint32_t mend = m + q + ((m & 1u) ? up >> 16 : up & 0xffffu);
+						if (binade_field(s) != b || mend >= 0x1000000u)
+							ok = false;
+						else
+							s = __uint_as_float((b << 23) | (mend & 0x7fffffu));
+					}
+					if (ok) {
+						s = __fadd_rn(s, c_t);
+						done = r + 1;
+					}
+				}
+			}
+		}
+		if (lane == 0) {
+			if (!ok)
+				for (uint32_t i = done ? sh.c_idx[done - 1] + 1 : 0; i < n; i++)
+					s = __fadd_rn(s, t[i]);
+			sh.result = s;
+		}
+	}
+	__syncthreads();
+	return sh.result;
+}
+
 // rmsnorm (reference src/llama.c:316-326) of x (+ add), then the
 // quantiser of the result into aq / ad, by the whole CTA: xs[i] = x[i] +
-// add[i] (x alone when add is null), ss = the ordered sum of xs[i]^2 (thread
-// 0), scale = 1 / sqrtf(ss / n + eps), v = xs[i] * scale * w[i] per element,
+// add[i] (x alone when add is null), ss = the ordered sum of xs[i]^2 (the
+// CTA's exact form, ordered_sum_nonneg_cta), scale = 1 / sqrtf(ss / n + eps), v = xs[i] * scale * w[i] per element,
 // one warp a 32-block. xs, sq, ws: n floats each of shared memory, 16-byte
 // aligned, ws holding w already (copied in by the caller). *scale_sh: a
 // shared float. Ends with a barrier; xs still holds x + add.
@@ -94,10 +359,11 @@ __device__ __forceinline__ void norm_quant_cta(const float *__restrict__ x,
 	}
 	cp_async_wait_all();
 	__syncthreads();
-	if (threadIdx.x == 0) {
-		const float ss = ordered_sum_seq(sq, n);
+	__shared__ OsumShared osum;
+	const float ss = n <= 4 * blockDim.x ? ordered_sum_nonneg_cta<4>(sq, n, osum)
+					     : ordered_sum_nonneg_cta<16>(sq, n, osum);
+	if (threadIdx.x == 0)
 		*scale_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-	}
 	__syncthreads();
 	const float scale = *scale_sh;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -308,7 +308,8 @@ class Layer:
                                                        stream or None)
 
     def ordered_sum_dev(self, a_ptr: int, n: int, out_ptr: int, stream: int = 0) -> int:
-        """The sequential fp32 sum of n non-negative device floats into out_ptr."""
+        """The sequential fp32 sum of n device floats, out_ptr[0] by one
+        thread and out_ptr[1] by one CTA (two device floats)."""
         return self.L.charsiu_gpu_ordered_sum_dev(self.h, a_ptr, n, out_ptr, stream or None)
 
     def row_dev(self, tid: int, row_ptr: int, out_ptr: int, stream: int = 0) -> int:

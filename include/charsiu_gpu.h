@@ -294,10 +294,12 @@ CHARSIU_GPU_API int charsiu_gpu_dead(const struct charsiu_gpu *g);
 CHARSIU_GPU_API int charsiu_gpu_block_dots(struct charsiu_gpu *g, int id, const int8_t *q,
 			   int32_t *dots);
 
-/* The decode step's ordered sum on the device: *out =
- * fl(...fl(fl(0 + a[0]) + a[1]) ... + a[n-1]), the sequential fp32 sum
- * (rmsnorm's sum of squares, src/llama.c:321-322, and the softmax sum).
- * a and out are device pointers, n <= 8192. Queued on `stream`. */
+/* The decode step's ordered sum on the device: the sequential fp32 sum
+ * fl(...fl(fl(0 + a[0]) + a[1]) ... + a[n-1]) (rmsnorm's sum of squares,
+ * src/llama.c:321-322, and the softmax sum), in both of the step's forms:
+ * out[0] by one thread, out[1] by one CTA (the form the rmsnorm uses; exact
+ * for non-negative finite terms, and the one-thread sum for any others).
+ * a and out (2 floats) are device pointers, n <= 8192. Queued on `stream`. */
 CHARSIU_GPU_API int charsiu_gpu_ordered_sum_dev(struct charsiu_gpu *g, const float *a,
 						unsigned n, float *out, void *stream);
 
