@@ -105,14 +105,10 @@ constexpr int OSUM_TMAX = 256;      // ties listed
 
 struct OsumShared {
 	float wf[32];                    // per-warp fp32 totals
-	float woff[33];                  // their prefix: warp w starts at woff[w]
 	unsigned long long wq[32];       // per-warp packed totals
-	unsigned long long wqoff[32];    // their exclusive prefix
 	uint32_t wbad[32];               // per-warp: a term that is not >= +0 and finite
-	uint32_t anybad;
 	uint32_t c_idx[OSUM_CMAX], c_qx[OSUM_CMAX], c_b[OSUM_CMAX], c_t[OSUM_CMAX];
 	uint32_t t_qx[OSUM_TMAX], t_k[OSUM_TMAX];
-	uint32_t ncross, nties;
 	float result;
 };
 
@@ -158,39 +154,37 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 		sh.wbad[wid] = bad;
 	}
 	__syncthreads();
-	// warp 0 turns the warp totals into each warp's starting value (the one
-	// value both the warp and the last lane of the warp before it use)
-	if (wid == 0) {
-		const uint32_t nw = nt / 32;
+	// every warp turns the warp totals into the warps' starting values itself
+	// (the same operations on the same values in every warp, so the same bits:
+	// warp w starts at woff(w), which the last lane of warp w - 1 also uses)
+	const uint32_t nw = nt / 32;
+	float woff_in;                          // lane l: the sum of warps 0..l
+	{
 		const float y = lane < nw ? sh.wf[lane] : 0.0f;
-		const bool wb = __any_sync(0xffffffffu, lane < nw && sh.wbad[lane]);
-		float wi = y;
+		bad = __any_sync(0xffffffffu, lane < nw && sh.wbad[lane]);
+		woff_in = y;
 #pragma unroll
 		for (int o = 1; o < 32; o <<= 1) {
-			const float z = __shfl_up_sync(0xffffffffu, wi, o);
+			const float z = __shfl_up_sync(0xffffffffu, woff_in, o);
 			if (lane >= (uint32_t)o)
-				wi = __fadd_rn(wi, z);
-		}
-		sh.woff[lane + 1] = wi;
-		if (lane == 0) {
-			sh.woff[0] = 0.0f;
-			sh.anybad = wb;
+				woff_in = __fadd_rn(woff_in, z);
 		}
 	}
-	__syncthreads();
-	if (sh.anybad) {
+	if (bad) {
 		if (tid == 0)
 			sh.result = ordered_sum_seq(t, n);
 		__syncthreads();
 		return sh.result;
 	}
-	float X = __fadd_rn(sh.woff[wid], ex);
+	const float w_start = wid ? __shfl_sync(0xffffffffu, woff_in, wid - 1) : 0.0f;
+	const float w_next = __shfl_sync(0xffffffffu, woff_in, wid);
+	float X = __fadd_rn(w_start, ex);
 	// the prediction after this thread's last term must be the very value the
 	// next thread starts from (its X), so that the runs of step 3 never mix
 	// two predicted grids: the next lane's X, or the next warp's first
 	float x_next = __shfl_down_sync(0xffffffffu, X, 1);
 	if (lane == 31)
-		x_next = sh.woff[wid + 1];
+		x_next = w_next;
 
 	// 2. grid offsets, ties, crossings
 	unsigned long long pk[EPT];
@@ -205,10 +199,15 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 		unsigned long long q = 1ull << 52;                      // a crossing
 		if (b == bn && b >= 23 && b <= 254 && i != n - 1) {
 			const float f = __fmul_rn(v[k], __uint_as_float((277u - b) << 23));  // t / u
-			if (f < 16777216.0f) {
-				const bool tie = __fsub_rn(f, truncf(f)) == 0.5f;
-				q = tie ? ((unsigned long long)__float2uint_rz(f) | 1ull << 40)
-					: (unsigned long long)__float2uint_rn(f);
+			if (f < 4194304.0f) {
+				// rne(f) by adding 1.5 * 2^23 (exact below 2^22); a tie is
+				// a rounding by exactly one half, taken down here
+				const float g = __fadd_rn(f, 12582912.0f);
+				const uint32_t r = __float_as_uint(g) - 0x4b400000u;
+				const float dr = __fsub_rn(__fsub_rn(g, 12582912.0f), f);
+				const bool tie = fabsf(dr) == 0.5f;
+				q = tie ? ((unsigned long long)(r - (dr > 0.0f)) | 1ull << 40)
+					: (unsigned long long)r;
 			}
 		}
 		pk[k] = ((uint32_t)k < ept && i < n) ? q : 0ull;
@@ -226,8 +225,9 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 	if (lane == 31)
 		sh.wq[wid] = qinc;
 	__syncthreads();
-	if (wid == 0) {
-		const uint32_t nw = nt / 32;
+	// (again every warp scans the warp totals itself)
+	unsigned long long q_all;
+	{
 		const unsigned long long y = lane < nw ? sh.wq[lane] : 0ull;
 		unsigned long long wi = y;
 #pragma unroll
@@ -236,16 +236,14 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 			if (lane >= (uint32_t)o)
 				wi += z;
 		}
-		sh.wqoff[lane] = wi - y;
-		if (lane == 31) {
-			sh.ncross = (uint32_t)(wi >> 52);
-			sh.nties = (uint32_t)(wi >> 40) & 0xfffu;
-		}
+		qex += __shfl_sync(0xffffffffu, wi - y, wid);
+		q_all = __shfl_sync(0xffffffffu, wi, 31);
 	}
-	__syncthreads();
-	qex += sh.wqoff[wid];
+	// (only the few threads holding a tie or a crossing list anything)
 #pragma unroll
 	for (int k = 0; k < EPT; k++) {
+		if (!(lsum >> 40))
+			break;
 		const uint32_t i = i0 + k;
 		if (pk[k] >> 52) {
 			const uint32_t r = (uint32_t)(qex >> 52);
@@ -271,60 +269,62 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 	//    parity of m at the run's start), then the chain over the crossings
 	//    in order, in registers
 	if (wid == 0) {
-		const uint32_t nc = sh.ncross, ntie = sh.nties;
+		const uint32_t nc = (uint32_t)(q_all >> 52), ntie = (uint32_t)(q_all >> 40) & 0xfffu;
 		bool ok = nc <= (uint32_t)OSUM_CMAX && ntie <= (uint32_t)OSUM_TMAX;
+		// per crossing: the term, the run's offset, and a word of the
+		// predicted binade (bits 0..7), whether a run precedes it (bit 8) and
+		// its ties' round-ups for m even (bits 9..17) and odd (18..26)
 		float tc[2];
-		uint32_t rb[2], rq[2], rup[2];     // rup: ties' round-ups (bit 0..15: m even, 16..: odd)
-		bool rrun[2];
+		uint32_t rq[2], rw[2];
 #pragma unroll
 		for (int h = 0; h < 2; h++) {
 			const uint32_t r = lane + 32 * h;
 			tc[h] = 0.0f;
-			rb[h] = rq[h] = rup[h] = 0;
-			rrun[h] = false;
+			rq[h] = rw[h] = 0;
 			if (ok && r < nc) {
 				const uint32_t c = sh.c_idx[r], st = r ? sh.c_idx[r - 1] + 1 : 0;
 				const uint32_t q0 = r ? sh.c_qx[r - 1] : 0, t0 = r ? sh.c_t[r - 1] : 0;
 				tc[h] = t[c];
-				rb[h] = sh.c_b[r];
 				rq[h] = sh.c_qx[r] - q0;
-				rrun[h] = c > st;
 				uint32_t up0 = 0, up1 = 0;
 				for (uint32_t j = t0; j < sh.c_t[r]; j++) {
 					const uint32_t o = sh.t_qx[j] - q0 + sh.t_k[j];
 					up0 += (o + up0) & 1u;
 					up1 += (1u + o + up1) & 1u;
 				}
-				rup[h] = (up0 & 0xffffu) | up1 << 16;
+				rw[h] = sh.c_b[r] | (c > st ? 1u << 8 : 0u) | up0 << 9 | up1 << 18;
 			}
 		}
-		// (batches of 8 crossings: a batch's shuffles do not wait on s)
+		// batches of 8 crossings: all of a batch's shuffles first, then the
+		// chain through them in registers
 		float s = 0.0f;
 		uint32_t done = 0;
 		for (uint32_t r0 = 0; ok && r0 < nc; r0 += 8) {
+			float bt[8];
+			uint32_t bq[8], bw[8];
+			const int h = (r0 >> 5) & 1;        // r0 + 7 stays in the same half
 #pragma unroll
 			for (int j = 0; j < 8; j++) {
-				const uint32_t r = r0 + j;
-				const int h = (r >> 5) & 1, src = r & 31;
-				const float c_t = __shfl_sync(0xffffffffu, h ? tc[1] : tc[0], src);
-				const uint32_t b = __shfl_sync(0xffffffffu, h ? rb[1] : rb[0], src);
-				const uint32_t q = __shfl_sync(0xffffffffu, h ? rq[1] : rq[0], src);
-				const uint32_t up = __shfl_sync(0xffffffffu, h ? rup[1] : rup[0], src);
-				const bool run = __shfl_sync(0xffffffffu, h ? rrun[1] : rrun[0], src);
-				if (ok && r < nc) {
-					if (run) {
-						const uint32_t m = (__float_as_uint(s) & 0x7fffffu) | 0x800000u;
-						const uint32_t mend = m + q + ((m & 1u) ? up >> 16 : up & 0xffffu);
-						if (binade_field(s) != b || mend >= 0x1000000u)
-							ok = false;
-						else
-							s = __uint_as_float((b << 23) | (mend & 0x7fffffu));
-					}
-					if (ok) {
-						s = __fadd_rn(s, c_t);
-						done = r + 1;
-					}
-				}
+				const int src = (r0 + j) & 31;
+				bt[j] = __shfl_sync(0xffffffffu, h ? tc[1] : tc[0], src);
+				bq[j] = __shfl_sync(0xffffffffu, h ? rq[1] : rq[0], src);
+				bw[j] = __shfl_sync(0xffffffffu, h ? rw[1] : rw[0], src);
+			}
+#pragma unroll
+			for (int j = 0; j < 8; j++) {
+				// (selects, no branches: the chain is the step's latency)
+				const uint32_t w = bw[j], b = w & 0xffu;
+				const bool run = w & (1u << 8), live = r0 + j < nc;
+				const uint32_t m = (__float_as_uint(s) & 0x7fffffu) | 0x800000u;
+				const uint32_t mend =
+					m + bq[j] + ((m & 1u) ? w >> 18 : (w >> 9) & 0x1ffu);
+				const bool bad = run && (binade_field(s) != b || mend >= 0x1000000u);
+				const float sg = run ? __uint_as_float((b << 23) | (mend & 0x7fffffu)) : s;
+				const float sn = __fadd_rn(sg, bt[j]);
+				const bool take = ok && live && !bad;
+				s = take ? sn : s;
+				done = take ? r0 + j + 1 : done;
+				ok = ok && !(live && bad);
 			}
 		}
 		if (lane == 0) {
