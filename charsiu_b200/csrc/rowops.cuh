@@ -367,7 +367,33 @@ __device__ __forceinline__ void norm_quant_cta(const float *__restrict__ x,
 	__syncthreads();
 	const float scale = *scale_sh;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	for (uint32_t b = warp; b < n / 32; b += blockDim.x / 32) {
+	const uint32_t nw = blockDim.x / 32;
+	uint32_t b = warp;
+	// four blocks of a warp at a time, their reductions and divisions
+	// interleaved (blocks b, b + nw, b + 2 nw, b + 3 nw)
+	for (; b + 3 * nw < n / 32; b += 4 * nw) {
+		float v[4], amax[4];
+#pragma unroll
+		for (int j = 0; j < 4; j++) {
+			const uint32_t i = (b + j * nw) * 32 + lane;
+			v[j] = __fmul_rn(__fmul_rn(xs[i], scale), ws[i]);
+			amax[j] = fabsf(v[j]);
+		}
+#pragma unroll
+		for (int o = 16; o; o >>= 1)
+#pragma unroll
+			for (int j = 0; j < 4; j++)
+				amax[j] = fmaxf(amax[j], __shfl_xor_sync(0xffffffffu, amax[j], o));
+#pragma unroll
+		for (int j = 0; j < 4; j++) {
+			const float dd = __fdiv_rn(amax[j], 127.0f);
+			const float inv = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+			aq[(b + j * nw) * 32 + lane] = (int8_t)__float2int_rn(__fmul_rn(v[j], inv));
+			if (lane == 0)
+				ad[b + j * nw] = dd;
+		}
+	}
+	for (; b < n / 32; b += nw) {
 		const uint32_t i = b * 32 + lane;
 		quantise_block_warp(__fmul_rn(__fmul_rn(xs[i], scale), ws[i]), lane, aq + b * 32,
 				    ad + b);
