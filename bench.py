@@ -431,7 +431,8 @@ def run_ours(args, rank, world, dist):
         npu_format = {"matvec_k2048_n8192": {"value": round(gbs, 1), "unit": "GB/s",
                                              "frac": round(gbs / peak, 4),
                                              "us_per_launch": round(us, 3)},
-                      "decode_e2e": npu_decode_e2e(path, args.steps)}
+                      "decode_e2e": npu_decode_e2e(path, args.steps),
+                      "decode_e2e_resident": npu_decode_e2e(path, args.steps, resident=True)}
 
     out = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
@@ -721,34 +722,45 @@ def npu_matvec_case(k: int, n: int, steps: int, warmup: int):
     return us, algo, copies, clk
 
 
-def npu_decode_e2e(path: str, steps: int):
+def npu_decode_e2e(path: str, steps: int, resident: bool = False):
     """The workload's greedy decode in the NPU number format through the C ABI
-    (charsiu_gpu_llama_forward after opening with CHARSIU_NPU_QUANT=1): every
-    projection and the head a charsiu_npu_* call with host buffers."""
+    (charsiu_gpu_llama_greedy after opening with CHARSIU_NPU_QUANT=1): every
+    projection and the head a charsiu_npu_* call with host buffers -- or, with
+    `resident`, the whole step on the device in that format
+    (charsiu_gpu_llama_set_resident: token and position in, the argmax out)."""
     from charsiu_b200.lib import Llama
 
     os.environ["CHARSIU_NPU_QUANT"] = "1"
     try:
         prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
         n_gen = SPEC["n_gen"]
-        reps = max(1, min(steps, 96) // n_gen)
+        reps = max(1, min(steps, 480 if resident else 96) // n_gen)
         total_ms, ok = 0.0, True
         with open(os.path.join(ROOT, "tests", "golden", "golden_decode.json")) as f:
             gold = json.load(f)["npu"]["llama1b_q8"]["tokens"]
-        with Llama(path, n_ctx=len(prompt) + n_gen + 1) as m:
-            m.greedy(prompt, n_gen)
+        with Llama(path, n_ctx=len(prompt) + n_gen + 1, resident=resident) as m:
+            for _ in range(2 if resident else 1):   # (the device step builds its graphs)
+                m.greedy(prompt, n_gen)
             for _ in range(reps):
                 toks, _, gen_ms = m.greedy(prompt, n_gen)
                 total_ms += gen_ms
                 ok = ok and toks.tolist() == gold
             calls = m.npu_calls
+            launches = m.step_launches
     finally:
         del os.environ["CHARSIU_NPU_QUANT"]
-    return {"value": round(reps * n_gen / (total_ms / 1e3), 2), "unit": UNIT,
-            "steps": reps * n_gen, "ms_per_step": round(total_ms / (reps * n_gen), 4),
-            "tokens_match_reference": ok, "npu_calls": calls,
-            "api": "charsiu_gpu_llama_greedy, opened with CHARSIU_NPU_QUANT=1: each "
-                   "projection and the head a charsiu_npu_* host call"}
+    out = {"value": round(reps * n_gen / (total_ms / 1e3), 2), "unit": UNIT,
+           "steps": reps * n_gen, "ms_per_step": round(total_ms / (reps * n_gen), 4),
+           "tokens_match_reference": ok, "npu_calls": calls}
+    if resident:
+        out.update(kernels_per_step=launches,
+                   api="charsiu_gpu_llama_greedy after charsiu_gpu_llama_set_resident(1), "
+                       "opened with CHARSIU_NPU_QUANT=1: token + position in, argmax out, "
+                       "one CUDA graph a token in the NPU number format")
+    else:
+        out["api"] = ("charsiu_gpu_llama_greedy, opened with CHARSIU_NPU_QUANT=1: each "
+                      "projection and the head a charsiu_npu_* host call")
+    return out
 
 
 def run_npu_case(args):

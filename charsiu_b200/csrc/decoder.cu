@@ -22,6 +22,7 @@
 
 #include "forward.cuh"
 #include "layer_internal.h"
+#include "npu_internal.h"
 
 using namespace cgpu;
 
@@ -188,6 +189,13 @@ struct charsiu_gpu_decoder {
 	std::vector<int> ids;
 	int embd_id = -1, head_id = -1;
 	bool pdl = true;
+	// charsiu's NPU number format: the projections and the head are this NPU
+	// layer's tensors, fed single-scale activations (q1, kp bytes, and *d1)
+	charsiu_npu *npu = nullptr;
+	int8_t *q1 = nullptr;
+	float *d1 = nullptr;
+	float *vf = nullptr;          // the fp32 attention / SiLU outputs before their q1
+	uint32_t kp_embd = 0, kp_ff = 0;
 	cudaStream_t st = nullptr;
 	float *exptab = nullptr;
 	float *norm = nullptr;        // [2 n_layer + 1][n_embd]: attn, ffn per layer, then out
@@ -250,9 +258,112 @@ bool matvec(charsiu_gpu_decoder *dec, const int *ids, unsigned n, float *const *
 	return true;
 }
 
+// NPU number format: rmsnorm with the single-scale quantiser into q1 / d1
+bool norm_q1(charsiu_gpu_decoder *dec, const float *add, const float *w)
+{
+	return launch(dec, fwd_norm_q1_kernel, 1, FWD_NORM_THREADS, fwd_norm_smem(dec->n_embd),
+		      dec->x, add, w, dec->n_embd, dec->eps, dec->kp_embd, dec->q1, dec->d1);
+}
+
+bool q1_of(charsiu_gpu_decoder *dec, const float *v, uint32_t n, uint32_t kp)
+{
+	return launch(dec, fwd_q1_kernel, 1, FWD_Q1_THREADS, (size_t)n * 4, v, n, kp, dec->q1,
+		      dec->d1);
+}
+
+bool npu_matvec(charsiu_gpu_decoder *dec, const int *ids, unsigned n, float *const *ys)
+{
+	const unsigned long before = npu_layer_launches(dec->npu);
+	if (npu_layer_matvec_dev_d1(dec->npu, ids, n, dec->q1, dec->d1, ys, dec->st))
+		return false;
+	dec->launches += (unsigned)(npu_layer_launches(dec->npu) - before);
+	return true;
+}
+
+// One token in the NPU number format (src/llama.c:110-312 with
+// CHARSIU_NPU_QUANT): llama_forward's steps as queue_step's, every projection
+// and the head an NPU-format matvec of a single-scale activation -- after
+// each rmsnorm, the attention output and SiLU's.
+bool queue_step_npu(charsiu_gpu_decoder *dec, bool want_logits)
+{
+	const uint32_t n = dec->n_embd, kvdim = dec->n_head_kv * dec->hd;
+	const size_t layer_kv = (size_t)dec->n_ctx * kvdim;
+	dec->launches = 0;
+	if (cudaMemcpyAsync(dec->io, dec->h_io, 2 * sizeof(int), cudaMemcpyHostToDevice, dec->st) !=
+	    cudaSuccess)
+		return fail(dec, "the step's input copy failed");
+	{
+		const unsigned long before = charsiu_gpu_launches(dec->g);
+		if (charsiu_gpu_row_dev(dec->g, dec->embd_id, dec->io + FWD_IO_TOKEN, dec->x, dec->st))
+			return fail(dec, "the embedding lookup failed");
+		dec->launches += (unsigned)(charsiu_gpu_launches(dec->g) - before);
+	}
+	const size_t attn_smem = fwd_attention_smem(dec->n_ctx, dec->hd);
+	for (uint32_t l = 0; l < dec->n_layer; l++) {
+		const int *id = dec->ids.data() + (size_t)l * P_N;
+		float *kc = dec->kc + l * layer_kv, *vc = dec->vc + l * layer_kv;
+		if (!norm_q1(dec, l ? dec->xb2 : nullptr, dec->norm + (size_t)(2 * l) * n))
+			return fail(dec, "a launch failed (attention rmsnorm)");
+		{
+			float *ys[3] = {dec->qv, dec->kv, dec->vv};
+			if (!npu_matvec(dec, id + P_Q, 3, ys))
+				return fail(dec, "the q, k, v matvec failed");
+		}
+		if (!launch(dec, fwd_attention_kernel, dec->n_head, FWD_ATTN_THREADS, attn_smem,
+			    (const float *)dec->qv, (const float *)dec->kv, (const float *)dec->vv,
+			    (const float *)dec->rope, kc, vc, (const int *)dec->io, dec->n_head,
+			    dec->n_head_kv, dec->hd, dec->n_ctx, fwd_attention_tile(dec->hd), dec->scale,
+			    (const float *)dec->exptab, (int8_t *)nullptr, (float *)nullptr, dec->vf) ||
+		    !q1_of(dec, dec->vf, n, dec->kp_embd))
+			return fail(dec, "a launch failed (attention)");
+		{
+			float *ys[1] = {dec->xb2};
+			if (!npu_matvec(dec, id + P_O, 1, ys))
+				return fail(dec, "the output projection failed");
+		}
+		if (!norm_q1(dec, dec->xb2, dec->norm + (size_t)(2 * l + 1) * n))
+			return fail(dec, "a launch failed (ffn rmsnorm)");
+		{
+			float *ys[2] = {dec->hb, dec->hb2};
+			if (!npu_matvec(dec, id + P_GATE, 2, ys))
+				return fail(dec, "the gate, up matvec failed");
+		}
+		if (!launch(dec, fwd_silu_quant_kernel, (dec->n_ff + 255) / 256, 256, 0,
+			    (const float *)dec->hb, (const float *)dec->hb2, dec->n_ff,
+			    (const float *)dec->exptab, (int8_t *)nullptr, (float *)nullptr, dec->vf) ||
+		    !q1_of(dec, dec->vf, dec->n_ff, dec->kp_ff))
+			return fail(dec, "a launch failed (silu)");
+		{
+			float *ys[1] = {dec->xb2};
+			if (!npu_matvec(dec, id + P_DOWN, 1, ys))
+				return fail(dec, "the down projection failed");
+		}
+	}
+	if (!norm_q1(dec, dec->xb2, dec->norm + (size_t)(2 * dec->n_layer) * n))
+		return fail(dec, "a launch failed (final rmsnorm)");
+	{
+		float *ys[1] = {dec->logits};
+		if (!npu_matvec(dec, &dec->head_id, 1, ys))
+			return fail(dec, "the output head failed");
+	}
+	if (!launch(dec, fwd_argmax_kernel, FWD_ARGMAX_CTAS, FWD_ARGMAX_THREADS, 0,
+		    (const float *)dec->logits, dec->n_vocab, dec->io,
+		    reinterpret_cast<uint32_t *>(dec->io + FWD_IO_TICKET), dec->part_v, dec->part_i))
+		return fail(dec, "a launch failed (argmax)");
+	if (cudaMemcpyAsync(dec->h_io + FWD_IO_NEXT, dec->io + FWD_IO_NEXT, sizeof(int),
+			    cudaMemcpyDeviceToHost, dec->st) != cudaSuccess)
+		return fail(dec, "the step's output copy failed");
+	if (want_logits && cudaMemcpyAsync(dec->h_logits, dec->logits, (size_t)dec->n_vocab * 4,
+					   cudaMemcpyDeviceToHost, dec->st) != cudaSuccess)
+		return fail(dec, "the logits copy failed");
+	return true;
+}
+
 // Queue one token's work on dec->st (eagerly or into a capture).
 bool queue_step(charsiu_gpu_decoder *dec, bool want_logits)
 {
+	if (dec->npu)
+		return queue_step_npu(dec, want_logits);
 	const uint32_t n = dec->n_embd, kvdim = dec->n_head_kv * dec->hd;
 	const size_t layer_kv = (size_t)dec->n_ctx * kvdim;
 	dec->launches = 0;
@@ -281,7 +392,7 @@ bool queue_step(charsiu_gpu_decoder *dec, bool want_logits)
 			    (const float *)dec->rope, kc, vc, (const int *)dec->io, dec->n_head,
 			    dec->n_head_kv, dec->hd, dec->n_ctx, fwd_attention_tile(dec->hd), dec->scale,
 			    (const float *)dec->exptab,
-			    dec->aq, dec->ad))
+			    dec->aq, dec->ad, (float *)nullptr))
 			return fail(dec, "a launch failed (attention)");
 		{
 			float *ys[1] = {dec->xb2};
@@ -297,7 +408,7 @@ bool queue_step(charsiu_gpu_decoder *dec, bool want_logits)
 		}
 		if (!launch(dec, fwd_silu_quant_kernel, (dec->n_ff + 255) / 256, 256, 0,
 			    (const float *)dec->hb, (const float *)dec->hb2, dec->n_ff,
-			    (const float *)dec->exptab, dec->aq, dec->ad))
+			    (const float *)dec->exptab, dec->aq, dec->ad, (float *)nullptr))
 			return fail(dec, "a launch failed (silu)");
 		{
 			float *ys[1] = {dec->xb2};
@@ -336,7 +447,7 @@ void release(charsiu_gpu_decoder *dec)
 			(void *)dec->x, (void *)dec->qv, (void *)dec->kv, (void *)dec->vv,
 			(void *)dec->xb2, (void *)dec->hb, (void *)dec->hb2, (void *)dec->logits,
 			(void *)dec->aq, (void *)dec->ad, (void *)dec->io, (void *)dec->part_v,
-			(void *)dec->part_i})
+			(void *)dec->part_i, (void *)dec->q1, (void *)dec->d1, (void *)dec->vf})
 		if (p)
 			cudaFree(p);
 	if (dec->h_io)
@@ -349,16 +460,18 @@ void release(charsiu_gpu_decoder *dec)
 		exptab_release(dec->device);
 }
 
-} // namespace
-
-extern "C" {
-
-struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
-						    const struct charsiu_gpu_decoder_desc *d)
+// The step of either format: npu null, the GGML formats on g; else the
+// projections and the head on npu (the embedding row still from g).
+charsiu_gpu_decoder *build(charsiu_gpu *g, charsiu_npu *npu,
+			   const struct charsiu_gpu_decoder_desc *d)
 {
 	if (!g || !d || !d->proj_ids || !d->attn_norm || !d->ffn_norm || !d->out_norm ||
-	    !d->rope_cs || charsiu_gpu_dead(g))
+	    !d->rope_cs || charsiu_gpu_dead(g) || (npu && npu_layer_dead(npu)))
 		return nullptr;
+	if (npu && npu_layer_device(npu) != layer_device(g)) {
+		layer_whine(g, "the NPU-format layer is on another GPU than the layer");
+		return nullptr;
+	}
 	if (!layer_whole(g)) {
 		layer_whine(g, "the decode step needs a layer that holds whole tensors (world 1)");
 		return nullptr;
@@ -377,6 +490,8 @@ struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
 	auto check = [&](int id, uint64_t k, uint64_t rows) {
 		uint64_t tk, tr;
 		uint32_t ty;
+		if (npu)
+			return npu_layer_tensor(npu, id, &tk, &tr, &ty) && tk == k && tr == rows;
 		return layer_tensor(g, id, &tk, &tr, &ty) && tk == k && tr == rows;
 	};
 	for (uint32_t l = 0; l < d->n_layer; l++) {
@@ -417,6 +532,9 @@ struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
 	dec->embd_id = d->embd_id;
 	dec->head_id = d->head_id;
 	dec->pdl = !layer_no_pdl(g);
+	dec->npu = npu;
+	dec->kp_embd = (n + 15) / 16 * 16;
+	dec->kp_ff = (d->n_ff + 15) / 16 * 16;
 	cudaSetDevice(dec->device);
 
 	std::string why;
@@ -451,6 +569,11 @@ struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
 			   cudaSuccess;
 	ok = ok && cudaHostAlloc(&dec->h_logits, (size_t)d->n_vocab * 4, cudaHostAllocDefault) ==
 			   cudaSuccess;
+	if (npu) {
+		ok = ok && cudaMalloc(&dec->q1, std::max(dec->kp_embd, dec->kp_ff)) == cudaSuccess;
+		ok = ok && cudaMalloc(&dec->d1, sizeof(float)) == cudaSuccess;
+		ok = ok && cudaMalloc(&dec->vf, (size_t)widest * 4) == cudaSuccess;
+	}
 	if (ok) {
 		for (uint32_t l = 0; l < d->n_layer && ok; l++) {
 			ok = cudaMemcpy(dec->norm + (size_t)(2 * l) * n, d->attn_norm[l], (size_t)n * 4,
@@ -467,9 +590,15 @@ struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
 		ok = ok && cudaMemset(dec->io, 0, FWD_IO_WORDS * sizeof(int)) == cudaSuccess;
 	}
 	if (ok && fwd_norm_smem(n) > 48 * 1024)
-		ok = cudaFuncSetAttribute((const void *)fwd_norm_quant_kernel,
+		ok = cudaFuncSetAttribute(npu ? (const void *)fwd_norm_q1_kernel
+					      : (const void *)fwd_norm_quant_kernel,
 					  cudaFuncAttributeMaxDynamicSharedMemorySize,
 					  (int)fwd_norm_smem(n)) == cudaSuccess;
+	if (ok && npu && (size_t)widest * 4 > 48 * 1024)
+		ok = widest * 4 <= 227 * 1024 &&
+		     cudaFuncSetAttribute((const void *)fwd_q1_kernel,
+					  cudaFuncAttributeMaxDynamicSharedMemorySize,
+					  (int)(widest * 4)) == cudaSuccess;
 	const size_t attn_smem = fwd_attention_smem(d->n_ctx, hd);
 	if (ok && attn_smem > 48 * 1024)
 		ok = cudaFuncSetAttribute((const void *)fwd_attention_kernel,
@@ -483,6 +612,23 @@ struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
 	}
 	memset(dec->h_io, 0, FWD_IO_WORDS * sizeof(int));
 	return dec;
+}
+
+} // namespace
+
+extern "C" {
+
+struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(struct charsiu_gpu *g,
+						    const struct charsiu_gpu_decoder_desc *d)
+{
+	return build(g, nullptr, d);
+}
+
+struct charsiu_gpu_decoder *charsiu_gpu_decoder_new_npu(struct charsiu_gpu *g,
+							struct charsiu_npu *npu,
+							const struct charsiu_gpu_decoder_desc *d)
+{
+	return npu ? build(g, npu, d) : nullptr;
 }
 
 void charsiu_gpu_decoder_free(struct charsiu_gpu_decoder *dec)

@@ -104,6 +104,48 @@ fwd_norm_quant_kernel(float *__restrict__ x, const float *__restrict__ add,
 			x[i] = xs[i];
 }
 
+// The same rmsnorm in charsiu's NPU number format: the result quantised with
+// one scale for the whole vector (quantise_one_cta) into q1 (kp bytes) and
+// *d1, for the NPU-format matvec after it (src/llama.c:255-290).
+__global__ void __launch_bounds__(FWD_NORM_THREADS)
+fwd_norm_q1_kernel(float *__restrict__ x, const float *__restrict__ add,
+		   const float *__restrict__ w, uint32_t n, float eps, uint32_t kp,
+		   int8_t *__restrict__ q1, float *__restrict__ d1)
+{
+	extern __shared__ __align__(16) float nsm[];
+	float *xs = nsm, *sq = nsm + n, *ws = nsm + 2 * n;      // fwd_norm_smem(n)
+	__shared__ float scale_s, red[32];
+	for (uint32_t i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+		cp_async16(ws + i, w + i);
+	pdl_wait();
+	pdl_launch_dependents();
+	const float scale = norm_scale_cta(x, add, n, eps, xs, sq, &scale_s);
+	quantise_one_cta([&](uint32_t i) { return __fmul_rn(__fmul_rn(xs[i], scale), ws[i]); }, n,
+			 kp, q1, d1, red);
+	if (add)
+		for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+			x[i] = xs[i];
+}
+
+// The NPU number format's activation of an fp32 vector (the attention output
+// before the o projection, SiLU's before down): one CTA, the n values staged
+// in shared memory, then quantise_one_cta into q1 (kp bytes) and *d1.
+constexpr int FWD_Q1_THREADS = 1024;
+
+__global__ void __launch_bounds__(FWD_Q1_THREADS)
+fwd_q1_kernel(const float *__restrict__ v, uint32_t n, uint32_t kp, int8_t *__restrict__ q1,
+	      float *__restrict__ d1)
+{
+	extern __shared__ __align__(16) float vsm[];            // n floats
+	__shared__ float red[32];
+	pdl_wait();
+	pdl_launch_dependents();
+	for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+		vsm[i] = v[i];
+	__syncthreads();
+	quantise_one_cta([&](uint32_t i) { return vsm[i]; }, n, kp, q1, d1, red);
+}
+
 // One head of attention at this token's position, RoPE and the KV cache
 // included (src/llama.c:364-383, 781-817):
 //   q and this head's k rotated by the position's (cos, sin) pairs, from a
@@ -114,7 +156,9 @@ fwd_norm_quant_kernel(float *__restrict__ x, const float *__restrict__ add,
 //   scores a_t = (sum_i q_i k_ti, in order) * scale; softmax (the max, expf,
 //   the sum over t in order, the division); out_i = sum_t att_t v_ti in order
 //   from 0; then the quantiser of the head's outputs (head_dim a multiple of
-//   32, so every 32-block of the attention output lies inside one head).
+//   32, so every 32-block of the attention output lies inside one head), or,
+//   when out_f is given, the outputs themselves into out_f[h * hd ..] (the NPU
+//   number format quantises the whole vector at once, after this kernel).
 // One CTA a head. K and V pass through shared memory a tile of positions at a
 // time (rows of hd + 4 floats: 16-byte copies, and a float4 read a row per
 // lane meets no bank conflict); the first tile's cache rows -- written by
@@ -150,7 +194,7 @@ fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
 		     float *__restrict__ kcache, float *__restrict__ vcache,
 		     const int *__restrict__ io, uint32_t n_head, uint32_t n_head_kv, uint32_t hd,
 		     uint32_t n_ctx, uint32_t tile, float scale, const float *__restrict__ exptab,
-		     int8_t *__restrict__ q, float *__restrict__ d)
+		     int8_t *__restrict__ q, float *__restrict__ d, float *__restrict__ out_f)
 {
 	extern __shared__ __align__(16) float fsm[];
 	const uint32_t rs = hd + 4;
@@ -273,6 +317,11 @@ fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
 			for (int t = 0; t < nt; t++)
 				o = __fadd_rn(o, __fmul_rn(att[t0 + t], vt[(size_t)t * rs + threadIdx.x]));
 	}
+	if (out_f) {
+		if (threadIdx.x < hd)
+			out_f[h * hd + threadIdx.x] = o;
+		return;
+	}
 	if (threadIdx.x < hd)
 		os[threadIdx.x] = o;
 	__syncthreads();
@@ -284,10 +333,12 @@ fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
 }
 
 // SiLU(gate) * up (src/llama.c:831-836: g *= 1 / (1 + expf(-g)); g * up),
-// then the quantiser of the result. One warp a 32-block.
+// then the quantiser of the result, one warp a 32-block -- or, when out_f is
+// given, the result itself into out_f (the NPU number format's path).
 __global__ void fwd_silu_quant_kernel(const float *__restrict__ gate, const float *__restrict__ up,
 				      uint32_t n, const float *__restrict__ exptab,
-				      int8_t *__restrict__ q, float *__restrict__ d)
+				      int8_t *__restrict__ q, float *__restrict__ d,
+				      float *__restrict__ out_f)
 {
 	pdl_wait();
 	pdl_launch_dependents();
@@ -298,7 +349,10 @@ __global__ void fwd_silu_quant_kernel(const float *__restrict__ gate, const floa
 		float g = gate[i];
 		const float e = exp_exact(-g, exptab);
 		g = __fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
-		quantise_block_warp(__fmul_rn(g, up[i]), lane, q + b * 32, d + b);
+		if (out_f)
+			out_f[i] = __fmul_rn(g, up[i]);
+		else
+			quantise_block_warp(__fmul_rn(g, up[i]), lane, q + b * 32, d + b);
 	}
 }
 

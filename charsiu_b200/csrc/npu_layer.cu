@@ -25,6 +25,7 @@
 
 #include "charsiu_npu.h"
 
+#include "npu_internal.h"
 #include "npumv.cuh"
 #include "ref_abi.h"
 
@@ -147,7 +148,7 @@ int check_group(charsiu_npu *g, const int *ids, unsigned n, uint64_t k)
 }
 
 void fill(charsiu_npu *g, NpuParams &p, const int *ids, unsigned n, float *const *ys, float d1,
-	  const int8_t *q1)
+	  const int8_t *q1, const float *d1p = nullptr)
 {
 	memset(&p, 0, sizeof(p));
 	uint32_t acc = 0;
@@ -164,6 +165,7 @@ void fill(charsiu_npu *g, NpuParams &p, const int *ids, unsigned n, float *const
 	p.total_rows = acc;
 	p.kp = g->ent[ids[0]].kp;
 	p.d1 = d1;
+	p.d1p = d1p;
 	p.q1 = q1;
 }
 
@@ -321,6 +323,49 @@ int run(charsiu_npu *g, const int *ids, unsigned n, const int8_t *q1, float d1, 
 }
 
 } // namespace
+
+// ---- what the decode step asks of the layer --------------------------------
+
+namespace cgpu {
+
+int npu_layer_device(const charsiu_npu *g)
+{
+	return g->device;
+}
+
+bool npu_layer_dead(const charsiu_npu *g)
+{
+	return g->dead != 0;
+}
+
+bool npu_layer_tensor(const charsiu_npu *g, int id, uint64_t *k, uint64_t *n, uint32_t *kp)
+{
+	if (id < 0 || (size_t)id >= g->ent.size())
+		return false;
+	*k = g->ent[id].k;
+	*n = g->ent[id].n;
+	*kp = g->ent[id].kp;
+	return true;
+}
+
+int npu_layer_matvec_dev_d1(charsiu_npu *g, const int *ids, unsigned n, const int8_t *q1,
+			    const float *d1, float *const *ys, cudaStream_t st)
+{
+	if (g->dead || !q1 || !d1 || !ys || ((uintptr_t)q1 & 15) || !ids || !n ||
+	    n > (unsigned)NPU_MAX_TENSORS || ids[0] < 0 || (size_t)ids[0] >= g->ent.size() ||
+	    check_group(g, ids, n, g->ent[ids[0]].k))
+		return -1;
+	NpuParams p;
+	fill(g, p, ids, n, ys, 0.0f, q1, d1);
+	return launch(g, p, nullptr, st);
+}
+
+unsigned long npu_layer_launches(const charsiu_npu *g)
+{
+	return g->launches;
+}
+
+} // namespace cgpu
 
 extern "C" {
 

@@ -42,6 +42,7 @@ struct NpuParams {
 	uint32_t ntensor, total_rows, kp;
 	uint32_t rows_per_warp;  // 1 .. the kernel's R
 	float d1;
+	const float *d1p;        // when set, d1 is read here (device) once the kernel before is done
 	const int8_t *q1;        // kp bytes (device); unused when the activation is inline
 	// direct host calls: when done_flag is set, the last CTA to finish
 	// writes `seq` there (mapped host memory) once every y is visible to the
@@ -123,6 +124,7 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 		for (uint32_t i = threadIdx.x; i < nch; i += blockDim.x)
 			act[i] = g4[i];
 	}
+	const float d1 = p.d1p ? *p.d1p : p.d1;
 	__syncthreads();
 	pdl_launch_dependents();
 
@@ -171,7 +173,7 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 		for (int j = 0; j < R; j++) {
 			const int s = __reduce_add_sync(0xffffffffu, acc[j]);
 			if (yp[j])
-				*yp[j] = __fmul_rn(__fmul_rn(__int2float_rn(s), p.d1), sc[j]);
+				*yp[j] = __fmul_rn(__fmul_rn(__int2float_rn(s), d1), sc[j]);
 		}
 	}
 	if (AW && p.done_flag) {

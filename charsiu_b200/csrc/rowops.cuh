@@ -338,17 +338,14 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 	return sh.result;
 }
 
-// rmsnorm (reference src/llama.c:316-326) of x (+ add), then the
-// quantiser of the result into aq / ad, by the whole CTA: xs[i] = x[i] +
-// add[i] (x alone when add is null), ss = the ordered sum of xs[i]^2 (the
-// CTA's exact form, ordered_sum_nonneg_cta), scale = 1 / sqrtf(ss / n + eps), v = xs[i] * scale * w[i] per element,
-// one warp a 32-block. xs, sq, ws: n floats each of shared memory, 16-byte
-// aligned, ws holding w already (copied in by the caller). *scale_sh: a
-// shared float. Ends with a barrier; xs still holds x + add.
-__device__ __forceinline__ void norm_quant_cta(const float *__restrict__ x,
-					       const float *__restrict__ add, uint32_t n, float eps,
-					       float *xs, float *sq, const float *ws, float *scale_sh,
-					       int8_t *aq, float *ad)
+// rmsnorm's scale (reference src/llama.c:316-326) of x (+ add), by the whole
+// CTA: xs[i] = x[i] + add[i] (x alone when add is null), ss = the ordered sum
+// of xs[i]^2 (the CTA's exact form, ordered_sum_nonneg_cta), and the returned
+// scale = 1 / sqrtf(ss / n + eps) (through *scale_sh, a shared float). xs, sq:
+// n floats each of shared memory, 16-byte aligned. Ends with a barrier.
+__device__ __forceinline__ float norm_scale_cta(const float *__restrict__ x,
+						const float *__restrict__ add, uint32_t n,
+						float eps, float *xs, float *sq, float *scale_sh)
 {
 	for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
 		float v = x[i];
@@ -365,7 +362,53 @@ __device__ __forceinline__ void norm_quant_cta(const float *__restrict__ x,
 	if (threadIdx.x == 0)
 		*scale_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
 	__syncthreads();
-	const float scale = *scale_sh;
+	return *scale_sh;
+}
+
+// charsiu_act_set's single-scale form (src/gguf.c:883-910), the NPU number
+// format's activation, of n values by the whole CTA: d1 = amax / 127 (a max,
+// so any order), q1[i] = lrintf(v_i * (1 / d1)) clamped to [-127, 127], zero
+// from n to kp. val(i) gives v_i (called twice per element); red: 32 floats
+// of shared memory. Ends with a barrier.
+template <class V>
+__device__ __forceinline__ void quantise_one_cta(V val, uint32_t n, uint32_t kp, int8_t *q1,
+						 float *d1, float *red)
+{
+	const uint32_t tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
+	float amax = 0.0f;
+	for (uint32_t i = tid; i < n; i += nt)
+		amax = fmaxf(amax, fabsf(val(i)));
+	for (int o = 16; o; o >>= 1)
+		amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+	if (lane == 0)
+		red[wid] = amax;
+	__syncthreads();
+	amax = 0.0f;
+	for (uint32_t w = 0; w < nt / 32; w++)
+		amax = fmaxf(amax, red[w]);
+	const float d = __fdiv_rn(amax, 127.0f);
+	const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+	if (tid == 0)
+		*d1 = d;
+	for (uint32_t i = tid; i < kp; i += nt) {
+		int v = 0;
+		if (i < n)
+			v = min(max(__float2int_rn(__fmul_rn(val(i), id)), -127), 127);
+		q1[i] = (int8_t)v;
+	}
+	__syncthreads();
+}
+
+// rmsnorm of x (+ add) as norm_scale_cta, then the quantiser of the result
+// v = xs[i] * scale * w[i] into aq / ad, one warp a 32-block. ws: n floats
+// of shared memory holding w already (copied in by the caller). Ends with a
+// barrier; xs still holds x + add.
+__device__ __forceinline__ void norm_quant_cta(const float *__restrict__ x,
+					       const float *__restrict__ add, uint32_t n, float eps,
+					       float *xs, float *sq, const float *ws, float *scale_sh,
+					       int8_t *aq, float *ad)
+{
+	const float scale = norm_scale_cta(x, add, n, eps, xs, sq, scale_sh);
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const uint32_t nw = blockDim.x / 32;
 	uint32_t b = warp;

@@ -681,7 +681,9 @@ static struct charsiu_gpu_decoder *make_decoder(struct charsiu_gpu_llama *m)
 
 	if (!ids || !an || !fn || !cs)
 		goto out;
-	if (m->tok != m->out) {
+	/* in the NPU format the head is an NPU-layer tensor: the embedding rows
+	 * come from a copy of token_embd on the GGML layer */
+	if (m->tok != m->out || m->npu_mode) {
 		embd_id = charsiu_gpu_add_blocks(m->dev, m->tok->type, m->tok->ne[0], m->tok->ne[1],
 						 m->tok->data, m->tok->name);
 		if (embd_id < 0)
@@ -712,7 +714,8 @@ static struct charsiu_gpu_decoder *make_decoder(struct charsiu_gpu_llama *m)
 	d.ffn_norm = fn;
 	d.out_norm = m->out_norm;
 	d.rope_cs = cs;
-	dec = charsiu_gpu_decoder_new(m->dev, &d);
+	dec = m->npu_mode ? charsiu_gpu_decoder_new_npu(m->dev, m->npu, &d)
+			  : charsiu_gpu_decoder_new(m->dev, &d);
 out:
 	free(ids);
 	free(an);
@@ -725,11 +728,6 @@ API int charsiu_gpu_llama_set_resident(struct charsiu_gpu_llama *m, int on)
 {
 	if (!m)
 		return -1;
-	if (on && m->npu_mode) {
-		fprintf(stderr, "charsiu: the device step runs the GGML formats, not the NPU "
-				"number format\n");
-		return -1;
-	}
 	if (on && !m->dec && !(m->dec = make_decoder(m)))
 		return -1;
 	m->resident = on != 0;

@@ -76,6 +76,7 @@ SIGNATURES = [
     ("charsiu_gpu_llama_npu", _vp, [_vp]),
     ("charsiu_gpu_row_dev", C.c_int, [_vp, C.c_int, _vp, _vp, _vp]),
     ("charsiu_gpu_decoder_new", _vp, [_vp, _vp]),
+    ("charsiu_gpu_decoder_new_npu", _vp, [_vp, _vp, _vp]),
     ("charsiu_gpu_decoder_free", None, [_vp]),
     ("charsiu_gpu_decoder_step", C.c_int, [_vp, C.c_int32, C.c_int, C.c_int, _vp]),
     ("charsiu_gpu_decoder_logits", C.POINTER(C.c_float), [_vp]),

@@ -263,6 +263,15 @@ struct charsiu_gpu_decoder_desc {
 
 CHARSIU_GPU_API struct charsiu_gpu_decoder *charsiu_gpu_decoder_new(
 	struct charsiu_gpu *g, const struct charsiu_gpu_decoder_desc *desc);
+/* The same step in charsiu's NPU number format (CHARSIU_NPU_QUANT,
+ * src/llama.c:110-312): proj_ids and head_id are tensors added to npu (the
+ * charsiu_npu_* layer of include/charsiu_npu.h, on g's GPU), each fed the
+ * single-scale activation of charsiu_act_set (src/gguf.c:883-910) of the
+ * rmsnorm, attention and SiLU outputs, computed on the device; embd_id is
+ * still a tensor of g. */
+struct charsiu_npu;
+CHARSIU_GPU_API struct charsiu_gpu_decoder *charsiu_gpu_decoder_new_npu(
+	struct charsiu_gpu *g, struct charsiu_npu *npu, const struct charsiu_gpu_decoder_desc *desc);
 CHARSIU_GPU_API void charsiu_gpu_decoder_free(struct charsiu_gpu_decoder *dec);
 /* One token at pos (positions run 0, 1, 2, ... as llama_forward's callers
  * step them): *next gets llama_argmax of its logits; with want_logits the
