@@ -198,9 +198,11 @@ int launch(charsiu_npu *g, const NpuParams &p, const void *inl, cudaStream_t st)
 		g->occ[slot] = occ;
 	}
 	const uint32_t rpw = rows_per_warp(sh.r, g->rows);
+	// one CTA a unit of rpw rows a warp while that leaves SMs idle; past that,
+	// every resident CTA, the rows split evenly over their warps
 	const uint32_t units = (p.total_rows + rpw * NPU_WARPS - 1) / (rpw * NPU_WARPS);
 	unsigned grid = (unsigned)g->occ[slot] * g->sm_count;
-	if (units < grid)
+	if (units <= (uint32_t)g->sm_count)
 		grid = units ? units : 1;
 	cudaLaunchConfig_t cfg = {};
 	cfg.gridDim = dim3(grid);

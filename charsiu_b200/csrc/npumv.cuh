@@ -11,8 +11,9 @@
 //
 // Device layout: each tensor's rows back to back, a row padded with zeros to
 // kp bytes (kp = K rounded up to 16), so a lane's 16-byte loads are aligned.
-// A warp takes up to R rows at a time (rows_per_warp, chosen by the host so
-// that small tensors still spread over every SM); lane L reads 16-byte chunks
+// The grid's warps split the rows into contiguous ranges of equal size (to a
+// row), so every SM carries the same bytes; a warp takes its range up to R
+// rows at a time (rows_per_warp, chosen by the host); lane L reads 16-byte chunks
 // L, L + 32, ... of each, U chunks of each row per step (R * U <= 16 loads in
 // flight a lane), and dots them with dp4a against the activation staged in
 // shared memory; one warp reduction a row, and lane j writes row j. The first
@@ -76,8 +77,11 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const uint32_t nw = gridDim.x * NPU_WARPS;
 
-	// rows r0 .. r0 + R - 1: their tensors and row pointers
+	// rows r0 .. r0 + R - 1 of this warp's range [r0, r_end): their tensors
+	// and row pointers
 	const uint32_t rpw = p.rows_per_warp;
+	const uint32_t gw = blockIdx.x * NPU_WARPS + warp;
+	const uint32_t r_end = (uint32_t)((uint64_t)(gw + 1) * p.total_rows / nw);
 	const int8_t *wr[R];
 	uint32_t ti[R];
 	auto setup = [&](uint32_t r0) {
@@ -88,7 +92,7 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 			while (t + 1 < p.ntensor && r >= p.t[t].row_end)
 				t++;
 			ti[j] = t;
-			wr[j] = ((uint32_t)j < rpw && r < p.total_rows)
+			wr[j] = ((uint32_t)j < rpw && r < r_end)
 				? p.t[t].w + (uint64_t)(r - (p.t[t].row_end - p.t[t].rows)) * p.kp
 				: nullptr;
 		}
@@ -109,7 +113,7 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 	// kernel before this one
 	if (rpw < 1 || rpw > (uint32_t)R)
 		return;
-	uint32_t r0 = (blockIdx.x * NPU_WARPS + warp) * rpw;
+	uint32_t r0 = (uint32_t)((uint64_t)gw * p.total_rows / nw);
 	setup(r0);
 	load(lane);
 	if (AW && p.done_flag && blockIdx.x == 0 && threadIdx.x == 0)
@@ -128,7 +132,7 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 	__syncthreads();
 	pdl_launch_dependents();
 
-	while (r0 < p.total_rows) {
+	while (r0 < r_end) {
 		int acc[R];
 #pragma unroll
 		for (int j = 0; j < R; j++)
@@ -166,7 +170,7 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 				sc[j] = t.scale[row];
 			}
 		}
-		r0 += nw * rpw;
+		r0 += rpw;
 		setup(r0);
 		load(lane);
 #pragma unroll
