@@ -1320,9 +1320,35 @@ int charsiu_gpu_matvec_batch_group_dev(struct charsiu_gpu *g, const int *ids, un
 		return launch_qmm(g, ids, n, q, d, m, ys, g->d_pack,
 				  stream ? (cudaStream_t)stream : g->stream);
 	}
-	for (unsigned i = 0; i < n; i++)
-		if (charsiu_gpu_matvec_batch_dev(g, ids[i], m, q, d, ys[i], stream))
-			return -1;
+	// the CUDA cores: the tensors of each quant type in one launch a chunk of
+	// activations (as queue_matvec_kernels does for host calls), each tensor's
+	// y[a][rows] at its own stride; q6_K one activation at a time
+	cudaStream_t st = stream ? (cudaStream_t)stream : g->stream;
+	const uint32_t nb = g->ent[ids[0]].nb, k = (uint32_t)g->ent[ids[0]].k;
+	for (uint32_t type : {TYPE_Q8_0, TYPE_Q4_0, TYPE_Q6_K}) {
+		int sub[QMV_MAX_TENSORS];
+		float *sy[QMV_MAX_TENSORS];
+		unsigned ns = 0;
+		for (unsigned i = 0; i < n; i++)
+			if (g->ent[ids[i]].type == type) {
+				sub[ns] = ids[i];
+				sy[ns++] = ys[i];
+			}
+		if (!ns)
+			continue;
+		for (unsigned m0 = 0, mc = 0; m0 < m; m0 += mc) {
+			mc = type == TYPE_Q6_K ? 1 : qmvm_chunk(m - m0, nb);
+			float *yd[QMV_MAX_TENSORS];
+			for (unsigned i = 0; i < ns; i++)
+				yd[i] = sy[i] + (size_t)m0 * g->ent[sub[i]].rows;
+			QmvParams p;
+			fill_params(g, p, sub, ns, yd, k, q + (size_t)m0 * nb * 32, d + (size_t)m0 * nb);
+			const int rc = mc == 1 ? launch_matvec1(g, sub, ns, yd, k, p.q, p.d, st)
+					       : launch_qmv(g, (int)mc, p, st);
+			if (rc)
+				return -1;
+		}
+	}
 	return 0;
 }
 

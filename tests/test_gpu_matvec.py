@@ -185,13 +185,15 @@ def _dev_acts(torch, xs, dev):
     return qs, ds, q_t, d_t
 
 
-@pytest.mark.parametrize("m", [2, 17, 64])
+@pytest.mark.parametrize("m", [2, 5, 8, 17, 64])
 @pytest.mark.parametrize("k", [2048, 2080, 544])
 def test_batch_group_dev_one_launch(layer, m, k):
-    """Several q8_0 tensors of one K in one tensor-core launch (as q/k/v and
-    gate/up are grouped; m = 2 takes the CUDA cores, one launch a tensor),
-    ragged N (a partial last 128-row tile, a partial last group) and K with a
-    partial last segment and chunk; every row of every tensor bit-exact."""
+    """Several q8_0 tensors of one K in one launch (as q/k/v and gate/up are
+    grouped): on the tensor cores from m = 9; below, on the CUDA cores, one
+    launch a chunk of 8, 4 or 2 activations and the M = 1 kernel for a last
+    single one (m = 5: 4 + 1). Ragged N (a partial last 128-row tile, a
+    partial last group) and K with a partial last segment and chunk; every
+    row of every tensor bit-exact."""
     torch = pytest.importorskip("torch")
     dev = torch.device("cuda:0")
     ns = [520, 136, 9, 2048]
