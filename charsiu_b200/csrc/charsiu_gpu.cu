@@ -325,7 +325,11 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
 	int threads = 0, slot = 0;
 	const bool q8 = p.t[0].type == TYPE_Q8_0;
 	const uint32_t nseg = nsegments(p.nb);
-	const int shape = nseg <= 4 ? 0 : nseg <= 8 ? 1 : nseg <= 16 ? 2 : 3;
+	// (M >= 4 with 9..16 segments takes the 16-warp shape, one segment a
+	// warp: its term buffers hold the CTA to one an SM, and the extra warps
+	// cover more latency -- the 1B decode step at M = 4 / 8: 0.506 -> 0.463,
+	// 0.797 -> 0.746 ms; at M = 2, with room for more CTAs, it lost 6 %)
+	const int shape = nseg <= 4 ? 0 : nseg <= 8 ? 1 : (nseg <= 16 && m < 4) ? 2 : 3;
 
 	if (m == 1) {
 		threads = qmv1_warps[shape] * 32;
