@@ -940,8 +940,12 @@ def run_reference(args, rank, world, dist):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "Llama-3.2-1B q8_0 greedy decode", "global_batch": 1,
-                       "seq_len": 1, "parallelism": f"{cores} host threads"},
+            "config": {"workload": "Llama-3.2-1B q8_0 greedy decode, per token: 112 "
+                                   "projections + 128256 tied head (charsiu's llama_forward "
+                                   "on the host cores, the rest of the step included)",
+                       "model": "Llama-3.2-1B architecture (16x2048, ffn 8192, 32/8 heads, "
+                                "vocab 128256)",
+                       "global_batch": 1, "seq_len": 1, "parallelism": f"{cores} host threads"},
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores,
                              "kind": kind, "sample": sample},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
