@@ -164,12 +164,14 @@ qmvm_kernel(const __grid_constant__ QmvParams p)
 		uint32_t ti, lg;
 		locate(G, ti, lg);
 		float *tb = terms + (size_t)(i & 1) * M * ts;
-		if (i)
-			load(G);
 		if (s0 < nseg)
 			segm_compute<Q8, M>(R0, seg_blocks(nb, s0), s0 * SB, aq, ad, asum, nb, lane, tb);
 		if (TWO && s1 < nseg)
 			segm_compute<Q8, M>(R1, seg_blocks(nb, s1), s1 * SB, aq, ad, asum, nb, lane, tb);
+		// the registers are free: the next group's weights go now, in flight
+		// through the barrier and the in-order sums below
+		if (G + gridDim.x < p.total_groups)
+			load(G + gridDim.x);
 		named_barrier(1, W * 32);
 		if (threadIdx.x < (unsigned)(M * RG)) {
 			const uint32_t a = threadIdx.x / RG, r = threadIdx.x % RG;
