@@ -147,8 +147,10 @@ CHARSIU_GPU_API int charsiu_gpu_matvec_batch_dev(struct charsiu_gpu *g, int id, 
 				 void *stream);
 /* The batched twin of charsiu_gpu_matvec_group (include/charsiu_llm.h:194-196
  * for one activation): m activations (q [m][K] int8, d [m][K/32] fp32) against
- * n <= 8 tensors of the same K, ys[i] = [m][rows of ids[i]]. q8_0 tensors share
- * one packing of the activations and one tensor-core launch. */
+ * n <= 8 tensors of the same K, ys[i] = [m][rows of ids[i]]. From 9
+ * activations, q8_0 tensors share one packing of the activations and one
+ * tensor-core launch; below, the tensors of each quant type share one CUDA-core
+ * launch a chunk of 8, 4 or 2 activations. */
 CHARSIU_GPU_API int charsiu_gpu_matvec_batch_group_dev(struct charsiu_gpu *g, const int *ids,
 						       unsigned n, unsigned m, const int8_t *q,
 						       const float *d, float *const *ys,
