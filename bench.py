@@ -312,8 +312,9 @@ def batched_steps(gg, dev, rank, world, dist, barrier, ms=(8, 32, 64), steps=50,
     out = {}
     for m in ms:
         chain = BatchChain(gg, m, dev, rank, world, dist)
-        ms_step, _ = time_chain(chain, steps, warmup, barrier, dist, world, dev, world == 1,
-                                False)
+        # one CUDA graph a step at every N (the all-gathers included: each
+        # rank captures the same collectives in the same order)
+        ms_step, _ = time_chain(chain, steps, warmup, barrier, dist, world, dev, True, False)
         chain.close()
         out[f"m{m}"] = {"value": round(m * 1000.0 / ms_step, 1), "unit": UNIT,
                         "ms_per_step": round(ms_step, 5)}
