@@ -320,22 +320,25 @@ struct layer {
 	int id[P_N];
 };
 
-/* where the token's time goes: the stages of src/llama.c:695-705 */
+/* where a token's time goes, one clock a step of the forward pass (the
+ * same split as the reference's CHARSIU_STAGES, src/llama.c:695-705) */
 enum {
-	ST_EMBD, ST_NORM1, ST_QKV, ST_ROPE, ST_ATTN, ST_WO, ST_RES1,
-	ST_NORM2, ST_GATEUP, ST_SILU, ST_DOWN, ST_RES2, ST_NORMF, ST_HEAD,
-	ST_N
+	T_EMBED, T_ATTN_NORM, T_QKV, T_ROTARY, T_HEADS, T_OUT_PROJ, T_ADD_ATTN,
+	T_FFN_NORM, T_GATE_UP, T_SWIGLU, T_DOWN, T_ADD_FFN, T_OUT_NORM, T_VOCAB,
+	T_COUNT
 };
 
-static const char *stage_name[ST_N] = {
-	"token embedding", "attn rmsnorm", "q k v", "rope + kv copy",
-	"attention", "o proj", "residual", "ffn rmsnorm", "gate + up",
-	"silu * up", "down", "residual", "final rmsnorm", "output head",
+static const char *stage_name[T_COUNT] = {
+	[T_EMBED] = "embed", [T_ATTN_NORM] = "norm/attn", [T_QKV] = "qkv",
+	[T_ROTARY] = "rotary+cache", [T_HEADS] = "attn heads", [T_OUT_PROJ] = "out proj",
+	[T_ADD_ATTN] = "add/attn", [T_FFN_NORM] = "norm/ffn", [T_GATE_UP] = "gate|up",
+	[T_SWIGLU] = "swiglu", [T_DOWN] = "down", [T_ADD_FFN] = "add/ffn",
+	[T_OUT_NORM] = "norm/out", [T_VOCAB] = "vocab head",
 };
 
 struct charsiu_gpu_llama {
 	struct gfile g;
-	double stage_ms[ST_N];
+	double stage_ms[T_COUNT];
 	unsigned stage_tok;
 	struct charsiu_gpu *dev;
 	uint32_t n_embd, n_layer, n_head, n_head_kv, n_ff, n_vocab, hd;
@@ -764,11 +767,11 @@ API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m)
 	if (getenv("CHARSIU_STAGES") && m->stage_tok) {
 		double tot = 0;
 
-		for (int i = 0; i < ST_N; i++)
+		for (int i = 0; i < T_COUNT; i++)
 			tot += m->stage_ms[i];
 		fprintf(stderr, "charsiu stages: %u tokens, %.3f ms a token\n", m->stage_tok,
 			tot / m->stage_tok);
-		for (int i = 0; i < ST_N; i++)
+		for (int i = 0; i < T_COUNT; i++)
 			fprintf(stderr, "  %-16s %8.3f ms a token   %5.1f%%\n", stage_name[i],
 				m->stage_ms[i] / m->stage_tok, 100.0 * m->stage_ms[i] / tot);
 	}
@@ -1042,7 +1045,7 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 	if (row_f32(m->tok, (uint64_t)token, m->x))
 		return NULL;
 	rope_angles(m->rope_cs, hd, pos, m->base);
-	STAGE(ST_EMBD);
+	STAGE(T_EMBED);
 
 	for (uint32_t l = 0; l < m->n_layer; l++) {
 		const struct layer *L = &m->L[l];
@@ -1050,7 +1053,7 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 		float *vc = m->vcache + ((size_t)l * m->n_ctx + pos) * kvdim;
 
 		rmsnorm(m->xb, m->x, L->attn_norm, m->n_embd, m->eps);
-		STAGE(ST_NORM1);
+		STAGE(T_ATTN_NORM);
 		{
 			int ids[3] = { L->id[P_Q], L->id[P_K], L->id[P_V] };
 			float *ys[3] = { m->q, m->k, m->v };
@@ -1058,19 +1061,19 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 			if (project(m, m->xb, m->n_embd, ids, ys, 3))
 				return NULL;
 		}
-		STAGE(ST_QKV);
+		STAGE(T_QKV);
 		rope(m->q, m->n_head, hd, m->rope_cs);
 		rope(m->k, m->n_head_kv, hd, m->rope_cs);
 		memcpy(kc, m->k, kvdim * sizeof(float));
 		memcpy(vc, m->v, kvdim * sizeof(float));
-		STAGE(ST_ROPE);
+		STAGE(T_ROTARY);
 
 		{
 			struct attn_job job = { m, l, pos, scale };
 
 			pool_run(m->pool, attn_head, &job, (int)m->n_head);
 		}
-		STAGE(ST_ATTN);
+		STAGE(T_HEADS);
 		{
 			int id = L->id[P_O];
 			float *ys[1] = { m->xb2 };
@@ -1078,13 +1081,13 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 			if (project(m, m->xb, m->n_embd, &id, ys, 1))
 				return NULL;
 		}
-		STAGE(ST_WO);
+		STAGE(T_OUT_PROJ);
 		for (uint32_t i = 0; i < m->n_embd; i++)
 			m->x[i] += m->xb2[i];
-		STAGE(ST_RES1);
+		STAGE(T_ADD_ATTN);
 
 		rmsnorm(m->xb, m->x, L->ffn_norm, m->n_embd, m->eps);
-		STAGE(ST_NORM2);
+		STAGE(T_FFN_NORM);
 		{
 			int ids[2] = { L->id[P_GATE], L->id[P_UP] };
 			float *ys[2] = { m->hb, m->hb2 };
@@ -1092,9 +1095,9 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 			if (project(m, m->xb, m->n_embd, ids, ys, 2))
 				return NULL;
 		}
-		STAGE(ST_GATEUP);
+		STAGE(T_GATE_UP);
 		pool_run(m->pool, silu_chunk, m, (int)((m->n_ff + SILU_CHUNK - 1) / SILU_CHUNK));
-		STAGE(ST_SILU);
+		STAGE(T_SWIGLU);
 		{
 			int id = L->id[P_DOWN];
 			float *ys[1] = { m->xb2 };
@@ -1102,20 +1105,20 @@ API const float *charsiu_gpu_llama_forward(struct charsiu_gpu_llama *m, int32_t 
 			if (project(m, m->hb, m->n_ff, &id, ys, 1))
 				return NULL;
 		}
-		STAGE(ST_DOWN);
+		STAGE(T_DOWN);
 		for (uint32_t i = 0; i < m->n_embd; i++)
 			m->x[i] += m->xb2[i];
-		STAGE(ST_RES2);
+		STAGE(T_ADD_FFN);
 	}
 	rmsnorm(m->xb, m->x, m->out_norm, m->n_embd, m->eps);
-	STAGE(ST_NORMF);
+	STAGE(T_OUT_NORM);
 	{
 		float *ys[1] = { m->logits };
 
 		if (project(m, m->xb, m->n_embd, &m->out_id, ys, 1))
 			return NULL;
 	}
-	STAGE(ST_HEAD);
+	STAGE(T_VOCAB);
 #undef STAGE
 	m->stage_tok++;
 	return m->logits;
@@ -1127,18 +1130,18 @@ API int charsiu_gpu_llama_stages(struct charsiu_gpu_llama *m, double *ms_per_tok
 {
 	if (!m)
 		return -1;
-	for (int i = 0; i < n && i < ST_N; i++)
+	for (int i = 0; i < n && i < T_COUNT; i++)
 		ms_per_token[i] = m->stage_tok ? m->stage_ms[i] / m->stage_tok : 0.0;
 	if (reset) {
 		memset(m->stage_ms, 0, sizeof(m->stage_ms));
 		m->stage_tok = 0;
 	}
-	return ST_N;
+	return T_COUNT;
 }
 
 API const char *charsiu_gpu_llama_stage_name(int i)
 {
-	return i >= 0 && i < ST_N ? stage_name[i] : "";
+	return i >= 0 && i < T_COUNT ? stage_name[i] : "";
 }
 
 API int32_t charsiu_gpu_llama_argmax(const float *logits, uint32_t n)

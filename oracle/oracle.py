@@ -1,9 +1,13 @@
 """ctypes access to the checkers. TEST INFRASTRUCTURE ONLY.
 
-Two libraries, both built by oracle/Makefile:
+Libraries built by oracle/Makefile:
   liboracle.so            the restatement in charsiu_oracle.c (always built);
   _ref/libcharsiu_ref.so  the reference compiled from its own sources plus
-                          ref_shim.c (built only where the reference tree is).
+                          ref_shim.c (built only where the reference tree is);
+  _ref/libcharsiu_ref_gpu.so, _ref/libcharsiu_ref_npu.so  the reference's
+                          decode loop linked to the GPU layer, routed and
+                          unchanged (ref_routed): the drop-in's proof, run by
+                          the GPU tests.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline and
 reference legs use this module, and only as the checker or the baseline.
@@ -19,6 +23,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libcharsiu_ref.so")
+# the reference's decode loop linked to the GPU layer: with the routing edit
+# applied (CHARSIU_GPU=1), and unchanged without its NPU device file
+REF_GPU_LIB = os.path.join(HERE, "_ref", "libcharsiu_ref_gpu.so")
+REF_NPU_LIB = os.path.join(HERE, "_ref", "libcharsiu_ref_npu.so")
 
 _i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
@@ -102,6 +110,39 @@ def ref():
         R.ref_npu_matvec.argtypes = [_i8p, _f32p, C.c_uint64, C.c_uint64, _i8p, C.c_float, _f32p]
         _ref = R
     return _ref
+
+
+def _greedy_argtypes(R):
+    R.ref_greedy.argtypes = [C.c_char_p, _i32p, C.c_int, C.c_int, C.c_int, _i32p,
+                             C.POINTER(C.c_double), C.POINTER(C.c_double), C.c_void_p]
+    R.ref_greedy.restype = C.c_int
+
+
+_routed = {}
+
+
+def ref_routed(kind: str):
+    """The reference's decode loop linked to the GPU layer: kind "gpu" (the
+    routing edit, plus the struct-form calls of ref_gpu_calls.c) or "npu"
+    (unchanged, its charsiu_npu_* calls resolved by the GPU layer). Each reads
+    its switches (CHARSIU_GPU, CHARSIU_NPU, CHARSIU_NPU_QUANT) from the
+    environment, some once a process: load it in a process started with them."""
+    if kind not in _routed:
+        path = {"gpu": REF_GPU_LIB, "npu": REF_NPU_LIB}[kind]
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        R = C.CDLL(path)
+        _greedy_argtypes(R)
+        if kind == "gpu":
+            R.refgpu_matvec.argtypes = [C.c_uint32, C.c_void_p, C.c_uint, C.c_uint64,
+                                        C.c_uint64, _f32p, _f32p, C.c_int]
+            R.refgpu_matvec.restype = C.c_int
+            R.refgpu_matmul_i8.argtypes = [C.c_uint, C.c_uint, C.c_uint, _u8p, _u8p, _i32p,
+                                           C.c_float, C.c_float, C.c_float, C.c_int, C.c_int,
+                                           C.c_int, _i8p]
+            R.refgpu_matmul_i8.restype = C.c_int
+        _routed[kind] = R
+    return _routed[kind]
 
 
 def _ptr(a: np.ndarray) -> int:
@@ -284,8 +325,9 @@ def ref_matvec(qtype: int, blocks: np.ndarray, k: int, n: int, x: np.ndarray):
 
 
 def ref_greedy(path: str, prompt, n_gen: int, n_ctx: int = 0, threads: int | None = None,
-               want_logits: int = 0):
-    """Greedy decode by the reference's own llama_forward.
+               want_logits: int = 0, build: str = ""):
+    """Greedy decode by the reference's own llama_forward (build "" the
+    reference itself; "gpu" or "npu" the builds of ref_routed).
 
     Returns (tokens, prompt_ms, gen_ms[, logits after the prompt]). The
     reference's pool reads CHARSIU_THREADS once per process."""
@@ -295,8 +337,9 @@ def ref_greedy(path: str, prompt, n_gen: int, n_ctx: int = 0, threads: int | Non
     p = np.ascontiguousarray(prompt, dtype=np.int32)
     pm, gm = C.c_double(), C.c_double()
     lg = np.zeros(want_logits, dtype=np.float32) if want_logits else None
-    n = ref().ref_greedy(path.encode(), p, p.size, n_gen, n_ctx, out, C.byref(pm), C.byref(gm),
-                         _ptr(lg) if lg is not None else None)
+    R = ref_routed(build) if build else ref()
+    n = R.ref_greedy(path.encode(), p, p.size, n_gen, n_ctx, out, C.byref(pm), C.byref(gm),
+                     _ptr(lg) if lg is not None else None)
     if n < 0:
         raise RuntimeError(f"reference could not load {path}")
     res = (out[:n], pm.value, gm.value)

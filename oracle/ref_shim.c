@@ -23,6 +23,9 @@
 #include "charsiu.h"
 #include "charsiu_llm.h"
 
+/* (REF_SHIM_NO_TOOL: the decode-only builds, whose libraries carry no NPU job
+ * code for the tool to call) */
+#ifndef REF_SHIM_NO_TOOL
 #define main charsiu_matmul_tool_main
 #include "charsiu_matmul.c"
 #undef main
@@ -55,6 +58,7 @@ int ref_matmul_i8(unsigned m, unsigned k, unsigned n, const uint8_t *a,
 	job.output_zero_point = out_zp;
 	return cpu_reference(&job, a, w, bias, out);
 }
+#endif /* REF_SHIM_NO_TOOL */
 
 size_t ref_sizeof_act(void)
 {

@@ -11,7 +11,10 @@ from charsiu_b200 import lib as L
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 INCLUDE = os.path.join(ROOT, "include")
-REF_INCLUDE = "/root/reference/include"
+# the reference's source tree: REF in the environment, else `reference` beside
+# this repository (as oracle/Makefile takes it)
+REF_INCLUDE = os.path.join(os.environ.get("REF", os.path.join(os.path.dirname(ROOT), "reference")),
+                           "include")
 
 
 def declared():
