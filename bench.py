@@ -1,38 +1,41 @@
 #!/usr/bin/env python
 """Benchmark: Llama-3.2-1B-shaped q8_0 decode, tokens per second.
 
-A step is one decode token's pass through the hot path: the 112 projections
-and the 128256-wide tied output head, issued as the decode loop issues them
-(q/k/v as one group launch, o, gate/up as one group launch, down, per layer;
-then the head): 65 launches of the block-quant matvec, 1.31 GB of q8_0
-weights. Synthetic seeded weights with the workload's distributions (no real
-checkpoint exists on these machines), random activations quantised on the
-device.
+A step is one greedy decode token: charsiu's whole llama_forward (the
+embedding row, 16 layers of rmsnorm, the q/k/v, o, gate/up and down
+projections, RoPE, the KV cache, attention, SiLU, the residuals; the final
+norm, the 128256-wide tied head and the argmax) on the device. Synthetic
+seeded weights with the workload's distributions (no real checkpoint exists on
+these machines); the 6 seeded prompt ids of the workload, then greedy tokens
+at positions 6..29, checked against the reference's.
 
-  value   tokens/s of that chain with weights and activations resident in
-          HBM, replayed as one CUDA graph per token, timed with CUDA events.
-          1.31 GB a token is far larger than the 126 MB L2, so every token
-          streams its weights from HBM.
-  e2e     tokens/s of the workload's greedy decode (6 prompt ids, 24 tokens)
-          through the public C ABI (charsiu_gpu_llama_greedy) with the whole
-          step on the device (charsiu_gpu_llama_set_resident): each token's
-          id and position copied in from pinned host memory and its argmax
-          copied back inside the timed region, one CUDA graph a token, logits
-          the reference's bit for bit. e2e.host_routed is the drop-in form:
-          charsiu's CPU rmsnorm/rope/attention/SwiGLU on the host and every
-          projection a host-buffer call (charsiu_gpu_llama_forward).
-  roofline the matvec kernel's algorithmic bytes per launch over its average
-          launch time in the timed region, against the measured HBM copy peak.
+  value    tokens/s with the inputs resident in HBM: the greedy steps queued
+           back to back with each step's argmax fed to the next on the device
+           (charsiu_gpu_decoder_generate), one CUDA graph a step, CUDA events
+           around the steps. 1.31 GB of weights a token, far above the 126 MB
+           L2, so every token streams its weights from HBM.
+  e2e      the same decode through the public C ABI with the host in the loop
+           (charsiu_gpu_llama_greedy with the step on the device): each token's
+           id and position copied in from pinned host memory and its argmax
+           copied back every step. e2e.host_routed is the drop-in form:
+           charsiu's CPU rmsnorm/rope/attention/SwiGLU on the host and every
+           projection a host-buffer call (charsiu_gpu_llama_forward).
+  roofline the block-quant matvec's algorithmic bytes per launch over its
+           average launch time, from the token's 65 matvec launches timed
+           alone (hot_path), against the measured HBM copy peak.
+  configs  the standalone matvec workloads (q8_0 2048x8192, q4_0 8192x2048)
+           and the int8 matmul shapes, each beside the reference's CPU code.
   cpu_baseline charsiu's own CPU decode (the reference compiled from its
-          sources, oracle/_ref) on this box's host cores.
+           sources, oracle/_ref) on this box's host cores.
 
 At N GPUs every GPU decodes its own stream with the whole model (no
-collective, weak scaling); the column_split key times one stream with every
-tensor split over the N GPUs (NCCL all-gathers, and the fused matvec +
-all-gather over NVLink).
+collective, weak scaling); `sharded` times the column splits the workload
+names -- the 128256-wide head and a token's 65 launches split over the N GPUs
+(NCCL all-gathers, and the fused matvec + all-gather over NVLink), and the
+batched step at M = 8, 32, 64 -- each checked bit for bit against one GPU.
 
-  python bench.py --resident    the e2e leg alone
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+  python bench.py --resident | --matvec Q:K:N[:M] | --batch M | --int8 M:K:N | --npu K:N
 """
 from __future__ import annotations
 
@@ -149,12 +152,13 @@ class TokenChain:
     NVLink and the next launch waits on the arrivals
     (charsiu_gpu_matvec_gather_dev)."""
 
-    def __init__(self, gg, dev, rank=0, world=1, dist=None, fused=False):
+    def __init__(self, gg, dev, rank=0, world=1, dist=None, fused=False, groups=None):
         import torch
         from charsiu_b200.lib import Layer
 
         self.torch, self.dev, self.world, self.dist = torch, dev, world, dist
-        self.groups = launch_groups(SHAPE)
+        self.gg, self.rank = gg, rank
+        self.groups = groups or launch_groups(SHAPE)
         names = [nm for g, _ in self.groups for nm in g]
         self.layer = Layer(max_k=max(SHAPE.n_embd, SHAPE.n_ff), max_n=SHAPE.n_vocab,
                            max_tensors=len(names) + 1, device=dev.index, rank=rank, world=world)
@@ -209,6 +213,28 @@ class TokenChain:
             self.gsum = [sum((gg.tensors[nm].n + 7) // 8 for nm in g) for g, _ in self.groups]
             dist.barrier()
 
+    def outputs(self):
+        """Every tensor's whole output (N floats) as this rank holds it after a
+        token: the slabs reassembled (NCCL), or the full buffer the peers
+        stored into (fused)."""
+        out = []
+        for j, (g, _) in enumerate(self.groups):
+            ns = [self.gg.tensors[nm].n for nm in g]
+            if self.fused:
+                for i, n in enumerate(ns):
+                    y = np.zeros(n, np.float32)
+                    self.layer.read_device(self.mine[j][i], y)
+                    out.append(y)
+                continue
+            buf = (self.full[j] if self.world > 1 else self.bufs[j][0]).cpu().numpy()
+            slabs = [shard.slab_rows(n, self.world) for n in ns]
+            pieces = buf.reshape(self.world, sum(slabs))
+            off = 0
+            for n, sl in zip(ns, slabs):
+                out.append(shard.assemble(pieces[:, off:off + sl], n, self.world))
+                off += sl
+        return out
+
     def token(self, stream):
         if self.fused:
             L, last = self.layer, len(self.groups) - 1
@@ -261,6 +287,7 @@ class BatchChain:
         from charsiu_b200.lib import Layer
 
         self.torch, self.dist, self.m = torch, dist, m
+        self.gg, self.world = gg, world
         self.groups = launch_groups(SHAPE)
         names = [nm for g, _ in self.groups for nm in g]
         self.layer = Layer(max_k=max(SHAPE.n_embd, SHAPE.n_ff), max_n=SHAPE.n_vocab,
@@ -292,6 +319,25 @@ class BatchChain:
                              if world > 1 else None)
         self.weight_bytes = sum(gg.tensors[nm].nbytes for nm in names)
 
+    def outputs(self):
+        """Every tensor's [M][N] outputs as this rank holds them after a step
+        (the gathered slabs reassembled when world > 1)."""
+        m, out = self.m, []
+        for (g, _), (buf, _), full in zip(self.groups, self.bufs, self.full):
+            ns = [self.gg.tensors[nm].n for nm in g]
+            w = self.world
+            data = (full if w > 1 else buf).cpu().numpy().reshape(w, -1)
+            off = 0
+            for n in ns:
+                size = m * shard.slab_rows(n, w)
+                y = np.empty((m, n), np.float32)
+                for r in range(w):
+                    row0, rows = shard.shard_rows(n, r, w)
+                    y[:, row0:row0 + rows] = data[r, off:off + m * rows].reshape(m, rows)
+                out.append(y)
+                off += size
+        return out
+
     def token(self, stream):
         for (g, k), (buf, ptrs), full in zip(self.groups, self.bufs, self.full):
             q, d = self.acts[k]
@@ -305,25 +351,84 @@ class BatchChain:
         self.layer.close()
 
 
+def same_bits(a, b) -> bool:
+    return all(x.shape == y.shape and np.array_equal(x.view(np.uint32), y.view(np.uint32))
+               for x, y in zip(a, b)) and len(a) == len(b)
+
+
+def all_ranks(flag: bool, world, dist, dev) -> bool:
+    """flag on every rank (MIN over ranks)."""
+    if world == 1:
+        return bool(flag)
+    import torch
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
 def batched_steps(gg, dev, rank, world, dist, barrier, ms=(8, 32, 64), steps=50, warmup=3):
-    """tok/s of one batched decode step at each M (config: every tensor split
-    over the world's GPUs when world > 1): M sequences a step, the max over
-    ranks of the step time."""
+    """tok/s of one batched decode step at each M (M sequences a step, the
+    max over ranks of the step time). world > 1: every tensor column-split
+    over the world's GPUs and each group's slabs NCCL-all-gathered; the same
+    step is timed on one GPU (this rank's, the whole model) and every rank
+    checks that its gathered outputs are the one-GPU outputs bit for bit."""
     out = {}
     for m in ms:
-        chain = BatchChain(gg, m, dev, rank, world, dist)
-        # one CUDA graph a step at every N (the all-gathers included: each
-        # rank captures the same collectives in the same order)
-        ms_step, _ = time_chain(chain, steps, warmup, barrier, dist, world, dev, True, False)
-        chain.close()
-        out[f"m{m}"] = {"value": round(m * 1000.0 / ms_step, 1), "unit": UNIT,
-                        "ms_per_step": round(ms_step, 5)}
+        single = BatchChain(gg, m, dev)
+        ms_single, _ = time_chain(single, steps, warmup, barrier, dist, world, dev, True, False)
+        want = single.outputs() if world > 1 else None
+        single.close()
+        row = {"value": round(m * 1000.0 / ms_single, 1), "unit": UNIT,
+               "ms_per_step": round(ms_single, 5)}
+        if world > 1:
+            chain = BatchChain(gg, m, dev, rank, world, dist)
+            # one CUDA graph a step, the all-gathers included (each rank
+            # captures the same collectives in the same order)
+            ms_step, _ = time_chain(chain, steps, warmup, barrier, dist, world, dev, True, False)
+            ok = all_ranks(same_bits(chain.outputs(), want), world, dist, dev)
+            chain.close()
+            row = {"value": round(m * 1000.0 / ms_step, 1), "unit": UNIT,
+                   "ms_per_step": round(ms_step, 5), "split_matches_single": ok,
+                   "single_gpu": row}
+        out[f"m{m}"] = row
     out["workload"] = ("one decode step of M sequences: the 112 projections and the head as "
                        "grouped batched matvecs (tcgen05 kind::i8 from M = 9, the CUDA cores "
-                       "below)" +
-                       (f", every tensor column-split over {world} GPUs and each group's "
-                        "slabs NCCL-all-gathered" if world > 1 else ""))
+                       f"below), {steps} steps as CUDA graph replays" +
+                       (f"; value: every tensor column-split over {world} GPUs and each "
+                        "group's slabs NCCL-all-gathered, checked bit for bit against the "
+                        "one-GPU step (single_gpu)" if world > 1 else ""))
     return out
+
+
+def head_split(gg, dev, rank, world, dist, barrier, steps=400):
+    """The 2048 -> 128256 q8_0 output head alone, column-split over the world's
+    GPUs: one GPU with the whole head (each rank's own), the split with an
+    NCCL all-gather, and the split whose kernel stores every row into every
+    rank's output over NVLink (qmv1_gather_kernel). `steps` heads back to back
+    as one CUDA graph, each waiting for the previous one's gather; us a head,
+    max over ranks; every rank's gathered head checked bit for bit against its
+    one-GPU head."""
+    groups = [(["token_embd.weight"], SHAPE.n_embd)]
+    single = TokenChain(gg, dev, groups=groups)
+    ms1, _ = time_chain(single, steps, 5, barrier, dist, world, dev, True, False)
+    want = single.outputs()
+    single.close()
+    hbytes = gg.tensors["token_embd.weight"].nbytes
+    peak, _ = peaks()
+    res = {"single_gpu_us": round(ms1 * 1e3, 3),
+           "single_gpu_frac": round(hbytes / (ms1 * 1e-3) / 1e9 / peak, 4)}
+    for key, fused in (("nccl", False), ("fused", True)):
+        ch = TokenChain(gg, dev, rank, world, dist, fused=fused, groups=groups)
+        msn, _ = time_chain(ch, steps, 5, barrier, dist, world, dev, True, False)
+        ok = all_ranks(same_bits(ch.outputs(), want), world, dist, dev)
+        ch.close()
+        res[key] = {"us": round(msn * 1e3, 3), "speedup_vs_single": round(ms1 / msn, 3),
+                    "split_matches_single": ok}
+    res["workload"] = (f"2048 -> 128256 q8_0 head ({hbytes / 1e6:.0f} MB), rows split in 8-row "
+                       f"groups over {world} GPUs, {steps} heads a CUDA graph, each after the "
+                       "last one's gather; nccl: matvec + all_gather_into_tensor; fused: one "
+                       "kernel, peer stores + arrival counters over NVLink")
+    return res
 
 
 def time_chain(chain, steps, warmup, barrier, dist, world, dev, graph_ok, sample_clocks):
@@ -366,6 +471,60 @@ def time_chain(chain, steps, warmup, barrier, dist, world, dev, graph_ok, sample
     return ms / steps, clk
 
 
+def run_decode(path, args, world, dist, dev, sample_clocks):
+    """The workload's greedy decode with the whole forward on the device and
+    the inputs resident in HBM: the 6 prompt ids through the device step
+    (untimed), then greedy steps queued back to back with no host round trip
+    between them (charsiu_gpu_decoder_generate: each step's argmax is the next
+    step's token on the device), timed with CUDA events on the decoder's
+    stream. Exactly `args.steps` steps are timed, in runs of at most the
+    workload's 24 (positions 6..29), each run from the prompt again. Every
+    run's tokens are checked against the reference's. At N GPUs every rank
+    decodes its own stream: (ms a token max over ranks, match, clocks,
+    kernels a step)."""
+    import torch
+    from charsiu_b200.lib import Llama
+
+    n_gen = SPEC["n_gen"]
+    prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
+    with open(os.path.join(ROOT, "tests", "golden", "golden_decode.json")) as f:
+        gold = json.load(f)["llama1b_q8"]["tokens"]
+    barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
+    barrier()
+    with Llama(path, n_ctx=len(prompt) + n_gen + 1, device=dev.index, resident=True) as m:
+        def run(n):
+            lp = None
+            for i, t in enumerate(prompt):
+                lp = m.forward(int(t), i)
+            first = int(np.argmax(lp))
+            toks, ms = m.generate_dev(first, len(prompt), n)
+            return [first] + toks.tolist(), ms
+
+        for _ in range(max(2, min(args.warmup, 4))):      # builds and captures the step graphs
+            run(n_gen)
+        torch.cuda.synchronize(dev)
+        barrier()
+        clocks = Clocks(dev.index) if sample_clocks else None
+        left, total_ms, match = args.steps, 0.0, True
+        while left > 0:
+            n = min(left, n_gen)
+            toks, ms = run(n)
+            total_ms += ms
+            left -= n
+            k = min(len(toks), len(gold))
+            match = match and toks[:k] == gold[:k]
+        torch.cuda.synchronize(dev)
+        barrier()
+        clk = clocks.stop() if clocks else None
+        launches = m.step_launches
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    match = all_ranks(match, world, dist, dev)
+    return total_ms / args.steps, match, clk, launches
+
+
 def run_ours(args, rank, world, dist):
     import torch
     from charsiu_b200.lib import lib
@@ -376,84 +535,115 @@ def run_ours(args, rank, world, dist):
     path = model_path(rank, barrier)
     gg = G.GGUFFile(path)
 
-    # every GPU decodes its own stream with the whole model: no collective
+    # the headline: greedy decode, whole forward on the device, inputs resident
+    ms_per_token, match, clk, step_kernels = run_decode(path, args, world, dist, dev, rank == 0)
+    value = world * 1000.0 / ms_per_token
+
+    # the hot path alone: the 65 matvec launches of a token, for the roofline
     chain = TokenChain(gg, dev)
-    ms_per_step, clk = time_chain(chain, args.steps, args.warmup, barrier, dist, world, dev,
-                                  True, rank == 0)
+    hot_steps = max(args.steps, 200)
+    ms_chain, _ = time_chain(chain, hot_steps, args.warmup, barrier, dist, world, dev, True,
+                             False)
     per_token_launches = len(chain.groups)
     tok_bytes = chain.bytes_per_token
     chain.close()
-    value = world * 1000.0 / ms_per_step
     peak, peak_kind = peaks()
-    achieved = tok_bytes / (ms_per_step * 1e-3) / 1e9
+    achieved = tok_bytes / (ms_chain * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
+                "traffic_source": "ncu DRAM bytes per launch of the same chain, "
+                                  "profiles/qmv_decode_llama1b.md",
                 "kernel": "cgpu::qmv1_kernel (M=1 block-quant matvec)", "peak_kind": peak_kind,
                 "bytes_per_launch": round(tok_bytes / per_token_launches),
-                "avg_launch_us": round(ms_per_step * 1e3 / per_token_launches, 3),
-                "per_gpu": True}
+                "avg_launch_us": round(ms_chain * 1e3 / per_token_launches, 3),
+                "per_gpu": True,
+                "timed": f"the token's 65 matvec launches, {hot_steps} tokens as CUDA graph "
+                         "replays, CUDA events on the launching stream"}
+    hot_path = {"value": round(world * 1000.0 / ms_chain, 2), "unit": UNIT,
+                "ms_per_token": round(ms_chain, 5), "gbs": round(achieved, 1),
+                "workload": "the hot path of one token alone: 112 projections + the 128256 "
+                            "head in 65 matvec launches, fixed activations, 1.31 GB of "
+                            "weights a token, no norms/attention between them"}
 
-    split = None
+    sharded = None
     if world > 1:
-        # the north star's sharded form: ONE stream, every tensor column-split
+        sharded = {"head": head_split(gg, dev, rank, world, dist, barrier)}
+        # one decode stream's hot path, every tensor column-split
         cs = TokenChain(gg, dev, rank, world, dist)
         ms_split, _ = time_chain(cs, max(1, min(args.steps, 200)), 3, barrier, dist, world, dev,
-                                 False, False)
+                                 True, False)
         cs.close()
-        split = {"value": round(1000.0 / ms_split, 2), "unit": UNIT,
-                 "ms_per_step": round(ms_split, 5),
-                 "workload": f"one decode stream, every tensor column-split over {world} GPUs, "
-                             "one NCCL all-gather per launch group (65 a token)"}
+        sharded["token_chain_nccl"] = {
+            "value": round(1000.0 / ms_split, 2), "unit": UNIT, "ms_per_step": round(ms_split, 5),
+            "workload": f"one stream's 65 launches, every tensor column-split over {world} "
+                        "GPUs, one NCCL all-gather per launch group, a CUDA graph a token"}
         fused = {"workload": "the same split, each launch storing its rows into every "
                              "rank's outputs over NVLink and waiting on arrival counters "
-                             "(matvec and all-gather in one kernel), as a CUDA graph a token"}
+                             "(matvec and all-gather in one kernel), a CUDA graph a token; "
+                             "every output checked against the one-GPU chain"}
         try:
+            single = TokenChain(gg, dev)
+            time_chain(single, 3, 1, barrier, dist, world, dev, False, False)
+            want = single.outputs()
+            single.close()
             fz = TokenChain(gg, dev, rank, world, dist, fused=True)
             ms_fused, _ = time_chain(fz, max(1, min(args.steps, 500)), 5, barrier, dist, world,
                                      dev, True, False)
+            ok = all_ranks(same_bits(fz.outputs(), want), world, dist, dev)
             fz.close()
             fused.update(value=round(1000.0 / ms_fused, 2), unit=UNIT,
-                         ms_per_step=round(ms_fused, 5))
+                         ms_per_step=round(ms_fused, 5), split_matches_single=ok)
         except (RuntimeError, AssertionError) as e:   # reported, not fatal to the headline
             fused["error"] = str(e)[:200]
-        split["fused"] = fused
+        sharded["token_chain_fused"] = fused
 
     batched = batched_steps(gg, dev, rank, world, dist, barrier)
 
     e2e = run_e2e_resident(path, args, world, dist, dev)
     e2e["host_routed"] = run_e2e(path, args, lib, world, dist, dev)
     npu_format = None
+    configs = None
     if world == 1:
         # charsiu's NPU number format (CHARSIU_NPU_QUANT): its matvec at the
         # gate/up shape, and the workload's decode with every projection on it
         us, algo, copies, _ = npu_matvec_case(2048, 8192, 200, 10)
-        peak, _ = peaks()
         gbs = algo / (us * 1e-6) / 1e9
         npu_format = {"matvec_k2048_n8192": {"value": round(gbs, 1), "unit": "GB/s",
                                              "frac": round(gbs / peak, 4),
                                              "us_per_launch": round(us, 3)},
                       "decode_e2e": npu_decode_e2e(path, args.steps),
                       "decode_e2e_resident": npu_decode_e2e(path, args.steps, resident=True)}
+        configs = matvec_configs()
+        configs["int8"] = int8_configs()
 
     out = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_token, 5),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
            "data": "synthetic (seeded random-init Llama-3.2-1B-shaped q8_0 GGUF; no checkpoint)",
-           "config": {"workload": "Llama-3.2-1B q8_0 greedy decode, hot path per token: 112 "
-                                  "projections + 128256 tied head in 65 matvec launches",
+           "config": {"workload": "Llama-3.2-1B q8_0 greedy decode (6 seeded prompt ids, then "
+                                  "greedy steps at positions 6..29): the whole llama_forward "
+                                  "on the device, 112 projections + 128256 tied head + norms, "
+                                  "RoPE, attention, SiLU, argmax, one CUDA graph a token, "
+                                  "the argmax fed to the next step on the device",
                       "model": "Llama-3.2-1B architecture (16x2048, ffn 8192, 32/8 heads, "
                                "vocab 128256)",
                       "weights_bytes_per_token": tok_bytes, "global_batch": world, "seq_len": 1,
                       "parallelism": f"data-parallel x{world}: one decode stream a GPU, "
-                                     "no collective" if world > 1 else "single GPU",
-                      "l2": "inputs larger than L2 (1.31 GB of weights per step vs 126 MB)"},
-           "roofline": roofline, "e2e": e2e, "gpu_launches": per_token_launches * args.steps,
-           "clocks": clk}
-    if split:
-        out["column_split"] = split
+                                     "no collective (the column splits are under `sharded`)"
+                                     if world > 1 else "single GPU",
+                      "l2": "inputs larger than L2 (1.31 GB of weights per step vs 126 MB)",
+                      "timed": "CUDA events on the decoder's stream around each run of "
+                               "device steps (the prompt outside), summed; max over ranks"},
+           "tokens_match_reference": match,
+           "roofline": roofline, "hot_path": hot_path, "e2e": e2e,
+           "gpu_launches": step_kernels * args.steps, "clocks": clk}
+    if sharded:
+        out["sharded"] = sharded
     if npu_format:
         out["npu_format"] = npu_format
     out["batched"] = batched
+    if configs:
+        out["configs"] = configs
     if rank == 0 and world == 1:
         out["cpu_baseline"] = cpu_baseline(path)
     return out
@@ -598,25 +788,23 @@ def cpu_baseline(path):
 
 # ---- one matvec on its own -------------------------------------------------------
 
-def run_matvec_case(args):
-    """--matvec q8_0:2048:8192[:M]: one block-quant matvec shape (M = 1 unless
-    given; M > 1 is the batched matvec of M activations), enough copies of the
-    weights rotated that every launch streams from HBM (their total is at
-    least twice the 126 MB L2), launches replayed as a CUDA graph."""
+def matvec_case(qname: str, k: int, n: int, m: int, steps: int, warmup: int):
+    """One block-quant matvec shape (M = 1, or the batched matvec of M
+    activations), enough copies of the weights rotated that every launch
+    streams from HBM (their total at least twice the 126 MB L2), `steps`
+    launches replayed as one CUDA graph and timed with CUDA events on the
+    launching stream: (us a launch, algorithmic bytes, copies, clocks, weight
+    bytes)."""
     import torch
     from charsiu_b200.lib import Layer
 
-    parts = args.matvec.split(":")
-    qname, k, n = parts[:3]
-    k, n = int(k), int(n)
-    m = int(parts[3]) if len(parts) > 3 else 1
     qtype = {"q8_0": G.GGML_Q8_0, "q4_0": G.GGML_Q4_0, "q6_K": G.GGML_Q6_K}[qname]
     blk, _ = W.matvec_inputs(qtype, k, n, seed=1)
     wbytes = blk.nbytes
     copies = max(2, -(-2 * 126 * 2 ** 20 // wbytes))
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
-    with Layer(max_k=k, max_n=n, max_tensors=copies) as L:
+    with Layer(max_k=k, max_n=n, max_tensors=copies, device=dev.index) as L:
         ids = [L.add_blocks(qtype, k, n, blk, f"copy{i}") for i in range(copies)]
         x = torch.randn(m, k, generator=torch.Generator().manual_seed(7)).to(dev)
         q = torch.empty((m, k), dtype=torch.int8, device=dev)
@@ -634,16 +822,16 @@ def run_matvec_case(args):
                 rc = L.batch_dev(ids[i % copies], m, q.data_ptr(), d.data_ptr(), y.data_ptr(),
                                  stream.cuda_stream)
             assert rc == 0, L.error()
-        for i in range(args.warmup):
+        for i in range(warmup):
             launch(i)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            for i in range(args.steps):
+            for i in range(steps):
                 launch(i)
         graph.replay()
         torch.cuda.synchronize()
-        clocks = Clocks(0)
+        clocks = Clocks(dev.index)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             e0.record(stream)
@@ -651,9 +839,18 @@ def run_matvec_case(args):
             e1.record(stream)
         torch.cuda.synchronize()
         clk = clocks.stop()
-        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        us = e0.elapsed_time(e1) * 1e3 / steps
         del graph
     algo = wbytes + m * (k + 4 * (k // 32)) + 4 * m * n
+    return us, algo, copies, clk, wbytes
+
+
+def run_matvec_case(args):
+    """--matvec q8_0:2048:8192[:M]: one matvec shape (M = 1 unless given)."""
+    parts = args.matvec.split(":")
+    qname, k, n = parts[0], int(parts[1]), int(parts[2])
+    m = int(parts[3]) if len(parts) > 3 else 1
+    us, algo, copies, clk, wbytes = matvec_case(qname, k, n, m, args.steps, args.warmup)
     peak, peak_kind = peaks()
     gbs = algo / (us * 1e-6) / 1e9
     return {"metric": "quant matvec HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
@@ -667,6 +864,96 @@ def run_matvec_case(args):
                          "frac": round(gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
                          "bytes_per_launch": algo, "avg_launch_us": round(us, 3)},
             "gpu_launches": args.steps * (1 if m == 1 else 2), "clocks": clk}
+
+
+# the block-quant matvec workloads: (name, quant type, K, N)
+MATVEC_CONFIGS = [("matvec_q8_0_2048x8192", "q8_0", 2048, 8192),
+                  ("matvec_q4_0_8192x2048", "q4_0", 8192, 2048)]
+
+
+def matvec_configs(steps: int = 400):
+    """Each block-quant matvec workload on the GPU (M = 1, weights rotated past
+    L2), with the reference's charsiu_act_set + gguf_matvec on this box's
+    host beside it: one thread, and every core through the decode loop's
+    row-split pool (the reference compiled from its sources, oracle/_ref;
+    the restated oracle, one thread, if that build is absent)."""
+    from oracle import oracle as O
+    peak, peak_kind = peaks()
+    cores = os.cpu_count() or 1
+    out = {}
+    for name, qname, k, n in MATVEC_CONFIGS:
+        us, algo, copies, _, wbytes = matvec_case(qname, k, n, 1, steps, 10)
+        gbs = algo / (us * 1e-6) / 1e9
+        row = {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+               "peak_kind": peak_kind, "bytes": algo, "launches": steps,
+               "weight_copies": copies}
+        qtype = {"q8_0": G.GGML_Q8_0, "q4_0": G.GGML_Q4_0}[qname]
+        blk, x = W.matvec_inputs(qtype, k, n, seed=1)
+        if O.have_ref():
+            one = O.ref_matvec_ms(qtype, blk, k, n, x, threads=1, reps=20)
+            pool = O.ref_matvec_ms(qtype, blk, k, n, x, threads=cores, reps=50)
+            cpu = {"kind": "reference", "us_1_thread": round(one * 1e3, 1),
+                   "gbs_1_thread": round(algo / (one * 1e-3) / 1e9, 2),
+                   f"us_{cores}_threads": round(pool * 1e3, 1),
+                   f"gbs_{cores}_threads": round(algo / (pool * 1e-3) / 1e9, 2), "cores": cores,
+                   "sample": "charsiu_act_set + gguf_matvec over all rows (src/gguf.c:829-911, "
+                             "1149-1215), 20 calls on 1 thread, 50 through the row-split pool "
+                             "of src/llama.c:27-105"}
+            row["gpu_vs_cpu_pool"] = round(pool * 1e3 / us, 1)
+        else:
+            t0 = time.perf_counter()
+            for _ in range(5):
+                O.matvec(qtype, blk, k, n, *O.act_quantise(x))
+            one = (time.perf_counter() - t0) / 5 * 1e3
+            cpu = {"kind": "port", "us_1_thread": round(one * 1e3, 1), "cores": 1,
+                   "sample": "the restated oracle, 5 calls"}
+        row["cpu_baseline"] = cpu
+        out[name] = row
+    return out
+
+
+def int8_configs(steps: int = 200):
+    """The int8 matmul with the NPU output stage at each workload shape
+    through the public C ABI (charsiu_gpu_matmul_i8_flat, host buffers: the
+    copies inside), us a call on the host clock, byte-exact against the
+    reference's cpu_reference; beside it cpu_reference (tools/charsiu_matmul.c:
+    41-81) and cpu_us (tools/charsiu_bench.c:74-95) on one host core."""
+    from charsiu_b200.lib import Layer
+    from oracle import oracle as O
+    out = {}
+    for name, (m, k, n, seed) in W.I8_SHAPES.items():
+        a, w, bias = W.i8_inputs(m, k, n, seed)
+        sc = W.i8_scales(m, k, n, seed)
+        with Layer(max_k=max(k, 32), max_n=n, max_tensors=1,
+                   device=int(os.environ.get("LOCAL_RANK", 0))) as L:
+            got = L.matmul_i8(a, w, bias, *sc)
+            for _ in range(10):
+                L.matmul_i8(a, w, bias, *sc)
+            l0 = L.launches
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                L.matmul_i8(a, w, bias, *sc)
+            dt = (time.perf_counter() - t0) / steps
+            launches = (L.launches - l0) / steps
+        have = O.have_ref()
+        refmm = O.ref_matmul_i8 if have else O.matmul_i8
+        exact = bool(np.array_equal(got, refmm(a, w, bias, *sc)))
+        reps = max(3, min(2000, int(0.3 / max(1e-7, m * n * k * 3e-9))))
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            refmm(a, w, bias, *sc)
+        cpu_ref = (time.perf_counter() - t0) / reps
+        row = {"us_call": round(dt * 1e6, 2), "launches_per_call": launches,
+               "byte_exact_vs_reference": exact,
+               "cpu_reference_us": round(cpu_ref * 1e6, 2),
+               "cpu_kind": "reference" if have else "port", "cpu_cores": 1}
+        if have:
+            row["cpu_us"] = round(O.ref_cpu_us(a, w, sc[3], sc[4], reps=max(10, reps)), 2)
+        out[name] = row
+    out["workload"] = ("(M,K,N) = (1,64,64), (1,512,1024), (224,64,64), (3136,33,64): uniform "
+                       "u8 operands around zero point 128, bias in [-4096, 4096]; us_call is "
+                       f"the mean of {steps} host calls, copies in and out included")
+    return out
 
 
 # ---- charsiu's NPU number format (CHARSIU_NPU_QUANT) ----------------------------------

@@ -210,8 +210,14 @@ struct charsiu_gpu_decoder {
 	uint32_t *part_i = nullptr;
 	int *h_io = nullptr;          // pinned
 	float *h_logits = nullptr;    // pinned
-	cudaGraphExec_t exec[2] = {nullptr, nullptr};   // [want_logits]
-	bool warm[2] = {false, false};
+	// [mode]: 0 a host step, 1 a host step with the logits copied back, 2 a
+	// step of the device-side greedy run (no copies; the argmax becomes the
+	// next token on the device)
+	cudaGraphExec_t exec[3] = {nullptr, nullptr, nullptr};
+	bool warm[3] = {false, false, false};
+	int32_t *gen_out = nullptr;   // [n_ctx] tokens of a device-side run
+	int32_t *h_gen = nullptr;     // pinned copy of them
+	cudaEvent_t ev[2] = {nullptr, nullptr};
 	unsigned launches = 0;        // kernels a step
 };
 
@@ -284,13 +290,13 @@ bool npu_matvec(charsiu_gpu_decoder *dec, const int *ids, unsigned n, float *con
 // CHARSIU_NPU_QUANT): llama_forward's steps as queue_step's, every projection
 // and the head an NPU-format matvec of a single-scale activation -- after
 // each rmsnorm, the attention output and SiLU's.
-bool queue_step_npu(charsiu_gpu_decoder *dec, bool want_logits)
+bool queue_step_npu(charsiu_gpu_decoder *dec, int mode)
 {
 	const uint32_t n = dec->n_embd, kvdim = dec->n_head_kv * dec->hd;
 	const size_t layer_kv = (size_t)dec->n_ctx * kvdim;
 	dec->launches = 0;
-	if (cudaMemcpyAsync(dec->io, dec->h_io, 2 * sizeof(int), cudaMemcpyHostToDevice, dec->st) !=
-	    cudaSuccess)
+	if (mode != 2 && cudaMemcpyAsync(dec->io, dec->h_io, 2 * sizeof(int),
+					 cudaMemcpyHostToDevice, dec->st) != cudaSuccess)
 		return fail(dec, "the step's input copy failed");
 	{
 		const unsigned long before = charsiu_gpu_launches(dec->g);
@@ -350,25 +356,28 @@ bool queue_step_npu(charsiu_gpu_decoder *dec, bool want_logits)
 		    (const float *)dec->logits, dec->n_vocab, dec->io,
 		    reinterpret_cast<uint32_t *>(dec->io + FWD_IO_TICKET), dec->part_v, dec->part_i))
 		return fail(dec, "a launch failed (argmax)");
+	if (mode == 2)
+		return launch(dec, fwd_advance_kernel, 1, 32, 0, dec->io, dec->gen_out) ||
+		       fail(dec, "a launch failed (advance)");
 	if (cudaMemcpyAsync(dec->h_io + FWD_IO_NEXT, dec->io + FWD_IO_NEXT, sizeof(int),
 			    cudaMemcpyDeviceToHost, dec->st) != cudaSuccess)
 		return fail(dec, "the step's output copy failed");
-	if (want_logits && cudaMemcpyAsync(dec->h_logits, dec->logits, (size_t)dec->n_vocab * 4,
-					   cudaMemcpyDeviceToHost, dec->st) != cudaSuccess)
+	if (mode == 1 && cudaMemcpyAsync(dec->h_logits, dec->logits, (size_t)dec->n_vocab * 4,
+					 cudaMemcpyDeviceToHost, dec->st) != cudaSuccess)
 		return fail(dec, "the logits copy failed");
 	return true;
 }
 
 // Queue one token's work on dec->st (eagerly or into a capture).
-bool queue_step(charsiu_gpu_decoder *dec, bool want_logits)
+bool queue_step(charsiu_gpu_decoder *dec, int mode)
 {
 	if (dec->npu)
-		return queue_step_npu(dec, want_logits);
+		return queue_step_npu(dec, mode);
 	const uint32_t n = dec->n_embd, kvdim = dec->n_head_kv * dec->hd;
 	const size_t layer_kv = (size_t)dec->n_ctx * kvdim;
 	dec->launches = 0;
-	if (cudaMemcpyAsync(dec->io, dec->h_io, 2 * sizeof(int), cudaMemcpyHostToDevice, dec->st) !=
-	    cudaSuccess)
+	if (mode != 2 && cudaMemcpyAsync(dec->io, dec->h_io, 2 * sizeof(int),
+					 cudaMemcpyHostToDevice, dec->st) != cudaSuccess)
 		return fail(dec, "the step's input copy failed");
 	{
 		const unsigned long before = charsiu_gpu_launches(dec->g);
@@ -427,13 +436,37 @@ bool queue_step(charsiu_gpu_decoder *dec, bool want_logits)
 		    (const float *)dec->logits, dec->n_vocab, dec->io,
 		    reinterpret_cast<uint32_t *>(dec->io + FWD_IO_TICKET), dec->part_v, dec->part_i))
 		return fail(dec, "a launch failed (argmax)");
+	if (mode == 2)
+		return launch(dec, fwd_advance_kernel, 1, 32, 0, dec->io, dec->gen_out) ||
+		       fail(dec, "a launch failed (advance)");
 	if (cudaMemcpyAsync(dec->h_io + FWD_IO_NEXT, dec->io + FWD_IO_NEXT, sizeof(int),
 			    cudaMemcpyDeviceToHost, dec->st) != cudaSuccess)
 		return fail(dec, "the step's output copy failed");
-	if (want_logits && cudaMemcpyAsync(dec->h_logits, dec->logits, (size_t)dec->n_vocab * 4,
-					   cudaMemcpyDeviceToHost, dec->st) != cudaSuccess)
+	if (mode == 1 && cudaMemcpyAsync(dec->h_logits, dec->logits, (size_t)dec->n_vocab * 4,
+					 cudaMemcpyDeviceToHost, dec->st) != cudaSuccess)
 		return fail(dec, "the logits copy failed");
 	return true;
+}
+
+// Queue one step of `mode` (see exec): eagerly the first time (warming every
+// launch cache and attribute outside any capture), captured into a graph the
+// second, replayed after that.
+bool run_step(charsiu_gpu_decoder *dec, int mode)
+{
+	if (dec->exec[mode])
+		return cudaGraphLaunch(dec->exec[mode], dec->st) == cudaSuccess;
+	if (!dec->warm[mode]) {
+		dec->warm[mode] = queue_step(dec, mode);
+		return dec->warm[mode];
+	}
+	cudaGraph_t graph = nullptr;
+	bool ok = cudaStreamBeginCapture(dec->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+	const bool queued = ok && queue_step(dec, mode);
+	ok = cudaStreamEndCapture(dec->st, &graph) == cudaSuccess && queued;
+	ok = ok && cudaGraphInstantiate(&dec->exec[mode], graph, 0) == cudaSuccess;
+	if (graph)
+		cudaGraphDestroy(graph);
+	return ok && cudaGraphLaunch(dec->exec[mode], dec->st) == cudaSuccess;
 }
 
 void release(charsiu_gpu_decoder *dec)
@@ -447,11 +480,17 @@ void release(charsiu_gpu_decoder *dec)
 			(void *)dec->x, (void *)dec->qv, (void *)dec->kv, (void *)dec->vv,
 			(void *)dec->xb2, (void *)dec->hb, (void *)dec->hb2, (void *)dec->logits,
 			(void *)dec->aq, (void *)dec->ad, (void *)dec->io, (void *)dec->part_v,
-			(void *)dec->part_i, (void *)dec->q1, (void *)dec->d1, (void *)dec->vf})
+			(void *)dec->part_i, (void *)dec->q1, (void *)dec->d1, (void *)dec->vf,
+			(void *)dec->gen_out})
 		if (p)
 			cudaFree(p);
+	for (cudaEvent_t &e : dec->ev)
+		if (e)
+			cudaEventDestroy(e);
 	if (dec->h_io)
 		cudaFreeHost(dec->h_io);
+	if (dec->h_gen)
+		cudaFreeHost(dec->h_gen);
 	if (dec->h_logits)
 		cudaFreeHost(dec->h_logits);
 	if (dec->st)
@@ -569,6 +608,11 @@ charsiu_gpu_decoder *build(charsiu_gpu *g, charsiu_npu *npu,
 			   cudaSuccess;
 	ok = ok && cudaHostAlloc(&dec->h_logits, (size_t)d->n_vocab * 4, cudaHostAllocDefault) ==
 			   cudaSuccess;
+	ok = ok && cudaMalloc(&dec->gen_out, (size_t)d->n_ctx * sizeof(int32_t)) == cudaSuccess;
+	ok = ok && cudaHostAlloc(&dec->h_gen, (size_t)d->n_ctx * sizeof(int32_t),
+				 cudaHostAllocDefault) == cudaSuccess;
+	ok = ok && cudaEventCreate(&dec->ev[0]) == cudaSuccess &&
+	     cudaEventCreate(&dec->ev[1]) == cudaSuccess;
 	if (npu) {
 		ok = ok && cudaMalloc(&dec->q1, std::max(dec->kp_embd, dec->kp_ff)) == cudaSuccess;
 		ok = ok && cudaMalloc(&dec->d1, sizeof(float)) == cudaSuccess;
@@ -642,6 +686,51 @@ void charsiu_gpu_decoder_free(struct charsiu_gpu_decoder *dec)
 	delete dec;
 }
 
+int charsiu_gpu_decoder_generate(struct charsiu_gpu_decoder *dec, int32_t token, int pos,
+				 unsigned n, int32_t *out, float *device_ms)
+{
+	if (!dec || !out || charsiu_gpu_dead(dec->g))
+		return -1;
+	if (pos < 0 || token < 0 || (uint32_t)token >= dec->n_vocab || !n ||
+	    (uint64_t)pos + n > dec->n_ctx) {
+		layer_whine(dec->g, "token or positions out of range");
+		return -1;
+	}
+	cudaSetDevice(dec->device);
+	dec->h_io[FWD_IO_TOKEN] = token;
+	dec->h_io[FWD_IO_POS] = pos;
+	dec->h_io[FWD_IO_STEP] = 0;
+	bool ok = cudaMemcpyAsync(dec->io + FWD_IO_TOKEN, dec->h_io + FWD_IO_TOKEN, 2 * sizeof(int),
+				  cudaMemcpyHostToDevice, dec->st) == cudaSuccess &&
+		  cudaMemcpyAsync(dec->io + FWD_IO_STEP, dec->h_io + FWD_IO_STEP, sizeof(int),
+				  cudaMemcpyHostToDevice, dec->st) == cudaSuccess &&
+		  cudaEventRecord(dec->ev[0], dec->st) == cudaSuccess;
+	// (the first step of a run may warm or capture the graph; the run's
+	// device time still covers every step)
+	for (unsigned i = 0; i < n && ok; i++)
+		ok = run_step(dec, 2);
+	ok = ok && cudaEventRecord(dec->ev[1], dec->st) == cudaSuccess &&
+	     cudaMemcpyAsync(dec->h_gen, dec->gen_out, (size_t)n * sizeof(int32_t),
+			     cudaMemcpyDeviceToHost, dec->st) == cudaSuccess;
+	if (!ok) {
+		layer_whine(dec->g, "the device-side greedy run would not launch");
+		cudaStreamSynchronize(dec->st);
+		cudaGetLastError();
+		return -1;
+	}
+	const cudaError_t e = cudaStreamSynchronize(dec->st);
+	if (e != cudaSuccess) {
+		layer_whine(dec->g, cudaGetErrorString(e));
+		return -1;
+	}
+	if (charsiu_gpu_kernel_error(dec->g))
+		return -1;
+	memcpy(out, dec->h_gen, (size_t)n * sizeof(int32_t));
+	if (device_ms && cudaEventElapsedTime(device_ms, dec->ev[0], dec->ev[1]) != cudaSuccess)
+		*device_ms = -1.0f;
+	return 0;
+}
+
 int charsiu_gpu_decoder_step(struct charsiu_gpu_decoder *dec, int32_t token, int pos,
 			     int want_logits, int32_t *next)
 {
@@ -652,28 +741,9 @@ int charsiu_gpu_decoder_step(struct charsiu_gpu_decoder *dec, int32_t token, int
 		return -1;
 	}
 	cudaSetDevice(dec->device);
-	const int v = want_logits ? 1 : 0;
 	dec->h_io[FWD_IO_TOKEN] = token;
 	dec->h_io[FWD_IO_POS] = pos;
-	bool ok = true;
-	if (dec->exec[v]) {
-		ok = cudaGraphLaunch(dec->exec[v], dec->st) == cudaSuccess;
-	} else if (dec->warm[v]) {
-		// the second step of a kind captures it (the first warmed every
-		// launch cache and attribute outside any capture)
-		cudaGraph_t graph = nullptr;
-		ok = cudaStreamBeginCapture(dec->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
-		const bool queued = ok && queue_step(dec, v);
-		ok = cudaStreamEndCapture(dec->st, &graph) == cudaSuccess && queued;
-		ok = ok && cudaGraphInstantiate(&dec->exec[v], graph, 0) == cudaSuccess;
-		if (graph)
-			cudaGraphDestroy(graph);
-		ok = ok && cudaGraphLaunch(dec->exec[v], dec->st) == cudaSuccess;
-	} else {
-		ok = queue_step(dec, v);
-		dec->warm[v] = ok;
-	}
-	if (!ok) {
+	if (!run_step(dec, want_logits ? 1 : 0)) {
 		layer_whine(dec->g, "the decode step would not launch");
 		cudaStreamSynchronize(dec->st);
 		cudaGetLastError();

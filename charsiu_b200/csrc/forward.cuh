@@ -29,9 +29,10 @@ constexpr uint32_t EXPTAB_E0 = 101, EXPTAB_NE = 33;
 constexpr uint64_t EXPTAB_ENTRIES = 2ull * EXPTAB_NE << 23;
 
 // The step's small device inputs and outputs: the token, its position, the
-// argmax of its logits, and the argmax's arrival ticket (zero between steps).
+// argmax of its logits, the argmax's arrival ticket (zero between steps), and
+// the index of the next token a device-side greedy run writes.
 constexpr int FWD_IO_TOKEN = 0, FWD_IO_POS = 1, FWD_IO_NEXT = 2, FWD_IO_TICKET = 3,
-	      FWD_IO_WORDS = 4;
+	      FWD_IO_STEP = 4, FWD_IO_WORDS = 5;
 
 __device__ __forceinline__ float exp_exact(float x, const float *__restrict__ tab)
 {
@@ -433,6 +434,22 @@ fwd_argmax_kernel(const float *__restrict__ x, uint32_t n, int *__restrict__ io,
 			const float x0 = x[0];
 			io[FWD_IO_NEXT] = (x0 != x0 || fi == ARGMAX_NONE) ? 0 : (int)fi;
 		}
+	}
+}
+
+// The greedy loop's step on the device (tools/charsiu_run.c:295-317 without
+// the host): the argmax just taken becomes the next step's token, at the next
+// position, and is appended to out. The host checked that every position the
+// run reaches is inside the context, so the caches are never indexed past it.
+__global__ void fwd_advance_kernel(int *__restrict__ io, int32_t *__restrict__ out)
+{
+	pdl_wait();
+	if (threadIdx.x == 0) {
+		const int next = io[FWD_IO_NEXT];
+		out[io[FWD_IO_STEP]] = next;
+		io[FWD_IO_STEP] += 1;
+		io[FWD_IO_TOKEN] = next;
+		io[FWD_IO_POS] += 1;
 	}
 }
 

@@ -80,6 +80,7 @@ SIGNATURES = [
     ("charsiu_gpu_decoder_free", None, [_vp]),
     ("charsiu_gpu_decoder_step", C.c_int, [_vp, C.c_int32, C.c_int, C.c_int, _vp]),
     ("charsiu_gpu_decoder_logits", C.POINTER(C.c_float), [_vp]),
+    ("charsiu_gpu_decoder_generate", C.c_int, [_vp, C.c_int32, C.c_int, C.c_uint, _vp, _vp]),
     ("charsiu_gpu_decoder_launches", C.c_uint, [_vp]),
     ("charsiu_gpu_ordered_sum_dev", C.c_int, [_vp, _vp, C.c_uint, _vp, _vp]),
     ("charsiu_npu_open", _vp, [C.c_uint, C.c_uint, C.c_uint]),
@@ -394,6 +395,20 @@ class Llama:
         if not p:
             raise GpuError(f"forward failed: {self.L.charsiu_gpu_error(self.layer_handle)}")
         return np.ctypeslib.as_array(p, shape=(self.n_vocab,)).copy()
+
+    def generate_dev(self, token: int, pos: int, n: int):
+        """n greedy steps on the device from token at pos, no host round trip
+        between them (charsiu_gpu_decoder_generate; resident mode only):
+        (the n argmax tokens, device ms of the n steps)."""
+        dec = self.L.charsiu_gpu_llama_decoder(self.h)
+        if not dec:
+            raise GpuError("generate_dev needs the device step (set_resident)")
+        out = np.zeros(n, dtype=np.int32)
+        ms = C.c_float()
+        if self.L.charsiu_gpu_decoder_generate(dec, int(token), int(pos), n, _p(out),
+                                               C.byref(ms)):
+            raise GpuError(f"generate failed: {self.L.charsiu_gpu_error(self.layer_handle)}")
+        return out, float(ms.value)
 
     def greedy(self, prompt, n_gen: int, want_logits: bool = False):
         p = np.ascontiguousarray(prompt, dtype=np.int32)

@@ -281,6 +281,17 @@ CHARSIU_GPU_API void charsiu_gpu_decoder_free(struct charsiu_gpu_decoder *dec);
  * the next step. 0 on success, -1 on failure (charsiu_gpu_error says why). */
 CHARSIU_GPU_API int charsiu_gpu_decoder_step(struct charsiu_gpu_decoder *dec, int32_t token,
 					     int pos, int want_logits, int32_t *next);
+/* The greedy loop of tools/charsiu_run.c:295-317 with the host taken out:
+ * n steps from `token` at `pos`, each step's argmax the next step's token at
+ * the next position, all queued at once (the argmax never leaves the device
+ * between steps); out[i] gets the argmax of step i, so out[0] is what
+ * charsiu_gpu_decoder_step would return for (token, pos). pos + n must not
+ * pass the context. *device_ms (if given) gets the device time of the n
+ * steps, from CUDA events on the decoder's stream. 0 on success, -1 on
+ * failure. No counterpart in the reference. */
+CHARSIU_GPU_API int charsiu_gpu_decoder_generate(struct charsiu_gpu_decoder *dec, int32_t token,
+						 int pos, unsigned n, int32_t *out,
+						 float *device_ms);
 CHARSIU_GPU_API const float *charsiu_gpu_decoder_logits(const struct charsiu_gpu_decoder *dec);
 /* kernels one step launches */
 CHARSIU_GPU_API unsigned charsiu_gpu_decoder_launches(const struct charsiu_gpu_decoder *dec);

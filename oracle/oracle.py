@@ -108,6 +108,12 @@ def ref():
         R.ref_act_q1.argtypes = [_f32p, C.c_int, _i8p, C.POINTER(C.c_float)]
         R.ref_act_q1.restype = C.c_int
         R.ref_npu_matvec.argtypes = [_i8p, _f32p, C.c_uint64, C.c_uint64, _i8p, C.c_float, _f32p]
+        R.ref_matvec_time.argtypes = [C.c_uint32, C.c_void_p, C.c_uint64, C.c_uint64, _f32p,
+                                      C.c_int, C.c_int, C.POINTER(C.c_double)]
+        R.ref_matvec_time.restype = C.c_int
+        R.ref_cpu_us.argtypes = [C.c_uint, C.c_uint, C.c_uint, _u8p, _u8p, C.c_int, C.c_int,
+                                 C.c_uint]
+        R.ref_cpu_us.restype = C.c_double
         _ref = R
     return _ref
 
@@ -322,6 +328,29 @@ def ref_matvec(qtype: int, blocks: np.ndarray, k: int, n: int, x: np.ndarray):
     rc = ref().ref_matvec(qtype, _ptr(blocks), k, n, x, y, q, d)
     assert rc == 0
     return y, q, d
+
+
+def ref_matvec_ms(qtype: int, blocks: np.ndarray, k: int, n: int, x: np.ndarray,
+                  threads: int = 1, reps: int = 10) -> float:
+    """ms a call of the reference's charsiu_act_set + gguf_matvec over all n
+    rows, on `threads` host threads splitting the rows as its decode loop's
+    pool does (src/llama.c:63-73)."""
+    ms = C.c_double()
+    rc = ref().ref_matvec_time(qtype, _ptr(blocks), k, n, np.ascontiguousarray(x, np.float32),
+                               threads, reps, C.byref(ms))
+    if rc:
+        raise RuntimeError("ref_matvec_time failed")
+    return ms.value
+
+
+def ref_cpu_us(a, w, in_zp: int = 128, wt_zp: int = 128, reps: int = 10) -> float:
+    """The reference's own one-core int8 denominator, cpu_us of
+    tools/charsiu_bench.c:74-95 (one activation row against every weight
+    row), microseconds a call."""
+    m, k = a.shape
+    n = w.shape[0]
+    return ref().ref_cpu_us(m, k, n, np.ascontiguousarray(a), np.ascontiguousarray(w), in_zp,
+                            wt_zp, reps)
 
 
 def ref_greedy(path: str, prompt, n_gen: int, n_ctx: int = 0, threads: int | None = None,

@@ -18,6 +18,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <pthread.h>
 #include <time.h>
 
 #include "charsiu.h"
@@ -97,6 +98,119 @@ static double now_ms(void)
 
 	clock_gettime(CLOCK_MONOTONIC, &t);
 	return (double)t.tv_sec * 1e3 + (double)t.tv_nsec / 1e6;
+}
+
+/*
+ * The CPU baseline of one matvec: charsiu_act_set of x, then gguf_matvec over
+ * all n rows, `reps` times; *ms gets the mean time a call. With threads > 1
+ * the rows are split as the decode loop's pool splits them (src/llama.c:63-73:
+ * worker i takes rows [i * per, i * per + per) with per = ceil(n / threads))
+ * over that many threads, started once and released each call by a barrier,
+ * the caller quantising first as matvec() does (src/llama.c:178-182).
+ */
+struct mv_job {
+	const struct gguf_tensor *w;
+	const struct charsiu_act *a;
+	float *y;
+	uint64_t n;
+	int threads, reps;
+	pthread_barrier_t go, done;
+};
+
+struct mv_worker {
+	struct mv_job *j;
+	int id;
+};
+
+static void mv_slice(const struct mv_job *j, int id)
+{
+	uint64_t per = (j->n + (uint64_t)j->threads - 1) / (uint64_t)j->threads;
+	uint64_t r0 = per * (uint64_t)id, cnt;
+
+	if (r0 >= j->n)
+		return;
+	cnt = j->n - r0 < per ? j->n - r0 : per;
+	gguf_matvec(j->w, j->a, j->y, r0, cnt);
+}
+
+static void *mv_worker_main(void *arg)
+{
+	struct mv_worker *wk = arg;
+
+	for (int r = 0; r < wk->j->reps; r++) {
+		pthread_barrier_wait(&wk->j->go);
+		mv_slice(wk->j, wk->id);
+		pthread_barrier_wait(&wk->j->done);
+	}
+	return NULL;
+}
+
+int ref_matvec_time(uint32_t type, const void *blocks, uint64_t k, uint64_t n, const float *x,
+		    int threads, int reps, double *ms)
+{
+	struct gguf_tensor w;
+	struct charsiu_act a;
+	struct mv_job j;
+	pthread_t th[256];
+	struct mv_worker wk[256];
+	double t0;
+	int nt = 0, rc = 0;
+
+	if (threads < 1 || threads > 256 || reps < 1)
+		return -1;
+	memset(&w, 0, sizeof(w));
+	w.n_dims = 2;
+	w.ne[0] = k;
+	w.ne[1] = n;
+	w.ne[2] = w.ne[3] = 1;
+	w.type = type;
+	w.data = blocks;
+	if (charsiu_act_alloc(&a, (int)k) < 0)
+		return -1;
+	memset(&j, 0, sizeof(j));
+	j.w = &w;
+	j.a = &a;
+	j.y = malloc((size_t)n * sizeof(float));
+	j.n = n;
+	j.threads = threads;
+	j.reps = reps;
+	if (!j.y) {
+		charsiu_act_free(&a);
+		return -1;
+	}
+	if (threads > 1) {
+		pthread_barrier_init(&j.go, NULL, (unsigned)threads);
+		pthread_barrier_init(&j.done, NULL, (unsigned)threads);
+		for (nt = 0; nt < threads - 1; nt++) {
+			wk[nt].j = &j;
+			wk[nt].id = nt + 1;
+			if (pthread_create(&th[nt], NULL, mv_worker_main, &wk[nt])) {
+				rc = -1;
+				break;
+			}
+		}
+	}
+	if (!rc) {
+		t0 = now_ms();
+		for (int r = 0; r < reps; r++) {
+			charsiu_act_set(&a, x, (int)k);
+			if (threads > 1)
+				pthread_barrier_wait(&j.go);
+			mv_slice(&j, 0);
+			if (threads > 1)
+				pthread_barrier_wait(&j.done);
+		}
+		*ms = (now_ms() - t0) / reps;
+	}
+	for (int i = 0; i < nt; i++)
+		pthread_join(th[i], NULL);
+	if (threads > 1) {
+		pthread_barrier_destroy(&j.go);
+		pthread_barrier_destroy(&j.done);
+	}
+	free(j.y);
+	charsiu_act_free(&a);
+	return rc;
 }
 
 /*

@@ -132,3 +132,32 @@ def test_embedding_row(qtype, k, n):
         assert g.kernel_error() != 0
         assert bool((out == 7.0).all())
         assert g.dead
+
+
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4_q6k", "llama1b_q8"])
+def test_device_side_greedy_run(name, tmp_path):
+    """charsiu_gpu_decoder_generate: the greedy loop with each step's argmax
+    fed to the next step on the device, no host round trip between steps.
+    Three runs from the prompt in a row (the first warms the step, the second
+    captures its graph, the third replays it) each give the reference's
+    tokens."""
+    spec, gold = W.DECODE[name], GOLD[name]
+    path = str(tmp_path / f"{name}.gguf")
+    G.write_llama(path, spec["shape"], spec["qtype"], spec["seed"],
+                  embd_qtype=spec.get("embd_qtype"))
+    prompt = np.array(gold["prompt"], np.int32)
+    n = spec["n_gen"] - 1
+    with Llama(path, n_ctx=len(prompt) + n, resident=True) as m:
+        for _ in range(3):
+            lp = None
+            for i, t in enumerate(prompt):
+                lp = m.forward(int(t), i)
+            first = int(np.argmax(lp))
+            toks, ms = m.generate_dev(first, len(prompt), n)
+            assert [first] + toks.tolist() == gold["tokens"]
+            assert ms > 0
+        # embedding + 8 a layer + final norm, head, argmax, and the step that
+        # feeds the argmax on
+        assert m.step_launches == 1 + 8 * spec["shape"].n_layer + 4
+        with pytest.raises(Exception):
+            m.generate_dev(first, len(prompt), n + 1)     # past the context: refused
