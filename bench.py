@@ -924,7 +924,7 @@ def int8_configs(steps: int = 200):
     for name, (m, k, n, seed) in W.I8_SHAPES.items():
         a, w, bias = W.i8_inputs(m, k, n, seed)
         sc = W.i8_scales(m, k, n, seed)
-        with Layer(max_k=max(k, 32), max_n=n, max_tensors=1,
+        with Layer(max_k=(max(k, 32) + 31) // 32 * 32, max_n=n, max_tensors=1,
                    device=int(os.environ.get("LOCAL_RANK", 0))) as L:
             got = L.matmul_i8(a, w, bias, *sc)
             for _ in range(10):
@@ -1086,7 +1086,7 @@ def run_int8_case(args):
     m, k, n = (int(v) for v in args.int8.split(":"))
     a, w, bias = W.i8_inputs(m, k, n, 0)
     sc = W.i8_scales(m, k, n, 0)
-    with Layer(max_k=max(k, 32), max_n=n, max_tensors=1) as L:
+    with Layer(max_k=(max(k, 32) + 31) // 32 * 32, max_n=n, max_tensors=1) as L:
         out = L.matmul_i8(a, w, bias, *sc)
         for _ in range(args.warmup):
             L.matmul_i8(a, w, bias, *sc)
@@ -1254,6 +1254,10 @@ def main():
                     help="time the NPU-format (CHARSIU_NPU_QUANT) matvec at one shape")
     ap.add_argument("--resident", action="store_true",
                     help="time only the device-resident greedy decode (the e2e leg)")
+    ap.add_argument("--hot-path", action="store_true",
+                    help="time only the token's 65 matvec launches (the roofline's chain)")
+    ap.add_argument("--decode", action="store_true",
+                    help="time only the headline decode (inputs resident, device-side loop)")
     ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N[:M]",
                     help="time one matvec shape instead of the decode (e.g. q8_0:2048:8192; "
                          "q8_0:2048:8192:64 for 64 activations)")
@@ -1285,6 +1289,29 @@ def main():
             return
         if args.npu:
             print(json.dumps(run_npu_case(args)), flush=True)
+            return
+        if args.hot_path or args.decode:
+            import torch
+            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+            torch.cuda.set_device(dev)
+            barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
+            path = model_path(rank, barrier)
+            if args.decode:
+                ms, match, clk, kernels = run_decode(path, args, world, dist, dev, rank == 0)
+                out = {"decode_tok_s": round(world * 1000.0 / ms, 2), "ms_per_token": round(ms, 5),
+                       "tokens_match_reference": match, "kernels_per_step": kernels,
+                       "clocks": clk}
+            else:
+                chain = TokenChain(G.GGUFFile(path), dev)
+                ms, clk = time_chain(chain, args.steps, args.warmup, barrier, dist, world, dev,
+                                     True, rank == 0)
+                gbs = chain.bytes_per_token / (ms * 1e-3) / 1e9
+                chain.close()
+                out = {"hot_path_tok_s": round(world * 1000.0 / ms, 2),
+                       "ms_per_token": round(ms, 5), "gbs": round(gbs, 1),
+                       "frac": round(gbs / peaks()[0], 4), "clocks": clk}
+            if rank == 0:
+                print(json.dumps(out), flush=True)
             return
         if args.resident:
             import torch

@@ -41,6 +41,10 @@ struct QmvParams {
 	uint32_t *done_flag;     // [0] seq, [1] kernel ns
 	unsigned long long *t_start;
 	uint32_t seq;
+	// 1: let the next launch start as soon as every CTA of this one has
+	// started (its weights then stream in while this one computes); 0: once
+	// every CTA has staged the activation
+	uint32_t early_trigger;
 };
 
 } // namespace cgpu

@@ -206,6 +206,8 @@ __device__ __forceinline__ void qmv1_body(const QmvParams &p, const uint4 *inl,
 			seg_load<Q8>(R1, seg_ptr(ti, lg, s1), seg_blocks(nb, s1), lane);
 	};
 
+	if (p.early_trigger)
+		pdl_launch_dependents();
 	// weights do not depend on the previous kernel: the first group's go now
 	uint32_t G = blockIdx.x;
 	if (G < p.total_groups)
@@ -263,7 +265,8 @@ __device__ __forceinline__ void qmv1_body(const QmvParams &p, const uint4 *inl,
 		}
 		__syncthreads();
 	}
-	pdl_launch_dependents();
+	if (!p.early_trigger)
+		pdl_launch_dependents();
 
 	for (uint32_t i = 0; G < p.total_groups; i++, G += gridDim.x) {
 		uint32_t ti, lg;
