@@ -1265,6 +1265,16 @@ def main():
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
 
+    # the JSON line goes to the original stdout; everything else a library
+    # prints there (NCCL's version banner) goes to stderr
+    out_fd = os.dup(1)
+    os.dup2(2, 1)
+    json_out = os.fdopen(out_fd, "w")
+
+    def emit(obj):
+        json_out.write(json.dumps(obj) + "\n")
+        json_out.flush()
+
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     dist = None
@@ -1279,16 +1289,16 @@ def main():
                                 timeout=datetime.timedelta(seconds=600))
     try:
         if args.matvec:
-            print(json.dumps(run_matvec_case(args)), flush=True)
+            emit(run_matvec_case(args))
             return
         if args.batch:
-            print(json.dumps(run_batch_case(args)), flush=True)
+            emit(run_batch_case(args))
             return
         if args.int8:
-            print(json.dumps(run_int8_case(args)), flush=True)
+            emit(run_int8_case(args))
             return
         if args.npu:
-            print(json.dumps(run_npu_case(args)), flush=True)
+            emit(run_npu_case(args))
             return
         if args.hot_path or args.decode:
             import torch
@@ -1311,7 +1321,7 @@ def main():
                        "ms_per_token": round(ms, 5), "gbs": round(gbs, 1),
                        "frac": round(gbs / peaks()[0], 4), "clocks": clk}
             if rank == 0:
-                print(json.dumps(out), flush=True)
+                emit(out)
             return
         if args.resident:
             import torch
@@ -1320,14 +1330,14 @@ def main():
             barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
             out = run_e2e_resident(model_path(rank, barrier), args, world, dist, dev)
             if rank == 0:
-                print(json.dumps(out), flush=True)
+                emit(out)
             return
         if args.impl == "reference":
             out = run_reference(args, rank, world, dist)
         else:
             out = run_ours(args, rank, world, dist)
         if rank == 0 and out is not None:
-            print(json.dumps(out), flush=True)
+            emit(out)
     finally:
         if dist is not None:
             dist.destroy_process_group()

@@ -189,15 +189,22 @@ inline size_t fwd_attention_smem(uint32_t n_ctx, uint32_t hd)
 		2 * (size_t)fwd_attention_tile(hd) * (hd + 4)) * sizeof(float);
 }
 
-__global__ void __launch_bounds__(FWD_ATTN_THREADS)
-fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
-		     const float *__restrict__ vv, const float *__restrict__ rope_cs,
-		     float *__restrict__ kcache, float *__restrict__ vcache,
-		     const int *__restrict__ io, uint32_t n_head, uint32_t n_head_kv, uint32_t hd,
-		     uint32_t n_ctx, uint32_t tile, float scale, const float *__restrict__ exptab,
-		     int8_t *__restrict__ q, float *__restrict__ d, float *__restrict__ out_f)
+// One head h of the attention above, by the threads of G: fsm is the dynamic
+// shared memory (fwd_attention_smem bytes), red 32 floats and *sum_sh one of
+// shared memory. `wait` runs once the first tile's cache rows are on their
+// way and before anything of this token's is read (the wait on the kernel or
+// stage before).
+template <class G, class Wait>
+__device__ __forceinline__ void
+attention_head(uint32_t h, float *fsm, float *red, float *sum_sh, Wait wait,
+	       const float *__restrict__ qv, const float *__restrict__ kv,
+	       const float *__restrict__ vv, const float *__restrict__ rope_cs,
+	       float *__restrict__ kcache, float *__restrict__ vcache, const int *__restrict__ io,
+	       uint32_t n_head, uint32_t n_head_kv, uint32_t hd, uint32_t n_ctx, uint32_t tile,
+	       float scale, const float *__restrict__ exptab, int8_t *__restrict__ q,
+	       float *__restrict__ d, float *__restrict__ out_f)
 {
-	extern __shared__ __align__(16) float fsm[];
+	const uint32_t tid = G::tid(), nthr = G::size();
 	const uint32_t rs = hd + 4;
 	float *att = fsm;                  // n_ctx scores
 	float *qs = att + fwd_attention_att_floats(n_ctx);     // this head's q, rotated
@@ -206,9 +213,7 @@ fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
 	float *os = vp + hd;               // this head's outputs
 	float *kt = os + hd;               // tile rows of K
 	float *vt = kt + (size_t)tile * rs;
-	__shared__ float red[FWD_ATTN_THREADS / 32];
-	__shared__ float sum_s;
-	const uint32_t h = blockIdx.x, kvdim = n_head_kv * hd, gqa = n_head / n_head_kv;
+	const uint32_t kvdim = n_head_kv * hd, gqa = n_head / n_head_kv;
 	const uint32_t kvh = h / gqa;
 	// the position came in with the step's first copy, before any kernel of it
 	const int pos = io[FWD_IO_POS], np = pos + 1;
@@ -216,26 +221,25 @@ fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
 	// cache rows t0 .. t0 + nt - 1 below pos into a tile
 	auto issue = [&](float *dst, const float *cache, int t0, int nt) {
 		const uint32_t q4 = hd / 4;
-		for (uint32_t j = threadIdx.x; j < (uint32_t)nt * q4; j += blockDim.x) {
+		for (uint32_t j = tid; j < (uint32_t)nt * q4; j += nthr) {
 			const int t = t0 + (int)(j / q4);
 			const uint32_t i = (j % q4) * 4;
 			if (t < pos)
 				cp_async16(dst + (size_t)(t - t0) * rs + i, cache + (size_t)t * kvdim + i);
 		}
 	};
-	// and row pos, when the tile holds it, from this CTA's own copy
+	// and row pos, when the tile holds it, from this head's own copy
 	auto own_row = [&](float *dst, const float *own, int t0, int nt) {
 		if (pos >= t0 && pos < t0 + nt)
-			for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x)
+			for (uint32_t i = tid; i < hd; i += nthr)
 				dst[(size_t)(pos - t0) * rs + i] = own[i];
 	};
 	const int nt0 = np < (int)tile ? np : (int)tile;
 	issue(kt, kc, 0, nt0);
 	issue(vt, vc, 0, nt0);
-	pdl_wait();
-	pdl_launch_dependents();
+	wait();
 	const float *cs = rope_cs + (size_t)pos * hd;
-	for (uint32_t i = threadIdx.x; i < hd / 2; i += blockDim.x) {
+	for (uint32_t i = tid; i < hd / 2; i += nthr) {
 		const float c = cs[2 * i], s = cs[2 * i + 1];
 		float x0 = qv[h * hd + 2 * i], x1 = qv[h * hd + 2 * i + 1];
 		qs[2 * i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
@@ -245,29 +249,29 @@ fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
 		kp[2 * i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
 		kp[2 * i + 1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
 	}
-	for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x)
+	for (uint32_t i = tid; i < hd; i += nthr)
 		vp[i] = vv[kvh * hd + i];
-	__syncthreads();
+	G::sync();
 	if (h % gqa == 0)
-		for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
+		for (uint32_t i = tid; i < hd; i += nthr) {
 			kc[(size_t)pos * kvdim + i] = kp[i];
 			vc[(size_t)pos * kvdim + i] = vp[i];
 		}
 	own_row(kt, kp, 0, nt0);
 	own_row(vt, vp, 0, nt0);
 	cp_async_wait_all();
-	__syncthreads();
+	G::sync();
 	for (int t0 = 0; t0 < np; t0 += (int)tile) {
 		const int nt = np - t0 < (int)tile ? np - t0 : (int)tile;
 		if (t0) {
-			__syncthreads();
+			G::sync();
 			issue(kt, kc, t0, nt);
 			own_row(kt, kp, t0, nt);
 			cp_async_wait_all();
-			__syncthreads();
+			G::sync();
 		}
-		if ((int)threadIdx.x < nt) {
-			const float4 *k4 = reinterpret_cast<const float4 *>(kt + (size_t)threadIdx.x * rs);
+		if ((int)tid < nt) {
+			const float4 *k4 = reinterpret_cast<const float4 *>(kt + (size_t)tid * rs);
 			float a = 0.0f;
 			for (uint32_t i = 0; i < hd / 4; i++) {
 				const float4 k = k4[i];
@@ -276,61 +280,78 @@ fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
 				a = __fadd_rn(a, __fmul_rn(qs[4 * i + 2], k.z));
 				a = __fadd_rn(a, __fmul_rn(qs[4 * i + 3], k.w));
 			}
-			att[t0 + threadIdx.x] = __fmul_rn(a, scale);
+			att[t0 + tid] = __fmul_rn(a, scale);
 		}
 	}
-	__syncthreads();
+	G::sync();
 	// the max: any order gives the reference's value for NaN-free scores (a NaN
 	// needs a non-finite weight or delta)
 	float mx = -__int_as_float(0x7f800000);
-	for (int t = threadIdx.x; t < np; t += blockDim.x)
+	for (int t = tid; t < np; t += nthr)
 		mx = fmaxf(mx, att[t]);
 	for (int o = 16; o; o >>= 1)
 		mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-	if ((threadIdx.x & 31) == 0)
-		red[threadIdx.x >> 5] = mx;
-	__syncthreads();
+	if ((tid & 31) == 0)
+		red[tid >> 5] = mx;
+	G::sync();
 	mx = red[0];
-	for (int wi = 1; wi < FWD_ATTN_THREADS / 32; wi++)
+	for (uint32_t wi = 1; wi < nthr / 32; wi++)
 		mx = fmaxf(mx, red[wi]);
-	for (int t = threadIdx.x; t < np; t += blockDim.x)
+	for (int t = tid; t < np; t += nthr)
 		att[t] = exp_exact(__fsub_rn(att[t], mx), exptab);
-	__syncthreads();
-	if (threadIdx.x == 0)
-		sum_s = ordered_sum_seq(att, (uint32_t)np);
-	__syncthreads();
-	const float sum = sum_s;
-	for (int t = threadIdx.x; t < np; t += blockDim.x)
+	G::sync();
+	if (tid == 0)
+		*sum_sh = ordered_sum_seq(att, (uint32_t)np);
+	G::sync();
+	const float sum = *sum_sh;
+	for (int t = tid; t < np; t += nthr)
 		att[t] = __fdiv_rn(att[t], sum);
-	__syncthreads();
+	G::sync();
 	float o = 0.0f;
 	for (int t0 = 0; t0 < np; t0 += (int)tile) {
 		const int nt = np - t0 < (int)tile ? np - t0 : (int)tile;
 		if (t0) {
-			__syncthreads();
+			G::sync();
 			issue(vt, vc, t0, nt);
 			own_row(vt, vp, t0, nt);
 			cp_async_wait_all();
-			__syncthreads();
+			G::sync();
 		}
-		if (threadIdx.x < hd)
+		if (tid < hd)
 #pragma unroll 4
 			for (int t = 0; t < nt; t++)
-				o = __fadd_rn(o, __fmul_rn(att[t0 + t], vt[(size_t)t * rs + threadIdx.x]));
+				o = __fadd_rn(o, __fmul_rn(att[t0 + t], vt[(size_t)t * rs + tid]));
 	}
 	if (out_f) {
-		if (threadIdx.x < hd)
-			out_f[h * hd + threadIdx.x] = o;
+		if (tid < hd)
+			out_f[h * hd + tid] = o;
 		return;
 	}
-	if (threadIdx.x < hd)
-		os[threadIdx.x] = o;
-	__syncthreads();
-	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	for (uint32_t b = warp; b < hd / 32; b += blockDim.x / 32) {
+	if (tid < hd)
+		os[tid] = o;
+	G::sync();
+	const int warp = tid >> 5, lane = tid & 31;
+	for (uint32_t b = warp; b < hd / 32; b += nthr / 32) {
 		const uint32_t e = h * hd + b * 32;
 		quantise_block_warp(os[b * 32 + lane], lane, q + e, d + e / 32);
 	}
+}
+
+__global__ void __launch_bounds__(FWD_ATTN_THREADS)
+fwd_attention_kernel(const float *__restrict__ qv, const float *__restrict__ kv,
+		     const float *__restrict__ vv, const float *__restrict__ rope_cs,
+		     float *__restrict__ kcache, float *__restrict__ vcache,
+		     const int *__restrict__ io, uint32_t n_head, uint32_t n_head_kv, uint32_t hd,
+		     uint32_t n_ctx, uint32_t tile, float scale, const float *__restrict__ exptab,
+		     int8_t *__restrict__ q, float *__restrict__ d, float *__restrict__ out_f)
+{
+	extern __shared__ __align__(16) float fsm[];
+	__shared__ float red[32];
+	__shared__ float sum_s;
+	attention_head<CtaGroup>(blockIdx.x, fsm, red, &sum_s,
+				 [] { pdl_wait(); pdl_launch_dependents(); }, qv, kv, vv, rope_cs,
+				 kcache, vcache, io, n_head, n_head_kv, hd, n_ctx, tile, scale, exptab,
+				 q, d, out_f);
 }
 
 // SiLU(gate) * up (src/llama.c:831-836: g *= 1 / (1 + expf(-g)); g * up),

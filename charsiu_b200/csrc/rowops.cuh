@@ -16,6 +16,25 @@
 
 namespace cgpu {
 
+// The threads a row operation runs on: the whole CTA (the decode step's own
+// kernels), or NW warps from warp W0 on, synchronised by named barrier BAR
+// (the persistent step kernel, whose other warps stream weights meanwhile).
+struct CtaGroup {
+	__device__ static uint32_t tid() { return threadIdx.x; }
+	__device__ static uint32_t size() { return blockDim.x; }
+	__device__ static void sync() { __syncthreads(); }
+};
+
+template <int W0, int NW, int BAR>
+struct WarpGroup {
+	__device__ static uint32_t tid() { return threadIdx.x - W0 * 32; }
+	__device__ static constexpr uint32_t size() { return NW * 32; }
+	__device__ static void sync()
+	{
+		asm volatile("bar.sync %0, %1;" :: "n"(BAR), "n"(NW * 32) : "memory");
+	}
+};
+
 // charsiu_act_set of one 32-block held one element a lane (src/gguf.c:852-881):
 // amax by max (order-free), d = amax / 127, q = round-to-nearest-even of
 // v * (1 / d). Lane 0 writes d.
@@ -117,10 +136,10 @@ __device__ __forceinline__ uint32_t binade_field(float v)
 	return (__float_as_uint(v) >> 23) & 0xffu;
 }
 
-template <int EPT>
+template <int EPT, class G = CtaGroup>
 __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &sh)
 {
-	const uint32_t tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
+	const uint32_t tid = G::tid(), nt = G::size(), lane = tid & 31, wid = tid >> 5;
 	const uint32_t ept = (n + nt - 1) / nt;
 	const uint32_t i0 = tid * ept;
 	float v[EPT];
@@ -153,7 +172,7 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 		sh.wf[wid] = inc;
 		sh.wbad[wid] = bad;
 	}
-	__syncthreads();
+	G::sync();
 	// every warp turns the warp totals into the warps' starting values itself
 	// (the same operations on the same values in every warp, so the same bits:
 	// warp w starts at woff(w), which the last lane of warp w - 1 also uses)
@@ -173,7 +192,7 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 	if (bad) {
 		if (tid == 0)
 			sh.result = ordered_sum_seq(t, n);
-		__syncthreads();
+		G::sync();
 		return sh.result;
 	}
 	const float w_start = wid ? __shfl_sync(0xffffffffu, woff_in, wid - 1) : 0.0f;
@@ -224,7 +243,7 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 	unsigned long long qex = qinc - lsum;
 	if (lane == 31)
 		sh.wq[wid] = qinc;
-	__syncthreads();
+	G::sync();
 	// (again every warp scans the warp totals itself)
 	unsigned long long q_all;
 	{
@@ -262,7 +281,7 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 		}
 		qex += pk[k];
 	}
-	__syncthreads();
+	G::sync();
 
 	// 3. warp 0: each lane prepares crossings lane and lane + 32 -- the run of
 	//    grid terms before it (its offset, and what its ties add for either
@@ -334,7 +353,7 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 			sh.result = s;
 		}
 	}
-	__syncthreads();
+	G::sync();
 	return sh.result;
 }
 
@@ -343,11 +362,12 @@ __device__ float ordered_sum_nonneg_cta(const float *t, uint32_t n, OsumShared &
 // of xs[i]^2 (the CTA's exact form, ordered_sum_nonneg_cta), and the returned
 // scale = 1 / sqrtf(ss / n + eps) (through *scale_sh, a shared float). xs, sq:
 // n floats each of shared memory, 16-byte aligned. Ends with a barrier.
+template <class G = CtaGroup>
 __device__ __forceinline__ float norm_scale_cta(const float *__restrict__ x,
 						const float *__restrict__ add, uint32_t n,
 						float eps, float *xs, float *sq, float *scale_sh)
 {
-	for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+	for (uint32_t i = G::tid(); i < n; i += G::size()) {
 		float v = x[i];
 		if (add)
 			v = __fadd_rn(v, add[i]);
@@ -355,13 +375,13 @@ __device__ __forceinline__ float norm_scale_cta(const float *__restrict__ x,
 		sq[i] = __fmul_rn(v, v);
 	}
 	cp_async_wait_all();
-	__syncthreads();
+	G::sync();
 	__shared__ OsumShared osum;
-	const float ss = n <= 4 * blockDim.x ? ordered_sum_nonneg_cta<4>(sq, n, osum)
-					     : ordered_sum_nonneg_cta<16>(sq, n, osum);
-	if (threadIdx.x == 0)
+	const float ss = n <= 4 * G::size() ? ordered_sum_nonneg_cta<4, G>(sq, n, osum)
+					    : ordered_sum_nonneg_cta<16, G>(sq, n, osum);
+	if (G::tid() == 0)
 		*scale_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-	__syncthreads();
+	G::sync();
 	return *scale_sh;
 }
 
@@ -403,14 +423,15 @@ __device__ __forceinline__ void quantise_one_cta(V val, uint32_t n, uint32_t kp,
 // v = xs[i] * scale * w[i] into aq / ad, one warp a 32-block. ws: n floats
 // of shared memory holding w already (copied in by the caller). Ends with a
 // barrier; xs still holds x + add.
+template <class G = CtaGroup>
 __device__ __forceinline__ void norm_quant_cta(const float *__restrict__ x,
 					       const float *__restrict__ add, uint32_t n, float eps,
 					       float *xs, float *sq, const float *ws, float *scale_sh,
 					       int8_t *aq, float *ad)
 {
-	const float scale = norm_scale_cta(x, add, n, eps, xs, sq, scale_sh);
-	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const uint32_t nw = blockDim.x / 32;
+	const float scale = norm_scale_cta<G>(x, add, n, eps, xs, sq, scale_sh);
+	const int warp = G::tid() >> 5, lane = G::tid() & 31;
+	const uint32_t nw = G::size() / 32;
 	uint32_t b = warp;
 	// four blocks of a warp at a time, their reductions and divisions
 	// interleaved (blocks b, b + nw, b + 2 nw, b + 3 nw)
@@ -441,7 +462,7 @@ __device__ __forceinline__ void norm_quant_cta(const float *__restrict__ x,
 		quantise_block_warp(__fmul_rn(__fmul_rn(xs[i], scale), ws[i]), lane, aq + b * 32,
 				    ad + b);
 	}
-	__syncthreads();
+	G::sync();
 }
 
 } // namespace cgpu
