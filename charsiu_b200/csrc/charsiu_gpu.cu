@@ -146,6 +146,7 @@ struct charsiu_gpu {
 	QmvInline<QMV_INLINE_MAX_WORDS> *inl = nullptr;    // the direct call's kernel arguments
 	bool direct = true;  // CHARSIU_GPU_DIRECT=0: every host call through a graph with copies
 	bool smem_set[64] = {};
+	uint8_t *noalloc_scratch = nullptr;  // the allocation-free call's array, on this device
 	// CTAs per SM for (m, nb): asked of the driver once, never during capture
 	std::vector<std::pair<uint64_t, int>> occ;
 
@@ -967,23 +968,21 @@ static constexpr size_t NOALLOC_SCRATCH_BYTES = (size_t)1 << 20;
 static __device__ __align__(256) uint8_t noalloc_scratch[NOALLOC_SCRATCH_BYTES];
 
 // In host code `noalloc_scratch` is only a stand-in for the device array, so
-// its device address is looked up once per device (with that device current)
-// and passed to the kernels.
-static uint8_t *noalloc_scratch_addr[256];
-
-static uint8_t *noalloc_scratch_on(int device)
+// its device address is looked up (with the layer's device current) by each
+// layer's first allocation-free call and kept in that layer: a layer opened
+// after a device reset looks it up afresh, and no table is shared between
+// threads.
+static uint8_t *noalloc_scratch_of(charsiu_gpu *g)
 {
-	if (device < 0 || device >= 256)
-		return nullptr;
-	if (!noalloc_scratch_addr[device]) {
+	if (!g->noalloc_scratch) {
 		void *ptr = nullptr;
 		if (cudaGetSymbolAddress(&ptr, noalloc_scratch) != cudaSuccess) {
 			cudaGetLastError();
 			return nullptr;
 		}
-		noalloc_scratch_addr[device] = static_cast<uint8_t *>(ptr);
+		g->noalloc_scratch = static_cast<uint8_t *>(ptr);
 	}
-	return noalloc_scratch_addr[device];
+	return g->noalloc_scratch;
 }
 
 extern "C" {
@@ -1527,7 +1526,7 @@ int charsiu_gpu_matvec_batch_noalloc(struct charsiu_gpu *g, int id, unsigned m, 
 		return -1;
 	}
 	cudaSetDevice(g->device);
-	uint8_t *scratch = noalloc_scratch_on(g->device);
+	uint8_t *scratch = noalloc_scratch_of(g);
 	if (!scratch) {
 		whine(g, "the allocation-free scratch has no device address on device %d", g->device);
 		return -1;

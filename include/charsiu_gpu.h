@@ -208,10 +208,12 @@ CHARSIU_GPU_API int charsiu_gpu_matvec_gather_dev(struct charsiu_gpu *g, const i
  * every GPU that loads it until exit. q8_0 tensors only; the m activations
  * are packed in tiles of 16 or 32 and must fit that array (m <= 64 up to
  * K = 14336), else -1 with the reason in charsiu_gpu_error. All calls on a GPU
- * share the array, so two calls running on it at the same time race. The
- * first call on each GPU looks up the array's device address; make it before
- * any stream capture. Same results as charsiu_gpu_matvec_batch_dev, bit for
- * bit. No counterpart in the reference. */
+ * share the array, so two calls running on it at the same time race. A
+ * layer's first call looks up the array's device address (on the layer's
+ * GPU) and keeps it; make that call before any stream capture. Every m, from
+ * 1, runs on the tensor cores here (charsiu_gpu_matvec_batch_dev takes m
+ * below CHARSIU_GPU_QMM_MIN_M to the CUDA cores); both are gguf_matvec bit
+ * for bit, so the results are the same. No counterpart in the reference. */
 CHARSIU_GPU_API int charsiu_gpu_matvec_batch_noalloc(struct charsiu_gpu *g, int id, unsigned m,
 						     const int8_t *q, const float *d, float *y,
 						     void *stream);

@@ -36,7 +36,9 @@ def test_noalloc_matches_batch_dev_on_two_calls_in_a_row():
         tid = L.add_blocks(G.GGML_Q8_0, k, n, blk, "noalloc")
         stream = torch.cuda.current_stream().cuda_stream
         cases = []
-        for m, seed in ((48, 1), (9, 2)):       # tiles of 32, then of 16 activations
+        # tiles of 32, then of 16 activations; then 1 and 8, which the _dev
+        # form sends to the CUDA cores and this one to the tensor cores
+        for m, seed in ((48, 1), (9, 2), (1, 3), (8, 4)):
             q, d = _device_activations(torch, L, m, k, seed, dev, stream)
             ref = torch.full((m, n), float("nan"), device=dev)
             assert L.batch_dev(tid, m, q.data_ptr(), d.data_ptr(), ref.data_ptr(), stream) == 0
@@ -65,5 +67,29 @@ def test_noalloc_refuses_what_the_scratch_cannot_hold():
         d = torch.zeros((m, k // 32), dtype=torch.float32, device=dev)
         y = torch.zeros((m, n), dtype=torch.float32, device=dev)
         assert L.batch_noalloc(tid, m, q.data_ptr(), d.data_ptr(), y.data_ptr()) == -1
+        assert "allocation-free" in L.error()
+        assert not L.dead
+
+
+def test_noalloc_at_the_limit_and_one_past_it():
+    """The documented largest case, 64 activations at K = 14336 (1,032,192 of
+    the 1,048,576 bytes), runs and matches the _dev form; 65 activations are
+    refused with the layer left alive."""
+    torch = pytest.importorskip("torch")
+    k, n = 14336, 40
+    dev = torch.device("cuda:0")
+    with Layer(max_k=k, max_n=n, max_tensors=2) as L:
+        blk, _ = W.matvec_inputs(G.GGML_Q8_0, k, n, seed=33)
+        tid = L.add_blocks(G.GGML_Q8_0, k, n, blk, "limit")
+        stream = torch.cuda.current_stream().cuda_stream
+        q, d = _device_activations(torch, L, 65, k, 5, dev, stream)
+        ref = torch.full((64, n), float("nan"), device=dev)
+        y = torch.full((64, n), float("nan"), device=dev)
+        assert L.batch_dev(tid, 64, q.data_ptr(), d.data_ptr(), ref.data_ptr(), stream) == 0
+        assert L.batch_noalloc(tid, 64, q.data_ptr(), d.data_ptr(), y.data_ptr(), stream) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.cpu().numpy().view(np.uint32))
+        y65 = torch.zeros((65, n), dtype=torch.float32, device=dev)
+        assert L.batch_noalloc(tid, 65, q.data_ptr(), d.data_ptr(), y65.data_ptr(), stream) == -1
         assert "allocation-free" in L.error()
         assert not L.dead
