@@ -525,6 +525,43 @@ def run_decode(path, args, world, dist, dev, sample_clocks):
     return total_ms / args.steps, match, clk, launches
 
 
+def sharded_paths(gg, dev, rank, world, dist, barrier, args):
+    """The column splits of the workload over the world's GPUs, each checked
+    bit for bit against one GPU: the 128256-wide head alone, and one stream's
+    65 launches, with NCCL all-gathers and with the fused matvec + gather."""
+    sharded = {"head": head_split(gg, dev, rank, world, dist, barrier)}
+    # one decode stream's hot path, every tensor column-split
+    cs = TokenChain(gg, dev, rank, world, dist)
+    ms_split, _ = time_chain(cs, max(1, min(args.steps, 200)), 3, barrier, dist, world, dev,
+                             True, False)
+    cs.close()
+    sharded["token_chain_nccl"] = {
+        "value": round(1000.0 / ms_split, 2), "unit": UNIT, "ms_per_step": round(ms_split, 5),
+        "workload": f"one stream's 65 launches, every tensor column-split over {world} "
+                    "GPUs, one NCCL all-gather per launch group, a CUDA graph a token"}
+    fused = {"workload": "the same split, each launch storing its rows into every "
+                         "rank's outputs over NVLink and waiting on arrival counters "
+                         "(matvec and all-gather in one kernel), a CUDA graph a token; "
+                         "every output checked against the one-GPU chain"}
+    try:
+        single = TokenChain(gg, dev)
+        time_chain(single, 3, 1, barrier, dist, world, dev, False, False)
+        want = single.outputs()
+        single.close()
+        fz = TokenChain(gg, dev, rank, world, dist, fused=True)
+        ms_fused, _ = time_chain(fz, max(1, min(args.steps, 500)), 5, barrier, dist, world,
+                                 dev, True, False)
+        ok = all_ranks(same_bits(fz.outputs(), want), world, dist, dev)
+        fz.close()
+        fused.update(value=round(1000.0 / ms_fused, 2), unit=UNIT,
+                     ms_per_step=round(ms_fused, 5), split_matches_single=ok)
+    except (RuntimeError, AssertionError) as e:   # reported, not fatal to the headline
+        fused["error"] = str(e)[:200]
+    sharded["token_chain_fused"] = fused
+
+    return sharded
+
+
 def run_ours(args, rank, world, dist):
     import torch
     from charsiu_b200.lib import lib
@@ -565,37 +602,7 @@ def run_ours(args, rank, world, dist):
                             "head in 65 matvec launches, fixed activations, 1.31 GB of "
                             "weights a token, no norms/attention between them"}
 
-    sharded = None
-    if world > 1:
-        sharded = {"head": head_split(gg, dev, rank, world, dist, barrier)}
-        # one decode stream's hot path, every tensor column-split
-        cs = TokenChain(gg, dev, rank, world, dist)
-        ms_split, _ = time_chain(cs, max(1, min(args.steps, 200)), 3, barrier, dist, world, dev,
-                                 True, False)
-        cs.close()
-        sharded["token_chain_nccl"] = {
-            "value": round(1000.0 / ms_split, 2), "unit": UNIT, "ms_per_step": round(ms_split, 5),
-            "workload": f"one stream's 65 launches, every tensor column-split over {world} "
-                        "GPUs, one NCCL all-gather per launch group, a CUDA graph a token"}
-        fused = {"workload": "the same split, each launch storing its rows into every "
-                             "rank's outputs over NVLink and waiting on arrival counters "
-                             "(matvec and all-gather in one kernel), a CUDA graph a token; "
-                             "every output checked against the one-GPU chain"}
-        try:
-            single = TokenChain(gg, dev)
-            time_chain(single, 3, 1, barrier, dist, world, dev, False, False)
-            want = single.outputs()
-            single.close()
-            fz = TokenChain(gg, dev, rank, world, dist, fused=True)
-            ms_fused, _ = time_chain(fz, max(1, min(args.steps, 500)), 5, barrier, dist, world,
-                                     dev, True, False)
-            ok = all_ranks(same_bits(fz.outputs(), want), world, dist, dev)
-            fz.close()
-            fused.update(value=round(1000.0 / ms_fused, 2), unit=UNIT,
-                         ms_per_step=round(ms_fused, 5), split_matches_single=ok)
-        except (RuntimeError, AssertionError) as e:   # reported, not fatal to the headline
-            fused["error"] = str(e)[:200]
-        sharded["token_chain_fused"] = fused
+    sharded = sharded_paths(gg, dev, rank, world, dist, barrier, args) if world > 1 else None
 
     batched = batched_steps(gg, dev, rank, world, dist, barrier)
 
@@ -1258,6 +1265,8 @@ def main():
                     help="time only the token's 65 matvec launches (the roofline's chain)")
     ap.add_argument("--decode", action="store_true",
                     help="time only the headline decode (inputs resident, device-side loop)")
+    ap.add_argument("--sharded", action="store_true",
+                    help="at N > 1: only the column splits (head, token chain, batched)")
     ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N[:M]",
                     help="time one matvec shape instead of the decode (e.g. q8_0:2048:8192; "
                          "q8_0:2048:8192:64 for 64 activations)")
@@ -1299,6 +1308,17 @@ def main():
             return
         if args.npu:
             emit(run_npu_case(args))
+            return
+        if args.sharded and world > 1:
+            import torch
+            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+            torch.cuda.set_device(dev)
+            barrier = lambda: dist.barrier()
+            gg = G.GGUFFile(model_path(rank, barrier))
+            out = {"sharded": sharded_paths(gg, dev, rank, world, dist, barrier, args),
+                   "batched": batched_steps(gg, dev, rank, world, dist, barrier)}
+            if rank == 0:
+                emit(out)
             return
         if args.hot_path or args.decode:
             import torch

@@ -159,6 +159,13 @@ struct charsiu_gpu {
 	// start once all its CTAs have started, not once they have staged the
 	// activation (1B decode step 0.653 -> 0.626 ms, token chain 0.302 -> 0.295)
 	int pdl_early = 1;
+	// CHARSIU_GPU_GATHER_PDL (default 1): the fused matvec + gather launches
+	// with programmatic dependence too. Its CTAs then start while the launch
+	// before is still running on this GPU and load their first weights; each
+	// waits for that launch to finish (griddepcontrol.wait) before it waits
+	// on the other ranks' arrivals, so it never waits on a kernel of its own
+	// GPU that might not be running.
+	int gather_pdl = 1;
 	uint32_t qmm_na = 0;   // CHARSIU_GPU_QMM_NA: activations a tensor-core tile (16, 32; 0 = by m)
 	bool qmm_pre = false;  // CHARSIU_GPU_QMM_PRE=1: the MMA adds the float-bias constant (slower)
 	// CHARSIU_GPU_QMM_MIN_M: q8_0 batches of fewer activations run on the CUDA
@@ -395,9 +402,9 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
 	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 	cfg.attrs = attr;
-	cfg.numAttrs = g->no_pdl || gth ? 0 : 1;
+	cfg.numAttrs = g->no_pdl || (gth && !g->gather_pdl) ? 0 : 1;
 	QmvParams arg = p;
-	arg.early_trigger = g->pdl_early && !gth ? 1u : 0u;
+	arg.early_trigger = g->pdl_early && (!gth || g->gather_pdl) ? 1u : 0u;
 	if (inl)
 		reinterpret_cast<QmvParams *>(const_cast<void *>(inl))->early_trigger =
 			arg.early_trigger;
@@ -1019,6 +1026,8 @@ struct charsiu_gpu *charsiu_gpu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	g->no_pdl = getenv("CHARSIU_GPU_NO_PDL") != nullptr;
 	if (const char *e = getenv("CHARSIU_GPU_PDL_EARLY"))
 		g->pdl_early = atoi(e) != 0;
+	if (const char *e = getenv("CHARSIU_GPU_GATHER_PDL"))
+		g->gather_pdl = atoi(e) != 0;
 	if (const char *dir = getenv("CHARSIU_GPU_DIRECT"))
 		g->direct = strcmp(dir, "0") != 0;
 	if (const char *na = getenv("CHARSIU_GPU_QMM_NA"))
@@ -1445,8 +1454,16 @@ int charsiu_gpu_gather_epoch_dev(struct charsiu_gpu *g, uint32_t *sync_local, vo
 	if (!g || g->dead || !sync_local)
 		return -1;
 	cudaSetDevice(g->device);
-	gather_epoch_kernel<<<1, 32, 0, stream ? (cudaStream_t)stream : g->stream>>>(sync_local);
-	if (cudaGetLastError() != cudaSuccess)
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = dim3(1);
+	cfg.blockDim = dim3(32);
+	cfg.stream = stream ? (cudaStream_t)stream : g->stream;
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = attr;
+	cfg.numAttrs = g->no_pdl || !g->gather_pdl ? 0 : 1;
+	if (cudaLaunchKernelEx(&cfg, gather_epoch_kernel, sync_local) != cudaSuccess)
 		return -1;
 	g->launches++;
 	return 0;

@@ -83,8 +83,13 @@ __device__ __forceinline__ void red_release_sys_add(uint32_t *p, uint32_t v)
 	asm volatile("red.release.sys.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
 }
 
+// Launched with programmatic dependence, it lets the next launch start at
+// once (that one's weights then stream in meanwhile) and adds to the epoch
+// only once the launch before it -- whose CTAs read the epoch -- is done.
 __global__ void gather_epoch_kernel(uint32_t *sync_local)
 {
+	pdl_launch_dependents();
+	pdl_wait();
 	if (threadIdx.x == 0 && blockIdx.x == 0)
 		sync_local[0] += 1;
 }
