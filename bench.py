@@ -282,12 +282,12 @@ class BatchChain:
     rows for all M sequences) and each group's slabs all-gathered with one
     NCCL collective, so every rank holds the whole batch's outputs."""
 
-    def __init__(self, gg, m, dev, rank=0, world=1, dist=None):
+    def __init__(self, gg, m, dev, rank=0, world=1, dist=None, fused=False):
         import torch
         from charsiu_b200.lib import Layer
 
         self.torch, self.dist, self.m = torch, dist, m
-        self.gg, self.world = gg, world
+        self.gg, self.world, self.rank = gg, world, rank
         self.groups = launch_groups(SHAPE)
         names = [nm for g, _ in self.groups for nm in g]
         self.layer = Layer(max_k=max(SHAPE.n_embd, SHAPE.n_ff), max_n=SHAPE.n_vocab,
@@ -318,11 +318,37 @@ class BatchChain:
             self.full.append(torch.zeros(world * sum(sizes), dtype=torch.float32, device=dev)
                              if world > 1 else None)
         self.weight_bytes = sum(gg.tensors[nm].nbytes for nm in names)
+        self.fused = fused and world > 1
+        if self.fused:
+            # this rank's full [M][N] outputs and sync words, shared by IPC
+            # handle; every launch stores its rows into every rank's
+            L = self.layer
+            self.mine = [[L.ipc_alloc(4 * m * gg.tensors[nm].n) for nm in g]
+                         for g, _ in self.groups]
+            self.mine_sync = L.ipc_alloc(4 * (len(self.groups) + 8))
+            own = [[L.ipc_handle(p) for p in row] for row in self.mine] + \
+                [[L.ipc_handle(self.mine_sync)]]
+            allh = [None] * world
+            dist.all_gather_object(allh, own)
+            self.peer = {r: [[L.ipc_open(h) for h in row] for row in allh[r]]
+                         for r in range(world) if r != rank}
+            view = lambda r: (self.mine + [[self.mine_sync]]) if r == rank else self.peer[r]
+            self.syncs = [view(r)[-1][0] for r in range(world)]
+            self.flat = [[view(r)[j][i] for r in range(world) for i in range(len(g))]
+                         for j, (g, _) in enumerate(self.groups)]
+            dist.barrier()
 
     def outputs(self):
         """Every tensor's [M][N] outputs as this rank holds them after a step
         (the gathered slabs reassembled when world > 1)."""
         m, out = self.m, []
+        if self.fused:
+            for j, (g, _) in enumerate(self.groups):
+                for i, nm in enumerate(g):
+                    y = np.zeros((m, self.gg.tensors[nm].n), np.float32)
+                    self.layer.read_device(self.mine[j][i], y)
+                    out.append(y)
+            return out
         for (g, _), (buf, _), full in zip(self.groups, self.bufs, self.full):
             ns = [self.gg.tensors[nm].n for nm in g]
             w = self.world
@@ -339,6 +365,19 @@ class BatchChain:
         return out
 
     def token(self, stream):
+        if self.fused:
+            L, last = self.layer, len(self.groups) - 1
+            assert L.gather_epoch_dev(self.mine_sync, stream.cuda_stream) == 0
+            for j, (g, k) in enumerate(self.groups):
+                q, d = self.acts[k]
+                prev = j - 1 if j else last      # launch 0 waits for the last step's head
+                rc = L.batch_gather_dev([self.ids[nm] for nm in g], self.m, q.data_ptr(),
+                                        d.data_ptr(), self.flat[j], self.syncs,
+                                        signal_idx=1 + j, wait_idx=1 + prev,
+                                        wait_mult=self.world, wait_adj=0 if j else -1,
+                                        stream=stream.cuda_stream)
+                assert rc == 0, L.error()
+            return
         for (g, k), (buf, ptrs), full in zip(self.groups, self.bufs, self.full):
             q, d = self.acts[k]
             rc = self.layer.batch_group_dev([self.ids[nm] for nm in g], self.m, q.data_ptr(),
@@ -348,6 +387,20 @@ class BatchChain:
                 self.dist.all_gather_into_tensor(full, buf)
 
     def close(self):
+        if self.fused:
+            self.torch.cuda.synchronize()
+            if self.layer.kernel_error():
+                raise RuntimeError("a fused-gather wait gave up: " + self.layer.error())
+            self.dist.barrier()
+            for rows in self.peer.values():
+                for row in rows:
+                    for p in row:
+                        self.layer.ipc_free(p, True)
+            self.dist.barrier()
+            for row in self.mine:
+                for p in row:
+                    self.layer.ipc_free(p, False)
+            self.layer.ipc_free(self.mine_sync, False)
         self.layer.close()
 
 
@@ -390,13 +443,24 @@ def batched_steps(gg, dev, rank, world, dist, barrier, ms=(8, 32, 64), steps=50,
             row = {"value": round(m * 1000.0 / ms_step, 1), "unit": UNIT,
                    "ms_per_step": round(ms_step, 5), "split_matches_single": ok,
                    "single_gpu": row}
+            if m >= 9:
+                # the same split, the tensor-core epilogue storing every rank's
+                # rows over NVLink (no NCCL)
+                fz = BatchChain(gg, m, dev, rank, world, dist, fused=True)
+                ms_f, _ = time_chain(fz, steps, warmup, barrier, dist, world, dev, True, False)
+                okf = all_ranks(same_bits(fz.outputs(), want), world, dist, dev)
+                fz.close()
+                row["fused"] = {"value": round(m * 1000.0 / ms_f, 1), "unit": UNIT,
+                                "ms_per_step": round(ms_f, 5), "split_matches_single": okf}
         out[f"m{m}"] = row
     out["workload"] = ("one decode step of M sequences: the 112 projections and the head as "
                        "grouped batched matvecs (tcgen05 kind::i8 from M = 9, the CUDA cores "
                        f"below), {steps} steps as CUDA graph replays" +
                        (f"; value: every tensor column-split over {world} GPUs and each "
-                        "group's slabs NCCL-all-gathered, checked bit for bit against the "
-                        "one-GPU step (single_gpu)" if world > 1 else ""))
+                        "group's slabs NCCL-all-gathered; fused (M >= 9): the tensor-core "
+                        "epilogue stores every rank's rows into every rank's outputs over "
+                        "NVLink, arrival counters instead of NCCL; each checked bit for bit "
+                        "against the one-GPU step (single_gpu)" if world > 1 else ""))
     return out
 
 

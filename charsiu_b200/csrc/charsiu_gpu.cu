@@ -457,7 +457,8 @@ size_t qmm_pack_bytes(uint32_t na, uint32_t m, uint32_t nb)
 }
 
 int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, const float *d,
-	       uint32_t m, float *const *ys, uint8_t *pack, cudaStream_t st)
+	       uint32_t m, float *const *ys, uint8_t *pack, cudaStream_t st,
+	       const QmmGather *gth = nullptr)
 {
 	if (!n || n > (unsigned)QMM_MAX_TENSORS)
 		return -1;
@@ -527,7 +528,8 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	cfg.stream = st;
 	cfg.attrs = attr;
 	cfg.numAttrs = g->no_pdl ? 0 : 1;
-	void *args[1] = {&p};
+	QmmGather garg = gth ? *gth : QmmGather{};
+	void *args[2] = {&p, &garg};
 	if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess)
 		return -1;
 	g->launches++;
@@ -1447,6 +1449,56 @@ int charsiu_gpu_kernel_error(struct charsiu_gpu *g)
 		retire(g, "a kernel wait gave up");
 	}
 	return e;
+}
+
+int charsiu_gpu_matvec_batch_gather_dev(struct charsiu_gpu *g, const int *ids, unsigned n,
+					unsigned m, const int8_t *q, const float *d,
+					float *const *full_ys, uint32_t *const *syncs,
+					unsigned signal_idx, unsigned wait_idx, unsigned wait_mult,
+					int wait_adj, void *stream)
+{
+	if (!g || g->dead || !ids || !q || !d || !full_ys || !syncs || ((uintptr_t)q & 15) ||
+	    g->world > (unsigned)QMM_MAX_RANKS || !n || n > (unsigned)QMM_MAX_TENSORS ||
+	    m < g->qmm_min_m)
+		return -1;
+	for (unsigned i = 0; i < n; i++)
+		if (ids[i] < 0 || (size_t)ids[i] >= g->ent.size() ||
+		    g->ent[ids[i]].type != TYPE_Q8_0 || g->ent[ids[i]].k != g->ent[ids[0]].k)
+			return -1;
+	cudaSetDevice(g->device);
+	QmmGather gth = {};
+	for (unsigned r = 0; r < g->world; r++) {
+		if (!syncs[r])
+			return -1;
+		gth.sync[r] = syncs[r];
+		for (unsigned i = 0; i < n; i++) {
+			if (!full_ys[r * n + i])
+				return -1;
+			gth.y[r][i] = full_ys[r * n + i];
+		}
+	}
+	for (unsigned i = 0; i < n; i++) {
+		gth.row0[i] = (uint32_t)g->ent[ids[i]].row0;
+		gth.ncols[i] = (uint32_t)g->ent[ids[i]].n;
+	}
+	if (!g->d_gather_count) {
+		if (cudaMalloc((void **)&g->d_gather_count, sizeof(uint32_t)) != cudaSuccess ||
+		    cudaMemset(g->d_gather_count, 0, sizeof(uint32_t)) != cudaSuccess)
+			return -1;
+	}
+	gth.cta_count = g->d_gather_count;
+	gth.world = g->world;
+	gth.rank = g->rank;
+	gth.signal_idx = signal_idx;
+	gth.wait_idx = wait_idx;
+	gth.wait_mult = wait_mult;
+	gth.wait_adj = wait_adj;
+	const uint32_t nb = g->ent[ids[0]].nb;
+	if (!grow_dev(g->d_pack, g->cap_pack, qmm_pack_bytes(qmm_na(g, m), m, nb)))
+		return -1;
+	float *unused[QMM_MAX_TENSORS] = {};
+	return launch_qmm(g, ids, n, q, d, m, unused, g->d_pack,
+			  stream ? (cudaStream_t)stream : g->stream, &gth);
 }
 
 int charsiu_gpu_gather_epoch_dev(struct charsiu_gpu *g, uint32_t *sync_local, void *stream)

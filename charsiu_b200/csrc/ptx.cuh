@@ -111,6 +111,20 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *addr, uint32_
 	return old;
 }
 
+// system-scope acquire load and release add: the arrival words other GPUs
+// write over NVLink (the matvecs fused with their all-gather)
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
+{
+	uint32_t v;
+	asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+	return v;
+}
+
+__device__ __forceinline__ void red_release_sys_add(uint32_t *p, uint32_t v)
+{
+	asm volatile("red.release.sys.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
 // sum of four (unsigned byte of a) * (signed byte of b), plus c
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)
 {

@@ -140,9 +140,29 @@ struct QmmParams {
 	int *err;
 };
 
+// The batched matvec fused with its all-gather (every tensor column-split
+// over `world` GPUs, one process a GPU), as qmv1.cuh does it for one
+// activation: each y this rank computes is stored straight into every rank's
+// full output y[r][tensor] ([m][ncols], at column row0 + row) over NVLink;
+// once all this launch's CTAs are done, the last adds 1 to word signal_idx of
+// every rank's sync array (a system-scope release). With wait_mult > 0 the
+// producer first waits, before it copies the activations in, until its own
+// word wait_idx reaches (epoch + wait_adj) * wait_mult, the epoch being word
+// 0 (gather_epoch_kernel). world 0: no gather.
+constexpr int QMM_MAX_RANKS = 8;
+
+struct QmmGather {
+	float *y[QMM_MAX_RANKS][QMM_MAX_TENSORS];
+	uint32_t *sync[QMM_MAX_RANKS];
+	uint32_t *cta_count;            // this GPU's: CTAs done, zero between launches
+	uint32_t row0[QMM_MAX_TENSORS], ncols[QMM_MAX_TENSORS];
+	uint32_t world, rank, signal_idx, wait_idx, wait_mult;
+	int32_t wait_adj;
+};
+
 template <int NA, int EC, bool PRE>
 __global__ void __launch_bounds__(qmm_threads(EC), 1)
-qmm_tc_kernel(const __grid_constant__ QmmParams p)
+qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGather gth)
 {
 	constexpr int CW = QMM_EPI_COLS;                   // activations an epilogue warp
 	constexpr int EW = 4 * (EC / CW);                  // epilogue warps
@@ -224,9 +244,25 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 							 wbytes, &full[st]);
 					if (!waited_act) {
 						// weights never depend on the kernel before; the
-						// packed activations do
+						// packed activations do (and, fused with the
+						// gather, the other ranks' part of them)
 						pdl_wait();
 						waited_act = 1;
+						if (gth.wait_mult) {
+							const uint32_t *syn = gth.sync[gth.rank];
+							const uint32_t target =
+								(uint32_t)((int32_t)ld_acquire_sys(&syn[0]) +
+									   gth.wait_adj) * gth.wait_mult;
+							const uint64_t w0 = globaltimer_ns();
+							while ((int32_t)(ld_acquire_sys(&syn[gth.wait_idx]) -
+									 target) < 0) {
+								if (globaltimer_ns() - w0 > WAIT_LIMIT_NS) {
+									*(volatile int *)p.err = 13;
+									break;
+								}
+								__nanosleep(64);
+							}
+						}
 					}
 					bulk_g2s(stage_a(st), act + (uint64_t)s * ASEG, ASEG, &full[st]);
 				}
@@ -431,8 +467,16 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 #pragma unroll
 				for (int c = 0; c < CW; c++) {
 					const uint32_t a = a0 + c;
-					if (a < p.m)
-						T.y[(uint64_t)a * T.rows + row] = c & 1 ? hi2(acc[c / 2]) : lo2(acc[c / 2]);
+					const float v = c & 1 ? hi2(acc[c / 2]) : lo2(acc[c / 2]);
+					if (a >= p.m)
+						continue;
+					if (gth.world) {
+						for (uint32_t r = 0; r < gth.world; r++)
+							gth.y[r][ti][(uint64_t)a * gth.ncols[ti] + gth.row0[ti] +
+								     row] = v;
+					} else {
+						T.y[(uint64_t)a * T.rows + row] = v;
+					}
 				}
 			}
 		}
@@ -441,6 +485,16 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p)
 	__syncthreads();
 	if (warp == 1)
 		tmem_dealloc(taddr, NCOLS);
+	// every rank's stores of this CTA (peer ones included) reach thread 0
+	// through the barrier and are released at device scope by its count; the
+	// last CTA acquires them all and, after one system fence, tells every rank
+	if (gth.world && threadIdx.x == 0 &&
+	    atom_add_acq_rel_gpu(gth.cta_count, 1u) == gridDim.x - 1) {
+		*gth.cta_count = 0;
+		__threadfence_system();
+		for (uint32_t r = 0; r < gth.world; r++)
+			red_release_sys_add(gth.sync[r] + gth.signal_idx, 1u);
+	}
 }
 
 } // namespace cgpu

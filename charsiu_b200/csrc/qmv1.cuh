@@ -71,18 +71,6 @@ struct QmvGather {
 	int32_t wait_adj;                           // (wait_mult 0: no wait)
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
-{
-	uint32_t v;
-	asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-	return v;
-}
-
-__device__ __forceinline__ void red_release_sys_add(uint32_t *p, uint32_t v)
-{
-	asm volatile("red.release.sys.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
-}
-
 // Launched with programmatic dependence, it lets the next launch start at
 // once (that one's weights then stream in meanwhile) and adds to the epoch
 // only once the launch before it -- whose CTAs read the epoch -- is done.

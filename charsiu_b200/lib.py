@@ -52,6 +52,9 @@ SIGNATURES = [
     ("charsiu_gpu_read_device", C.c_int, [_vp, _vp, _vp, C.c_size_t]),
     ("charsiu_gpu_matvec_gather_dev", C.c_int,
      [_vp, _vp, C.c_uint, _vp, _vp, _vp, _vp, C.c_uint, C.c_uint, C.c_uint, C.c_int, _vp]),
+    ("charsiu_gpu_matvec_batch_gather_dev", C.c_int,
+     [_vp, _vp, C.c_uint, C.c_uint, _vp, _vp, _vp, _vp, C.c_uint, C.c_uint, C.c_uint, C.c_int,
+      _vp]),
     ("charsiu_gpu_matvec_batch_noalloc", C.c_int, [_vp, C.c_int, C.c_uint, _vp, _vp, _vp, _vp]),
     ("charsiu_gpu_act_quantise_dev", C.c_int, [_vp, _vp, C.c_uint, C.c_uint, _vp, _vp, _vp]),
     ("charsiu_gpu_calls", C.c_ulong, [_vp]),
@@ -302,6 +305,19 @@ class Layer:
                                                     d_ptr, C.addressof(farr), C.addressof(sarr),
                                                     signal_idx, wait_idx, wait_mult, wait_adj,
                                                     stream or None)
+
+    def batch_gather_dev(self, ids, m: int, q_ptr: int, d_ptr: int, full_ptrs, sync_ptrs,
+                         signal_idx: int, wait_idx: int = 0, wait_mult: int = 0,
+                         wait_adj: int = 0, stream: int = 0) -> int:
+        """The batched matvec fused with its all-gather; full_ptrs rank-major
+        [world][len(ids)] device pointers to [m][N] outputs."""
+        ids = list(ids)
+        idarr = (C.c_int * len(ids))(*ids)
+        farr = (C.c_void_p * len(full_ptrs))(*full_ptrs)
+        sarr = (C.c_void_p * len(sync_ptrs))(*sync_ptrs)
+        return self.L.charsiu_gpu_matvec_batch_gather_dev(
+            self.h, C.addressof(idarr), len(ids), m, q_ptr, d_ptr, C.addressof(farr),
+            C.addressof(sarr), signal_idx, wait_idx, wait_mult, wait_adj, stream or None)
 
     def batch_noalloc(self, tid: int, m: int, q_ptr: int, d_ptr: int, y_ptr: int,
                       stream: int = 0) -> int:

@@ -198,6 +198,19 @@ CHARSIU_GPU_API int charsiu_gpu_matvec_gather_dev(struct charsiu_gpu *g, const i
 						  float *const *full_ys, uint32_t *const *syncs,
 						  unsigned signal_idx, unsigned wait_idx,
 						  unsigned wait_mult, int wait_adj, void *stream);
+/* The batched form of charsiu_gpu_matvec_gather_dev: m activations (q [m][K]
+ * int8, d [m][K/32] fp32, m at least CHARSIU_GPU_QMM_MIN_M, so on the tensor
+ * cores) against n <= 8 q8_0 tensors of one K. Each rank's rows go straight
+ * into every rank's full output full_ys[r * n + i] ([m][N] floats) from the
+ * tensor-core epilogue; the waits and the arrival words are as above, except
+ * that each rank adds 1 a launch (so wait_mult is the world size). No
+ * counterpart in the reference. */
+CHARSIU_GPU_API int charsiu_gpu_matvec_batch_gather_dev(struct charsiu_gpu *g, const int *ids,
+							unsigned n, unsigned m, const int8_t *q,
+							const float *d, float *const *full_ys,
+							uint32_t *const *syncs, unsigned signal_idx,
+							unsigned wait_idx, unsigned wait_mult,
+							int wait_adj, void *stream);
 
 /* The batched matvec of charsiu_gpu_matvec_batch_dev, for callers that
  * cannot allocate GPU memory while they run -- a server whose own memory
