@@ -159,7 +159,8 @@ class TokenChain:
         self.torch, self.dev, self.world, self.dist = torch, dev, world, dist
         self.gg, self.rank = gg, rank
         self.groups = groups or launch_groups(SHAPE)
-        names = [nm for g, _ in self.groups for nm in g]
+        # (a tensor named in several launch groups is added once)
+        names = list(dict.fromkeys(nm for g, _ in self.groups for nm in g))
         self.layer = Layer(max_k=max(SHAPE.n_embd, SHAPE.n_ff), max_n=SHAPE.n_vocab,
                            max_tensors=len(names) + 1, device=dev.index, rank=rank, world=world)
         self.ids, self.rows = {}, {}
@@ -472,9 +473,14 @@ def head_split(gg, dev, rank, world, dist, barrier, steps=400):
     as one CUDA graph, each waiting for the previous one's gather; us a head,
     max over ranks; every rank's gathered head checked bit for bit against its
     one-GPU head."""
-    groups = [(["token_embd.weight"], SHAPE.n_embd)]
+    # HEADS heads a graph replay, so a replay's own launch gap is not a
+    # head's; every head a launch of its own, each after the last's gather
+    heads = 16
+    groups = [(["token_embd.weight"], SHAPE.n_embd)] * heads
+    reps = max(1, steps // heads)
     single = TokenChain(gg, dev, groups=groups)
-    ms1, _ = time_chain(single, steps, 5, barrier, dist, world, dev, True, False)
+    ms1, _ = time_chain(single, reps, 3, barrier, dist, world, dev, True, False)
+    ms1 /= heads
     want = single.outputs()
     single.close()
     hbytes = gg.tensors["token_embd.weight"].nbytes
@@ -483,15 +489,17 @@ def head_split(gg, dev, rank, world, dist, barrier, steps=400):
            "single_gpu_frac": round(hbytes / (ms1 * 1e-3) / 1e9 / peak, 4)}
     for key, fused in (("nccl", False), ("fused", True)):
         ch = TokenChain(gg, dev, rank, world, dist, fused=fused, groups=groups)
-        msn, _ = time_chain(ch, steps, 5, barrier, dist, world, dev, True, False)
+        msn, _ = time_chain(ch, reps, 3, barrier, dist, world, dev, True, False)
+        msn /= heads
         ok = all_ranks(same_bits(ch.outputs(), want), world, dist, dev)
         ch.close()
         res[key] = {"us": round(msn * 1e3, 3), "speedup_vs_single": round(ms1 / msn, 3),
                     "split_matches_single": ok}
     res["workload"] = (f"2048 -> 128256 q8_0 head ({hbytes / 1e6:.0f} MB), rows split in 8-row "
-                       f"groups over {world} GPUs, {steps} heads a CUDA graph, each after the "
-                       "last one's gather; nccl: matvec + all_gather_into_tensor; fused: one "
-                       "kernel, peer stores + arrival counters over NVLink")
+                       f"groups over {world} GPUs, {heads} heads a CUDA graph replayed {reps} "
+                       "times, each head after the last one's gather; nccl: matvec + "
+                       "all_gather_into_tensor; fused: one kernel, peer stores + arrival "
+                       "counters over NVLink")
     return res
 
 
