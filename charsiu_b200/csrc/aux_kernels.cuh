@@ -175,7 +175,28 @@ struct I8Params {
 constexpr int I8_TK = 64;
 constexpr int I8_PAD = I8_TK + 4;
 
-__global__ void __launch_bounds__(256) i8mm_simt_kernel(const __grid_constant__ I8Params p)
+// The operands of a small job carried in the launch's own parameters (a
+// direct host call): a [m][k] at byte 0, w [n][k] at off_w, bias [n] at off_b;
+// out is mapped host memory, and the last CTA to finish raises *done_flag =
+// seq once every byte of it is visible to the host.
+// The launch copies the whole parameter block, so the block comes in three
+// sizes (words of 16 bytes) and a job takes the smallest that holds it.
+constexpr uint32_t I8_INLINE_BYTES = 30 * 1024;
+
+template <int W>
+struct I8Inline {
+	I8Params p;
+	uint32_t off_w, off_b;
+	uint32_t *done_count;      // device, zero between launches
+	uint32_t *done_flag;       // mapped host memory
+	uint32_t seq;
+	uint4 data[W];
+};
+constexpr int I8_INLINE_W0 = 384, I8_INLINE_W1 = 1280, I8_INLINE_W2 = I8_INLINE_BYTES / 16;
+static_assert(sizeof(I8Inline<I8_INLINE_W2>) <= 32764, "kernel parameter space");
+
+__device__ __forceinline__ void i8mm_simt_body(const I8Params &p, const uint8_t *pa,
+					       const uint8_t *pw, const int32_t *pbias)
 {
 	__shared__ __align__(16) int8_t As[32][I8_PAD];
 	__shared__ __align__(16) int8_t Ws[32][I8_PAD];
@@ -188,8 +209,8 @@ __global__ void __launch_bounds__(256) i8mm_simt_kernel(const __grid_constant__ 
 			const int rr = i / I8_TK, kk = i % I8_TK;
 			const uint32_t gk = k0 + kk;
 			const uint32_t ma = m0 + rr, nw = n0 + rr;
-			As[rr][kk] = (ma < p.m && gk < p.k) ? (int8_t)(p.a[(uint64_t)ma * p.k + gk] ^ 0x80) : 0;
-			Ws[rr][kk] = (nw < p.n && gk < p.k) ? (int8_t)(p.w[(uint64_t)nw * p.k + gk] ^ 0x80) : 0;
+			As[rr][kk] = (ma < p.m && gk < p.k) ? (int8_t)(pa[(uint64_t)ma * p.k + gk] ^ 0x80) : 0;
+			Ws[rr][kk] = (nw < p.n && gk < p.k) ? (int8_t)(pw[(uint64_t)nw * p.k + gk] ^ 0x80) : 0;
 		}
 		__syncthreads();
 #pragma unroll 4
@@ -214,9 +235,32 @@ __global__ void __launch_bounds__(256) i8mm_simt_kernel(const __grid_constant__ 
 		const uint32_t row = m0 + ty + 8 * j;
 		if (row >= p.m)
 			continue;
-		const int64_t total = (int64_t)p.bias[col] + acc[j] + cw * sa[j] + ca * sw +
+		const int64_t total = (int64_t)pbias[col] + acc[j] + cw * sa[j] + ca * sw +
 				      (int64_t)p.k * ca * cw;
 		p.out[(uint64_t)row * p.n + col] = output_stage(total, p.mult, p.zp_out);
+	}
+}
+
+__global__ void __launch_bounds__(256) i8mm_simt_kernel(const __grid_constant__ I8Params p)
+{
+	i8mm_simt_body(p, p.a, p.w, p.bias);
+}
+
+template <int W>
+__global__ void __launch_bounds__(256)
+i8mm_simt_inline_kernel(const __grid_constant__ I8Inline<W> a)
+{
+	const uint8_t *base = reinterpret_cast<const uint8_t *>(a.data);
+	i8mm_simt_body(a.p, base, base + a.off_w, reinterpret_cast<const int32_t *>(base + a.off_b));
+	// out is host memory: this CTA's stores reach thread 0 through the barrier
+	// and are released at device scope by its count; the last CTA acquires
+	// them all and orders them before the flag with one system fence
+	__syncthreads();
+	if (threadIdx.x == 0 &&
+	    atom_add_acq_rel_gpu(a.done_count, 1u) == gridDim.x * gridDim.y - 1) {
+		*a.done_count = 0;
+		__threadfence_system();
+		*(volatile uint32_t *)a.done_flag = a.seq;
 	}
 }
 

@@ -144,6 +144,7 @@ struct charsiu_gpu {
 	uint32_t *d_flag = nullptr;
 	uint32_t seq = 0;
 	QmvInline<QMV_INLINE_MAX_WORDS> *inl = nullptr;    // the direct call's kernel arguments
+	I8Inline<I8_INLINE_W2> *i8inl = nullptr;            // and the int8 direct call's
 	bool direct = true;  // CHARSIU_GPU_DIRECT=0: every host call through a graph with copies
 	bool smem_set[64] = {};
 	uint8_t *noalloc_scratch = nullptr;  // the allocation-free call's array, on this device
@@ -701,45 +702,12 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 	return 0;
 }
 
-// The direct host call, for one activation against tensors of one quant type
-// (every call charsiu's decode makes): the activation travels inside the
-// launch's own parameters (qmv1_inline_kernel), the matvec writes every y
-// straight into mapped host memory, and its last CTA raises a sequence flag
-// there, which the host spins on. One launch; no copy-engine transfer, graph
-// or event sits in the call.
-int run_direct(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, const float *d,
-	       unsigned k, double mb, float **ys, double t0)
+// Spin until a direct call's kernel raises the sequence flag (mapped host
+// memory), under the reference's budget (src/npudev.c:560-573) as finish()
+// applies it: a CUDA error, a launch that finished without signalling or one
+// that never finishes retires the layer, and three slow calls in a row too.
+int wait_direct(charsiu_gpu *g, uint32_t seq, double t0, double mb, unsigned k)
 {
-	float *y_dev = dev_view(g->h_y);
-	if (!y_dev) {
-		whine(g, "a staging buffer has no device address");
-		return -1;
-	}
-	const uint32_t nb = k / 32;
-	float *yd[QMV_MAX_TENSORS];
-	size_t off = 0;
-	for (unsigned i = 0; i < n; i++) {
-		yd[i] = y_dev + off;
-		off += g->ent[ids[i]].rows;
-	}
-	const uint32_t seq = ++g->seq ? g->seq : ++g->seq;     // never 0, the flag's reset value
-	QmvInline<QMV_INLINE_MAX_WORDS> &a = *g->inl;
-	fill_params(g, a.p, ids, n, yd, k, nullptr, nullptr);
-	a.p.done_count = g->d_sync;
-	a.p.done_flag = g->d_flag;
-	a.p.t_start = reinterpret_cast<unsigned long long *>(g->d_sync + 2);
-	a.p.seq = seq;
-	uint8_t *words = reinterpret_cast<uint8_t *>(a.act);
-	memcpy(words, q, (size_t)nb * 32);
-	memcpy(words + (size_t)nb * 32, d, (size_t)nb * sizeof(float));
-	bool ok = !launch_qmv(g, 1, a.p, g->stream, &a);
-	if (!ok) {
-		whine(g, "the launch failed: %s", cudaGetErrorString(cudaGetLastError()));
-		retire(g, "a launch failed");
-		return -1;
-	}
-	const double t1 = now_us();
-
 	// the reference's budget (src/npudev.c:560-573), as finish() applies it
 	const double budget = g->slow_us + mb * 1000.0;
 	for (uint64_t spins = 1; g->h_flag[0] != seq; spins++) {
@@ -785,6 +753,50 @@ int run_direct(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	} else {
 		g->strikes = 0;
 	}
+	return 0;
+}
+
+// The direct host call, for one activation against tensors of one quant type
+// (every call charsiu's decode makes): the activation travels inside the
+// launch's own parameters (qmv1_inline_kernel), the matvec writes every y
+// straight into mapped host memory, and its last CTA raises a sequence flag
+// there, which the host spins on. One launch; no copy-engine transfer, graph
+// or event sits in the call.
+int run_direct(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, const float *d,
+	       unsigned k, double mb, float **ys, double t0)
+{
+	float *y_dev = dev_view(g->h_y);
+	if (!y_dev) {
+		whine(g, "a staging buffer has no device address");
+		return -1;
+	}
+	const uint32_t nb = k / 32;
+	float *yd[QMV_MAX_TENSORS];
+	size_t off = 0;
+	for (unsigned i = 0; i < n; i++) {
+		yd[i] = y_dev + off;
+		off += g->ent[ids[i]].rows;
+	}
+	const uint32_t seq = ++g->seq ? g->seq : ++g->seq;     // never 0, the flag's reset value
+	QmvInline<QMV_INLINE_MAX_WORDS> &a = *g->inl;
+	fill_params(g, a.p, ids, n, yd, k, nullptr, nullptr);
+	a.p.done_count = g->d_sync;
+	a.p.done_flag = g->d_flag;
+	a.p.t_start = reinterpret_cast<unsigned long long *>(g->d_sync + 2);
+	a.p.seq = seq;
+	uint8_t *words = reinterpret_cast<uint8_t *>(a.act);
+	memcpy(words, q, (size_t)nb * 32);
+	memcpy(words + (size_t)nb * 32, d, (size_t)nb * sizeof(float));
+	bool ok = !launch_qmv(g, 1, a.p, g->stream, &a);
+	if (!ok) {
+		whine(g, "the launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+		retire(g, "a launch failed");
+		return -1;
+	}
+	const double t1 = now_us();
+	if (wait_direct(g, seq, t0, mb, k))
+		return -1;
+	const double t2 = now_us();
 	off = 0;
 	for (unsigned i = 0; i < n; i++) {
 		const size_t cnt = g->ent[ids[i]].rows;
@@ -1098,6 +1110,7 @@ void charsiu_gpu_close(struct charsiu_gpu *g)
 	if (g->h_flag)
 		cudaFreeHost((void *)g->h_flag);
 	delete g->inl;
+	delete g->i8inl;
 	cudaFree(g->d_sync);
 	cudaFree(g->d_gather_count);
 	cudaFreeHost(g->h_act);
@@ -1647,6 +1660,85 @@ int charsiu_gpu_row_dev(struct charsiu_gpu *g, int id, const int32_t *row, float
 	return 0;
 }
 
+} // extern "C"
+
+// A small int8 job as one direct call (i8mm_simt_inline_kernel): the operands
+// in the launch's own parameters, the bytes written into mapped host memory,
+// the last CTA raising the sequence flag the host spins on. One launch; no
+// copy-engine transfer or event sits in the call.
+static int matmul_i8_direct(charsiu_gpu *g, unsigned m, unsigned k, unsigned n,
+			    const uint8_t *a, const uint8_t *w, const int32_t *bias, float in_scale,
+			    float wt_scale, float out_scale, int in_zp, int wt_zp, int out_zp,
+			    int8_t *out)
+{
+	const size_t sa = (size_t)m * k, sw = (size_t)n * k, sb = (size_t)n * 4;
+	const size_t ow = (sa + 15) & ~(size_t)15, ob = (ow + sw + 15) & ~(size_t)15;
+	if (!g->i8inl)
+		g->i8inl = new (std::nothrow) I8Inline<I8_INLINE_W2>;
+	if (!g->i8inl || !grow_host(g->h_i8, g->cap_hi8, (size_t)m * n)) {
+		whine(g, "a staging buffer would not allocate");
+		return -1;
+	}
+	int8_t *out_dev = reinterpret_cast<int8_t *>(dev_view(g->h_i8));
+	if (!out_dev) {
+		whine(g, "a staging buffer has no device address");
+		return -1;
+	}
+	const double t0 = now_us();
+	I8Inline<I8_INLINE_W2> &x = *g->i8inl;
+	uint8_t *data = reinterpret_cast<uint8_t *>(x.data);
+	memcpy(data, a, sa);
+	memcpy(data + ow, w, sw);
+	memcpy(data + ob, bias, sb);
+	const uint32_t seq = ++g->seq ? g->seq : ++g->seq;     // never 0, the flag's reset value
+	x.p.a = nullptr;
+	x.p.w = nullptr;
+	x.p.bias = nullptr;
+	x.p.out = out_dev;
+	x.p.m = m;
+	x.p.k = k;
+	x.p.n = n;
+	x.p.mult = in_scale * wt_scale / out_scale;     // tools/charsiu_matmul.c:45
+	x.p.zp_out = (float)out_zp;
+	x.p.zp_a = in_zp;
+	x.p.zp_w = wt_zp;
+	x.off_w = (uint32_t)ow;
+	x.off_b = (uint32_t)ob;
+	x.done_count = g->d_sync;
+	x.done_flag = g->d_flag;
+	x.seq = seq;
+	// the smallest parameter block that holds the job (its first bytes are
+	// the same in every size)
+	const dim3 grid((n + 31) / 32, (m + 31) / 32);
+	const size_t used = ob + sb;
+	const void *fn = used <= I8_INLINE_W0 * 16 ? (const void *)i8mm_simt_inline_kernel<I8_INLINE_W0>
+			 : used <= I8_INLINE_W1 * 16 ? (const void *)i8mm_simt_inline_kernel<I8_INLINE_W1>
+						     : (const void *)i8mm_simt_inline_kernel<I8_INLINE_W2>;
+	void *args[1] = {&x};
+	if (cudaLaunchKernel(fn, grid, dim3(256), args, 0, g->stream) != cudaSuccess ||
+	    cudaGetLastError() != cudaSuccess) {
+		whine(g, "the int8 launch failed");
+		retire(g, "a launch failed");
+		return -1;
+	}
+	g->launches++;
+	const double t1 = now_us();
+	const double mb = (double)(sa + sw) / 1e6;
+	if (wait_direct(g, seq, t0, mb, k))
+		return -1;
+	const double t2 = now_us();
+	memcpy(out, g->h_i8, (size_t)m * n);
+	const double t3 = now_us();
+	g->calls++;
+	g->weight_mb += mb;
+	g->h2d_us += t1 - t0;
+	g->d2h_us += t3 - t2;
+	g->busy_us += t3 - t0;
+	return 0;
+}
+
+extern "C" {
+
 int charsiu_gpu_matmul_i8_flat(struct charsiu_gpu *g, unsigned m, unsigned k, unsigned n,
 			       const uint8_t *a, const uint8_t *w, const int32_t *bias,
 			       float in_scale, float wt_scale, float out_scale, int in_zp,
@@ -1670,6 +1762,9 @@ int charsiu_gpu_matmul_i8_flat(struct charsiu_gpu *g, unsigned m, unsigned k, un
 	const size_t sa = (size_t)m * k, sw = (size_t)n * k, sb = (size_t)n * 4;
 	const size_t oa = 0, ow = (sa + 15) & ~(size_t)15, ob = (ow + sw + 15) & ~(size_t)15;
 	const size_t oo = (ob + sb + 15) & ~(size_t)15, total = oo + (size_t)m * n;
+	if (g->direct && oo <= I8_INLINE_BYTES)
+		return matmul_i8_direct(g, m, k, n, a, w, bias, in_scale, wt_scale, out_scale, in_zp,
+					wt_zp, out_zp, out);
 	if (!grow_dev(g->d_i8, g->cap_di8, total) || !grow_host(g->h_i8, g->cap_hi8, total)) {
 		whine(g, "a staging buffer would not allocate");
 		return -1;
