@@ -50,36 +50,6 @@ struct NpuEnt {
 	double weight_mb;
 };
 
-// The kernel for kp-byte rows: R rows a warp at most, U chunks a row a step
-// (R * U = 16 loads in flight a lane).
-struct Shape {
-	int r, u;
-};
-
-Shape shape_for(uint32_t kp)
-{
-	const uint32_t ch = (kp / 16 + 31) / 32;      // 16-byte chunks a lane a row
-	if (ch <= 1)
-		return {16, 1};
-	if (ch <= 2)
-		return {8, 2};
-	if (ch <= 4)
-		return {4, 4};
-	if (ch <= 8)
-		return {2, 8};
-	return {1, 16};
-}
-
-// Rows a warp takes: the kernel's R, or CHARSIU_GPU_NPU_ROWS (`fixed`) when
-// set. Fewer rows a warp for the smaller tensors, to spread them over every
-// SM, measured slower (K=2048: N=8192 6.5 against 5.2 us, N=2048 3.7 against
-// 3.3 us): these launches pay a fixed ~3 us (N=512 takes 2.9 us), not a
-// shortage of loads in flight.
-uint32_t rows_per_warp(int r_max, int fixed)
-{
-	return (uint32_t)(fixed > 0 && fixed < r_max ? fixed : r_max);
-}
-
 } // namespace
 
 struct charsiu_npu {
@@ -96,12 +66,11 @@ struct charsiu_npu {
 	uint32_t *d_flag = nullptr;
 	uint32_t seq = 0;
 	NpuInline<NPU_INLINE_WORDS> *inl = nullptr;
-	bool smem_set[16] = {};
-	int occ[16] = {};
+	bool smem_set[12] = {};
+	int occ[12] = {};                  // CTAs an SM of each kernel form, asked once
 	unsigned long calls = 0, launches = 0;
 	double busy_us = 0, kern_ms = 0, weight_mb = 0, slow_us = 100000;
 	int strikes = 0, dead = 0, whined = 0, no_pdl = 0;
-	int rows = 0;                      // CHARSIU_GPU_NPU_ROWS: rows a warp (0: by size)
 	std::string err;
 };
 
@@ -170,43 +139,48 @@ void fill(charsiu_npu *g, NpuParams &p, const int *ids, unsigned n, float *const
 }
 
 // One launch: the inline form when `inl` (its .p is p), else q1 from p.q1.
+// npumv_kernel<W, U>: W warps split K, U chunks a lane a row a pass -- K up
+// to 2048 four warps (eight CTAs an SM), 4096 eight, 8192 sixteen, past that
+// sixteen with two chunks a lane. (At K = 8192 eight warps with two chunks a
+// lane measured 4.7-4.8 against 4.4-4.7 us.)
 int launch(charsiu_npu *g, const NpuParams &p, const void *inl, cudaStream_t st)
 {
-#define NPU_FNS(R, U) \
-	{(const void *)npumv_kernel<R, U>, (const void *)npumv_inline_kernel<R, U, 128>, \
-	 (const void *)npumv_inline_kernel<R, U, NPU_INLINE_WORDS>}
-	static const void *const fns[5][3] = {NPU_FNS(16, 1), NPU_FNS(8, 2), NPU_FNS(4, 4),
-					      NPU_FNS(2, 8), NPU_FNS(1, 16)};
+#define NPU_FNS(W, U) \
+	{(const void *)npumv_kernel<W, U>, (const void *)npumv_inline_kernel<W, U, 128>, \
+	 (const void *)npumv_inline_kernel<W, U, NPU_INLINE_WORDS>}
+	static const void *const fns[4][3] = {NPU_FNS(4, 1), NPU_FNS(8, 1), NPU_FNS(16, 1),
+					      NPU_FNS(16, 2)};
 #undef NPU_FNS
-	const Shape sh = shape_for(p.kp);
-	const int si = sh.r == 16 ? 0 : sh.r == 8 ? 1 : sh.r == 4 ? 2 : sh.r == 2 ? 3 : 4;
+	static const int warps[4] = {4, 8, 16, 16};
+	const uint32_t nch = p.kp / 16;
+	const int si = nch <= 128 ? 0 : nch <= 256 ? 1 : nch <= 512 ? 2 : 3;
 	const int form = inl ? (p.kp <= 128 * 16 ? 1 : 2) : 0;
 	const void *fn = fns[si][form];
 	const int slot = si * 3 + form;
-	const size_t smem = p.kp;
+	const int threads = warps[si] * 32;
+	const size_t smem = npumv_smem_bytes(p.kp, warps[si]);
+	if (smem > NPU_SMEM_MAX)
+		return -1;
 	if (!g->smem_set[slot]) {
 		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-					 (int)(16 * 1024)) != cudaSuccess)
+					 (int)NPU_SMEM_MAX) != cudaSuccess)
 			return -1;
 		g->smem_set[slot] = true;
 	}
 	if (!g->occ[slot]) {
 		int occ = 0;
-		if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, NPU_WARPS * 32,
-								  16 * 1024) != cudaSuccess || occ < 1)
+		if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, NPU_SMEM_MAX) !=
+			    cudaSuccess || occ < 1)
 			return -1;
 		g->occ[slot] = occ;
 	}
-	const uint32_t rpw = rows_per_warp(sh.r, g->rows);
-	// one CTA a unit of rpw rows a warp while that leaves SMs idle; past that,
-	// every resident CTA, the rows split evenly over their warps
-	const uint32_t units = (p.total_rows + rpw * NPU_WARPS - 1) / (rpw * NPU_WARPS);
+	const uint32_t groups = (p.total_rows + NPU_GROUP_ROWS - 1) / NPU_GROUP_ROWS;
 	unsigned grid = (unsigned)g->occ[slot] * g->sm_count;
-	if (units <= (uint32_t)g->sm_count)
-		grid = units ? units : 1;
+	if (groups < grid)
+		grid = groups ? groups : 1;
 	cudaLaunchConfig_t cfg = {};
 	cfg.gridDim = dim3(grid);
-	cfg.blockDim = dim3(NPU_WARPS * 32);
+	cfg.blockDim = dim3(threads);
 	cfg.dynamicSmemBytes = smem;
 	cfg.stream = st;
 	cudaLaunchAttribute attr[1];
@@ -214,11 +188,7 @@ int launch(charsiu_npu *g, const NpuParams &p, const void *inl, cudaStream_t st)
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 	cfg.attrs = attr;
 	cfg.numAttrs = g->no_pdl ? 0 : 1;
-	NpuParams arg = p;
-	arg.rows_per_warp = rpw;
-	if (inl)
-		static_cast<NpuInline<NPU_INLINE_WORDS> *>(const_cast<void *>(inl))->p.rows_per_warp = rpw;
-	void *args[1] = {inl ? const_cast<void *>(inl) : (void *)&arg};
+	void *args[1] = {inl ? const_cast<void *>(inl) : const_cast<NpuParams *>(&p)};
 	if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess)
 		return -1;
 	g->launches++;
@@ -407,8 +377,6 @@ struct charsiu_npu *charsiu_npu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	if (const char *e = getenv("CHARSIU_GPU_SLOW_US"))
 		g->slow_us = (double)strtoul(e, nullptr, 0);
 	g->no_pdl = getenv("CHARSIU_GPU_NO_PDL") != nullptr;
-	if (const char *e = getenv("CHARSIU_GPU_NPU_ROWS"))
-		g->rows = atoi(e);
 	g->ent.reserve(max_tensors);
 	g->cap_y = (size_t)max_n * NPU_MAX_TENSORS;
 	g->inl = new (std::nothrow) NpuInline<NPU_INLINE_WORDS>();

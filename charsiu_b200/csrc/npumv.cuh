@@ -11,14 +11,25 @@
 //
 // Device layout: each tensor's rows back to back, a row padded with zeros to
 // kp bytes (kp = K rounded up to 16), so a lane's 16-byte loads are aligned.
-// The grid's warps split the rows into contiguous ranges of equal size (to a
-// row), so every SM carries the same bytes; a warp takes its range up to R
-// rows at a time (rows_per_warp, chosen by the host); lane L reads 16-byte chunks
-// L, L + 32, ... of each, U chunks of each row per step (R * U <= 16 loads in
-// flight a lane), and dots them with dp4a against the activation staged in
-// shared memory; one warp reduction a row, and lane j writes row j. The first
-// rows' first chunks are loaded before the wait on the previous kernel, and
-// each next batch's while the current one's sums are reduced.
+//
+// Organised as the q8_0 decode matvec (qmv1.cuh): rows in 8-row groups dealt
+// round robin over a persistent grid of small CTAs (up to eight an SM at
+// K = 2048), the W warps of a CTA splitting K. Chunk c (16 bytes) of a row is
+// read by warp (c / 32) % W, lane c % 32, in register slot (c / 32W) % U of
+// pass c / (32WU), so every warp-load instruction reads 512 contiguous bytes
+// of one row and a lane holds one chunk of each of the group's 8 rows a slot.
+// A row's warp partial is one __reduce_add_sync; the W partials meet in
+// shared memory (int32: exact in any order) and thread j of the CTA scales
+// row j. The first group's loads go out before the wait on the previous
+// kernel, each next group's as soon as the current group's are consumed, so
+// they fly through the barrier and the stores; every CTA lets the next launch
+// start as soon as it has started.
+//
+// Measured against the form it replaced (a warp owning up to 4 whole rows,
+// 16 loads in flight a lane, 109 registers, two CTAs of 8 warps an SM), same
+// bits: K=2048 N=8192 5.25 -> 3.78 us a launch, K=8192 N=2048 5.1 -> 4.2 us,
+// the 2048 -> 128256 head 42.9 -> 38.8 us; the early trigger alone is
+// 4.3-4.5 -> 3.78 us of that at K=2048 N=8192.
 #pragma once
 
 #include <cstdint>
@@ -28,7 +39,6 @@
 namespace cgpu {
 
 constexpr int NPU_MAX_TENSORS = 8;
-constexpr int NPU_WARPS = 8;
 constexpr int NPU_INLINE_WORDS = 896;        // the activation in kernel parameters, up to K = 14336
 
 struct NpuTensor {
@@ -41,7 +51,6 @@ struct NpuTensor {
 struct NpuParams {
 	NpuTensor t[NPU_MAX_TENSORS];
 	uint32_t ntensor, total_rows, kp;
-	uint32_t rows_per_warp;  // 1 .. the kernel's R
 	float d1;
 	const float *d1p;        // when set, d1 is read here (device) once the kernel before is done
 	const int8_t *q1;        // kp bytes (device); unused when the activation is inline
@@ -68,54 +77,82 @@ __device__ __forceinline__ int dp4a_s(uint32_t a, uint32_t b, int c)
 	return __dp4a((int)a, (int)b, c);
 }
 
-template <int R, int U, int AW>
+constexpr uint32_t NPU_GROUP_ROWS = 8;
+constexpr size_t NPU_SMEM_MAX = 16 * 1024;
+
+// the activation, then two [W][8] buffers of warp partials
+inline size_t npumv_smem_bytes(uint32_t kp, int w)
+{
+	return (size_t)kp + (size_t)2 * w * NPU_GROUP_ROWS * sizeof(int);
+}
+static_assert(NPU_INLINE_WORDS * 16 + 2 * 16 * NPU_GROUP_ROWS * sizeof(int) <= NPU_SMEM_MAX,
+	      "the largest K's activation and partials fit the shared memory asked for");
+
+template <int W, int U, int AW>
 __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 {
 	extern __shared__ __align__(16) uint8_t npu_smem[];
+	constexpr uint32_t G8 = NPU_GROUP_ROWS;
 	const uint32_t nch = p.kp / 16;
 	uint4 *act = reinterpret_cast<uint4 *>(npu_smem);
+	int *part = reinterpret_cast<int *>(npu_smem + p.kp);     // [2][W][8]
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const uint32_t nw = gridDim.x * NPU_WARPS;
+	const uint32_t groups = (p.total_rows + G8 - 1) / G8;
+	constexpr uint32_t PASS = 32u * W * U;                      // chunks a pass
+	const uint32_t npass = (nch + PASS - 1) / PASS;
 
-	// rows r0 .. r0 + R - 1 of this warp's range [r0, r_end): their tensors
-	// and row pointers
-	const uint32_t rpw = p.rows_per_warp;
-	const uint32_t gw = blockIdx.x * NPU_WARPS + warp;
-	const uint32_t r_end = (uint32_t)((uint64_t)(gw + 1) * p.total_rows / nw);
-	const int8_t *wr[R];
-	uint32_t ti[R];
-	auto setup = [&](uint32_t r0) {
+	// row j of group G: its tensor and its bytes (nullptr past the last row)
+	auto row_of = [&](uint32_t r, uint32_t &t) {
+		t = 0;
+		while (t + 1 < p.ntensor && r >= p.t[t].row_end)
+			t++;
+		return r - (p.t[t].row_end - p.t[t].rows);
+	};
+	const int8_t *wr[G8];
+	auto setup = [&](uint32_t G) {
 #pragma unroll
-		for (int j = 0; j < R; j++) {
-			const uint32_t r = r0 + j;
-			uint32_t t = 0;
-			while (t + 1 < p.ntensor && r >= p.t[t].row_end)
-				t++;
-			ti[j] = t;
-			wr[j] = ((uint32_t)j < rpw && r < r_end)
-				? p.t[t].w + (uint64_t)(r - (p.t[t].row_end - p.t[t].rows)) * p.kp
-				: nullptr;
+		for (uint32_t j = 0; j < G8; j++) {
+			const uint32_t r = G * G8 + j;
+			uint32_t t;
+			const uint32_t lr = row_of(r < p.total_rows ? r : 0, t);
+			wr[j] = r < p.total_rows ? p.t[t].w + (uint64_t)lr * p.kp : nullptr;
 		}
 	};
-	uint4 wv[R][U];
-	auto load = [&](uint32_t c0) {
+	uint4 wv[G8][U];
+	auto load = [&](uint32_t pass) {
 #pragma unroll
-		for (int j = 0; j < R; j++)
+		for (int u = 0; u < U; u++) {
+			const uint32_t c = pass * PASS + (uint32_t)(u * 32 * W + warp * 32 + lane);
 #pragma unroll
-			for (int u = 0; u < U; u++) {
-				const uint32_t c = c0 + 32 * u;
+			for (uint32_t j = 0; j < G8; j++)
 				wv[j][u] = (wr[j] && c < nch) ? ldg_stream((const uint8_t *)wr[j] + c * 16)
 							     : make_uint4(0, 0, 0, 0);
-			}
+		}
+	};
+	// thread j < 8: its row's output and scale, loaded ahead of the sums
+	auto out_of = [&](uint32_t G, float *&yp, float &sc) {
+		const uint32_t r = G * G8 + threadIdx.x;
+		yp = nullptr;
+		sc = 0.0f;
+		if (threadIdx.x < G8 && r < p.total_rows) {
+			uint32_t t;
+			const uint32_t lr = row_of(r, t);
+			yp = p.t[t].y + lr;
+			sc = p.t[t].scale[lr];
+		}
 	};
 
-	// the first rows' first chunks go now: weights never depend on the
+	pdl_launch_dependents();
+	// the first group's first pass goes now: weights never depend on the
 	// kernel before this one
-	if (rpw < 1 || rpw > (uint32_t)R)
-		return;
-	uint32_t r0 = (uint32_t)((uint64_t)gw * p.total_rows / nw);
-	setup(r0);
-	load(lane);
+	uint32_t G = blockIdx.x;
+	float *yp = nullptr;
+	float sc = 0.0f;
+	if (G < groups) {
+		setup(G);
+		load(0);
+		out_of(G, yp, sc);
+	}
 	if (AW && p.done_flag && blockIdx.x == 0 && threadIdx.x == 0)
 		*p.t_start = globaltimer_ns();
 	if (AW) {
@@ -130,23 +167,22 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 	}
 	const float d1 = p.d1p ? *p.d1p : p.d1;
 	__syncthreads();
-	pdl_launch_dependents();
 
-	while (r0 < r_end) {
-		int acc[R];
+	for (uint32_t i = 0; G < groups; i++, G += gridDim.x) {
+		int acc[G8];
 #pragma unroll
-		for (int j = 0; j < R; j++)
+		for (uint32_t j = 0; j < G8; j++)
 			acc[j] = 0;
-		for (uint32_t c0 = lane; c0 < nch; c0 += 32 * U) {
-			if (c0 != (uint32_t)lane)
-				load(c0);
+		for (uint32_t ps = 0; ps < npass; ps++) {
+			if (ps)
+				load(ps);
 #pragma unroll
 			for (int u = 0; u < U; u++) {
-				const uint32_t c = c0 + 32 * u;
+				const uint32_t c = ps * PASS + (uint32_t)(u * 32 * W + warp * 32 + lane);
 				if (c < nch) {
 					const uint4 a = act[c];
 #pragma unroll
-					for (int j = 0; j < R; j++) {
+					for (uint32_t j = 0; j < G8; j++) {
 						acc[j] = dp4a_s(wv[j][u].x, a.x, acc[j]);
 						acc[j] = dp4a_s(wv[j][u].y, a.y, acc[j]);
 						acc[j] = dp4a_s(wv[j][u].z, a.z, acc[j]);
@@ -155,30 +191,32 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 				}
 			}
 		}
-		// where this batch's rows go, then the next batch's first chunks in
-		// flight while this one's sums are reduced and stored
-		float *yp[R];
-		float sc[R];
-#pragma unroll
-		for (int j = 0; j < R; j++) {
-			yp[j] = nullptr;
-			sc[j] = 0.0f;
-			if (lane == j && wr[j]) {
-				const NpuTensor &t = p.t[ti[j]];
-				const uint32_t row = r0 + j - (t.row_end - t.rows);
-				yp[j] = t.y + row;
-				sc[j] = t.scale[row];
-			}
+		// the next group's first pass in flight before the sums
+		const uint32_t Gn = G + gridDim.x;
+		float *yp_n = nullptr;
+		float sc_n = 0.0f;
+		if (Gn < groups) {
+			setup(Gn);
+			load(0);
+			out_of(Gn, yp_n, sc_n);
 		}
-		r0 += rpw;
-		setup(r0);
-		load(lane);
+		int *pb = part + (i & 1) * W * G8;
 #pragma unroll
-		for (int j = 0; j < R; j++) {
+		for (uint32_t j = 0; j < G8; j++) {
 			const int s = __reduce_add_sync(0xffffffffu, acc[j]);
-			if (yp[j])
-				*yp[j] = __fmul_rn(__fmul_rn(__int2float_rn(s), d1), sc[j]);
+			if ((uint32_t)lane == j)
+				pb[warp * G8 + j] = s;
 		}
+		named_barrier(1, W * 32);
+		if (yp) {
+			int s = 0;
+#pragma unroll
+			for (int w = 0; w < W; w++)
+				s += pb[w * G8 + threadIdx.x];
+			*yp = __fmul_rn(__fmul_rn(__int2float_rn(s), d1), sc);
+		}
+		yp = yp_n;
+		sc = sc_n;
 	}
 	if (AW && p.done_flag) {
 		// y is mapped host memory: this CTA's stores reach thread 0 through
@@ -198,18 +236,18 @@ __device__ __forceinline__ void npumv_body(const NpuParams &p, const uint4 *inl)
 	}
 }
 
-template <int R, int U>
-__global__ void __launch_bounds__(NPU_WARPS * 32)
+template <int W, int U>
+__global__ void __launch_bounds__(W * 32)
 npumv_kernel(const __grid_constant__ NpuParams p)
 {
-	npumv_body<R, U, 0>(p, nullptr);
+	npumv_body<W, U, 0>(p, nullptr);
 }
 
-template <int R, int U, int AW>
-__global__ void __launch_bounds__(NPU_WARPS * 32)
+template <int W, int U, int AW>
+__global__ void __launch_bounds__(W * 32)
 npumv_inline_kernel(const __grid_constant__ NpuInline<AW> a)
 {
-	npumv_body<R, U, AW>(a.p, a.act);
+	npumv_body<W, U, AW>(a.p, a.act);
 }
 
 } // namespace cgpu

@@ -102,6 +102,12 @@ __device__ __forceinline__ void pdl_launch_dependents()
 	asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// barrier `id` (1..15) over `threads` threads of the CTA
+__device__ __forceinline__ void named_barrier(int id, int threads)
+{
+	asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
+}
+
 // atomic add at device scope with acquire-release ordering; returns the old value
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *addr, uint32_t v)
 {

@@ -154,11 +154,6 @@ __device__ __forceinline__ void seg_compute(const SegRegs<Q8> &R, uint32_t sb, u
 	}
 }
 
-__device__ __forceinline__ void named_barrier(int id, int threads)
-{
-	asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
-}
-
 // W warps a CTA; all tensors of one launch share one quant type (Q8). A warp
 // handles segment warp of each group and, when TWO, also warp + W (so
 // nseg <= W, or nseg <= 2W with TWO); both are loaded before either is
