@@ -117,8 +117,10 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *addr, uint32_
 	return old;
 }
 
-// system-scope acquire load and release add: the arrival words other GPUs
-// write over NVLink (the matvecs fused with their all-gather)
+// The arrival words other GPUs write over NVLink (the matvecs fused with
+// their all-gather): a system-scope acquire load on the waiting side; on the
+// signalling side a system-scope acq_rel fence and relaxed system-scope adds
+// after it, which together release everything ordered before the fence.
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
 {
 	uint32_t v;
@@ -126,9 +128,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
 	return v;
 }
 
-__device__ __forceinline__ void red_release_sys_add(uint32_t *p, uint32_t v)
+__device__ __forceinline__ void fence_acq_rel_sys()
 {
-	asm volatile("red.release.sys.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+	asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+__device__ __forceinline__ void red_relaxed_sys_add(uint32_t *p, uint32_t v)
+{
+	asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
 }
 
 // sum of four (unsigned byte of a) * (signed byte of b), plus c

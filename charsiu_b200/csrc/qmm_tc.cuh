@@ -487,13 +487,15 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 		tmem_dealloc(taddr, NCOLS);
 	// every rank's stores of this CTA (peer ones included) reach thread 0
 	// through the barrier and are released at device scope by its count; the
-	// last CTA acquires them all and, after one system fence, tells every rank
+	// last CTA acquires them all and tells every rank with relaxed
+	// system-scope adds after one system-scope acq_rel fence (a release
+	// pattern, as the M = 1 gather's end)
 	if (gth.world && threadIdx.x == 0 &&
 	    atom_add_acq_rel_gpu(gth.cta_count, 1u) == gridDim.x - 1) {
 		*gth.cta_count = 0;
-		__threadfence_system();
+		fence_acq_rel_sys();
 		for (uint32_t r = 0; r < gth.world; r++)
-			red_release_sys_add(gth.sync[r] + gth.signal_idx, 1u);
+			red_relaxed_sys_add(gth.sync[r] + gth.signal_idx, 1u);
 	}
 }
 
