@@ -347,7 +347,7 @@ int launch_qmv(charsiu_gpu *g, int m, const QmvParams &p, cudaStream_t st,
 	if (m == 1) {
 		threads = qmv1_warps[shape] * 32;
 		smem = qmv1_smem_bytes(p.nb);
-		// 10..17, inline 24..31, gather 56..63; the tensor cores 20..23, M > 1 32..55
+		// 10..17, inline 24..31, gather 56..63; q6_K 4..7, the tensor cores 19..23, M > 1 32..55
 		slot = (gth ? 56 : inl ? 24 : 10) + 2 * shape + (q8 ? 1 : 0);
 		fn = (gth ? qmv1_gather_fns : inl ? qmv1_inline_fns : qmv1_fns)[shape][q8 ? 1 : 0];
 	} else if (inl || gth) {
@@ -549,7 +549,8 @@ unsigned qmvm_chunk(unsigned left, uint32_t nb)
 
 // One launch per quant type present among ids (the M = 1 kernel takes one
 // type a launch; a decode's groups are always a single type).
-// q6_K: q6k_kernel, one launch a tensor, a warp for 16 rows at a time.
+// q6_K: q6k_kernel<W, U>, one launch a tensor: W = 4 warps at K <= 2048
+// (U = 1 to K = 1024), 8 to K = 4096, 16 beyond; 8-row groups over the grid.
 int launch_q6k(charsiu_gpu *g, const Ent &e, float *y, const int8_t *q, const float *d,
 	       cudaStream_t st)
 {
@@ -562,32 +563,41 @@ int launch_q6k(charsiu_gpu *g, const Ent &e, float *y, const int8_t *q, const fl
 	p.d = d;
 	if (!p.rows)
 		return 0;
+	static const void *const fns[4] = {
+		(const void *)q6k_kernel<4, 1>, (const void *)q6k_kernel<4, 2>,
+		(const void *)q6k_kernel<8, 2>, (const void *)q6k_kernel<16, 2>};
+	static const int warps[4] = {4, 4, 8, 16};
+	const int si = p.nsb <= 4 ? 0 : p.nsb <= 8 ? 1 : p.nsb <= 16 ? 2 : 3;
+	const void *fn = fns[si];
+	const int slot = 4 + si;          // 4..7
+	const unsigned threads = (unsigned)warps[si] * 32;
 	const size_t smem = q6k_smem_bytes(p.nsb);
-	const int slot = 18;
+	if (smem > QMV_SMEM_MAX)
+		return -1;
 	if (!g->smem_set[slot]) {
-		if (cudaFuncSetAttribute((const void *)q6k_kernel,
-					 cudaFuncAttributeMaxDynamicSharedMemorySize,
+		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
 					 (int)QMV_SMEM_MAX) != cudaSuccess)
 			return -1;
 		g->smem_set[slot] = true;
 	}
+	const uint64_t key = (uint64_t)slot << 32 | p.nsb;
 	int occ = 0;
-	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, q6k_kernel, Q6K_WARPS * 32, smem) !=
-		    cudaSuccess || occ < 1)
-		return -1;
-	// rows a warp: enough that the resident warps cover the tensor in one
-	// pass, at most Q6K_ROWS
-	const unsigned warps = (unsigned)occ * g->sm_count * Q6K_WARPS;
-	unsigned rpw = (p.rows + warps - 1) / warps;
-	rpw = rpw < 1 ? 1 : rpw > (unsigned)Q6K_ROWS ? (unsigned)Q6K_ROWS : rpw;
-	p.rows_per_warp = rpw;
+	for (const auto &kv : g->occ)
+		if (kv.first == key)
+			occ = kv.second;
+	if (!occ) {
+		if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, (int)threads, smem) !=
+			    cudaSuccess || occ < 1)
+			return -1;
+		g->occ.emplace_back(key, occ);
+	}
+	const unsigned groups = (p.rows + RG - 1) / RG;
 	unsigned grid = (unsigned)occ * g->sm_count;
-	const unsigned need = (p.rows + Q6K_WARPS * rpw - 1) / (Q6K_WARPS * rpw);
-	if (need < grid)
-		grid = need;
+	if (groups < grid)
+		grid = groups;
 	cudaLaunchConfig_t cfg = {};
 	cfg.gridDim = dim3(grid);
-	cfg.blockDim = dim3(Q6K_WARPS * 32);
+	cfg.blockDim = dim3(threads);
 	cfg.dynamicSmemBytes = smem;
 	cfg.stream = st;
 	cudaLaunchAttribute attr[1];
@@ -596,7 +606,7 @@ int launch_q6k(charsiu_gpu *g, const Ent &e, float *y, const int8_t *q, const fl
 	cfg.attrs = attr;
 	cfg.numAttrs = g->no_pdl ? 0 : 1;
 	void *args[1] = {&p};
-	if (cudaLaunchKernelExC(&cfg, (const void *)q6k_kernel, args) != cudaSuccess)
+	if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess)
 		return -1;
 	g->launches++;
 	return 0;

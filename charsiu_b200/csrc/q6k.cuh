@@ -18,15 +18,27 @@
 //
 // Device layout (repacked at add, 16-byte aligned): a row is its super-blocks'
 // first 208 bytes (ql, qh, scales) back to back, then the fp16 d's, padded to
-// 16 bytes. Lane L of a warp takes super-block i0 + L/4, half (L/2)&1 and
-// g = L&1 -- three 16-byte loads, one 8-byte load of the half's scales -- and
-// computes its four terms with dp4a (unsigned 6-bit weights, so the -32 comes
-// off as 32 * sum(activation)). A warp takes up to 8 rows at a time (fewer
-// when the tensor has too few rows to fill the GPU): the terms of each row's
-// 8 super-blocks go to that row's line of a per-warp buffer, then lane r adds
-// row r's line in term order -- the reference's sequence -- so the ordered
-// sums run side by side (a lane-0 sum of one row at a time is 12% slower on
-// the head). Each item's bytes are loaded two items ahead.
+// 16 bytes.
+//
+// Organised as the q8_0 decode matvec (qmv1.cuh): 8-row groups dealt round
+// robin over a persistent grid of small CTAs whose W warps split a group's
+// super-blocks. Lane L of warp w takes row L/4, half (L/2)&1 and g = L&1 of
+// super-block w + W*u (slot u of U; passes of W*U super-blocks) -- three
+// 16-byte loads and the half's 8 scale bytes -- so one warp-load covers 64
+// contiguous bytes of each of the 8 rows, and computes its four terms with
+// dp4a (unsigned 6-bit weights, so the -32 comes off as 32 * sum(activation)).
+// The terms go to the row's line of a term buffer at the reference's position
+// ((i*2 + h)*2 + g)*4 + k; after one barrier lanes 0..7 of warp 0 add their
+// row's line in that order while the other warps load the next group. The
+// first group's bytes are loaded before the wait on the previous kernel, and
+// every CTA lets the next launch start as soon as it starts.
+//
+// Measured against the form it replaced (a warp taking 8 whole rows, each
+// row's 8 super-blocks an item loaded two items ahead, 8-warp CTAs, no load
+// before the wait), same bits: the 2048 -> 128256 head 66.2 -> 43.1 us
+// (3.26 -> 5.0 TB/s), K=2048 N=8192 8.3 -> 4.9 us, K=4096 N=4096 11.1 ->
+// 5.3 us, K=8192 N=2048 14.7 -> 6.05 us (four warps in four passes there
+// measured 20.8 us, hence W by K).
 #pragma once
 
 #include "layout.h"
@@ -34,13 +46,6 @@
 #include "qmv1.cuh"
 
 namespace cgpu {
-
-constexpr int Q6K_WARPS = 8;
-// rows a warp sums side by side (lane r: row r). Measured on the 2048 x 128256
-// head: 1 (a lane-0 sum) 74 us, 4 70 us, 8 66 us, 16 92 us (its term buffers
-// cost occupancy).
-constexpr int Q6K_ROWS = 8;
-constexpr int Q6K_TSTRIDE = 129;      // floats a row of the term buffer: 128 + 1 (banks)
 
 // GGUF rows (210-byte super-blocks) -> the device layout; one thread a
 // super-block. Load time only.
@@ -64,18 +69,24 @@ struct Q6kParams {
 	const uint8_t *w;          // this GPU's rows in the device layout
 	float *y;
 	uint32_t rows, nsb;
-	uint32_t rows_per_warp;    // 1 .. Q6K_ROWS: rows a warp sums side by side
 	const int8_t *q;           // activation [nsb * 256]
 	const float *d;            // activation deltas [nsb * 8]
 };
 
+// W warps a CTA, U super-blocks a warp a pass.
+__host__ __device__ inline uint32_t q6k_tstride(uint32_t nsb)
+{
+	return nsb * 16 + 4;           // floats a row's line: its terms + 4 (banks, 16-byte rows)
+}
+
 inline size_t q6k_smem_bytes(uint32_t nsb)
 {
 	return (size_t)nsb * 256 + (size_t)nsb * 8 * sizeof(float) +
-	       (size_t)Q6K_WARPS * Q6K_ROWS * Q6K_TSTRIDE * sizeof(float);
+	       (size_t)2 * RG * q6k_tstride(nsb) * sizeof(float);
 }
 
-__global__ void __launch_bounds__(Q6K_WARPS * 32)
+template <int W, int U>
+__global__ void __launch_bounds__(W * 32)
 q6k_kernel(const __grid_constant__ Q6kParams p)
 {
 	extern __shared__ __align__(128) uint8_t smem[];
@@ -83,88 +94,52 @@ q6k_kernel(const __grid_constant__ Q6kParams p)
 	int8_t *aq = reinterpret_cast<int8_t *>(smem);
 	float *ad = reinterpret_cast<float *>(smem + (size_t)nsb * 256);
 	float *terms = ad + (size_t)nsb * 8;
-
-	pdl_wait();
-	{
-		const uint4 *gq = reinterpret_cast<const uint4 *>(p.q);
-		uint4 *sq = reinterpret_cast<uint4 *>(aq);
-		for (uint32_t i = threadIdx.x; i < nsb * 16; i += blockDim.x)
-			sq[i] = gq[i];
-		for (uint32_t i = threadIdx.x; i < nsb * 8; i += blockDim.x)
-			ad[i] = p.d[i];
-	}
-	__syncthreads();
-	pdl_launch_dependents();
-
+	const uint32_t ts = q6k_tstride(nsb);
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const uint32_t h = (lane >> 1) & 1, g = lane & 1;
+	const uint32_t r = lane >> 2, h = (lane >> 1) & 1, g = lane & 1;
 	const uint64_t rs = q6k_row_bytes(nsb);
-	float *tw = terms + warp * Q6K_ROWS * Q6K_TSTRIDE;
-	if (p.rows_per_warp < 1 || p.rows_per_warp > (uint32_t)Q6K_ROWS)
-		return;
+	const uint32_t groups = (p.rows + RG - 1) / RG;
+	constexpr uint32_t PASS = W * U;
+	const uint32_t npass = (nsb + PASS - 1) / PASS;
 
-	// one item = (row, 8 super-blocks from i0); items go in the order (rows
-	// base.. base + nr - 1 of a chunk, chunk, base), and each item's bytes are
-	// loaded two items ahead
 	struct Regs {
 		uint4 ql0, ql1, qh;
 		uint2 sc;
 		uint16_t d;
 	};
-	struct Cursor {
-		uint32_t base, i0, r;
-	};
-	const uint32_t rpw = p.rows_per_warp;
-	const uint32_t step = gridDim.x * Q6K_WARPS * rpw;
-	auto rows_at = [&](uint32_t base) { return p.rows - base < rpw ? p.rows - base : rpw; };
-	auto advance = [&](Cursor &c) {
-		if (++c.r == rows_at(c.base)) {
-			c.r = 0;
-			c.i0 += 8;
-			if (c.i0 >= nsb) {
-				c.i0 = 0;
-				c.base += step;
+	Regs R[U];
+	auto load = [&](uint32_t G, uint32_t ps) {
+		const uint32_t row = G * RG + r;
+		const uint8_t *wr = p.w + (uint64_t)(row < p.rows ? row : 0) * rs;
+#pragma unroll
+		for (int u = 0; u < U; u++) {
+			const uint32_t i = ps * PASS + (uint32_t)(u * W + warp);
+			if (row < p.rows && i < nsb) {
+				const uint8_t *sb = wr + (size_t)i * 208;
+				R[u].ql0 = ldg_stream(sb + h * 64 + g * 16);
+				R[u].ql1 = ldg_stream(sb + h * 64 + 32 + g * 16);
+				R[u].qh = ldg_stream(sb + 128 + h * 32 + g * 16);
+				R[u].sc = *reinterpret_cast<const uint2 *>(sb + 192 + h * 8);
+				R[u].d = ldg_stream_u16(wr + (size_t)nsb * 208 + 2 * i);
+			} else {
+				R[u] = Regs{};
 			}
 		}
 	};
-	auto load = [&](const Cursor &c, Regs &R) {
-		const uint32_t i = c.i0 + (lane >> 2);
-		if (i >= nsb)
-			return;
-		const uint8_t *wr = p.w + (uint64_t)(c.base + c.r) * rs;
-		const uint8_t *sb = wr + (size_t)i * 208;
-		R.ql0 = ldg_stream(sb + h * 64 + g * 16);
-		R.ql1 = ldg_stream(sb + h * 64 + 32 + g * 16);
-		R.qh = ldg_stream(sb + 128 + h * 32 + g * 16);
-		R.sc = *reinterpret_cast<const uint2 *>(sb + 192 + h * 8);
-		R.d = ldg_stream_u16(wr + (size_t)nsb * 208 + 2 * i);
-	};
-	Cursor cc = {(blockIdx.x * Q6K_WARPS + warp) * rpw, 0, 0};
-	Cursor lc = cc;
-	Regs r0 = {}, r1 = {}, r2 = {};
-	if (lc.base < p.rows) {
-		load(lc, r0);
-		advance(lc);
-	}
-	if (lc.base < p.rows) {
-		load(lc, r1);
-		advance(lc);
-	}
-	float s = 0.0f;
-	while (cc.base < p.rows) {
-		if (lc.base < p.rows) {
-			load(lc, r2);
-			advance(lc);
-		}
-		const uint32_t i = cc.i0 + (lane >> 2);
-		float tv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-		if (i < nsb) {
-			const float dd = half_bits_to_float(r0.d);
+	auto compute = [&](uint32_t ps, float *tb) {
+#pragma unroll
+		for (int u = 0; u < U; u++) {
+			const uint32_t i = ps * PASS + (uint32_t)(u * W + warp);
+			if (i >= nsb)
+				continue;
+			const Regs &Q = R[u];
+			const float dd = half_bits_to_float(Q.d);
 			const int8_t *xq = aq + (size_t)i * 256 + h * 128 + g * 16;
 			const float *xd = ad + (size_t)i * 8 + h * 4;
-			const uint32_t ql0w[4] = {r0.ql0.x, r0.ql0.y, r0.ql0.z, r0.ql0.w};
-			const uint32_t ql1w[4] = {r0.ql1.x, r0.ql1.y, r0.ql1.z, r0.ql1.w};
-			const uint32_t qhw[4] = {r0.qh.x, r0.qh.y, r0.qh.z, r0.qh.w};
+			const uint32_t ql0w[4] = {Q.ql0.x, Q.ql0.y, Q.ql0.z, Q.ql0.w};
+			const uint32_t ql1w[4] = {Q.ql1.x, Q.ql1.y, Q.ql1.z, Q.ql1.w};
+			const uint32_t qhw[4] = {Q.qh.x, Q.qh.y, Q.qh.z, Q.qh.w};
+			float tv[4];
 #pragma unroll
 			for (int k = 0; k < 4; k++) {
 				int t = 0, xs = 0;
@@ -181,37 +156,56 @@ q6k_kernel(const __grid_constant__ Q6kParams p)
 				}
 				t -= 32 * xs;
 				const int sidx = g + 2 * k;
-				const int8_t sc = (int8_t)(((sidx < 4 ? r0.sc.x : r0.sc.y) >>
+				const int8_t sc = (int8_t)(((sidx < 4 ? Q.sc.x : Q.sc.y) >>
 							    (8 * (sidx & 3))) & 0xff);
 				tv[k] = __fmul_rn(__fmul_rn(__fmul_rn(dd, (float)sc), xd[k]),
 						  __int2float_rn(t));
 			}
+			*reinterpret_cast<float4 *>(tb + (size_t)r * ts + ((i * 2 + h) * 2 + g) * 4) =
+				make_float4(tv[0], tv[1], tv[2], tv[3]);
 		}
-		// term lane * 4 + k of the chunk at [r][k * 32 + lane]
-#pragma unroll
-		for (int k = 0; k < 4; k++)
-			tw[cc.r * Q6K_TSTRIDE + k * 32 + lane] = tv[k];
-		const uint32_t nr = rows_at(cc.base);
-		if (cc.r + 1 == nr) {
-			// the chunk of every row of this base is in: lane r adds row r's
-			__syncwarp();
-			if ((uint32_t)lane < nr) {
-				const uint32_t nl = (nsb - cc.i0 < 8 ? nsb - cc.i0 : 8) * 4;
-				const float *t = tw + lane * Q6K_TSTRIDE;
-				for (uint32_t l = 0; l < nl; l++)
-#pragma unroll
-					for (int k = 0; k < 4; k++)
-						s = __fadd_rn(s, t[k * 32 + l]);
-				if (cc.i0 + 8 >= nsb) {
-					p.y[cc.base + lane] = s;
-					s = 0.0f;
+	};
+
+	pdl_launch_dependents();
+	uint32_t G = blockIdx.x;
+	if (G < groups)
+		load(G, 0);
+	pdl_wait();
+	{
+		const uint4 *gq = reinterpret_cast<const uint4 *>(p.q);
+		uint4 *sq = reinterpret_cast<uint4 *>(aq);
+		for (uint32_t i = threadIdx.x; i < nsb * 16; i += blockDim.x)
+			sq[i] = gq[i];
+		for (uint32_t i = threadIdx.x; i < nsb * 8; i += blockDim.x)
+			ad[i] = p.d[i];
+	}
+	__syncthreads();
+
+	for (uint32_t it = 0; G < groups; it++, G += gridDim.x) {
+		float *tb = terms + (size_t)(it & 1) * RG * ts;
+		for (uint32_t ps = 0; ps < npass; ps++) {
+			if (ps)
+				load(G, ps);
+			compute(ps, tb);
+		}
+		if (G + gridDim.x < groups)
+			load(G + gridDim.x, 0);
+		named_barrier(1, W * 32);
+		if (warp == 0 && lane < RG) {
+			const uint32_t row = G * RG + lane;
+			if (row < p.rows) {
+				const float4 *t = reinterpret_cast<const float4 *>(tb + (size_t)lane * ts);
+				float s = 0.0f;
+				for (uint32_t j = 0; j < nsb * 4; j++) {
+					const float4 v = t[j];
+					s = __fadd_rn(s, v.x);
+					s = __fadd_rn(s, v.y);
+					s = __fadd_rn(s, v.z);
+					s = __fadd_rn(s, v.w);
 				}
+				p.y[row] = s;
 			}
-			__syncwarp();
 		}
-		r0 = r1;
-		r1 = r2;
-		advance(cc);
 	}
 }
 
