@@ -26,7 +26,10 @@
 // super-block w + W*u (slot u of U; passes of W*U super-blocks) -- three
 // 16-byte loads and the half's 8 scale bytes -- so one warp-load covers 64
 // contiguous bytes of each of the 8 rows, and computes its four terms with
-// dp4a (unsigned 6-bit weights, so the -32 comes off as 32 * sum(activation)).
+// dp4a (unsigned 6-bit weights, so the -32 comes off as 32 * sum(activation):
+// each 16-byte run's activation sum is made once, while the activation is
+// staged, and the staged halves are padded apart so the lanes reading them
+// together hit different banks).
 // The terms go to the row's line of a term buffer at the reference's position
 // ((i*2 + h)*2 + g)*4 + k; after one barrier lanes 0..7 of warp 0 add their
 // row's line in that order while the other warps load the next group. The
@@ -38,7 +41,10 @@
 // before the wait), same bits: the 2048 -> 128256 head 66.2 -> 43.1 us
 // (3.26 -> 5.0 TB/s), K=2048 N=8192 8.3 -> 4.9 us, K=4096 N=4096 11.1 ->
 // 5.3 us, K=8192 N=2048 14.7 -> 6.05 us (four warps in four passes there
-// measured 20.8 us, hence W by K).
+// measured 20.8 us, hence W by K). The run sums made at staging and the padded
+// activation then took the head to 38.0 us, K=8192 N=2048 to 5.66 us; holding
+// the 4-warp form to 64 registers (8 CTAs an SM instead of 7) lost on the head
+// (41.5 us).
 #pragma once
 
 #include "layout.h"
@@ -79,10 +85,16 @@ __host__ __device__ inline uint32_t q6k_tstride(uint32_t nsb)
 	return nsb * 16 + 4;           // floats a row's line: its terms + 4 (banks, 16-byte rows)
 }
 
+// Shared memory: the activation's super-blocks at Q6K_ASB bytes each, half h
+// at h * Q6K_AHALF (the two halves' words then fall in different banks for
+// the lanes that read them together); each 16-byte run's byte sum as int32
+// [i][h][g][k]; the activation deltas; two term buffers.
+constexpr uint32_t Q6K_AHALF = 160, Q6K_ASB = 320;
+
 inline size_t q6k_smem_bytes(uint32_t nsb)
 {
-	return (size_t)nsb * 256 + (size_t)nsb * 8 * sizeof(float) +
-	       (size_t)2 * RG * q6k_tstride(nsb) * sizeof(float);
+	return (size_t)nsb * Q6K_ASB + (size_t)nsb * 16 * sizeof(int32_t) +
+	       (size_t)nsb * 8 * sizeof(float) + (size_t)2 * RG * q6k_tstride(nsb) * sizeof(float);
 }
 
 template <int W, int U>
@@ -91,8 +103,9 @@ q6k_kernel(const __grid_constant__ Q6kParams p)
 {
 	extern __shared__ __align__(128) uint8_t smem[];
 	const uint32_t nsb = p.nsb;
-	int8_t *aq = reinterpret_cast<int8_t *>(smem);
-	float *ad = reinterpret_cast<float *>(smem + (size_t)nsb * 256);
+	uint8_t *aq = smem;
+	int32_t *xsum = reinterpret_cast<int32_t *>(smem + (size_t)nsb * Q6K_ASB);
+	float *ad = reinterpret_cast<float *>(xsum + (size_t)nsb * 16);
 	float *terms = ad + (size_t)nsb * 8;
 	const uint32_t ts = q6k_tstride(nsb);
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -134,7 +147,9 @@ q6k_kernel(const __grid_constant__ Q6kParams p)
 				continue;
 			const Regs &Q = R[u];
 			const float dd = half_bits_to_float(Q.d);
-			const int8_t *xq = aq + (size_t)i * 256 + h * 128 + g * 16;
+			const uint8_t *xq = aq + (size_t)i * Q6K_ASB + h * Q6K_AHALF + g * 16;
+			const int4 xs4 = *reinterpret_cast<const int4 *>(xsum + (size_t)i * 16 + h * 8 + g * 4);
+			const int xs[4] = {xs4.x, xs4.y, xs4.z, xs4.w};
 			const float *xd = ad + (size_t)i * 8 + h * 4;
 			const uint32_t ql0w[4] = {Q.ql0.x, Q.ql0.y, Q.ql0.z, Q.ql0.w};
 			const uint32_t ql1w[4] = {Q.ql1.x, Q.ql1.y, Q.ql1.z, Q.ql1.w};
@@ -142,19 +157,18 @@ q6k_kernel(const __grid_constant__ Q6kParams p)
 			float tv[4];
 #pragma unroll
 			for (int k = 0; k < 4; k++) {
-				int t = 0, xs = 0;
-				const uint32_t *x4 = reinterpret_cast<const uint32_t *>(xq + k * 32);
+				const uint4 xv = *reinterpret_cast<const uint4 *>(xq + k * 32);
+				const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+				int t = 0;
 #pragma unroll
 				for (int wd = 0; wd < 4; wd++) {
 					const uint32_t lo = (k & 1) ? ql1w[wd] : ql0w[wd];
 					const uint32_t nib = (k & 2) ? (lo >> 4) & 0x0f0f0f0fu
 								     : lo & 0x0f0f0f0fu;
 					const uint32_t hi = (qhw[wd] >> (2 * k)) & 0x03030303u;
-					const uint32_t x = x4[wd];
-					t = dp4a_us(nib | (hi << 4), x, t);
-					xs = dp4a_ss(0x01010101u, x, xs);
+					t = dp4a_us(nib | (hi << 4), xw[wd], t);
 				}
-				t -= 32 * xs;
+				t -= 32 * xs[k];
 				const int sidx = g + 2 * k;
 				const int8_t sc = (int8_t)(((sidx < 4 ? Q.sc.x : Q.sc.y) >>
 							    (8 * (sidx & 3))) & 0xff);
@@ -172,10 +186,20 @@ q6k_kernel(const __grid_constant__ Q6kParams p)
 		load(G, 0);
 	pdl_wait();
 	{
+		// 16-byte chunk c of super-block i: half c / 8, run (k, g) = ((c % 8) / 2,
+		// c % 2); its byte sum goes to [i][h][g][k]
 		const uint4 *gq = reinterpret_cast<const uint4 *>(p.q);
-		uint4 *sq = reinterpret_cast<uint4 *>(aq);
-		for (uint32_t i = threadIdx.x; i < nsb * 16; i += blockDim.x)
-			sq[i] = gq[i];
+		for (uint32_t n = threadIdx.x; n < nsb * 16; n += blockDim.x) {
+			const uint32_t i = n / 16, c = n % 16, hh = c / 8, kk = (c % 8) / 2, gg = c % 2;
+			const uint4 v = gq[n];
+			*reinterpret_cast<uint4 *>(aq + (size_t)i * Q6K_ASB + hh * Q6K_AHALF +
+						   (c % 8) * 16) = v;
+			int sum = dp4a_ss(0x01010101u, v.x, 0);
+			sum = dp4a_ss(0x01010101u, v.y, sum);
+			sum = dp4a_ss(0x01010101u, v.z, sum);
+			sum = dp4a_ss(0x01010101u, v.w, sum);
+			xsum[i * 16 + hh * 8 + gg * 4 + kk] = sum;
+		}
 		for (uint32_t i = threadIdx.x; i < nsb * 8; i += blockDim.x)
 			ad[i] = p.d[i];
 	}
