@@ -991,6 +991,32 @@ def matvec_configs(steps: int = 400):
     return out
 
 
+def i8_call_us(L, a, w, bias, sc, steps: int, warm: int = 10):
+    """us a call of charsiu_gpu_matmul_i8_flat called straight through ctypes
+    on host buffers made once (the reference's own bench times its C function
+    the same way), and the output of the last call."""
+    from charsiu_b200.lib import _p
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    bias = np.ascontiguousarray(bias, dtype=np.int32)
+    m, k = a.shape
+    n = w.shape[0]
+    out = np.full((m, n), 0x5a, dtype=np.int8)
+    f = L.L.charsiu_gpu_matmul_i8_flat
+    args = (L.h, m, k, n, _p(a), _p(w), _p(bias), *sc, _p(out))
+    for _ in range(warm):
+        if f(*args):
+            raise RuntimeError(L.error())
+    rc = 0
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        rc |= f(*args)
+    dt = (time.perf_counter() - t0) / steps
+    if rc:
+        raise RuntimeError(L.error())
+    return dt * 1e6, out
+
+
 def int8_configs(steps: int = 200):
     """The int8 matmul with the NPU output stage at each workload shape
     through the public C ABI (charsiu_gpu_matmul_i8_flat, host buffers: the
@@ -1005,15 +1031,10 @@ def int8_configs(steps: int = 200):
         sc = W.i8_scales(m, k, n, seed)
         with Layer(max_k=(max(k, 32) + 31) // 32 * 32, max_n=n, max_tensors=1,
                    device=int(os.environ.get("LOCAL_RANK", 0))) as L:
-            got = L.matmul_i8(a, w, bias, *sc)
-            for _ in range(10):
-                L.matmul_i8(a, w, bias, *sc)
             l0 = L.launches
-            t0 = time.perf_counter()
-            for _ in range(steps):
-                L.matmul_i8(a, w, bias, *sc)
-            dt = (time.perf_counter() - t0) / steps
-            launches = (L.launches - l0) / steps
+            us, got = i8_call_us(L, a, w, bias, sc, steps)
+            dt = us * 1e-6
+            launches = (L.launches - l0) / (steps + 10)
         have = O.have_ref()
         refmm = O.ref_matmul_i8 if have else O.matmul_i8
         exact = bool(np.array_equal(got, refmm(a, w, bias, *sc)))
@@ -1031,7 +1052,8 @@ def int8_configs(steps: int = 200):
         out[name] = row
     out["workload"] = ("(M,K,N) = (1,64,64), (1,512,1024), (224,64,64), (3136,33,64): uniform "
                        "u8 operands around zero point 128, bias in [-4096, 4096]; us_call is "
-                       f"the mean of {steps} host calls, copies in and out included")
+                       f"the mean of {steps} host calls, copies in and out included, "
+                       "the C entry called through ctypes on buffers made once")
     return out
 
 
@@ -1166,14 +1188,11 @@ def run_int8_case(args):
     a, w, bias = W.i8_inputs(m, k, n, 0)
     sc = W.i8_scales(m, k, n, 0)
     with Layer(max_k=(max(k, 32) + 31) // 32 * 32, max_n=n, max_tensors=1) as L:
-        out = L.matmul_i8(a, w, bias, *sc)
-        for _ in range(args.warmup):
-            L.matmul_i8(a, w, bias, *sc)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            L.matmul_i8(a, w, bias, *sc)
-        dt = (time.perf_counter() - t0) / args.steps
-        launches = L.launches
+        l0 = L.launches
+        us, out = i8_call_us(L, a, w, bias, sc, args.steps, warm=args.warmup)
+        dt = us * 1e-6
+        # the timed calls' launches (every call launches the same number)
+        launches = (L.launches - l0) * args.steps // (args.steps + args.warmup)
     ref = O.ref_matmul_i8(a, w, bias, *sc) if O.have_ref() else O.matmul_i8(a, w, bias, *sc)
     if not np.array_equal(out, ref):
         raise RuntimeError("int8 matmul differs from the reference")

@@ -168,7 +168,28 @@ struct I8Params {
 	uint32_t m, k, n;
 	float mult, zp_out;
 	int zp_a, zp_w;
+	// a direct host call (out is mapped host memory): the last CTA to finish
+	// raises *done_flag = seq once every byte is visible to the host; null: none
+	uint32_t *done_count;      // device, zero between launches
+	uint32_t *done_flag;
+	uint32_t seq;
 };
+
+// The end of a direct call: this CTA's stores reach thread 0 through the
+// barrier and are released at device scope by its count; the last CTA
+// acquires them all and orders them before the flag with one system fence.
+// Every thread of the CTA calls it.
+__device__ __forceinline__ void i8_raise_flag(uint32_t *done_count, uint32_t *done_flag,
+					      uint32_t seq)
+{
+	__syncthreads();
+	if (threadIdx.x == 0 &&
+	    atom_add_acq_rel_gpu(done_count, 1u) == gridDim.x * gridDim.y - 1) {
+		*done_count = 0;
+		__threadfence_system();
+		*(volatile uint32_t *)done_flag = seq;
+	}
+}
 
 // CUDA cores, dp4a: a 32 (m) x 32 (n) tile per 256-thread CTA, K in steps of
 // 64 through shared memory; each thread keeps 4 m rows of one column.
@@ -226,24 +247,90 @@ __device__ __forceinline__ void i8mm_simt_body(const I8Params &p, const uint8_t 
 		}
 		__syncthreads();
 	}
+	// (no early return: the direct calls' flag needs every thread at a barrier)
 	const uint32_t col = n0 + tx;
-	if (col >= p.n)
-		return;
-	const int64_t ca = 128 - p.zp_a, cw = 128 - p.zp_w;
+	if (col < p.n) {
+		const int64_t ca = 128 - p.zp_a, cw = 128 - p.zp_w;
 #pragma unroll
-	for (int j = 0; j < 4; j++) {
-		const uint32_t row = m0 + ty + 8 * j;
-		if (row >= p.m)
-			continue;
-		const int64_t total = (int64_t)pbias[col] + acc[j] + cw * sa[j] + ca * sw +
-				      (int64_t)p.k * ca * cw;
-		p.out[(uint64_t)row * p.n + col] = output_stage(total, p.mult, p.zp_out);
+		for (int j = 0; j < 4; j++) {
+			const uint32_t row = m0 + ty + 8 * j;
+			if (row >= p.m)
+				continue;
+			const int64_t total = (int64_t)pbias[col] + acc[j] + cw * sa[j] + ca * sw +
+					      (int64_t)p.k * ca * cw;
+			p.out[(uint64_t)row * p.n + col] = output_stage(total, p.mult, p.zp_out);
+		}
 	}
 }
 
-__global__ void __launch_bounds__(256) i8mm_simt_kernel(const __grid_constant__ I8Params p)
+// M = 1 (a matvec): a warp per output column, 16 columns a CTA of 8 warps.
+// A lane reads 16-byte chunks lane, lane + 32, ... of the column's weight
+// row (bytes one by one when K is not a multiple of 16, the rows then not
+// being aligned) and the same chunks of the activation; the three integer
+// sums of i8mm_simt_body (exact in any order) meet in a warp reduction, and
+// the column's output stage is the same. The CTA's 16 output bytes leave in
+// one 16-byte store when they are all there and aligned (out may be mapped
+// host memory). Against the tiled form (i8mm_simt_body, 32x32 tiles) at
+// (1,512,1024): 64 CTAs instead of 32, and 16-byte loads instead of a K loop
+// of byte loads through shared memory.
+constexpr uint32_t I8MV_COLS = 16;
+
+__global__ void __launch_bounds__(256) i8mv_kernel(const __grid_constant__ I8Params p)
 {
-	i8mm_simt_body(p, p.a, p.w, p.bias);
+	__shared__ __align__(16) int8_t ob[I8MV_COLS];
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const uint32_t c0 = blockIdx.x * I8MV_COLS;
+	const bool vec = (p.k & 15u) == 0;
+	const int64_t ca = 128 - p.zp_a, cw = 128 - p.zp_w;
+#pragma unroll
+	for (int h = 0; h < 2; h++) {
+		const uint32_t col = c0 + warp + 8 * h;
+		int acc = 0, sw = 0, sa = 0;
+		if (col < p.n) {
+			const uint8_t *wr = p.w + (uint64_t)col * p.k;
+			if (vec) {
+				for (uint32_t c = lane; c < p.k / 16; c += 32) {
+					const uint4 wv = ldg_stream(wr + (size_t)c * 16);
+					const uint4 av = *reinterpret_cast<const uint4 *>(p.a + (size_t)c * 16);
+					const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+					const uint32_t aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+					for (int j = 0; j < 4; j++) {
+						const uint32_t ws = ww[j] ^ 0x80808080u, as = aa[j] ^ 0x80808080u;
+						acc = dp4a_ss(as, ws, acc);
+						sw = dp4a_ss(ws, 0x01010101u, sw);
+						sa = dp4a_ss(as, 0x01010101u, sa);
+					}
+				}
+			} else {
+				for (uint32_t kk = lane; kk < p.k; kk += 32) {
+					const int av = (int)p.a[kk] - 128, wv = (int)wr[kk] - 128;
+					acc += av * wv;
+					sw += wv;
+					sa += av;
+				}
+			}
+		}
+		acc = __reduce_add_sync(0xffffffffu, acc);
+		sw = __reduce_add_sync(0xffffffffu, sw);
+		sa = __reduce_add_sync(0xffffffffu, sa);
+		if (lane == 0 && col < p.n) {
+			const int64_t total = (int64_t)p.bias[col] + acc + cw * sa + ca * sw +
+					      (int64_t)p.k * ca * cw;
+			ob[warp + 8 * h] = output_stage(total, p.mult, p.zp_out);
+		}
+	}
+	__syncthreads();
+	if (threadIdx.x == 0) {
+		const uint32_t cnt = p.n - c0 < I8MV_COLS ? p.n - c0 : I8MV_COLS;
+		if (cnt == I8MV_COLS && (c0 & 15u) == 0)
+			*reinterpret_cast<uint4 *>(p.out + c0) = *reinterpret_cast<const uint4 *>(ob);
+		else
+			for (uint32_t j = 0; j < cnt; j++)
+				p.out[c0 + j] = ob[j];
+	}
+	if (p.done_flag)
+		i8_raise_flag(p.done_count, p.done_flag, p.seq);
 }
 
 template <int W>
@@ -252,16 +339,7 @@ i8mm_simt_inline_kernel(const __grid_constant__ I8Inline<W> a)
 {
 	const uint8_t *base = reinterpret_cast<const uint8_t *>(a.data);
 	i8mm_simt_body(a.p, base, base + a.off_w, reinterpret_cast<const int32_t *>(base + a.off_b));
-	// out is host memory: this CTA's stores reach thread 0 through the barrier
-	// and are released at device scope by its count; the last CTA acquires
-	// them all and orders them before the flag with one system fence
-	__syncthreads();
-	if (threadIdx.x == 0 &&
-	    atom_add_acq_rel_gpu(a.done_count, 1u) == gridDim.x * gridDim.y - 1) {
-		*a.done_count = 0;
-		__threadfence_system();
-		*(volatile uint32_t *)a.done_flag = a.seq;
-	}
+	i8_raise_flag(a.done_count, a.done_flag, a.seq);
 }
 
 } // namespace cgpu

@@ -29,6 +29,11 @@
 #include "qmm_tc.cuh"
 #include "ref_abi.h"
 
+extern "C" {
+#include "../host/pool.h"
+}
+#include <unistd.h>
+
 using namespace cgpu;
 
 namespace {
@@ -145,6 +150,8 @@ struct charsiu_gpu {
 	uint32_t seq = 0;
 	QmvInline<QMV_INLINE_MAX_WORDS> *inl = nullptr;    // the direct call's kernel arguments
 	I8Inline<I8_INLINE_W2> *i8inl = nullptr;            // and the int8 direct call's
+	struct pool *copy_pool = nullptr;   // host threads for the large int8 jobs' copies
+	bool copy_pool_tried = false;
 	bool direct = true;  // CHARSIU_GPU_DIRECT=0: every host call through a graph with copies
 	bool smem_set[64] = {};
 	uint8_t *noalloc_scratch = nullptr;  // the allocation-free call's array, on this device
@@ -1121,6 +1128,7 @@ void charsiu_gpu_close(struct charsiu_gpu *g)
 		cudaFreeHost((void *)g->h_flag);
 	delete g->inl;
 	delete g->i8inl;
+	pool_free(g->copy_pool);
 	cudaFree(g->d_sync);
 	cudaFree(g->d_gather_count);
 	cudaFreeHost(g->h_act);
@@ -1672,6 +1680,56 @@ int charsiu_gpu_row_dev(struct charsiu_gpu *g, int id, const int32_t *row, float
 
 } // extern "C"
 
+// Host copies of up to three segments, as one run of bytes cut into 32 KB
+// items for the layer's host threads (CHARSIU_GPU_THREADS, else min(cores - 1,
+// 8)): the large int8 jobs' operands into the pinned staging buffer and their
+// output out of it. A single thread copies 512 KB at about 10 GB/s, which is
+// most of a (1,512,1024) call.
+struct ParCopy {
+	struct Seg {
+		uint8_t *dst;
+		const uint8_t *src;
+		size_t n, start;
+	} seg[3];
+	int nseg = 0;
+	size_t total = 0;
+	static constexpr size_t CHUNK = 32 * 1024;
+	void add(void *dst, const void *src, size_t n)
+	{
+		seg[nseg++] = {static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src), n, total};
+		total += n;
+	}
+	static void item(void *arg, int it)
+	{
+		const ParCopy *pc = static_cast<const ParCopy *>(arg);
+		const size_t lo = (size_t)it * CHUNK, hi = lo + CHUNK;
+		for (int i = 0; i < pc->nseg; i++) {
+			const Seg &sg = pc->seg[i];
+			const size_t a = lo > sg.start ? lo : sg.start;
+			const size_t b = hi < sg.start + sg.n ? hi : sg.start + sg.n;
+			if (a < b)
+				memcpy(sg.dst + (a - sg.start), sg.src + (a - sg.start), b - a);
+		}
+	}
+};
+
+static void par_copy(charsiu_gpu *g, ParCopy &pc)
+{
+	if (pc.total >= 4 * ParCopy::CHUNK && !g->copy_pool_tried) {
+		g->copy_pool_tried = true;
+		const char *e = getenv("CHARSIU_GPU_THREADS");
+		const long cpus = sysconf(_SC_NPROCESSORS_ONLN);
+		const int threads = e ? atoi(e) : (int)(cpus > 2 ? (cpus - 1 < 8 ? cpus - 1 : 8) : 0);
+		g->copy_pool = pool_new(threads);      // NULL: the caller copies alone
+	}
+	const int items = (int)((pc.total + ParCopy::CHUNK - 1) / ParCopy::CHUNK);
+	if (items >= 4 && g->copy_pool)
+		pool_run(g->copy_pool, ParCopy::item, &pc, items);
+	else
+		for (int i = 0; i < items; i++)
+			ParCopy::item(&pc, i);
+}
+
 // A small int8 job as one direct call (i8mm_simt_inline_kernel): the operands
 // in the launch's own parameters, the bytes written into mapped host memory,
 // the last CTA raising the sequence flag the host spins on. One launch; no
@@ -1701,6 +1759,7 @@ static int matmul_i8_direct(charsiu_gpu *g, unsigned m, unsigned k, unsigned n,
 	memcpy(data + ow, w, sw);
 	memcpy(data + ob, bias, sb);
 	const uint32_t seq = ++g->seq ? g->seq : ++g->seq;     // never 0, the flag's reset value
+	x.p = I8Params{};
 	x.p.a = nullptr;
 	x.p.w = nullptr;
 	x.p.bias = nullptr;
@@ -1779,18 +1838,41 @@ int charsiu_gpu_matmul_i8_flat(struct charsiu_gpu *g, unsigned m, unsigned k, un
 		whine(g, "a staging buffer would not allocate");
 		return -1;
 	}
+	// a direct call (the default): the kernel writes the bytes into mapped
+	// host memory and its last CTA raises the sequence flag -- no read-back
+	// copy and no event in the call
+	int8_t *out_map = nullptr;
+	if (g->direct) {
+		out_map = reinterpret_cast<int8_t *>(dev_view(g->h_i8));
+		if (!out_map) {
+			whine(g, "a staging buffer has no device address");
+			return -1;
+		}
+		out_map += oo;
+	}
 	const double t0 = now_us();
-	memcpy(g->h_i8 + oa, a, sa);
-	memcpy(g->h_i8 + ow, w, sw);
-	memcpy(g->h_i8 + ob, bias, sb);
+	{
+		ParCopy pc;
+		pc.add(g->h_i8 + oa, a, sa);
+		pc.add(g->h_i8 + ow, w, sw);
+		pc.add(g->h_i8 + ob, bias, sb);
+		par_copy(g, pc);
+	}
 	cudaMemcpyAsync(g->d_i8, g->h_i8, oo, cudaMemcpyHostToDevice, g->stream);
 	const double t1 = now_us();
 
-	I8Params p;
+	I8Params p = {};
 	p.a = g->d_i8 + oa;
 	p.w = g->d_i8 + ow;
 	p.bias = reinterpret_cast<const int32_t *>(g->d_i8 + ob);
-	p.out = reinterpret_cast<int8_t *>(g->d_i8 + oo);
+	p.out = out_map ? out_map : reinterpret_cast<int8_t *>(g->d_i8 + oo);
+	uint32_t seq = 0;
+	if (out_map) {
+		seq = ++g->seq ? g->seq : ++g->seq;     // never 0, the flag's reset value
+		p.done_count = g->d_sync;
+		p.done_flag = g->d_flag;
+		p.seq = seq;
+	}
 	p.m = m;
 	p.k = k;
 	p.n = n;
@@ -1798,10 +1880,11 @@ int charsiu_gpu_matmul_i8_flat(struct charsiu_gpu *g, unsigned m, unsigned k, un
 	p.zp_out = (float)out_zp;
 	p.zp_a = in_zp;
 	p.zp_w = wt_zp;
-	cudaEventRecord(g->ev_k0, g->stream);
+	if (!out_map)
+		cudaEventRecord(g->ev_k0, g->stream);
 	// M = 1 (a matvec): dp4a on the CUDA cores; M > 1: the tensor cores
 	if (m == 1)
-		i8mm_simt_kernel<<<dim3((n + 31) / 32, (m + 31) / 32), 256, 0, g->stream>>>(p);
+		i8mv_kernel<<<(n + I8MV_COLS - 1) / I8MV_COLS, 256, 0, g->stream>>>(p);
 	else if (n <= 64)
 		i8mm_tc_kernel<64><<<dim3((n + 63) / 64, (m + I8TC_M - 1) / I8TC_M), 128, 0,
 				    g->stream>>>(p, g->d_err);
@@ -1814,6 +1897,22 @@ int charsiu_gpu_matmul_i8_flat(struct charsiu_gpu *g, unsigned m, unsigned k, un
 		return -1;
 	}
 	g->launches++;
+	if (out_map) {
+		const double mbd = (double)(sa + sw) / 1e6;
+		if (wait_direct(g, seq, t0, mbd, k))
+			return -1;
+		const double t2 = now_us();
+		ParCopy pc;
+		pc.add(out, g->h_i8 + oo, (size_t)m * n);
+		par_copy(g, pc);
+		const double t3 = now_us();
+		g->calls++;
+		g->weight_mb += mbd;
+		g->h2d_us += t1 - t0;
+		g->d2h_us += t3 - t2;
+		g->busy_us += t3 - t0;
+		return 0;
+	}
 	cudaEventRecord(g->ev_k1, g->stream);
 	cudaMemcpyAsync(g->h_i8 + oo, g->d_i8 + oo, (size_t)m * n, cudaMemcpyDeviceToHost,
 			g->stream);

@@ -2,7 +2,7 @@
 // The int8 matmul with the NPU's output stage on the tensor cores, for M > 1
 // (batched decode, prefill): tcgen05.mma kind::i8, int32 accumulator in
 // tensor memory. Byte-exact against cpu_reference (tools/charsiu_matmul.c:41-81)
-// by the same arithmetic as i8mm_simt_kernel (aux_kernels.cuh): signed
+// by the same arithmetic as i8mm_simt_body (aux_kernels.cuh): signed
 // operands a ^ 0x80 and w ^ 0x80, zero points folded in afterwards, the
 // reference's float requant.
 //
@@ -112,6 +112,10 @@ __global__ void __launch_bounds__(128) i8mm_tc_kernel(const __grid_constant__ I8
 			tmem_ld16(taddr + ((uint32_t)(warp * 32) << 16) + c, r);
 			tmem_wait_ld();
 			if (row < p.m) {
+				// 16 columns of one row: one 16-byte store when they are all
+				// there and aligned (out may be mapped host memory, where a
+				// byte store is a bus transaction of its own)
+				uint32_t pk[4] = {0, 0, 0, 0};
 #pragma unroll
 				for (int j = 0; j < 16; j++) {
 					const uint32_t col = n0 + c + j;
@@ -119,9 +123,19 @@ __global__ void __launch_bounds__(128) i8mm_tc_kernel(const __grid_constant__ I8
 						const int64_t total = (int64_t)p.bias[col] + (int32_t)r[j] +
 							cw * sa[warp * 32 + lane] + ca * sw[c + j] +
 							(int64_t)p.k * ca * cw;
-						p.out[(uint64_t)row * p.n + col] =
-							output_stage(total, p.mult, p.zp_out);
+						const int8_t o = output_stage(total, p.mult, p.zp_out);
+						pk[j >> 2] |= (uint32_t)(uint8_t)o << (8 * (j & 3));
 					}
+				}
+				const uint64_t o0 = (uint64_t)row * p.n + n0 + c;
+				if (n0 + c + 16 <= p.n && (o0 & 15) == 0) {
+					*reinterpret_cast<uint4 *>(p.out + o0) =
+						make_uint4(pk[0], pk[1], pk[2], pk[3]);
+				} else {
+#pragma unroll
+					for (int j = 0; j < 16; j++)
+						if (n0 + c + j < p.n)
+							p.out[o0 + j] = (int8_t)(pk[j >> 2] >> (8 * (j & 3)));
 				}
 			}
 		}
@@ -130,6 +144,8 @@ __global__ void __launch_bounds__(128) i8mm_tc_kernel(const __grid_constant__ I8
 	__syncthreads();
 	if (warp == 0)
 		tmem_dealloc(taddr, NT < 32 ? 32 : NT);
+	if (p.done_flag)
+		i8_raise_flag(p.done_count, p.done_flag, p.seq);
 }
 
 } // namespace cgpu
