@@ -440,8 +440,9 @@ uint32_t qmm_na(const charsiu_gpu *g, uint32_t m)
 
 // The (NA, EC) of one launch of `tiles` row tiles: the smallest units that
 // still run in one round on the SMs. An epilogue warp's share of a unit is
-// the same in every shape (32 rows, 8 activations), so a smaller unit takes
-// no longer than a larger one and more of them run side by side; once they
+// the same in every shape (32 rows, 8 activations; 4 in the 4-wide units), so
+// a smaller unit takes no longer than a larger one and more of them run side
+// by side; once they
 // no longer fit one round, the larger units' fewer rounds win. At m = 64 the
 // 2048-row launches (o, down) run 128 units of (tile, 8 activations) instead
 // of 32 of (tile, 32). A forced NA (CHARSIU_GPU_QMM_NA) or PRE keeps EC = NA.
@@ -457,6 +458,13 @@ void qmm_launch_shape(const charsiu_gpu *g, uint32_t m, uint32_t tiles, uint32_t
 		return;
 	na = 16;
 	ec = 2 * u16 <= sms ? 8 : 16;
+	// units of 4 activations while even they fit one round: the 2048-row
+	// launches at M = 16 / 32 (32 -> 64 units) and every launch of a column
+	// split's slabs (1B step at M = 16 1.266 -> 1.217 ms, M = 32 1.338 ->
+	// 1.305, bit-exact; an L2 prefetch of the weight segments two stages
+	// ahead measured slower on top of it)
+	if (ec == 8 && 4 * u16 <= sms)
+		ec = 4;
 }
 
 size_t qmm_pack_bytes(uint32_t na, uint32_t m, uint32_t nb)
@@ -516,11 +524,12 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	const bool pre = g->qmm_pre && ec == na;
 	const void *fn = na == 32 ? (pre ? (const void *)qmm_tc_kernel<32, 32, true>
 					 : (const void *)qmm_tc_kernel<32, 32, false>)
+			 : ec == 4 ? (const void *)qmm_tc_kernel<16, 4, false>
 			 : ec == 8 ? (const void *)qmm_tc_kernel<16, 8, false>
 				   : (pre ? (const void *)qmm_tc_kernel<16, 16, true>
 					  : (const void *)qmm_tc_kernel<16, 16, false>);
-	// smem_set slots: 20..23 (NA, PRE), 19 the 8-activation slices
-	const int slot = ec == 8 ? 19 : 20 + (na == 32 ? 2 : 0) + (pre ? 1 : 0);
+	// smem_set slots: 20..23 (NA, PRE), 19 the 8-activation slices, 18 the 4-activation
+	const int slot = ec == 4 ? 18 : ec == 8 ? 19 : 20 + (na == 32 ? 2 : 0) + (pre ? 1 : 0);
 	const size_t smem = qmm_smem_bytes(na, ec);
 	if (!g->smem_set[slot]) {
 		if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -19,14 +19,15 @@
 // activation tile fastest so the CTAs sharing a weight tile run together (the
 // second and later reads of it hit L2). With EC < NA each CTA still issues
 // the whole NA-wide MMA (the tensor pipe is nearly idle here) and its
-// epilogue takes only its slice: twice the units, for launches too small to
-// fill the SMs otherwise. Warp
+// epilogue takes only its slice: two or four times the units, for launches
+// too small to fill the SMs otherwise. Warp
 // roles: warp 0 lane 0 issues the single-destination bulk copies of one K
 // segment (16 blocks) a stage -- the tile's 16 groups' weight segments as
 // they lie in the device layout (layout.h), already MMA core matrices, and
 // the packed activation tile (qmm_pack_kernel) -- into a double-buffered
 // stage; warp 1 owns tensor memory and lane 0 issues the MMAs; EW = 4 * EC/8
-// epilogue warps (a tensor-memory lane quarter and 8 activations each) read
+// epilogue warps (a tensor-memory lane quarter and 8 activations each; four
+// warps of 4 activations for a 4-wide slice) read
 // the int32 tiles with tcgen05.ld and accumulate: per chunk, the four blocks'
 // products first (independent, so they overlap), then the four in-order sums.
 // Every step uses the packed fp32x2 operations (two columns an instruction,
@@ -76,15 +77,22 @@ __host__ __device__ constexpr uint32_t qmm_bar_bytes()
 	return 24 * sizeof(uint64_t) + 16;
 }
 
+// epilogue warps: four (one a tensor-memory lane quarter) for each 8
+// activations of a unit's slice; a 4-wide slice takes four warps of 4
+__host__ __device__ constexpr int qmm_epi_warps(int ec)
+{
+	return 4 * (ec < QMM_EPI_COLS ? 1 : ec / QMM_EPI_COLS);
+}
+
 __host__ inline size_t qmm_smem_bytes(uint32_t na, uint32_t ec)
 {
 	return 2 * ((size_t)QMM_WSTAGE + qmm_act_seg_bytes(na)) + qmm_bar_bytes() +
-	       (size_t)4 * (ec / QMM_EPI_COLS) * QMM_PRIV_BYTES;
+	       (size_t)qmm_epi_warps((int)ec) * QMM_PRIV_BYTES;
 }
 
 __host__ __device__ constexpr int qmm_threads(int ec)
 {
-	return (2 + 4 * (ec / QMM_EPI_COLS)) * 32;
+	return (2 + qmm_epi_warps(ec)) * 32;
 }
 
 // tensor-memory columns: QMM_TBUFS chunk buffers of QMM_CHUNK blocks of NA columns
@@ -164,8 +172,9 @@ template <int NA, int EC, bool PRE>
 __global__ void __launch_bounds__(qmm_threads(EC), 1)
 qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGather gth)
 {
-	constexpr int CW = QMM_EPI_COLS;                   // activations an epilogue warp
-	constexpr int EW = 4 * (EC / CW);                  // epilogue warps
+	constexpr int CW = EC < QMM_EPI_COLS ? EC : QMM_EPI_COLS;   // activations an epilogue warp
+	constexpr int EW = qmm_epi_warps(EC);              // epilogue warps
+	static_assert(CW == 8 || (CW == 4 && EC == 4), "epilogue warps of 8 activations, or one 4-wide slice");
 	constexpr uint32_t SL = NA / EC;                   // slices a tile
 	static_assert(NA % EC == 0 && EC % CW == 0 && (!PRE || EC == NA),
 		      "slices of whole epilogue warps; PRE fills every column it reads");
@@ -375,11 +384,13 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 								stage_w(st) + (g0 + gl) * MAX_SEG_BYTES +
 								sb * RG * 32 + w * 16);
 					}
-					const uint32_t bi = lane >> 1, hf = lane & 1;
-					reinterpret_cast<uint4 *>(priv + QMM_PRIV_DW)[lane] =
-						*reinterpret_cast<const uint4 *>(
-							stage_a(st) + SB * 2 * NA * 16 +
-							(bi * NA + cb + 4 * hf) * 4);
+					// (CW = 4: lane L < 16 copies block L's 4)
+					const uint32_t bi = CW == 8 ? lane >> 1 : lane, hf = CW == 8 ? lane & 1 : 0;
+					if (CW == 8 || lane < SB)
+						reinterpret_cast<uint4 *>(priv + QMM_PRIV_DW)[lane] =
+							*reinterpret_cast<const uint4 *>(
+								stage_a(st) + SB * 2 * NA * 16 +
+								(bi * NA + cb + 4 * hf) * 4);
 				}
 				__syncwarp();
 				if (lane == 0)
@@ -397,14 +408,22 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 					}
 					tc_fence_after();
 					// the chunk's tiles as packed float bits 1.5 * 2^23 + t
-					static_assert(CW == 8 && QMM_CHUNK == 4, "tmem_ld_chunk4 shape");
+					static_assert(QMM_CHUNK == 4, "tmem_ld_chunk4 shape");
 					uint64_t tp[QMM_CHUNK][CW / 2];
 					const uint32_t col0 = taddr + lane_base + buf * QMM_CHUNK * NA + cb;
-					if (nblk == QMM_CHUNK)
-						tmem_ld_chunk4<!PRE>(col0, NA, tp);
-					else
-						for (int j = 0; j < (int)nblk; j++)
-							tmem_ld_block<!PRE>(col0 + j * NA, tp[j]);
+					if constexpr (CW == 8) {
+						if (nblk == QMM_CHUNK)
+							tmem_ld_chunk4<!PRE>(col0, NA, tp);
+						else
+							for (int j = 0; j < (int)nblk; j++)
+								tmem_ld_block<!PRE>(col0 + j * NA, tp[j]);
+					} else {
+						if (nblk == QMM_CHUNK)
+							tmem_ld_chunk4_c4(col0, NA, tp);
+						else
+							for (int j = 0; j < (int)nblk; j++)
+								tmem_ld_block_c4(col0 + j * NA, tp[j]);
+					}
 					if (PRE) {
 #pragma unroll
 						for (int j = 0; j < QMM_CHUNK; j++)

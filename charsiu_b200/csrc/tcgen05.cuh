@@ -253,6 +253,67 @@ __device__ __forceinline__ void tmem_ld_block(uint32_t taddr, uint64_t (&p)[4])
 			     : "memory");
 }
 
+// Four blocks' tiles of one chunk, 32 lanes x 4 columns each (an epilogue
+// warp that owns 4 activations), with the integer-to-float add of
+// tmem_ld_chunk4<true>: p[j] = block j's columns in pairs.
+__device__ __forceinline__ void tmem_ld_chunk4_c4(uint32_t taddr, uint32_t stride,
+						  uint64_t (&p)[4][2])
+{
+	asm volatile("{\n\t.reg .b32 r<16>;\n\t"
+		     "tcgen05.ld.sync.aligned.32x32b.x4.b32 {r0, r1, r2, r3}, [%8];\n\t"
+		     "tcgen05.ld.sync.aligned.32x32b.x4.b32 {r4, r5, r6, r7}, [%9];\n\t"
+		     "tcgen05.ld.sync.aligned.32x32b.x4.b32 {r8, r9, r10, r11}, [%10];\n\t"
+		     "tcgen05.ld.sync.aligned.32x32b.x4.b32 {r12, r13, r14, r15}, [%11];\n\t"
+		     "tcgen05.wait::ld.sync.aligned;\n\t"
+		     "add.u32 r0, r0, 0x4b400000;\n\t"
+		     "add.u32 r1, r1, 0x4b400000;\n\t"
+		     "add.u32 r2, r2, 0x4b400000;\n\t"
+		     "add.u32 r3, r3, 0x4b400000;\n\t"
+		     "add.u32 r4, r4, 0x4b400000;\n\t"
+		     "add.u32 r5, r5, 0x4b400000;\n\t"
+		     "add.u32 r6, r6, 0x4b400000;\n\t"
+		     "add.u32 r7, r7, 0x4b400000;\n\t"
+		     "add.u32 r8, r8, 0x4b400000;\n\t"
+		     "add.u32 r9, r9, 0x4b400000;\n\t"
+		     "add.u32 r10, r10, 0x4b400000;\n\t"
+		     "add.u32 r11, r11, 0x4b400000;\n\t"
+		     "add.u32 r12, r12, 0x4b400000;\n\t"
+		     "add.u32 r13, r13, 0x4b400000;\n\t"
+		     "add.u32 r14, r14, 0x4b400000;\n\t"
+		     "add.u32 r15, r15, 0x4b400000;\n\t"
+		     "mov.b64 %0, {r0, r1};\n\t"
+		     "mov.b64 %1, {r2, r3};\n\t"
+		     "mov.b64 %2, {r4, r5};\n\t"
+		     "mov.b64 %3, {r6, r7};\n\t"
+		     "mov.b64 %4, {r8, r9};\n\t"
+		     "mov.b64 %5, {r10, r11};\n\t"
+		     "mov.b64 %6, {r12, r13};\n\t"
+		     "mov.b64 %7, {r14, r15};\n\t"
+		     "}"
+		     : "=l"(p[0][0]), "=l"(p[0][1]), "=l"(p[1][0]), "=l"(p[1][1]), "=l"(p[2][0]),
+		       "=l"(p[2][1]), "=l"(p[3][0]), "=l"(p[3][1])
+		     : "r"(taddr), "r"(taddr + stride), "r"(taddr + 2 * stride), "r"(taddr + 3 * stride)
+		     : "memory");
+}
+
+// The same for one block, for a chunk's ragged tail.
+__device__ __forceinline__ void tmem_ld_block_c4(uint32_t taddr, uint64_t (&p)[2])
+{
+	asm volatile("{\n\t.reg .b32 r<4>;\n\t"
+		     "tcgen05.ld.sync.aligned.32x32b.x4.b32 {r0, r1, r2, r3}, [%2];\n\t"
+		     "tcgen05.wait::ld.sync.aligned;\n\t"
+		     "add.u32 r0, r0, 0x4b400000;\n\t"
+		     "add.u32 r1, r1, 0x4b400000;\n\t"
+		     "add.u32 r2, r2, 0x4b400000;\n\t"
+		     "add.u32 r3, r3, 0x4b400000;\n\t"
+		     "mov.b64 %0, {r0, r1};\n\t"
+		     "mov.b64 %1, {r2, r3};\n\t"
+		     "}"
+		     : "=l"(p[0]), "=l"(p[1])
+		     : "r"(taddr)
+		     : "memory");
+}
+
 // The same 32 lanes x 16 columns, every word set to `v`.
 __device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t v)
 {
