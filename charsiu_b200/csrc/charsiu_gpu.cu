@@ -150,8 +150,10 @@ struct charsiu_gpu {
 	uint32_t seq = 0;
 	QmvInline<QMV_INLINE_MAX_WORDS> *inl = nullptr;    // the direct call's kernel arguments
 	I8Inline<I8_INLINE_W2> *i8inl = nullptr;            // and the int8 direct call's
-	struct pool *copy_pool = nullptr;   // host threads for the large int8 jobs' copies
-	bool copy_pool_tried = false;
+	// host threads for large copies: the layer's own, or lent by the decode
+	// loop that owns this layer (one set of threads serving both)
+	struct pool *copy_pool = nullptr;
+	bool copy_pool_tried = false, copy_pool_owned = false;
 	bool direct = true;  // CHARSIU_GPU_DIRECT=0: every host call through a graph with copies
 	bool smem_set[64] = {};
 	uint8_t *noalloc_scratch = nullptr;  // the allocation-free call's array, on this device
@@ -732,6 +734,59 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 // memory), under the reference's budget (src/npudev.c:560-573) as finish()
 // applies it: a CUDA error, a launch that finished without signalling or one
 // that never finishes retires the layer, and three slow calls in a row too.
+// Host copies of up to QMV_MAX_TENSORS segments, as one run of bytes cut into
+// 16 KB items for the layer's host threads (CHARSIU_GPU_THREADS, else
+// min(cores - 1, 8)) once it reaches 64 KB: the large int8 jobs' operands into
+// the pinned staging buffer, their output out of it, and the direct matvecs'
+// outputs out of mapped host memory (written by the GPU over PCIe, so not in
+// any CPU cache: one thread reads 64 KB of it in about 8 us). A single thread
+// copies 512 KB at about 10 GB/s, which is most of a (1,512,1024) int8 call.
+struct ParCopy {
+	struct Seg {
+		uint8_t *dst;
+		const uint8_t *src;
+		size_t n, start;
+	} seg[QMV_MAX_TENSORS];
+	int nseg = 0;
+	size_t total = 0;
+	static constexpr size_t CHUNK = 16 * 1024;
+	void add(void *dst, const void *src, size_t n)
+	{
+		seg[nseg++] = {static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src), n, total};
+		total += n;
+	}
+	static void item(void *arg, int it)
+	{
+		const ParCopy *pc = static_cast<const ParCopy *>(arg);
+		const size_t lo = (size_t)it * CHUNK, hi = lo + CHUNK;
+		for (int i = 0; i < pc->nseg; i++) {
+			const Seg &sg = pc->seg[i];
+			const size_t a = lo > sg.start ? lo : sg.start;
+			const size_t b = hi < sg.start + sg.n ? hi : sg.start + sg.n;
+			if (a < b)
+				memcpy(sg.dst + (a - sg.start), sg.src + (a - sg.start), b - a);
+		}
+	}
+};
+
+void par_copy(charsiu_gpu *g, ParCopy &pc)
+{
+	if (pc.total >= 4 * ParCopy::CHUNK && !g->copy_pool_tried) {
+		g->copy_pool_tried = true;
+		const char *e = getenv("CHARSIU_GPU_THREADS");
+		const long cpus = sysconf(_SC_NPROCESSORS_ONLN);
+		const int threads = e ? atoi(e) : (int)(cpus > 2 ? (cpus - 1 < 8 ? cpus - 1 : 8) : 0);
+		g->copy_pool = pool_new(threads);      // NULL: the caller copies alone
+		g->copy_pool_owned = g->copy_pool != nullptr;
+	}
+	const int items = (int)((pc.total + ParCopy::CHUNK - 1) / ParCopy::CHUNK);
+	if (items >= 4 && g->copy_pool)
+		pool_run(g->copy_pool, ParCopy::item, &pc, items);
+	else
+		for (int i = 0; i < items; i++)
+			ParCopy::item(&pc, i);
+}
+
 int wait_direct(charsiu_gpu *g, uint32_t seq, double t0, double mb, unsigned k)
 {
 	// the reference's budget (src/npudev.c:560-573), as finish() applies it
@@ -823,11 +878,15 @@ int run_direct(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	if (wait_direct(g, seq, t0, mb, k))
 		return -1;
 	const double t2 = now_us();
-	off = 0;
-	for (unsigned i = 0; i < n; i++) {
-		const size_t cnt = g->ent[ids[i]].rows;
-		memcpy(ys[i], g->h_y + off, cnt * sizeof(float));
-		off += cnt;
+	{
+		ParCopy pc;
+		off = 0;
+		for (unsigned i = 0; i < n; i++) {
+			const size_t cnt = g->ent[ids[i]].rows;
+			pc.add(ys[i], g->h_y + off, cnt * sizeof(float));
+			off += cnt;
+		}
+		par_copy(g, pc);
 	}
 	const double t3 = now_us();
 	g->calls++;
@@ -1137,7 +1196,8 @@ void charsiu_gpu_close(struct charsiu_gpu *g)
 		cudaFreeHost((void *)g->h_flag);
 	delete g->inl;
 	delete g->i8inl;
-	pool_free(g->copy_pool);
+	if (g->copy_pool_owned)
+		pool_free(g->copy_pool);
 	cudaFree(g->d_sync);
 	cudaFree(g->d_gather_count);
 	cudaFreeHost(g->h_act);
@@ -1689,56 +1749,6 @@ int charsiu_gpu_row_dev(struct charsiu_gpu *g, int id, const int32_t *row, float
 
 } // extern "C"
 
-// Host copies of up to three segments, as one run of bytes cut into 32 KB
-// items for the layer's host threads (CHARSIU_GPU_THREADS, else min(cores - 1,
-// 8)): the large int8 jobs' operands into the pinned staging buffer and their
-// output out of it. A single thread copies 512 KB at about 10 GB/s, which is
-// most of a (1,512,1024) call.
-struct ParCopy {
-	struct Seg {
-		uint8_t *dst;
-		const uint8_t *src;
-		size_t n, start;
-	} seg[3];
-	int nseg = 0;
-	size_t total = 0;
-	static constexpr size_t CHUNK = 32 * 1024;
-	void add(void *dst, const void *src, size_t n)
-	{
-		seg[nseg++] = {static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src), n, total};
-		total += n;
-	}
-	static void item(void *arg, int it)
-	{
-		const ParCopy *pc = static_cast<const ParCopy *>(arg);
-		const size_t lo = (size_t)it * CHUNK, hi = lo + CHUNK;
-		for (int i = 0; i < pc->nseg; i++) {
-			const Seg &sg = pc->seg[i];
-			const size_t a = lo > sg.start ? lo : sg.start;
-			const size_t b = hi < sg.start + sg.n ? hi : sg.start + sg.n;
-			if (a < b)
-				memcpy(sg.dst + (a - sg.start), sg.src + (a - sg.start), b - a);
-		}
-	}
-};
-
-static void par_copy(charsiu_gpu *g, ParCopy &pc)
-{
-	if (pc.total >= 4 * ParCopy::CHUNK && !g->copy_pool_tried) {
-		g->copy_pool_tried = true;
-		const char *e = getenv("CHARSIU_GPU_THREADS");
-		const long cpus = sysconf(_SC_NPROCESSORS_ONLN);
-		const int threads = e ? atoi(e) : (int)(cpus > 2 ? (cpus - 1 < 8 ? cpus - 1 : 8) : 0);
-		g->copy_pool = pool_new(threads);      // NULL: the caller copies alone
-	}
-	const int items = (int)((pc.total + ParCopy::CHUNK - 1) / ParCopy::CHUNK);
-	if (items >= 4 && g->copy_pool)
-		pool_run(g->copy_pool, ParCopy::item, &pc, items);
-	else
-		for (int i = 0; i < items; i++)
-			ParCopy::item(&pc, i);
-}
-
 // A small int8 job as one direct call (i8mm_simt_inline_kernel): the operands
 // in the launch's own parameters, the bytes written into mapped host memory,
 // the last CTA raising the sequence flag the host spins on. One launch; no
@@ -1988,6 +1998,21 @@ int charsiu_gpu_dead(const struct charsiu_gpu *g)
 
 // What the device actually did, printed whether it went well or not
 // (src/npudev.c:264-295).
+// Internal to the library (host/llama_gpu.c): the decode loop lends the
+// layer its pool for the large copies, so that two sets of spinning host
+// threads never compete for the cores; NULL takes it back (single-threaded
+// copies from then on). The layer never frees a lent pool.
+void charsiu_gpu_lend_pool(struct charsiu_gpu *g, struct pool *p)
+{
+	if (!g)
+		return;
+	if (g->copy_pool_owned)
+		pool_free(g->copy_pool);
+	g->copy_pool = p;
+	g->copy_pool_owned = false;
+	g->copy_pool_tried = true;
+}
+
 void charsiu_gpu_report(const struct charsiu_gpu *g)
 {
 	if (!g)

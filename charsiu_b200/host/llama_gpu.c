@@ -25,6 +25,10 @@
 #include "charsiu_npu.h"
 #include "pool.h"
 
+/* internal to the library (csrc/charsiu_gpu.cu): lend the layer this loop's
+ * host threads for its large copies; NULL takes them back */
+void charsiu_gpu_lend_pool(struct charsiu_gpu *g, struct pool *p);
+
 #define API
 
 enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q6_K = 14 };
@@ -775,6 +779,7 @@ API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m)
 			fprintf(stderr, "  %-16s %8.3f ms a token   %5.1f%%\n", stage_name[i],
 				m->stage_ms[i] / m->stage_tok, 100.0 * m->stage_ms[i] / tot);
 	}
+	charsiu_gpu_lend_pool(m->dev, NULL);
 	pool_free(m->pool);
 	charsiu_gpu_decoder_free(m->dec);
 	if (m->npu && getenv("CHARSIU_GPU_REPORT"))
@@ -864,6 +869,7 @@ API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *path, int n_ctx
 		int threads = e ? atoi(e) : (int)(cpus > 2 ? (cpus - 1 < 8 ? cpus - 1 : 8) : 0);
 
 		m->pool = pool_new(threads);
+		charsiu_gpu_lend_pool(m->dev, m->pool);
 	}
 	{
 		const char *e = getenv("CHARSIU_NPU_QUANT");
