@@ -29,9 +29,7 @@
 #include "qmm_tc.cuh"
 #include "ref_abi.h"
 
-extern "C" {
-#include "../host/pool.h"
-}
+#include "host_copy.h"
 #include <unistd.h>
 
 using namespace cgpu;
@@ -734,41 +732,8 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 // memory), under the reference's budget (src/npudev.c:560-573) as finish()
 // applies it: a CUDA error, a launch that finished without signalling or one
 // that never finishes retires the layer, and three slow calls in a row too.
-// Host copies of up to QMV_MAX_TENSORS segments, as one run of bytes cut into
-// 16 KB items for the layer's host threads (CHARSIU_GPU_THREADS, else
-// min(cores - 1, 8)) once it reaches 64 KB: the large int8 jobs' operands into
-// the pinned staging buffer, their output out of it, and the direct matvecs'
-// outputs out of mapped host memory (written by the GPU over PCIe, so not in
-// any CPU cache: one thread reads 64 KB of it in about 8 us). A single thread
-// copies 512 KB at about 10 GB/s, which is most of a (1,512,1024) int8 call.
-struct ParCopy {
-	struct Seg {
-		uint8_t *dst;
-		const uint8_t *src;
-		size_t n, start;
-	} seg[QMV_MAX_TENSORS];
-	int nseg = 0;
-	size_t total = 0;
-	static constexpr size_t CHUNK = 16 * 1024;
-	void add(void *dst, const void *src, size_t n)
-	{
-		seg[nseg++] = {static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src), n, total};
-		total += n;
-	}
-	static void item(void *arg, int it)
-	{
-		const ParCopy *pc = static_cast<const ParCopy *>(arg);
-		const size_t lo = (size_t)it * CHUNK, hi = lo + CHUNK;
-		for (int i = 0; i < pc->nseg; i++) {
-			const Seg &sg = pc->seg[i];
-			const size_t a = lo > sg.start ? lo : sg.start;
-			const size_t b = hi < sg.start + sg.n ? hi : sg.start + sg.n;
-			if (a < b)
-				memcpy(sg.dst + (a - sg.start), sg.src + (a - sg.start), b - a);
-		}
-	}
-};
-
+// The layer's large copies on its host threads: the pool the decode loop
+// lent it, else one of its own made at the first copy of 64 KB or more.
 void par_copy(charsiu_gpu *g, ParCopy &pc)
 {
 	if (pc.total >= 4 * ParCopy::CHUNK && !g->copy_pool_tried) {
@@ -779,12 +744,7 @@ void par_copy(charsiu_gpu *g, ParCopy &pc)
 		g->copy_pool = pool_new(threads);      // NULL: the caller copies alone
 		g->copy_pool_owned = g->copy_pool != nullptr;
 	}
-	const int items = (int)((pc.total + ParCopy::CHUNK - 1) / ParCopy::CHUNK);
-	if (items >= 4 && g->copy_pool)
-		pool_run(g->copy_pool, ParCopy::item, &pc, items);
-	else
-		for (int i = 0; i < items; i++)
-			ParCopy::item(&pc, i);
+	pc.run(g->copy_pool);
 }
 
 int wait_direct(charsiu_gpu *g, uint32_t seq, double t0, double mb, unsigned k)

@@ -25,6 +25,7 @@
 
 #include "charsiu_npu.h"
 
+#include "host_copy.h"
 #include "npu_internal.h"
 #include "npumv.cuh"
 #include "ref_abi.h"
@@ -72,6 +73,7 @@ struct charsiu_npu {
 	double busy_us = 0, kern_ms = 0, weight_mb = 0, slow_us = 100000;
 	int strikes = 0, dead = 0, whined = 0, no_pdl = 0;
 	std::string err;
+	struct pool *pool = nullptr;       // lent by the decode loop for large read-backs
 };
 
 namespace {
@@ -281,11 +283,16 @@ int run(charsiu_npu *g, const int *ids, unsigned n, const int8_t *q1, float d1, 
 	} else {
 		g->strikes = 0;
 	}
-	off = 0;
-	for (unsigned i = 0; i < n; i++) {
-		const size_t cnt = g->ent[ids[i]].n;
-		memcpy(ys[i], g->h_y + off, cnt * sizeof(float));
-		off += cnt;
+	{
+		// the outputs out of mapped memory, on the lent threads when large
+		ParCopy pc;
+		off = 0;
+		for (unsigned i = 0; i < n; i++) {
+			const size_t cnt = g->ent[ids[i]].n;
+			pc.add(ys[i], g->h_y + off, cnt * sizeof(float));
+			off += cnt;
+		}
+		pc.run(g->pool);
 	}
 	g->calls++;
 	g->weight_mb += mb;
@@ -397,6 +404,14 @@ struct charsiu_npu *charsiu_npu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	for (int i = 0; i < 4; i++)
 		g->h_flag[i] = 0;
 	return g;
+}
+
+// Internal to the library (host/llama_gpu.c): the decode loop lends its host
+// threads for the large read-backs; NULL takes them back. Never freed here.
+void charsiu_npu_lend_pool(struct charsiu_npu *g, struct pool *p)
+{
+	if (g)
+		g->pool = p;
 }
 
 void charsiu_npu_close(struct charsiu_npu *g)

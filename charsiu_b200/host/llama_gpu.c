@@ -28,6 +28,7 @@
 /* internal to the library (csrc/charsiu_gpu.cu): lend the layer this loop's
  * host threads for its large copies; NULL takes them back */
 void charsiu_gpu_lend_pool(struct charsiu_gpu *g, struct pool *p);
+void charsiu_npu_lend_pool(struct charsiu_npu *g, struct pool *p);
 
 #define API
 
@@ -780,6 +781,7 @@ API void charsiu_gpu_llama_close(struct charsiu_gpu_llama *m)
 				m->stage_ms[i] / m->stage_tok, 100.0 * m->stage_ms[i] / tot);
 	}
 	charsiu_gpu_lend_pool(m->dev, NULL);
+	charsiu_npu_lend_pool(m->npu, NULL);
 	pool_free(m->pool);
 	charsiu_gpu_decoder_free(m->dec);
 	if (m->npu && getenv("CHARSIU_GPU_REPORT"))
@@ -882,6 +884,7 @@ API struct charsiu_gpu_llama *charsiu_gpu_llama_open(const char *path, int n_ctx
 		m->aq1 = calloc((size_t)(widest + 31) / 32 * 32, 1);
 		if (!m->npu || !m->aq1)
 			goto fail;
+		charsiu_npu_lend_pool(m->npu, m->pool);
 	}
 	m->L = calloc(m->n_layer, sizeof(*m->L));
 	if (!m->L)
