@@ -732,6 +732,8 @@ int queue_matvec_kernels(charsiu_gpu *g, const int *ids, unsigned n, unsigned k,
 // memory), under the reference's budget (src/npudev.c:560-573) as finish()
 // applies it: a CUDA error, a launch that finished without signalling or one
 // that never finishes retires the layer, and three slow calls in a row too.
+static_assert(QMV_MAX_TENSORS <= ParCopy::MAX_SEG, "a launch group's outputs in one copy");
+
 // The layer's large copies on its host threads: the pool the decode loop
 // lent it, else one of its own made at the first copy of 64 KB or more.
 void par_copy(charsiu_gpu *g, ParCopy &pc)

@@ -406,6 +406,8 @@ struct charsiu_npu *charsiu_npu_open_ex(unsigned max_k, unsigned max_n, unsigned
 	return g;
 }
 
+static_assert(NPU_MAX_TENSORS <= ParCopy::MAX_SEG, "a launch group's outputs in one copy");
+
 // Internal to the library (host/llama_gpu.c): the decode loop lends its host
 // threads for the large read-backs; NULL takes them back. Never freed here.
 void charsiu_npu_lend_pool(struct charsiu_npu *g, struct pool *p)

@@ -48,7 +48,8 @@ def test_probes(layer):
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 1, 1), (3, 7, 5), (33, 33, 65), (2, 257, 31),
-                                   (64, 4096, 3), (129, 64, 200)])
+                                   (64, 4096, 3), (129, 64, 200), (300, 512, 80),
+                                   (1, 4096, 1000)])
 @pytest.mark.parametrize("zp", [(128, 128, 0), (0, 255, 7), (77, 140, -20)])
 def test_shapes_and_zero_points(layer, m, k, n, zp):
     rng = np.random.default_rng(m + 31 * k + 7 * n)

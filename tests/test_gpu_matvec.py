@@ -68,8 +68,8 @@ def test_ragged_shapes_vs_oracle(layer, qt, k, n):
     assert np.array_equal(layer.block_dots(tid, q), O.block_dots(qt, blk, k, n, q))
 
 
-@pytest.mark.parametrize("k,n", [(256, 1), (256, 7), (2048, 40), (2048, 1000), (8192, 9),
-                                 (2048, 128256)])
+@pytest.mark.parametrize("k,n", [(256, 1), (256, 7), (768, 33), (1280, 17), (2048, 40),
+                                 (2048, 1000), (4096, 130), (8192, 9), (2048, 128256)])
 def test_q6k_vs_oracle(layer, k, n):
     """q6_K (the tied head of llama.cpp's q4_0 files), 256-weight super-blocks,
     ragged N and the 2048 -> 128256 head: bit-exact, as a single call, inside a
@@ -145,6 +145,18 @@ def test_output_head_shape(layer):
     q, d = O.act_quantise(x)
     (y,) = layer.matvec([tid], q, d, k)
     assert same(y, O.matvec(G.GGML_Q8_0, blk, k, n, q, d))
+
+
+def test_q6k_more_than_one_pass():
+    """K = 12288: 48 super-blocks, more than one pass of the 16-warp q6_K
+    kernel's 32 (the loads of a later pass issued after the last's dots)."""
+    k, n = 12288, 24
+    with Layer(max_k=k, max_n=n, max_tensors=1) as L:
+        blk, x = W.matvec_inputs(G.GGML_Q6_K, k, n, seed=5)
+        tid = L.add_blocks(G.GGML_Q6_K, k, n, blk)
+        q, d = O.act_quantise(x)
+        (y,) = L.matvec([tid], q, d, k)
+        assert same(y, O.matvec(G.GGML_Q6_K, blk, k, n, q, d))
 
 
 @pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 9, 13, 32, 64, 100])
