@@ -73,12 +73,20 @@ def peaks():
     return PEAKS_FALLBACK["hbm_gbs"], "fallback"
 
 
-def model_path(rank: int, barrier) -> str:
+def decode_spec(name: str):
+    """The decode workload `name`: the headline llama1b_q8, or one of
+    W.DECODE_EXTRA (llama1b_q4_q6k: the same shape as a llama.cpp q4_0 file)."""
+    return W.DECODE[name] if name in W.DECODE else W.DECODE_EXTRA[name]
+
+
+def model_path(rank: int, barrier, name: str = "llama1b_q8") -> str:
+    spec = decode_spec(name)
     d = os.path.join(tempfile.gettempdir(), "charsiu_bench")
     os.makedirs(d, exist_ok=True)
-    path = os.path.join(d, f"llama1b_q8_seed{SPEC['seed']}.gguf")
+    path = os.path.join(d, f"{name}_seed{spec['seed']}.gguf")
     if rank == 0 and not os.path.exists(path):
-        G.write_llama(path, SHAPE, SPEC["qtype"], SPEC["seed"])
+        G.write_llama(path, spec["shape"], spec["qtype"], spec["seed"],
+                      embd_qtype=spec.get("embd_qtype"))
     barrier()
     return path
 
@@ -543,7 +551,7 @@ def time_chain(chain, steps, warmup, barrier, dist, world, dev, graph_ok, sample
     return ms / steps, clk
 
 
-def run_decode(path, args, world, dist, dev, sample_clocks):
+def run_decode(path, args, world, dist, dev, sample_clocks, name: str = "llama1b_q8"):
     """The workload's greedy decode with the whole forward on the device and
     the inputs resident in HBM: the 6 prompt ids through the device step
     (untimed), then greedy steps queued back to back with no host round trip
@@ -557,10 +565,11 @@ def run_decode(path, args, world, dist, dev, sample_clocks):
     import torch
     from charsiu_b200.lib import Llama
 
-    n_gen = SPEC["n_gen"]
-    prompt = W.prompt_ids(SHAPE.n_vocab, SPEC["seed"])
+    spec = decode_spec(name)
+    n_gen = spec["n_gen"]
+    prompt = W.prompt_ids(spec["shape"].n_vocab, spec["seed"])
     with open(os.path.join(ROOT, "tests", "golden", "golden_decode.json")) as f:
-        gold = json.load(f)["llama1b_q8"]["tokens"]
+        gold = json.load(f)[name]["tokens"]
     barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
     barrier()
     with Llama(path, n_ctx=len(prompt) + n_gen + 1, device=dev.index, resident=True) as m:
@@ -1356,6 +1365,9 @@ def main():
                     help="time only the token's 65 matvec launches (the roofline's chain)")
     ap.add_argument("--decode", action="store_true",
                     help="time only the headline decode (inputs resident, device-side loop)")
+    ap.add_argument("--model", default="llama1b_q8", choices=["llama1b_q8", "llama1b_q4_q6k"],
+                    help="with --decode: the model (llama1b_q4_q6k: the same shape as a "
+                         "llama.cpp q4_0 file, its tied head in q6_K)")
     ap.add_argument("--sharded", action="store_true",
                     help="at N > 1: only the column splits (head, token chain, batched)")
     ap.add_argument("--matvec", default=None, metavar="QTYPE:K:N[:M]",
@@ -1416,10 +1428,12 @@ def main():
             dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
             torch.cuda.set_device(dev)
             barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
-            path = model_path(rank, barrier)
+            path = model_path(rank, barrier, args.model if args.decode else "llama1b_q8")
             if args.decode:
-                ms, match, clk, kernels = run_decode(path, args, world, dist, dev, rank == 0)
-                out = {"decode_tok_s": round(world * 1000.0 / ms, 2), "ms_per_token": round(ms, 5),
+                ms, match, clk, kernels = run_decode(path, args, world, dist, dev, rank == 0,
+                                                     args.model)
+                out = {"model": args.model,
+                       "decode_tok_s": round(world * 1000.0 / ms, 2), "ms_per_token": round(ms, 5),
                        "tokens_match_reference": match, "kernels_per_step": kernels,
                        "clocks": clk}
             else:

@@ -51,6 +51,14 @@ DECODE = {
                     "n_gen": 24, "n_ctx": 64},
 }
 
+# Decode workloads outside the test matrix (their golden tokens are recorded
+# all the same, for the bench): the Llama-3.2-1B shape as a llama.cpp q4_0
+# file, token_embd and so the tied head in q6_K.
+DECODE_EXTRA = {
+    "llama1b_q4_q6k": {"shape": LLAMA_3_2_1B, "qtype": GGML_Q4_0, "embd_qtype": GGML_Q6_K,
+                       "seed": 0, "n_gen": 24, "n_ctx": 64},
+}
+
 
 def matvec_inputs(qtype: int, k: int, n: int, seed: int):
     rng = np.random.default_rng([seed])

@@ -12,7 +12,10 @@ sources by oracle/Makefile) and records what the reference computes:
                      models (q8_0; q4_0; q4_0 with a q6_K embedding and head)
                      and the Llama-3.2-1B-shaped one; under "npu", the same
                      in charsiu's NPU number format (CHARSIU_NPU_QUANT=1, its
-                     CPU model), added by  python tests/golden/make_golden.py --npu
+                     CPU model), added by  python tests/golden/make_golden.py --npu;
+                     the decode workloads outside the test matrix
+                     (W.DECODE_EXTRA: the 1B shape as a q4_0 file with a q6_K
+                     head), added by  python tests/golden/make_golden.py --extra
 
 Inputs are regenerated from the recorded seeds (numpy PCG64); a sha256 of each
 input is stored beside it so generator drift is caught rather than trusted.
@@ -102,6 +105,33 @@ def main() -> None:
         json.dump(dec, f, indent=1)
 
 
+def extra() -> None:
+    """Add the decode goldens of W.DECODE_EXTRA to golden_decode.json, leaving
+    every other entry as it is."""
+    O.build()
+    assert O.have_ref(), "the reference tree is needed to make golden vectors"
+    path = os.path.join(HERE, "golden_decode.json")
+    with open(path) as f:
+        dec = json.load(f)
+    with tempfile.TemporaryDirectory() as td:
+        for name, spec in W.DECODE_EXTRA.items():
+            gpath = os.path.join(td, f"{name}.gguf")
+            G.write_llama(gpath, spec["shape"], spec["qtype"], spec["seed"],
+                          embd_qtype=spec.get("embd_qtype"))
+            prompt = W.prompt_ids(spec["shape"].n_vocab, spec["seed"])
+            toks, pm, gm, lg = O.ref_greedy(gpath, prompt, spec["n_gen"], n_ctx=spec["n_ctx"],
+                                            threads=os.cpu_count(),
+                                            want_logits=spec["shape"].n_vocab)
+            with open(gpath, "rb") as f:
+                fsha = hashlib.sha256(f.read()).hexdigest()
+            dec[name] = {"prompt": prompt.tolist(), "tokens": toks.tolist(),
+                         "logits_sha256": sha(lg), "logits_head": lg[:8].tolist(),
+                         "gguf_sha256": fsha, "gen_ms": gm}
+            print(name, toks.tolist(), f"gen {gm:.0f} ms")
+    with open(path, "w") as f:
+        json.dump(dec, f, indent=1)
+
+
 def npu_child(out_path: str) -> None:
     """In a process started with CHARSIU_NPU_QUANT=1: the reference's greedy
     decode in the NPU number format (its CPU model, src/npuquant.c) on every
@@ -149,5 +179,7 @@ if __name__ == "__main__":
         npu_child(sys.argv[2])
     elif len(sys.argv) > 1 and sys.argv[1] == "--npu":
         npu()
+    elif len(sys.argv) > 1 and sys.argv[1] == "--extra":
+        extra()
     else:
         main()

@@ -98,6 +98,17 @@ def test_int8_probes_analytic():
     assert len(np.unique(out)) >= 60
 
 
+@pytest.mark.parametrize("name", list(W.DECODE_EXTRA))
+def test_decode_extra_goldens_recorded(name):
+    """The decode workloads outside the test matrix (the bench's --model
+    choices) have the reference's tokens recorded, for their seeded prompt."""
+    spec, gold = W.DECODE_EXTRA[name], GOLD_DECODE[name]
+    assert gold["prompt"] == W.prompt_ids(spec["shape"].n_vocab, spec["seed"]).tolist()
+    assert len(gold["tokens"]) == spec["n_gen"]
+    assert all(0 <= t < spec["shape"].n_vocab for t in gold["tokens"])
+    assert len(gold["gguf_sha256"]) == 64 and len(gold["logits_sha256"]) == 64
+
+
 def test_half_to_float_all_values():
     h = np.arange(65536, dtype=np.uint16)
     lib = O.lib()
