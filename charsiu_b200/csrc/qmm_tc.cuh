@@ -10,9 +10,10 @@
 //     s[n][a] = s[n][a] + (d_w[n][b] * d_a[a][b]) * (float)t[n][a]
 // in block order, so the fp32 sums are the reference's exactly. The MMA
 // cannot accumulate across blocks (each block has its own scales); it writes
-// a fresh int32 tile per block. Tiles are grouped in CHUNKS of four blocks,
-// one commit a chunk, into four chunk buffers of tensor memory, so the
-// epilogue drains one chunk while the MMAs fill the others.
+// a fresh int32 tile per block. Tiles are grouped in CHUNKS of blocks (a
+// whole 16-block segment at 16 activations, four blocks at 32), one commit a
+// chunk, into two or four chunk buffers of tensor memory, so the epilogue
+// drains one chunk while the MMAs fill the others.
 //
 // Work units are (128-row tile of one tensor, NA activations, a slice of EC
 // of those activations); a persistent grid deals them round robin, slice and
@@ -28,7 +29,7 @@
 // stage; warp 1 owns tensor memory and lane 0 issues the MMAs; EW = 4 * EC/8
 // epilogue warps (a tensor-memory lane quarter and 8 activations each; four
 // warps of 4 activations for a 4-wide slice) read
-// the int32 tiles with tcgen05.ld and accumulate: per chunk, the four blocks'
+// the int32 tiles with tcgen05.ld and accumulate: four blocks a read, their
 // products first (independent, so they overlap), then the four in-order sums.
 // Every step uses the packed fp32x2 operations (two columns an instruction,
 // each lane rounded as the scalar operation rounds).
@@ -48,11 +49,24 @@ namespace cgpu {
 
 constexpr int QMM_TILE_GROUPS = 16;                       // 128 weight rows
 constexpr uint32_t QMM_WSTAGE = QMM_TILE_GROUPS * MAX_SEG_BYTES;   // 69632
-// Four blocks a commit, four chunk buffers (the MMAs may run three chunks
-// ahead of the epilogue). Measured against 2/4, 8/2 and 2/4: within a few
-// percent, this the best at 64 activations.
-constexpr int QMM_CHUNK = 4;                              // blocks a commit
-constexpr int QMM_TBUFS = 4;                              // chunk buffers in tensor memory
+// Blocks a commit and chunk buffers: two buffers of 256 / NA blocks, the 512
+// tensor-memory columns. One MMA of this shape (M = 128, K = 32, N <= 128)
+// occupies the tensor pipe about 72 cycles whatever N is, and each commit
+// the epilogue waits on and drains adds 200-280 cycles to the MMA chain, so
+// the fewer chunks the better while the epilogue still overlaps the next
+// chunk: 16 activations take a whole 16-block segment a commit, 32 take
+// half of one. (Four buffers of four blocks: the 1B step at M = 16 / 32 / 64
+// 1.206 / 1.299 / 1.594 ms, against 0.908 / 1.043 / 1.372 this way.) The
+// epilogue reads a chunk four blocks at a time.
+__host__ __device__ constexpr int qmm_chunk(int na)
+{
+	return 256 / na;
+}
+__host__ __device__ constexpr int qmm_tbufs(int)
+{
+	return 2;
+}
+constexpr int QMM_SUB = 4;                                // blocks an epilogue read
 constexpr int QMM_MAX_TENSORS = 8;
 
 // The packed activation tile of a NA-row slab of activations, per K segment:
@@ -95,10 +109,10 @@ __host__ __device__ constexpr int qmm_threads(int ec)
 	return (2 + qmm_epi_warps(ec)) * 32;
 }
 
-// tensor-memory columns: QMM_TBUFS chunk buffers of QMM_CHUNK blocks of NA columns
+// tensor-memory columns: qmm_tbufs chunk buffers of qmm_chunk blocks of NA columns
 __host__ __device__ constexpr uint32_t qmm_tmem_cols(int na)
 {
-	return QMM_TBUFS * QMM_CHUNK * na;
+	return qmm_tbufs(na) * qmm_chunk(na) * na;
 }
 
 // q int8 [m][nb*32], d f32 [m][nb] -> packed [m tiles][nseg][qmm_act_seg_bytes]
@@ -180,6 +194,8 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 		      "slices of whole epilogue warps; PRE fills every column it reads");
 	constexpr uint32_t ASEG = qmm_act_seg_bytes(NA);
 	constexpr uint32_t NCOLS = qmm_tmem_cols(NA);
+	constexpr uint32_t CH = qmm_chunk(NA), TB = qmm_tbufs(NA);   // blocks a chunk, buffers
+	static_assert(CH % QMM_SUB == 0 && 4 + 2 * TB <= 24, "chunk of whole reads; barrier space");
 	static_assert(NCOLS >= 32 && NCOLS <= 512 && (NCOLS & (NCOLS - 1)) == 0,
 		      "tensor memory is allocated in powers of two, 32 to 512 columns");
 	extern __shared__ __align__(128) uint8_t smem[];
@@ -187,8 +203,8 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 	auto stage_a = [&](uint32_t st) { return smem + 2 * QMM_WSTAGE + st * ASEG; };
 	uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 2 * (QMM_WSTAGE + ASEG));
 	uint64_t *full = bars, *freeb = bars + 2, *mma_done = bars + 4;
-	uint64_t *tfree = mma_done + QMM_TBUFS;
-	uint32_t *taddr_s = reinterpret_cast<uint32_t *>(tfree + QMM_TBUFS);
+	uint64_t *tfree = mma_done + TB;
+	uint32_t *taddr_s = reinterpret_cast<uint32_t *>(tfree + TB);
 	uint8_t *priv_all = smem + 2 * (QMM_WSTAGE + ASEG) + qmm_bar_bytes();
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -204,7 +220,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 			mbar_init(&full[i], 1);
 			mbar_init(&freeb[i], 1 + EW);
 		}
-		for (int i = 0; i < QMM_TBUFS; i++) {
+		for (uint32_t i = 0; i < TB; i++) {
 			mbar_init(&mma_done[i], 1);
 			mbar_init(&tfree[i], EW);
 		}
@@ -297,8 +313,8 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 						break;
 					}
 					tc_fence_after();
-					for (uint32_t b0 = 0; b0 < sb; b0 += QMM_CHUNK, c_cnt++) {
-						const uint32_t buf = c_cnt % QMM_TBUFS, use = c_cnt / QMM_TBUFS;
+					for (uint32_t b0 = 0; b0 < sb; b0 += CH, c_cnt++) {
+						const uint32_t buf = c_cnt % TB, use = c_cnt / TB;
 						// PRE: the epilogue's first release of each buffer is
 						// its fill with the constant
 						if ((PRE || use >= 1) &&
@@ -309,14 +325,14 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 							break;
 						}
 						tc_fence_after();
-						const uint32_t nblk = min((uint32_t)QMM_CHUNK, sb - b0);
+						const uint32_t nblk = min(CH, sb - b0);
 						for (uint32_t j = 0; j < nblk; j++) {
 							const uint32_t bi = b0 + j;
 							const uint64_t ad = smem_desc_k_nosw(
 								stage_w(st) + bi * RG * 32, RG * 16, MAX_SEG_BYTES);
 							const uint64_t bd = smem_desc_k_nosw(
 								stage_a(st) + bi * 2 * NA * 16, NA * 16, 128);
-							mma_i8(taddr + buf * QMM_CHUNK * NA + j * NA, ad, bd, idesc,
+							mma_i8(taddr + buf * CH * NA + j * NA, ad, bd, idesc,
 							       PRE);
 						}
 						mma_commit(&mma_done[buf]);
@@ -326,8 +342,8 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 				}
 			}
 			// the last chunk's MMAs must be done before tensor memory is freed
-			if (c_cnt && !mbar_wait_bounded(&mma_done[(c_cnt - 1) % QMM_TBUFS],
-							((c_cnt - 1) / QMM_TBUFS) & 1,
+			if (c_cnt && !mbar_wait_bounded(&mma_done[(c_cnt - 1) % TB],
+							((c_cnt - 1) / TB) & 1,
 							WAIT_LIMIT_NS))
 				*(volatile int *)p.err = 11;
 		}
@@ -346,7 +362,7 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 			tc_fence_before();
 			__syncwarp();
 			if (lane == 0)
-				for (int i = 0; i < QMM_TBUFS; i++)
+				for (uint32_t i = 0; i < TB; i++)
 					mbar_arrive(&tfree[i]);
 		}
 		pdl_wait();                  // y may still be read by the kernel before
@@ -397,81 +413,86 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 					mbar_arrive(&freeb[st]);
 				const uint16_t *dl = reinterpret_cast<const uint16_t *>(priv) + (lane / RG) * SB * RG;
 				const float *da = reinterpret_cast<const float *>(priv + QMM_PRIV_DW);
-				for (uint32_t b0 = 0; b0 < sb; b0 += QMM_CHUNK, c_cnt++) {
-					const uint32_t buf = c_cnt % QMM_TBUFS, nblk = min((uint32_t)QMM_CHUNK, sb - b0);
-					if (!mbar_wait_bounded(&mma_done[buf], (c_cnt / QMM_TBUFS) & 1,
-							       WAIT_LIMIT_NS)) {
+				for (uint32_t c0 = 0; c0 < sb; c0 += CH, c_cnt++) {
+					const uint32_t buf = c_cnt % TB, cblk = min(CH, sb - c0);
+					if (!mbar_wait_bounded(&mma_done[buf], (c_cnt / TB) & 1, WAIT_LIMIT_NS)) {
 						if (lane == 0)
 							*(volatile int *)p.err = 9;
 						ok = false;
 						break;
 					}
 					tc_fence_after();
-					// the chunk's tiles as packed float bits 1.5 * 2^23 + t
-					static_assert(QMM_CHUNK == 4, "tmem_ld_chunk4 shape");
-					uint64_t tp[QMM_CHUNK][CW / 2];
-					const uint32_t col0 = taddr + lane_base + buf * QMM_CHUNK * NA + cb;
-					if constexpr (CW == 8) {
-						if (nblk == QMM_CHUNK)
-							tmem_ld_chunk4<!PRE>(col0, NA, tp);
-						else
-							for (int j = 0; j < (int)nblk; j++)
-								tmem_ld_block<!PRE>(col0 + j * NA, tp[j]);
-					} else {
-						if (nblk == QMM_CHUNK)
-							tmem_ld_chunk4_c4(col0, NA, tp);
-						else
-							for (int j = 0; j < (int)nblk; j++)
-								tmem_ld_block_c4(col0 + j * NA, tp[j]);
-					}
-					if (PRE) {
-#pragma unroll
-						for (int j = 0; j < QMM_CHUNK; j++)
-							if (j < (int)nblk)
-								tmem_fill8(col0 + j * NA, INT_FLOAT_MAGIC);
-						tmem_wait_st();
-					}
-					tc_fence_before();
-					__syncwarp();
-					if (lane == 0)
-						mbar_arrive(&tfree[buf]);
-
-					// block j's products (d_w * d_a) * t, CW columns in pairs
-					auto products = [&](int j, uint64_t (&pr)[CW / 2]) {
-						const uint32_t bi = b0 + j;
-						const float dw = half_bits_to_float(dl[bi * RG + rr]);
-						const uint64_t dw2 = pack2(dw, dw);
-						const ulonglong2 *da2 = reinterpret_cast<const ulonglong2 *>(da + bi * CW);
-#pragma unroll
-						for (int c4 = 0; c4 < CW / 4; c4++) {
-							const ulonglong2 a = da2[c4];
-							const uint64_t f0 = add2_rn(tp[j][2 * c4], neg_bias);
-							const uint64_t f1 = add2_rn(tp[j][2 * c4 + 1], neg_bias);
-							pr[2 * c4] = mul2_rn(mul2_rn(dw2, a.x), f0);
-							pr[2 * c4 + 1] = mul2_rn(mul2_rn(dw2, a.y), f1);
+					for (uint32_t b0 = c0; b0 < c0 + cblk; b0 += QMM_SUB) {
+						const uint32_t nblk = min((uint32_t)QMM_SUB, c0 + cblk - b0);
+						// four blocks' tiles as packed float bits 1.5 * 2^23 + t
+						static_assert(QMM_SUB == 4, "tmem_ld_chunk4 shape");
+						uint64_t tp[QMM_SUB][CW / 2];
+						const uint32_t col0 = taddr + lane_base + buf * CH * NA + (b0 - c0) * NA + cb;
+						if constexpr (CW == 8) {
+							if (nblk == QMM_SUB)
+								tmem_ld_chunk4<!PRE>(col0, NA, tp);
+							else
+								for (int j = 0; j < (int)nblk; j++)
+									tmem_ld_block<!PRE>(col0 + j * NA, tp[j]);
+						} else {
+							if (nblk == QMM_SUB)
+								tmem_ld_chunk4_c4(col0, NA, tp);
+							else
+								for (int j = 0; j < (int)nblk; j++)
+									tmem_ld_block_c4(col0 + j * NA, tp[j]);
 						}
-					};
-					// s = s + product, block by block: fma(product, 1, s) with the
-					// 1 from the kernel's parameters is the rounded add (a packed
-					// add fed by the packed product would be contracted into one
-					// rounding, unlike the reference's two)
-					if (nblk == QMM_CHUNK) {
-						uint64_t pr[QMM_CHUNK][CW / 2];
+						if (PRE) {
 #pragma unroll
-						for (int j = 0; j < QMM_CHUNK; j++)
-							products(j, pr[j]);
+							for (int j = 0; j < QMM_SUB; j++)
+								if (j < (int)nblk)
+									tmem_fill8(col0 + j * NA, INT_FLOAT_MAGIC);
+							tmem_wait_st();
+						}
+						// the chunk's last read releases its buffer to the MMAs
+						if (b0 + QMM_SUB >= c0 + cblk) {
+							tc_fence_before();
+							__syncwarp();
+							if (lane == 0)
+								mbar_arrive(&tfree[buf]);
+						}
+
+						// block j's products (d_w * d_a) * t, CW columns in pairs
+						auto products = [&](int j, uint64_t (&pr)[CW / 2]) {
+							const uint32_t bi = b0 + j;
+							const float dw = half_bits_to_float(dl[bi * RG + rr]);
+							const uint64_t dw2 = pack2(dw, dw);
+							const ulonglong2 *da2 = reinterpret_cast<const ulonglong2 *>(da + bi * CW);
 #pragma unroll
-						for (int j = 0; j < QMM_CHUNK; j++)
+							for (int c4 = 0; c4 < CW / 4; c4++) {
+								const ulonglong2 a = da2[c4];
+								const uint64_t f0 = add2_rn(tp[j][2 * c4], neg_bias);
+								const uint64_t f1 = add2_rn(tp[j][2 * c4 + 1], neg_bias);
+								pr[2 * c4] = mul2_rn(mul2_rn(dw2, a.x), f0);
+								pr[2 * c4 + 1] = mul2_rn(mul2_rn(dw2, a.y), f1);
+							}
+						};
+						// s = s + product, block by block: fma(product, 1, s) with the
+						// 1 from the kernel's parameters is the rounded add (a packed
+						// add fed by the packed product would be contracted into one
+						// rounding, unlike the reference's two)
+						if (nblk == QMM_SUB) {
+							uint64_t pr[QMM_SUB][CW / 2];
 #pragma unroll
-							for (int c = 0; c < CW / 2; c++)
-								acc[c] = fma2_rn(pr[j][c], one2, acc[c]);
-					} else {
-						for (int j = 0; j < (int)nblk; j++) {
-							uint64_t pr[CW / 2];
-							products(j, pr);
+							for (int j = 0; j < QMM_SUB; j++)
+								products(j, pr[j]);
 #pragma unroll
-							for (int c = 0; c < CW / 2; c++)
-								acc[c] = fma2_rn(pr[c], one2, acc[c]);
+							for (int j = 0; j < QMM_SUB; j++)
+#pragma unroll
+								for (int c = 0; c < CW / 2; c++)
+									acc[c] = fma2_rn(pr[j][c], one2, acc[c]);
+						} else {
+							for (int j = 0; j < (int)nblk; j++) {
+								uint64_t pr[CW / 2];
+								products(j, pr);
+#pragma unroll
+								for (int c = 0; c < CW / 2; c++)
+									acc[c] = fma2_rn(pr[c], one2, acc[c]);
+							}
 						}
 					}
 				}
