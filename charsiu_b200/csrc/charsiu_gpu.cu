@@ -7,6 +7,7 @@
 // deadline, keeps the time split, retires itself after three slow or failed
 // calls, and says so.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>          // PFN_cuTensorMapEncodeTiled
 
 #include <atomic>
 #include <cstdarg>
@@ -467,6 +468,48 @@ void qmm_launch_shape(const charsiu_gpu *g, uint32_t m, uint32_t tiles, uint32_t
 		ec = 4;
 }
 
+// The driver's tensor-map encoder, looked up once (null if the driver has none).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+	static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+		void *f = nullptr;
+		cudaDriverEntryPointQueryResult res;
+		if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000,
+						     cudaEnableDefault, &res) != cudaSuccess ||
+		    res != cudaDriverEntryPointSuccess)
+			f = nullptr;
+		return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+	}();
+	return fn;
+}
+
+// The batched matvec's two activation boxes a stage, straight from q int8
+// [m][nb*32] and d f32 [m][nb]: q viewed as (16 bytes, m rows, 2*nb chunks)
+// with a box of (16, na, 32) lands as [32 chunks][na rows][16 B], the MMA's
+// core matrices; d as (nb, m) with a box of (16, na) lands as [na][16]. Out
+// of range reads zero, as the packing writes. false: not describable (q or d
+// not 16-byte aligned, a row of d not a multiple of 16 bytes, no encoder).
+bool qmm_act_maps(const int8_t *q, const float *d, uint32_t m, uint32_t nb, uint32_t na,
+		  CUtensorMap *qmap, CUtensorMap *dmap)
+{
+	const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+	if (!enc || ((uintptr_t)q & 15) || ((uintptr_t)d & 15) || (nb * 4) % 16 || !m)
+		return false;
+	const cuuint32_t ones[3] = {1, 1, 1};
+	const cuuint64_t qdim[3] = {16, m, (cuuint64_t)nb * 2};
+	const cuuint64_t qstride[2] = {(cuuint64_t)nb * 32, 16};
+	const cuuint32_t qbox[3] = {16, na, 2 * SB};
+	const cuuint64_t ddim[2] = {nb, m};
+	const cuuint64_t dstride[1] = {(cuuint64_t)nb * 4};
+	const cuuint32_t dbox[2] = {SB, na};
+	return enc(qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(q), qdim, qstride,
+		   qbox, ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+		   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
+	       enc(dmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(d), ddim, dstride,
+		   dbox, ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+		   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 size_t qmm_pack_bytes(uint32_t na, uint32_t m, uint32_t nb)
 {
 	return (size_t)((m + na - 1) / na) * nsegments(nb) * qmm_act_seg_bytes(na);
@@ -489,18 +532,21 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 
-	const uint64_t items = (uint64_t)mt * nseg * (SB * 2 * na + SB * na);
-	cudaLaunchConfig_t pc = {};
-	pc.gridDim = dim3((unsigned)((items + 255) / 256));
-	pc.blockDim = dim3(256);
-	pc.stream = st;
-	pc.attrs = attr;
-	pc.numAttrs = g->no_pdl ? 0 : 1;
-	if (cudaLaunchKernelEx(&pc, qmm_pack_kernel, q, d, m, nb, na, pack) != cudaSuccess)
-		return -1;
-	g->launches++;
-
 	QmmParams p = {};
+	p.use_map = qmm_act_maps(q, d, m, nb, na, &p.qmap, &p.dmap) ? 1u : 0u;
+	if (!p.use_map) {
+		const uint64_t items = (uint64_t)mt * nseg * (SB * 2 * na + SB * na);
+		cudaLaunchConfig_t pc = {};
+		pc.gridDim = dim3((unsigned)((items + 255) / 256));
+		pc.blockDim = dim3(256);
+		pc.stream = st;
+		pc.attrs = attr;
+		pc.numAttrs = g->no_pdl ? 0 : 1;
+		if (cudaLaunchKernelEx(&pc, qmm_pack_kernel, q, d, m, nb, na, pack) != cudaSuccess)
+			return -1;
+		g->launches++;
+	}
+
 	uint32_t tile_end = 0;
 	for (unsigned i = 0; i < n; i++) {
 		const Ent &e = g->ent[ids[i]];

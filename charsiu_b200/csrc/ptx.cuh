@@ -83,6 +83,29 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 		     : "memory");
 }
 
+// Tiled tensor copies, global -> shared memory of this CTA, through the tensor
+// map at generic address `map` (a __grid_constant__ kernel parameter): the
+// box at coordinates (x, y[, z]) lands densely, x fastest, and completes the
+// whole box's bytes on `bar` (out-of-range elements read as zero). x times
+// the element size must be a multiple of 16 bytes; no cluster multicast.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int x, int y,
+					    uint64_t *bar)
+{
+	asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+		     " [%0], [%1, {%2, %3}], [%4];"
+		     :: "r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+		     : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *map, int x, int y, int z,
+					    uint64_t *bar)
+{
+	asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+		     " [%0], [%1, {%2, %3, %4}], [%5];"
+		     :: "r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+		     : "memory");
+}
+
 // Order this thread's earlier generic-proxy accesses to shared memory before
 // later async-proxy (bulk copy) writes to it.
 __device__ __forceinline__ void fence_proxy_async_smem()

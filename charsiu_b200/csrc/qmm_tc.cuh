@@ -11,9 +11,9 @@
 // in block order, so the fp32 sums are the reference's exactly. The MMA
 // cannot accumulate across blocks (each block has its own scales); it writes
 // a fresh int32 tile per block. Tiles are grouped in CHUNKS of blocks (a
-// whole 16-block segment at 16 activations, four blocks at 32), one commit a
-// chunk, into two or four chunk buffers of tensor memory, so the epilogue
-// drains one chunk while the MMAs fill the others.
+// whole 16-block segment at 16 activations, half of one at 32), one commit a
+// chunk, into two chunk buffers of tensor memory, so the epilogue drains one
+// chunk while the MMAs fill the other.
 //
 // Work units are (128-row tile of one tensor, NA activations, a slice of EC
 // of those activations); a persistent grid deals them round robin, slice and
@@ -25,7 +25,7 @@
 // roles: warp 0 lane 0 issues the single-destination bulk copies of one K
 // segment (16 blocks) a stage -- the tile's 16 groups' weight segments as
 // they lie in the device layout (layout.h), already MMA core matrices, and
-// the packed activation tile (qmm_pack_kernel) -- into a double-buffered
+// the activation tile (two tiled tensor copies from q and d) -- into a double-buffered
 // stage; warp 1 owns tensor memory and lane 0 issues the MMAs; EW = 4 * EC/8
 // epilogue warps (a tensor-memory lane quarter and 8 activations each; four
 // warps of 4 activations for a 4-wide slice) read
@@ -40,6 +40,8 @@
 // (|t| <= 32 * 127 * 128 < 2^22). The epilogue writes the constant back after
 // each read. Every wait is bounded.
 #pragma once
+
+#include <cuda.h>              // CUtensorMap
 
 #include "layout.h"
 #include "ptx.cuh"
@@ -69,9 +71,15 @@ __host__ __device__ constexpr int qmm_tbufs(int)
 constexpr int QMM_SUB = 4;                                // blocks an epilogue read
 constexpr int QMM_MAX_TENSORS = 8;
 
-// The packed activation tile of a NA-row slab of activations, per K segment:
-// quants [16 blocks][2 chunks][NA rows][16 B] then deltas [16 blocks][NA] f32.
-// Rows past m and blocks past nb are zero.
+// The staged activation tile of a NA-row slab of activations, per K segment:
+// quants [16 blocks][2 chunks][NA rows][16 B] (MMA core matrices) then deltas
+// [NA rows][16 blocks] f32. Rows past m and blocks past nb are zero. Two tiled
+// tensor copies stage it straight from q and d (q viewed as [16-byte
+// chunks][rows][16 B], a box of 32 chunks x NA rows; d as [rows][blocks], a
+// box of NA x 16); where those cannot be described (q or d not 16-byte
+// aligned, or a row of d not a multiple of 16 bytes), qmm_pack_kernel lays
+// the same bytes out in global memory first and one bulk copy a stage
+// brings them in.
 __host__ __device__ constexpr uint32_t qmm_act_seg_bytes(uint32_t na)
 {
 	return SB * 2 * na * 16 + SB * na * 4;
@@ -139,9 +147,9 @@ __global__ void qmm_pack_kernel(const int8_t *__restrict__ q, const float *__res
 			v = *reinterpret_cast<const uint4 *>(q + ((uint64_t)a * nb + blk) * 32 + c * 16);
 		*reinterpret_cast<uint4 *>(base + ((bi * 2 + c) * na + row) * 16) = v;
 	} else {
-		const uint32_t w2 = w - SB * 2 * na, bi = w2 / na, row = w2 % na;
+		const uint32_t w2 = w - SB * 2 * na, row = w2 / SB, bi = w2 % SB;
 		const uint32_t a = tile * na + row, blk = seg * SB + bi;
-		reinterpret_cast<float *>(base + SB * 2 * na * 16)[bi * na + row] =
+		reinterpret_cast<float *>(base + SB * 2 * na * 16)[row * SB + bi] =
 			(a < m && blk < nb) ? d[(uint64_t)a * nb + blk] : 0.0f;
 	}
 }
@@ -155,8 +163,10 @@ struct QmmTensor {
 };
 
 struct QmmParams {
+	CUtensorMap qmap, dmap;    // q and d as the staged tile's two boxes (use_map)
 	QmmTensor t[QMM_MAX_TENSORS];
-	const uint8_t *act;        // qmm_pack_kernel output
+	const uint8_t *act;        // qmm_pack_kernel output (!use_map)
+	uint32_t use_map;
 	uint32_t ntensor, tiles, atiles, nb, m;
 	float one;                 // 1.0 (see the epilogue's sum)
 	int *err;
@@ -251,7 +261,8 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 				const QmmTensor &T = p.t[ti];
 				const uint32_t g0 = tile * QMM_TILE_GROUPS;
 				const uint32_t tgroups = min((uint32_t)QMM_TILE_GROUPS, T.groups - g0);
-				const uint8_t *act = p.act + (uint64_t)((u / SL) % p.atiles) * nseg * ASEG;
+				const uint32_t at = (u / SL) % p.atiles;
+				const uint8_t *act = p.act + (uint64_t)at * nseg * ASEG;
 				for (uint32_t s = 0; s < nseg; s++, s_cnt++) {
 					const uint32_t st = s_cnt & 1, sb = seg_blocks(nb, s);
 					if (s_cnt >= 2 &&
@@ -289,7 +300,14 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 							}
 						}
 					}
-					bulk_g2s(stage_a(st), act + (uint64_t)s * ASEG, ASEG, &full[st]);
+					if (p.use_map) {
+						tma_load_3d(stage_a(st), &p.qmap, 0, (int)(at * NA),
+							    (int)(s * 2 * SB), &full[st]);
+						tma_load_2d(stage_a(st) + SB * 2 * NA * 16, &p.dmap,
+							    (int)(s * SB), (int)(at * NA), &full[st]);
+					} else {
+						bulk_g2s(stage_a(st), act + (uint64_t)s * ASEG, ASEG, &full[st]);
+					}
 				}
 			}
 			// before leaving, let every copy issued land (already true unless
@@ -400,13 +418,15 @@ qmm_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ QmmGa
 								stage_w(st) + (g0 + gl) * MAX_SEG_BYTES +
 								sb * RG * 32 + w * 16);
 					}
-					// (CW = 4: lane L < 16 copies block L's 4)
+					// (CW = 4: lane L < 16 copies block L's 4), transposed from
+					// the stage's [row][block] order
 					const uint32_t bi = CW == 8 ? lane >> 1 : lane, hf = CW == 8 ? lane & 1 : 0;
-					if (CW == 8 || lane < SB)
-						reinterpret_cast<uint4 *>(priv + QMM_PRIV_DW)[lane] =
-							*reinterpret_cast<const uint4 *>(
-								stage_a(st) + SB * 2 * NA * 16 +
-								(bi * NA + cb + 4 * hf) * 4);
+					if (CW == 8 || lane < SB) {
+						const float *ds = reinterpret_cast<const float *>(
+							stage_a(st) + SB * 2 * NA * 16) + (cb + 4 * hf) * SB + bi;
+						reinterpret_cast<float4 *>(priv + QMM_PRIV_DW)[lane] =
+							make_float4(ds[0], ds[SB], ds[2 * SB], ds[3 * SB]);
+					}
 				}
 				__syncwarp();
 				if (lane == 0)
