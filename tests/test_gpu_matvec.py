@@ -228,6 +228,39 @@ def test_batch_group_dev_one_launch(layer, m, k):
             assert same(yc[i], O.matvec(G.GGML_Q8_0, blk, k, n, qs[i], ds[i])), f"n={n} row {i}"
 
 
+@pytest.mark.parametrize("k,d_off,launches", [(2176, 0, 1), (2080, 0, 2), (2048, 4, 2)])
+def test_batch_activation_staging_paths(layer, k, d_off, launches):
+    """The tensor-core launch stages the activations by two tiled tensor
+    copies straight from q and d when both can be described (16-byte
+    aligned, nb a multiple of 4): one launch a group, here with a partial
+    last K segment (nb = 68, 4 blocks). Otherwise (nb = 65, or d 4 bytes off
+    a 16-byte boundary) a packing launch goes first. Both bit-exact, with a
+    ragged last activation tile."""
+    torch = pytest.importorskip("torch")
+    dev = torch.device("cuda:0")
+    m, ns = 21, [520, 9]
+    ids, blks = [], []
+    for i, n in enumerate(ns):
+        blk, _ = W.matvec_inputs(G.GGML_Q8_0, k, n, seed=700 + i)
+        ids.append(layer.add_blocks(G.GGML_Q8_0, k, n, blk))
+        blks.append(blk)
+    xs = np.random.default_rng(k + d_off).normal(size=(m, k)).astype(np.float32)
+    qs, ds, q_t, d_t = _dev_acts(torch, xs, dev)
+    d_buf = torch.zeros(d_t.numel() + 4, dtype=torch.float32, device=dev)
+    d_buf[d_off // 4:d_off // 4 + d_t.numel()].copy_(d_t.reshape(-1))
+    ys = [torch.full((m, n), float("nan"), device=dev) for n in ns]
+    before = layer.launches
+    assert layer.batch_group_dev(ids, m, q_t.data_ptr(), d_buf.data_ptr() + d_off,
+                                 [y.data_ptr() for y in ys],
+                                 torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert layer.launches - before == launches
+    for blk, n, y in zip(blks, ns, ys):
+        yc = y.cpu().numpy()
+        for i in range(m):
+            assert same(yc[i], O.matvec(G.GGML_Q8_0, blk, k, n, qs[i], ds[i])), f"n={n} row {i}"
+
+
 @pytest.mark.parametrize("na,pre", [("16", "0"), ("16", "1"), ("32", "0"), ("32", "1")])
 def test_batch_tile_variants_agree(monkeypatch, na, pre):
     """Every tensor-core tile variant (16 or 32 activations a tile; the int32
