@@ -515,9 +515,12 @@ size_t qmm_pack_bytes(uint32_t na, uint32_t m, uint32_t nb)
 	return (size_t)((m + na - 1) / na) * nsegments(nb) * qmm_act_seg_bytes(na);
 }
 
+// pack_always: lay the activations out in `pack` even where the tensor copies
+// could read them from q and d (the allocation-free call keeps them in its
+// static array).
 int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, const float *d,
 	       uint32_t m, float *const *ys, uint8_t *pack, cudaStream_t st,
-	       const QmmGather *gth = nullptr)
+	       const QmmGather *gth = nullptr, bool pack_always = false)
 {
 	if (!n || n > (unsigned)QMM_MAX_TENSORS)
 		return -1;
@@ -533,7 +536,7 @@ int launch_qmm(charsiu_gpu *g, const int *ids, unsigned n, const int8_t *q, cons
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 
 	QmmParams p = {};
-	p.use_map = qmm_act_maps(q, d, m, nb, na, &p.qmap, &p.dmap) ? 1u : 0u;
+	p.use_map = !pack_always && qmm_act_maps(q, d, m, nb, na, &p.qmap, &p.dmap) ? 1u : 0u;
 	if (!p.use_map) {
 		const uint64_t items = (uint64_t)mt * nseg * (SB * 2 * na + SB * na);
 		cudaLaunchConfig_t pc = {};
@@ -1680,9 +1683,10 @@ int charsiu_gpu_matvec_gather_dev(struct charsiu_gpu *g, const int *ids, unsigne
 
 // The batched q8_0 matvec with nothing allocated: the same pack and
 // tensor-core kernels as charsiu_gpu_matvec_batch_dev, with the packed
-// activations in noalloc_scratch. The pack step writes every byte the matmul
-// then reads (padding zeroed), so no clearing is needed between calls; calls
-// that overlap on one GPU share the array and race.
+// activations always laid out in noalloc_scratch (not read from q and d by
+// tensor copies, as the _dev form does where it can). The pack step writes
+// every byte the matmul then reads (padding zeroed), so no clearing is needed
+// between calls; calls that overlap on one GPU share the array and race.
 int charsiu_gpu_matvec_batch_noalloc(struct charsiu_gpu *g, int id, unsigned m, const int8_t *q,
 				     const float *d, float *y, void *stream)
 {
@@ -1709,7 +1713,7 @@ int charsiu_gpu_matvec_batch_noalloc(struct charsiu_gpu *g, int id, unsigned m, 
 		return -1;
 	}
 	return launch_qmm(g, &id, 1, q, d, m, &y, scratch,
-			  stream ? (cudaStream_t)stream : g->stream);
+			  stream ? (cudaStream_t)stream : g->stream, nullptr, true);
 }
 
 int charsiu_gpu_act_quantise_dev(struct charsiu_gpu *g, const float *x, unsigned m, unsigned k,

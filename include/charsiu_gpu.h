@@ -219,7 +219,9 @@ CHARSIU_GPU_API int charsiu_gpu_matvec_batch_gather_dev(struct charsiu_gpu *g, c
  * a staging buffer with cudaMalloc on first use). This call allocates
  * nothing: its scratch is a fixed 1 MiB array inside the library, held on
  * every GPU that loads it until exit. q8_0 tensors only; the m activations
- * are packed in tiles of 16 or 32 and must fit that array (m <= 64 up to
+ * are always packed into that array first, in tiles of 16 or 32 (the _dev
+ * form reads them from q and d by tensor copies where it can), and must fit
+ * it (m <= 64 up to
  * K = 14336), else -1 with the reason in charsiu_gpu_error. All calls on a GPU
  * share the array, so two calls running on it at the same time race. A
  * layer's first call looks up the array's device address (on the layer's

@@ -45,11 +45,16 @@ def test_noalloc_matches_batch_dev_on_two_calls_in_a_row():
             cases.append((m, q, d, ref))
         torch.cuda.synchronize()
         outs = []
+        before = L.launches
         for m, q, d, _ in cases:                 # the two allocation-free calls, back to back
             y = torch.full((m, n), float("nan"), device=dev)
             assert L.batch_noalloc(tid, m, q.data_ptr(), d.data_ptr(), y.data_ptr(), stream) == 0
             outs.append(y)
         torch.cuda.synchronize()
+        # two launches a call: the packing into the library's array, then the
+        # tensor-core matvec reading it (never the tensor copies from q and d
+        # that the _dev form uses where it can)
+        assert L.launches - before == 2 * len(cases)
         for (m, _, _, ref), y in zip(cases, outs):
             a = y.cpu().numpy().view(np.uint32)
             b = ref.cpu().numpy().view(np.uint32)
